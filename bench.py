@@ -1,0 +1,434 @@
+"""Throughput of the fused Mamba S6 block forward on B200 (tokens/s = B*T / s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 0|1|2|3]
+
+Workload (default --config 0): one Mamba S6 block forward in float32,
+d_model=768, d_inner=1536, d_state=24, d_conv=4, dt_rank=48, batch 151 x 180
+tokens -- the shape the headline target is quoted on.  Synthetic seeded data:
+x ~ N(0,1); Kaiming-uniform linear weights; conv ~ U(-0.5, 0.5);
+A_log = log(1..S); D = 1; dt_proj.bias = softplus^-1(log-uniform[1e-3, 0.1]).
+Other configs are measurement aids: 1 = bf16 B=8 T=8192 (S=16); 2 = stateful
+decode B=64 (d_model 1024): metric over forward_step calls; 3 = int8 weights,
+d_model 1536, B=32 T=2048.
+
+Multi-GPU: one process per GPU (torchrun); each rank runs its own batch
+(weak scaling, no data-path collective); time = max over ranks of the
+CUDA-event time of the K timed steps.  Inputs rotate over >= 4 buffers whose
+total exceeds the 126 MB L2, and every step moves > 1 GB through HBM.
+
+--impl reference times the reference's CPU implementation on the host cores:
+the block composition in torch CPU ops (the same ATen calls the reference
+makes) around the reference's own compiled C++ scan op from oracle/_ref (the
+oracle's C restatement when that was not built).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "fused Mamba block tokens/s (B·T/s) at 1/2/4/8 B200; % of HBM roofline"
+L2_BYTES = 126 * 2 ** 20
+
+CONFIGS = {
+    0: dict(workload="mamba_block_fwd_f32_b151_t180", d_model=768, d_state=24, batch=151,
+            seqlen=180, dtype="f32", mode="forward"),
+    1: dict(workload="mamba_block_fwd_bf16_b8_t8192", d_model=768, d_state=16, batch=8,
+            seqlen=8192, dtype="bf16", mode="forward"),
+    2: dict(workload="mamba_block_step_f32_b64_dm1024", d_model=1024, d_state=16, batch=64,
+            seqlen=512, dtype="f32", mode="step", dt_rank=64),
+    3: dict(workload="mamba_block_fwd_int8_b32_t2048_dm1536", d_model=1536, d_state=16,
+            batch=32, seqlen=2048, dtype="f32", mode="forward", quant="int8", dt_rank=96),
+}
+
+
+def peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ----------------------------------------------------------------- helpers
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of the GPU's clocks during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        try:
+            self.index = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            self.index = str(device.index or 0)
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_params(cfg, seed):
+    """Seeded synthetic block parameters (same recipe as the oracle's generator,
+    restated here so the product path does not import the oracle)."""
+    g = torch.Generator().manual_seed(seed)
+    dm, S = cfg["d_model"], cfg["d_state"]
+    di = 2 * dm
+    R = cfg.get("dt_rank", math.ceil(dm / 16))
+
+    def lin(o, i):
+        if cfg.get("quant"):
+            w = torch.randn(o, i, generator=g) * 0.02
+            m = torch.rand(o, i, generator=g) < 0.01
+            return torch.where(m, torch.where(torch.rand(o, i, generator=g) < 0.5, -0.5, 0.5), w)
+        b = 1.0 / math.sqrt(i)
+        return (torch.rand(o, i, generator=g) * 2 - 1) * b
+
+    p = {"in_proj.weight": lin(2 * di, dm),
+         "conv1d.weight": torch.rand(di, 1, 4, generator=g) - 0.5,
+         "conv1d.bias": torch.rand(di, generator=g) - 0.5,
+         "x_proj.weight": lin(R + 2 * S, di), "dt_proj.weight": lin(di, R),
+         "out_proj.weight": lin(dm, di),
+         "A_log": torch.log(torch.arange(1, S + 1, dtype=torch.float32).repeat(di, 1)),
+         "D": torch.ones(di)}
+    u = torch.rand(di, generator=g)
+    dt = torch.exp(u * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3))
+    p["dt_proj.bias"] = dt + torch.log(-torch.expm1(-dt))
+    return p, R
+
+
+# ------------------------------------------------------------- our arm
+def run_ours(args, cfg):
+    from cpu_mamba_b200 import CPUMamba, QuantConfig, quantize_block
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    dtype = torch.float32 if cfg["dtype"] == "f32" else torch.bfloat16
+    p, R = make_params(cfg, seed=0)
+    m = CPUMamba(cfg["d_model"], d_state=cfg["d_state"], dt_rank=R).eval()
+    m.load_state_dict(p, strict=True)
+    m = m.to(device=dev, dtype=dtype)
+    if cfg.get("quant"):
+        quantize_block(m, QuantConfig(cfg["quant"]))
+    B, T, dm = cfg["batch"], cfg["seqlen"], cfg["d_model"]
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    step_mode = cfg["mode"] == "step"
+    in_shape = (B, dm) if step_mode else (B, T, dm)
+    in_bytes = math.prod(in_shape) * (4 if dtype == torch.float32 else 2)
+    nbuf = max(4, math.ceil(2 * L2_BYTES / in_bytes)) if not step_mode else 8
+    xs = [torch.randn(in_shape, generator=g, device=dev).to(dtype) for _ in range(nbuf)]
+    state = None
+    if step_mode:
+        with torch.no_grad():
+            prompt = torch.randn(B, T, dm, generator=g, device=dev).to(dtype)
+            _, state = m.forward_with_final_state(prompt)
+
+    def step(i):
+        with torch.no_grad():
+            if step_mode:
+                return m.forward_step(xs[i % nbuf], state)[0]
+            return m(xs[i % nbuf])
+
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    if ws > 1:
+        torch.distributed.barrier()
+    ms = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = t.item()
+    tokens_per_step = B * (1 if step_mode else T)
+    value = ws * tokens_per_step * args.steps / (ms / 1e3)
+
+    # end to end through the public API from pinned host buffers
+    host_in = torch.empty(in_shape, dtype=dtype, pin_memory=True)
+    host_in.copy_(xs[0].cpu())
+    host_out = torch.empty(in_shape, dtype=dtype, pin_memory=True)
+    e2e_ms = []
+    for i in range(max(3, min(args.steps, 10)) + 1):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        xd = host_in.to(dev, non_blocking=True)
+        y = step_e2e(m, xd, state, step_mode)
+        host_out.copy_(y, non_blocking=True)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        if i > 0:
+            e2e_ms.append(a.elapsed_time(b))
+    e2e_t = statistics.median(e2e_ms)
+    e2e = {"value": ws * tokens_per_step / (e2e_t / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": in_bytes}
+
+    stages = profile_stages(m, xs[0], cfg, dtype, args.steps) if not step_mode else {}
+    result = None
+    if rank == 0:
+        hbm, bf16, bf16_s, src = peaks()
+        roof = roofline(stages, cfg, hbm, bf16, src)
+        launches_per_step = 5
+        result = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": cfg["dtype"], "data": "synthetic (seeded; shapes of the configuration)",
+            "config": {"workload": cfg["workload"], "batch_per_gpu": B, "global_batch": B * ws,
+                       "seq_len": T if not step_mode else 1, "d_model": dm,
+                       "d_inner": 2 * dm, "d_state": cfg["d_state"], "dt_rank": R,
+                       "quant": cfg.get("quant"), "parallelism": f"batch-sharded x{ws}",
+                       "l2": f"inputs rotated over {nbuf} buffers ({nbuf * in_bytes / 2**20:.0f} MB > L2)"},
+            "roofline": roof, "stages_ms": stages, "e2e": e2e,
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return result
+
+
+def step_e2e(m, xd, state, step_mode):
+    with torch.no_grad():
+        if step_mode:
+            return m.forward_step(xd, state)[0]
+        return m(xd)
+
+
+def profile_stages(m, x, cfg, dtype, steps):
+    """Per-stage CUDA-event durations (same stream, averaged over `steps` runs)
+    of the five launches of one forward, issued through the stage entry points."""
+    from cpu_mamba_b200 import ops
+    from cpu_mamba_b200.quant import QuantizedLinear
+    if any(isinstance(getattr(m, n), QuantizedLinear) for n in ("in_proj", "x_proj", "out_proj")):
+        return {}
+    dev = x.device
+    B, T, dm = x.shape
+    di, S, R = m.d_inner, m.d_state, m.dt_rank
+    stream = torch.cuda.current_stream(dev)
+    split = {n: (m._tf32_split(n, getattr(m, n).weight) if dtype == torch.float32 else None)
+             for n in ("in_proj", "x_proj", "out_proj")}
+    x2 = x.reshape(B * T, dm)
+    times = {k: [] for k in ("in_proj", "conv1d_silu", "x_proj", "scan_fused", "out_proj")}
+    n = max(3, min(steps, 20))
+    for it in range(n + 1):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        with torch.no_grad():
+            ev[0].record(stream)
+            xz = ops.linear(x2, m.in_proj.weight, None, split["in_proj"])
+            ev[1].record(stream)
+            xc = ops.conv1d_silu(xz, m.conv1d.weight, m.conv1d.bias, B, T, di)
+            ev[2].record(stream)
+            xdbl = ops.linear(xc, m.x_proj.weight, None, split["x_proj"])
+            ev[3].record(stream)
+            y = ops.scan_fused(xc, xdbl, xz[:, di:], m.dt_proj.weight, m.dt_proj.bias, m.A_log,
+                               m.D, B, T)
+            ev[4].record(stream)
+            ops.linear(y, m.out_proj.weight, None, split["out_proj"])
+            ev[5].record(stream)
+        torch.cuda.synchronize(dev)
+        if it > 0:
+            for i, k in enumerate(times):
+                times[k].append(ev[i].elapsed_time(ev[i + 1]))
+    return {k: statistics.mean(v) for k, v in times.items()}
+
+
+def roofline(stages, cfg, hbm_gbs, bf16_tflops, src):
+    if not stages:
+        return None
+    B, T, dm, S = cfg["batch"], cfg["seqlen"], cfg["d_model"], cfg["d_state"]
+    di = 2 * dm
+    R = cfg.get("dt_rank", math.ceil(dm / 16))
+    es = 4 if cfg["dtype"] == "f32" else 2
+    N = B * T
+    flops = {"in_proj": 2 * N * dm * 2 * di, "x_proj": 2 * N * di * (R + 2 * S),
+             "out_proj": 2 * N * di * dm}
+    # algorithmic bytes of the HBM-bound stages (each tensor read / written once)
+    nbytes = {"conv1d_silu": N * di * es * 2,
+              "scan_fused": N * es * (3 * di + R + 2 * S)}
+    top = max(stages, key=stages.get)
+    t = stages[top] / 1e3
+    if top in flops:
+        ach = flops[top] / t / 1e12
+        return {"kernel": top, "bound": "tensor", "achieved": ach, "peak": bf16_tflops,
+                "unit": "TFLOP/s", "frac": ach / bf16_tflops, "traffic": None,
+                "peak_source": f"{src} bf16 dense"}
+    ach = nbytes[top] / t / 1e9
+    return {"kernel": top, "bound": "hbm", "achieved": ach, "peak": hbm_gbs, "unit": "GB/s",
+            "frac": ach / hbm_gbs, "traffic": None, "peak_source": f"{src} HBM copy"}
+
+
+# ------------------------------------------------------- reference arm / CPU
+def cpu_forward_setup(cfg, batch):
+    import oracle
+    p, R = make_params(cfg, seed=0)
+    op = oracle.load_ref_scan_op()
+    kind = "reference" if op is not None else "port"
+    g = torch.Generator().manual_seed(1234)
+    x = torch.randn(batch, cfg["seqlen"], cfg["d_model"], generator=g)
+    if cfg["dtype"] == "bf16":
+        p = {k: v.to(torch.bfloat16) for k, v in p.items()}
+        x = x.to(torch.bfloat16)
+    return oracle, p, op, kind, x
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(cfg, min_seconds=10.0, max_runs=10):
+    """The reference's CPU block forward on a bounded sample of the workload."""
+    if cfg["mode"] != "forward" or cfg.get("quant"):
+        return None
+    cores = cpu_cores()
+    torch.set_num_threads(cores)
+    batch = cfg["batch"] if cfg["batch"] * cfg["seqlen"] <= 30000 else 1
+    oracle, p, op, kind, x = cpu_forward_setup(cfg, batch)
+    oracle.block_forward(p, x, scan_op=op)            # warm-up
+    ts, t_start = [], time.perf_counter()
+    while len(ts) < 3 or (time.perf_counter() - t_start < min_seconds and len(ts) < max_runs):
+        t0 = time.perf_counter()
+        oracle.block_forward(p, x, scan_op=op)
+        ts.append(time.perf_counter() - t0)
+    tok = batch * cfg["seqlen"]
+    return {"value": tok / statistics.median(ts), "unit": "tokens/s", "cores": cores,
+            "kind": kind, "sample": f"{batch} x {cfg['seqlen']} tokens per forward, median of {len(ts)}"}
+
+
+def run_reference(args, cfg):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return None
+    if cfg["mode"] != "forward" or cfg.get("quant"):
+        return {"impl": "reference", "unavailable": "reference arm covers the forward workloads only"}
+    cores = cpu_cores()
+    torch.set_num_threads(cores)
+    batch = min(cfg["batch"], 16) if cfg["batch"] * cfg["seqlen"] <= 30000 else 1
+    oracle, p, op, kind, x = cpu_forward_setup(cfg, batch)
+    for _ in range(args.warmup):
+        oracle.block_forward(p, x, scan_op=op)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.block_forward(p, x, scan_op=op)
+    dt = time.perf_counter() - t0
+    tok = batch * cfg["seqlen"]
+    value = tok * args.steps / dt
+    sample = f"{batch} x {cfg['seqlen']} tokens per step (batch rows are independent)"
+    return {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic (seeded)",
+            "config": {"workload": cfg["workload"], "batch_sample": batch, "seq_len": cfg["seqlen"],
+                       "d_model": cfg["d_model"], "d_state": cfg["d_state"]},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", type=int, default=0, choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        res = run_reference(args, cfg)
+    else:
+        res = run_ours(args, cfg)
+        ws, rank, _ = dist_env()
+        if res is not None and ws == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline(cfg)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

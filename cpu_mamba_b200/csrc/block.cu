@@ -1,0 +1,235 @@
+// Block-level composition of the Mamba S6 forward (src/cpu_mamba/_mamba.py:204-265),
+// the forward_with_final_state state outputs (:165-202) and the single-token
+// step (:103-163), plus the linear-layer entry points.
+//
+// Forward pipeline (5 launches, caller-provided workspace, no allocation):
+//   1. in_proj            x (N, dm)       -> xz (N, 2di)
+//   2. conv1d + SiLU      xz[:, :di]      -> xc (N, di)   [+ conv tail]
+//   3. x_proj             xc              -> xdbl (N, ldx) segments dt_low | B | C,
+//                                            each starting on an 8-element boundary
+//   4. fused scan         xc, xdbl, xz[:, di:] -> y (N, di) [+ h_last]
+//      (dt_proj + softplus + exp(dt A) + recurrence + D skip + SiLU(z) gate)
+//   5. out_proj           y               -> out (N, dm)
+#include "common.cuh"
+
+namespace mb2 {
+
+int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
+              const float *scale, const void *bias, void *y, int64_t ld_y, int64_t M,
+              int64_t N, int64_t K, int64_t n1, int64_t off1, int64_t n2, int64_t off2,
+              cudaStream_t st);
+int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *w_split,
+            const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
+            int64_t n1, int64_t off1, int64_t n2, int64_t off2, cudaStream_t st, bool *used);
+int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const void *bias,
+                void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
+                int64_t d_inner, int64_t d_conv, cudaStream_t st);
+int scan_fused_segments(int dtype, const void *xc, int64_t ld_xc, const void *dl,
+                        const void *bm, const void *cm, int64_t ld_row, const void *z,
+                        int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
+                        const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
+                        int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
+                        int64_t dt_rank, cudaStream_t stream);
+
+// Dense linear: tensor-core kernel where it applies, CUDA-core kernel otherwise.
+static int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, void *y,
+                      int64_t ld_y, int64_t M, int64_t N, int64_t K, int64_t n1 = -1,
+                      int64_t off1 = 0, int64_t n2 = -1, int64_t off2 = 0,
+                      cudaStream_t st = nullptr) {
+    if (n1 < 0) n1 = N;
+    if (n2 < 0) n2 = N;
+    if (L.scheme != MB2_Q_NONE)
+        return gemm_simt(dtype, L.scheme, x, ld_x, L.weight_q, L.scale, L.bias, y, ld_y, M, N, K,
+                         n1, off1, n2, off2, st);
+    MB2_REQUIRE(L.weight, MB2_ERR_ARG, "linear: null weight");
+    bool used = false;
+    MB2_TRY(gemm_tc(dtype, x, ld_x, L.weight, L.weight_split, L.bias, y, ld_y, M, N, K, n1, off1,
+                    n2, off2, st, &used));
+    if (used) return MB2_OK;
+    return gemm_simt(dtype, MB2_Q_NONE, x, ld_x, L.weight, nullptr, L.bias, y, ld_y, M, N, K,
+                     n1, off1, n2, off2, st);
+}
+
+struct Layout {
+    int64_t N, di, dm, S, R, K;
+    int64_t RB, RC, ldx;   // x_dbl segment offsets and row length
+    size_t es;
+    size_t off_xz, off_xc, off_xdbl, off_y, total;
+};
+
+static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+static Layout make_layout(const mb2_block *b, int64_t rows) {
+    Layout l{};
+    l.N = rows;
+    l.di = b->d_inner; l.dm = b->d_model; l.S = b->d_state; l.R = b->dt_rank; l.K = b->d_conv;
+    l.RB = round_up(l.R, 8);
+    l.RC = l.RB + round_up(l.S, 8);
+    l.ldx = l.RC + round_up(l.S, 8);
+    l.es = dtype_size(b->dtype);
+    size_t off = 0;
+    l.off_xz = off; off = align256(off + (size_t)rows * 2 * l.di * l.es);
+    l.off_xc = off; off = align256(off + (size_t)rows * l.di * l.es);
+    l.off_xdbl = off; off = align256(off + (size_t)rows * l.ldx * l.es);
+    l.off_y = off; off = align256(off + (size_t)rows * l.di * l.es);
+    l.total = off;
+    return l;
+}
+
+static int check_block(const mb2_block *b) {
+    MB2_REQUIRE(b, MB2_ERR_ARG, "block: null descriptor");
+    MB2_REQUIRE(b->dtype == MB2_F32 || b->dtype == MB2_BF16, MB2_ERR_ARG, "block: bad dtype");
+    MB2_REQUIRE(b->d_model > 0 && b->d_inner > 0 && b->d_state >= 1 && b->d_state <= 256 &&
+                    b->dt_rank >= 1 && b->d_conv >= 2,
+                MB2_ERR_SHAPE, "block: bad dimensions");
+    MB2_REQUIRE(b->conv_w && b->A_log, MB2_ERR_ARG, "block: missing conv1d.weight / A_log");
+    // the fused scan keeps dt_proj's weight rows in registers: a quantised
+    // dt_proj passes its dequantised weight here as well
+    MB2_REQUIRE(b->dt_proj.weight, MB2_ERR_ARG, "block: dt_proj.weight (dense) is required");
+    if (b->dtype == MB2_BF16)
+        MB2_REQUIRE(b->d_inner % 2 == 0 && b->dt_rank % 2 == 0 && b->d_state % 2 == 0,
+                    MB2_ERR_UNSUPPORTED, "block(bf16): d_inner, dt_rank, d_state must be even");
+    return MB2_OK;
+}
+
+// ------------------------------------------------------------- step conv ---
+// forward_step's conv (_mamba.py:128-139): window = [conv_state | x], output
+// silu(bias + sum_k w[k] * window[k]), conv_state <- window[1:] (in place).
+template <typename T, int K>
+__global__ void conv_step_kernel(const T *__restrict__ xz, int64_t ld_xz, const T *__restrict__ w,
+                                 const T *__restrict__ bias, T *__restrict__ conv_state,
+                                 T *__restrict__ xc, int64_t batch, int64_t d_inner) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch * d_inner) return;
+    const int64_t b = i / d_inner, d = i - b * d_inner;
+    T *cs = conv_state + i * (K - 1);
+    float win[K];
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) win[k] = io<T>::to_f(cs[k]);
+    win[K - 1] = io<T>::to_f(xz[b * ld_xz + d]);
+    float acc = bias ? io<T>::to_f(bias[d]) : 0.0f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc = fmaf(io<T>::to_f(w[d * K + k]), win[k], acc);
+    xc[b * d_inner + d] = io<T>::from_f(silu_f(io<T>::round(acc)));
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) cs[k] = io<T>::from_f(win[k + 1]);
+}
+
+template <typename T>
+static int launch_conv_step(int K, const void *xz, int64_t ld_xz, const void *w, const void *bias,
+                            void *conv_state, void *xc, int64_t batch, int64_t di,
+                            cudaStream_t st) {
+    const unsigned grid = (unsigned)ceil_div(batch * di, 256);
+    switch (K) {
+#define MB2_CS(KK)                                                                          \
+    case KK:                                                                                \
+        conv_step_kernel<T, KK><<<grid, 256, 0, st>>>(                                      \
+            (const T *)xz, ld_xz, (const T *)w, (const T *)bias, (T *)conv_state, (T *)xc, \
+            batch, di);                                                                     \
+        return check_launch("conv_step_kernel");
+        MB2_CS(2) MB2_CS(3) MB2_CS(4) MB2_CS(5) MB2_CS(6) MB2_CS(7) MB2_CS(8)
+#undef MB2_CS
+    }
+    return fail(MB2_ERR_UNSUPPORTED, "step: d_conv %d not in [2, 8]", K);
+}
+
+}  // namespace mb2
+
+using namespace mb2;
+
+extern "C" int mb2_linear(int dtype, const void *x, int64_t ld_x, const void *w,
+                          const float *w_split, const void *bias, void *y, int64_t ld_y,
+                          int64_t M, int64_t N, int64_t K, mb2_stream_t stream) {
+    MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "linear: bad dtype");
+    MB2_REQUIRE(ld_x >= K && ld_y >= N, MB2_ERR_SHAPE, "linear: leading dimension too small");
+    mb2_linear_w L{w, w_split, nullptr, nullptr, bias, MB2_Q_NONE};
+    return linear_any(dtype, L, x, ld_x, y, ld_y, M, N, K, -1, 0, -1, 0, (cudaStream_t)stream);
+}
+
+extern "C" int mb2_qlinear(int scheme, int dtype, const void *x, int64_t ld_x,
+                           const void *weight_q, const float *scale, const void *bias, void *y,
+                           int64_t ld_y, int64_t M, int64_t N, int64_t K, mb2_stream_t stream) {
+    MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "qlinear: bad dtype");
+    MB2_REQUIRE(scheme == MB2_Q_INT8 || scheme == MB2_Q_INT4 || scheme == MB2_Q_NF4, MB2_ERR_ARG,
+                "unknown scheme %d", scheme);
+    MB2_REQUIRE(ld_x >= K && ld_y >= N, MB2_ERR_SHAPE, "qlinear: leading dimension too small");
+    return gemm_simt(dtype, scheme, x, ld_x, weight_q, scale, bias, y, ld_y, M, N, K, N, 0, N, 0,
+                     (cudaStream_t)stream);
+}
+
+extern "C" size_t mb2_block_workspace_bytes(const mb2_block *blk, int64_t batch, int64_t seqlen) {
+    if (!blk || batch < 0 || seqlen < 0) return 0;
+    return make_layout(blk, batch * seqlen).total;
+}
+
+extern "C" int mb2_block_forward(const mb2_block *blk, const void *x, void *out, int64_t batch,
+                                 int64_t seqlen, float *h_last, void *conv_tail, void *workspace,
+                                 size_t workspace_bytes, mb2_stream_t stream) {
+    MB2_TRY(check_block(blk));
+    MB2_REQUIRE(batch >= 0 && seqlen >= 0, MB2_ERR_SHAPE, "block: negative size");
+    const mb2_block &b = *blk;
+    cudaStream_t st = (cudaStream_t)stream;
+    const Layout l = make_layout(blk, batch * seqlen);
+    MB2_REQUIRE(workspace_bytes >= l.total, MB2_ERR_WORKSPACE,
+                "block: workspace %zu < required %zu", workspace_bytes, l.total);
+    if (batch == 0) return MB2_OK;
+    char *ws = static_cast<char *>(workspace);
+    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl, *y = ws + l.off_y;
+    const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
+    const size_t es = l.es;
+    if (N > 0) {
+        MB2_REQUIRE(x && out && workspace, MB2_ERR_ARG, "block: null pointer");
+        MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, N, 2 * di, l.dm, -1, 0, -1, 0, st));
+    }
+    MB2_TRY(conv1d_silu(b.dtype, xz, 2 * di, b.conv_w, b.conv_b, xc, di, conv_tail, batch, seqlen,
+                        di, b.d_conv, st));
+    if (N > 0) {
+        MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, R, l.RB - R,
+                           R + S, l.RC - l.RB - S, st));
+    }
+    MB2_TRY(scan_fused_segments(b.dtype, xc, di, xdbl, (char *)xdbl + l.RB * es,
+                                (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
+                                b.dt_proj.weight, b.dt_proj.bias, b.A_log, b.D, nullptr, h_last, y,
+                                di, batch, seqlen, di, S, R, st));
+    if (N > 0)
+        MB2_TRY(linear_any(b.dtype, b.out_proj, y, di, out, l.dm, N, l.dm, di, -1, 0, -1, 0, st));
+    return MB2_OK;
+}
+
+extern "C" size_t mb2_step_workspace_bytes(const mb2_block *blk, int64_t batch) {
+    if (!blk || batch < 0) return 0;
+    return make_layout(blk, batch).total;
+}
+
+extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, float *h,
+                              void *conv_state, int64_t batch, void *workspace,
+                              size_t workspace_bytes, mb2_stream_t stream) {
+    MB2_TRY(check_block(blk));
+    MB2_REQUIRE(batch >= 0, MB2_ERR_SHAPE, "step: negative batch");
+    const mb2_block &b = *blk;
+    cudaStream_t st = (cudaStream_t)stream;
+    const Layout l = make_layout(blk, batch);
+    MB2_REQUIRE(workspace_bytes >= l.total, MB2_ERR_WORKSPACE,
+                "step: workspace %zu < required %zu", workspace_bytes, l.total);
+    if (batch == 0) return MB2_OK;
+    MB2_REQUIRE(x && out && h && conv_state && workspace, MB2_ERR_ARG, "step: null pointer");
+    char *ws = static_cast<char *>(workspace);
+    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl, *y = ws + l.off_y;
+    const int64_t di = l.di, S = l.S, R = l.R;
+    const size_t es = l.es;
+    MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, batch, 2 * di, l.dm, -1, 0, -1, 0, st));
+    if (b.dtype == MB2_F32)
+        MB2_TRY(launch_conv_step<float>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b, conv_state,
+                                        xc, batch, di, st));
+    else
+        MB2_TRY(launch_conv_step<__nv_bfloat16>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b,
+                                                conv_state, xc, batch, di, st));
+    MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, batch, R + 2 * S, di, R, l.RB - R,
+                       R + S, l.RC - l.RB - S, st));
+    // one timestep of the fused scan, h read and written in place
+    MB2_TRY(scan_fused_segments(b.dtype, xc, di, xdbl, (char *)xdbl + l.RB * es,
+                                (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
+                                b.dt_proj.weight, b.dt_proj.bias, b.A_log, b.D, h, h, y, di, batch,
+                                1, di, S, R, st));
+    return linear_any(b.dtype, b.out_proj, y, di, out, l.dm, batch, l.dm, di, -1, 0, -1, 0, st);
+}

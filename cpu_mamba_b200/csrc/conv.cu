@@ -1,0 +1,129 @@
+// Causal depthwise conv1d + bias + SiLU (src/cpu_mamba/_mamba.py:211-215):
+//   xc[b,t,d] = silu(bias[d] + sum_k w[d,k] * x[b, t-(K-1)+k, d]),  x[b,<0,d] = 0
+// reading the x half of in_proj's output in place (row stride ld_in) and
+// writing xc token-major.  Optionally also writes the conv tail of
+// forward_with_final_state (_mamba.py:180): the last K-1 pre-conv inputs per
+// (b, d), zero-left-padded for short sequences.
+//
+// HBM-bound: each thread owns one channel and CONV_TT consecutive timesteps,
+// keeping the K-1 history in registers; consecutive threads are consecutive
+// channels, so every row access is a coalesced 128-byte-per-warp segment.
+#include "common.cuh"
+
+namespace mb2 {
+
+constexpr int CONV_TT = 32;   // timesteps per thread
+constexpr int CONV_KMAX = 8;  // max supported d_conv
+
+template <typename T, int K>
+__global__ void __launch_bounds__(128)
+conv1d_silu_kernel(const T *__restrict__ x, int64_t ld_in, const T *__restrict__ w,
+                   const T *__restrict__ bias, T *__restrict__ xc, int64_t ld_out,
+                   T *__restrict__ tail, int64_t seqlen, int64_t d_inner) {
+    const int64_t d = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t t0 = (int64_t)blockIdx.y * CONV_TT;
+    const int64_t b = blockIdx.z;
+    if (d >= d_inner) return;
+    float wk[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) wk[k] = io<T>::to_f(w[d * K + k]);
+    const float bv = bias ? io<T>::to_f(bias[d]) : 0.0f;
+    const int64_t row0 = b * seqlen;
+    float hist[K];  // hist[K-1] is the current input
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) {
+        const int64_t t = t0 - (K - 1) + k;
+        hist[k] = (t >= 0) ? io<T>::to_f(x[(row0 + t) * ld_in + d]) : 0.0f;
+    }
+    const int64_t t_end = (t0 + CONV_TT < seqlen) ? t0 + CONV_TT : seqlen;
+    for (int64_t t = t0; t < t_end; ++t) {
+        hist[K - 1] = io<T>::to_f(x[(row0 + t) * ld_in + d]);
+        float acc = bv;
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fmaf(wk[k], hist[k], acc);
+        const float v = io<T>::round(acc);
+        xc[(row0 + t) * ld_out + d] = io<T>::from_f(silu_f(v));
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k) hist[k] = hist[k + 1];
+    }
+    if (tail && t_end == seqlen) {
+        // after the loop hist[0..K-2] hold x[T-K+1 .. T-1] (zeros before t=0)
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k)
+            tail[(b * d_inner + d) * (K - 1) + k] = io<T>::from_f(hist[k]);
+    }
+}
+
+template <typename T, int K>
+static int launch_conv(const void *x, int64_t ld_in, const void *w, const void *bias, void *xc,
+                       int64_t ld_out, void *tail, int64_t batch, int64_t seqlen, int64_t di,
+                       cudaStream_t st) {
+    dim3 grid((unsigned)ceil_div(di, 128), (unsigned)ceil_div(seqlen, CONV_TT), (unsigned)batch);
+    conv1d_silu_kernel<T, K><<<grid, 128, 0, st>>>(
+        static_cast<const T *>(x), ld_in, static_cast<const T *>(w), static_cast<const T *>(bias),
+        static_cast<T *>(xc), ld_out, static_cast<T *>(tail), seqlen, di);
+    return check_launch("conv1d_silu_kernel");
+}
+
+template <typename T>
+static int dispatch_conv(int K, const void *x, int64_t ld_in, const void *w, const void *bias,
+                         void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
+                         int64_t di, cudaStream_t st) {
+    switch (K) {
+#define MB2_CONV_CASE(KK) \
+    case KK: return launch_conv<T, KK>(x, ld_in, w, bias, xc, ld_out, tail, batch, seqlen, di, st);
+        MB2_CONV_CASE(2) MB2_CONV_CASE(3) MB2_CONV_CASE(4) MB2_CONV_CASE(5)
+        MB2_CONV_CASE(6) MB2_CONV_CASE(7) MB2_CONV_CASE(8)
+#undef MB2_CONV_CASE
+    }
+    return fail(MB2_ERR_UNSUPPORTED, "conv1d: d_conv %d not in [2, %d]", K, CONV_KMAX);
+}
+
+// Zero the conv tail when the sequence is empty (the loop above never runs).
+template <typename T>
+__global__ void zero_kernel(T *p, int64_t n) {
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = io<T>::from_f(0.0f);
+}
+
+int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const void *bias,
+                void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
+                int64_t d_inner, int64_t d_conv, cudaStream_t st) {
+    MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "conv1d: bad dtype");
+    MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0, MB2_ERR_SHAPE, "conv1d: negative size");
+    MB2_REQUIRE(d_conv >= 2 && d_conv <= CONV_KMAX, MB2_ERR_UNSUPPORTED,
+                "conv1d: d_conv %lld not in [2, %d]", (long long)d_conv, CONV_KMAX);
+    MB2_REQUIRE(batch < 65536 && ceil_div(seqlen, CONV_TT) < 65536, MB2_ERR_SHAPE,
+                "conv1d: batch or seqlen too large");
+    if (batch == 0 || d_inner == 0) return MB2_OK;
+    MB2_REQUIRE(w, MB2_ERR_ARG, "conv1d: null weight");
+    if (seqlen == 0) {
+        if (tail) {
+            const int64_t n = batch * d_inner * (d_conv - 1);
+            if (dtype == MB2_F32)
+                zero_kernel<float><<<(unsigned)ceil_div(n, 256), 256, 0, st>>>((float *)tail, n);
+            else
+                zero_kernel<__nv_bfloat16><<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(
+                    (__nv_bfloat16 *)tail, n);
+            return check_launch("zero_kernel");
+        }
+        return MB2_OK;
+    }
+    MB2_REQUIRE(x_in && xc, MB2_ERR_ARG, "conv1d: null pointer");
+    MB2_REQUIRE(ld_in >= d_inner && ld_out >= d_inner, MB2_ERR_SHAPE, "conv1d: leading dim too small");
+    if (dtype == MB2_F32)
+        return dispatch_conv<float>((int)d_conv, x_in, ld_in, w, bias, xc, ld_out, tail, batch,
+                                    seqlen, d_inner, st);
+    return dispatch_conv<__nv_bfloat16>((int)d_conv, x_in, ld_in, w, bias, xc, ld_out, tail,
+                                        batch, seqlen, d_inner, st);
+}
+
+}  // namespace mb2
+
+extern "C" int mb2_conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w,
+                               const void *bias, void *xc, int64_t ld_out, void *conv_tail,
+                               int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_conv,
+                               mb2_stream_t stream) {
+    return mb2::conv1d_silu(dtype, x_in, ld_in, w, bias, xc, ld_out, conv_tail, batch, seqlen,
+                            d_inner, d_conv, (cudaStream_t)stream);
+}

@@ -1,0 +1,168 @@
+"""Weight-only int8 / int4 / nf4 quantisation with the API of
+src/cpu_mamba/quant.py: QuantConfig, quantize_/dequantize_{int8,int4,nf4},
+QuantizedLinear (buffers ``weight_q`` and ``scale``), quantize_block and
+memory_footprint.
+
+Codes, packed bytes, scales and dequantised weights are bit-exact with the
+reference (quant.py:60-134); the arithmetic runs in CUDA kernels
+(csrc/quant.cu).  QuantizedLinear.forward never materialises the dequantised
+weight: the GEMM's weight loader dequantises tiles on the fly (csrc/gemm_simt.cu).
+
+Tensors on the CPU are quantised on the current CUDA device and the results
+returned to the input's device, so a module can be quantised before or after
+``.cuda()``.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Iterable, Optional
+
+import torch
+import torch.nn as nn
+
+from . import ops
+
+_NF4_LUT_VALUES = (
+    -1.0, -0.6961928, -0.5250730, -0.39491748,
+    -0.28444138, -0.18477343, -0.09105602, 0.0,
+    0.07958029, 0.16093020, 0.24611230, 0.33791524,
+    0.44070983, 0.56261897, 0.72295684, 1.0,
+)  # QLoRA NormalFloat-4 code book, as in quant.py:35-40
+
+
+@dataclass
+class QuantConfig:
+    """quant.py:47-53."""
+    scheme: str = "int8"  # "int8" | "int4" | "nf4"
+
+    def __post_init__(self):
+        if self.scheme not in ("int8", "int4", "nf4"):
+            raise ValueError(f"unknown scheme {self.scheme!r}")
+
+
+def _on_gpu(t: torch.Tensor) -> torch.Tensor:
+    if t.is_cuda:
+        return t
+    if not torch.cuda.is_available():
+        raise RuntimeError("cpu_mamba_b200 quantisation runs on a CUDA device; none is available")
+    return t.to("cuda")
+
+
+def _quant(scheme, weight):
+    w = _on_gpu(weight.detach())
+    q, s, in_dim = ops.quantize(scheme, w)
+    return q.to(weight.device), s.to(weight.device), in_dim
+
+
+def _dequant(scheme, wq, scale, in_dim):
+    out = ops.dequantize(scheme, _on_gpu(wq), _on_gpu(scale), in_dim)
+    return out.to(wq.device)
+
+
+def quantize_int8(weight: torch.Tensor):
+    """Per-channel symmetric int8 -> (w_q int8 (out, in), scale (out,))."""
+    q, s, _ = _quant("int8", weight)
+    return q, s
+
+
+def dequantize_int8(w_q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    return _dequant("int8", w_q, scale, w_q.shape[1])
+
+
+def quantize_int4(weight: torch.Tensor):
+    """Per-channel symmetric int4, two codes per byte -> (packed, scale, in_dim)."""
+    return _quant("int4", weight)
+
+
+def dequantize_int4(packed: torch.Tensor, scale: torch.Tensor, in_dim: int) -> torch.Tensor:
+    return _dequant("int4", packed, scale, in_dim)
+
+
+def quantize_nf4(weight: torch.Tensor):
+    """Per-channel NF4 codes, two per byte -> (packed, scale, in_dim)."""
+    return _quant("nf4", weight)
+
+
+def dequantize_nf4(packed: torch.Tensor, scale: torch.Tensor, in_dim: int) -> torch.Tensor:
+    return _dequant("nf4", packed, scale, in_dim)
+
+
+class QuantizedLinear(nn.Module):
+    """Drop-in for nn.Linear with weight-only quantisation (quant.py:141-194).
+
+    Buffers: ``weight_q`` (int8, or uint8 packed pairs) and ``scale`` (out,)
+    float32; optional ``bias`` parameter.  ``scheme`` and ``_packed_in_dim``
+    are plain attributes, as in the reference.
+    """
+
+    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor], scheme: str):
+        super().__init__()
+        if scheme not in ("int8", "int4", "nf4"):
+            raise ValueError(f"unknown scheme {scheme!r}")
+        self.scheme = scheme
+        self.in_features = weight.shape[1]
+        self.out_features = weight.shape[0]
+        q, s, in_dim = _quant(scheme, weight)
+        self.register_buffer("weight_q", q)
+        self.register_buffer("scale", s)
+        self._packed_in_dim = in_dim
+        if bias is not None:
+            self.bias = nn.Parameter(bias.detach().clone())
+        else:
+            self.register_parameter("bias", None)
+        self._dense_cache = None  # (key, dequantised weight in a dtype)
+
+    def dequantize_weight(self) -> torch.Tensor:
+        return _dequant(self.scheme, self.weight_q, self.scale, self._packed_in_dim)
+
+    def dense_weight(self, dtype: torch.dtype) -> torch.Tensor:
+        """deq(W).to(dtype) on the module's device, cached while the buffers are unchanged."""
+        key = (self.weight_q.data_ptr(), self.weight_q._version, self.scale.data_ptr(),
+               self.scale._version, dtype)
+        if self._dense_cache is None or self._dense_cache[0] != key:
+            self._dense_cache = (key, self.dequantize_weight().to(dtype).contiguous())
+        return self._dense_cache[1]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.qlinear(x, self.scheme, self.weight_q, self.scale, self.bias, self.in_features)
+
+    def extra_repr(self) -> str:
+        return f"in={self.in_features}, out={self.out_features}, scheme={self.scheme!r}"
+
+
+_QUANTIZABLE_LINEARS = ("in_proj", "x_proj", "dt_proj", "out_proj")
+
+
+def quantize_block(module: nn.Module, config: QuantConfig,
+                   target_names: Iterable[str] = _QUANTIZABLE_LINEARS) -> int:
+    """Replace nn.Linear children named in target_names by QuantizedLinear,
+    recursively and in place; returns the number replaced (quant.py:205-226)."""
+    n_replaced = 0
+    target_set = set(target_names)
+    for _, parent in list(module.named_modules()):
+        for child_name, child in list(parent.named_children()):
+            if isinstance(child, nn.Linear) and child_name in target_set:
+                qlin = QuantizedLinear(
+                    weight=child.weight.detach(),
+                    bias=child.bias.detach() if child.bias is not None else None,
+                    scheme=config.scheme)
+                qlin = qlin.to(device=child.weight.device)
+                setattr(parent, child_name, qlin)
+                n_replaced += 1
+    return n_replaced
+
+
+def memory_footprint(module: nn.Module) -> dict:
+    """Parameter bytes vs quantised-buffer bytes (quant.py:229-245)."""
+    fp_bytes = 0
+    quant_bytes = 0
+    for p in module.parameters():
+        fp_bytes += p.numel() * p.element_size()
+    for name, b in module.named_buffers():
+        nbytes = b.numel() * b.element_size()
+        if name.endswith(".weight_q") or name.endswith(".scale"):
+            quant_bytes += nbytes
+        else:
+            fp_bytes += nbytes
+    return {"param_bytes": fp_bytes, "quant_buffer_bytes": quant_bytes,
+            "total_bytes": fp_bytes + quant_bytes}

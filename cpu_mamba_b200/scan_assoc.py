@@ -1,0 +1,24 @@
+"""The reference's associative-scan entry points (src/cpu_mamba/scan_assoc.py:58-132).
+
+The reference offers recursive-doubling scans as alternative backends that
+compute the same recurrence h_t = exp(dt_t A) h_{t-1} + dt_t B_t x_t as its C++
+op (within fp32 reordering).  On the GPU one sequential-in-time kernel keeps h
+in registers and is bound by the exponentials, not by the time dependence, so
+both names map to it; chunk_T is accepted for API compatibility.
+"""
+from __future__ import annotations
+
+from .ops import selective_scan
+
+
+def selective_scan_assoc(x, dt, A, Bp, Cp, D):
+    """y = scan(x, dt, A, B, C) + D*x, (B, T, d_inner) float32 CUDA tensors."""
+    return selective_scan(x.contiguous(), dt.contiguous(), A.contiguous(), Bp.contiguous(),
+                          Cp.contiguous(), D.contiguous())
+
+
+def selective_scan_assoc_chunked(x, dt, A, Bp, Cp, D, chunk_T: int = 32):
+    """Chunked variant of the reference (scan_assoc.py:81-132); same result."""
+    if chunk_T <= 0:
+        raise ValueError("chunk_T must be positive")
+    return selective_scan_assoc(x, dt, A, Bp, Cp, D)

@@ -1,0 +1,191 @@
+/*
+ * mamba_b200.h -- C ABI of the B200 (sm_100a) Mamba S6 block library.
+ *
+ * Every entry point takes DEVICE pointers (caller-allocated inputs, outputs
+ * and workspace), int64 shapes, a cudaStream_t, and returns an int status
+ * (MB2_OK == 0).  Nothing here allocates device memory.  On failure
+ * mb2_last_error() returns a thread-local message; the Python host layer
+ * turns it into RuntimeError / ValueError like the reference's TORCH_CHECK.
+ *
+ * Layouts are row-major with the last index contiguous.  Activations are
+ * token-major: row n = b * seqlen + t.
+ *
+ * dtype codes: MB2_F32 (float) or MB2_BF16 (__nv_bfloat16 bits as uint16).
+ * Scan state h is always float32; conv state is in the activation dtype,
+ * matching src/cpu_mamba/_mamba.py:87-101.
+ */
+#ifndef MAMBA_B200_H
+#define MAMBA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *mb2_stream_t; /* == cudaStream_t */
+
+enum mb2_status {
+    MB2_OK = 0,
+    MB2_ERR_ARG = 1,          /* null pointer / bad enum */
+    MB2_ERR_SHAPE = 2,        /* inconsistent or unsupported sizes */
+    MB2_ERR_ALIGN = 3,        /* pointer or leading dimension misaligned */
+    MB2_ERR_UNSUPPORTED = 4,  /* valid request this build does not handle */
+    MB2_ERR_CUDA = 5,         /* launch / runtime error */
+    MB2_ERR_WORKSPACE = 6     /* workspace too small */
+};
+
+enum mb2_dtype { MB2_F32 = 0, MB2_BF16 = 1 };
+
+/* Quantisation schemes of src/cpu_mamba/quant.py:47-53 (QuantConfig.scheme). */
+enum mb2_scheme { MB2_Q_NONE = 0, MB2_Q_INT8 = 1, MB2_Q_INT4 = 2, MB2_Q_NF4 = 3 };
+
+/* Library identity and the last error message of the calling thread. */
+int mb2_version(void);
+const char *mb2_last_error(void);
+
+/* ------------------------------------------------------------------------
+ * Selective scan -- drop-in for selective_scan_cpu(x, dt, A, B, C, D) -> y
+ * (src/cpu_mamba/selective_scan_cpu.cpp:19-26, bound at
+ * src/cpu_mamba/_mamba.py:37-43 and called at :244).
+ *   x, dt: (batch, seqlen, d_inner)  A: (d_inner, d_state) (negative)
+ *   B, C:  (batch, seqlen, d_state)  D: (d_inner)
+ *   y:     (batch, seqlen, d_inner)  -- fully overwritten
+ * All contiguous float32; 1 <= d_state <= 256 as in the reference (cpp:39).
+ * h0 (batch, d_inner, d_state) may be NULL (zero initial state); h_last may
+ * be NULL, else receives the final state (the time loop of
+ * forward_with_final_state, src/cpu_mamba/_mamba.py:191-199).
+ * ------------------------------------------------------------------------ */
+int mb2_selective_scan(const float *x, const float *dt, const float *A,
+                       const float *B, const float *C, const float *D,
+                       float *y, int64_t batch, int64_t seqlen,
+                       int64_t d_inner, int64_t d_state, const float *h0,
+                       float *h_last, mb2_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Causal depthwise conv1d + bias + SiLU over the x half of in_proj's output
+ * (src/cpu_mamba/_mamba.py:211-215).
+ *   x_in: (batch*seqlen, ld_in) rows, channels [0, d_inner) are read
+ *   w: (d_inner, d_conv)  bias: (d_inner) or NULL
+ *   xc: (batch*seqlen, ld_out)
+ *   conv_tail (batch, d_inner, d_conv-1) or NULL: the last d_conv-1 pre-conv
+ *   inputs, zero-left-padded when seqlen < d_conv-1 (_mamba.py:180).
+ * ------------------------------------------------------------------------ */
+int mb2_conv1d_silu(int dtype, const void *x_in, int64_t ld_in,
+                    const void *w, const void *bias, void *xc, int64_t ld_out,
+                    void *conv_tail, int64_t batch, int64_t seqlen,
+                    int64_t d_inner, int64_t d_conv, mb2_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Fused scan stage: dt_proj + softplus (_mamba.py:219-220), A = -exp(A_log)
+ * (:222), selective scan + D skip (cpp:68-83), cast and SiLU(z) gate
+ * (_mamba.py:263-264).
+ *   xc:   (N, ld_xc)   conv+SiLU output
+ *   xdbl: (N, ld_xdbl) x_proj output, columns [dt_low (R) | B (S) | C (S)]
+ *   z:    (N, ld_z)    gate input (the z half of in_proj's output)
+ *   w_dt: (d_inner, R) b_dt: (d_inner)   A_log: (d_inner, S)   D: (d_inner)
+ *   (weights in the activation dtype; A_log and D as stored by the module)
+ *   y:    (N, ld_y)    gated output
+ *   h0 / h_last: optional (batch, d_inner, S) float32 initial / final state.
+ * ------------------------------------------------------------------------ */
+int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc,
+                   const void *xdbl, int64_t ld_xdbl, const void *z,
+                   int64_t ld_z, const void *w_dt, const void *b_dt,
+                   const void *A_log, const void *D, const float *h0,
+                   float *h_last, void *y, int64_t ld_y, int64_t batch,
+                   int64_t seqlen, int64_t d_inner, int64_t d_state,
+                   int64_t dt_rank, mb2_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Linear layer y = x W^T (+ bias): nn.Linear as used by in_proj, x_proj,
+ * dt_proj, out_proj (_mamba.py:67,74-75,84).
+ *   x: (M, ld_x)  W: (N, K) row-major  bias: (N) or NULL  y: (M, ld_y)
+ * dtype F32: fp32-faithful.  With w_split (the TF32 halves of W from
+ *   mb2_split_tf32) the tensor cores compute x_hi W_hi + x_hi W_lo + x_lo W_hi;
+ *   with w_split == NULL the CUDA-core fp32 FMA kernel runs.
+ * dtype BF16: bf16 operands, fp32 accumulation, bf16 output.
+ * ------------------------------------------------------------------------ */
+int mb2_linear(int dtype, const void *x, int64_t ld_x, const void *w,
+               const float *w_split, const void *bias, void *y, int64_t ld_y,
+               int64_t M, int64_t N, int64_t K, mb2_stream_t stream);
+
+/* Split an fp32 tensor of numel elements into its TF32 halves:
+ * out[0:numel] = hi = tf32_rn(w), out[numel:2 numel] = lo = tf32_rn(w - hi),
+ * so w == hi + lo to within 2^-22 |w|.  A derived cache of the weights for
+ * mb2_linear's F32 tensor-core path (not module state). */
+int mb2_split_tf32(const float *w, float *out, int64_t numel,
+                   mb2_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Weight-only quantisation (src/cpu_mamba/quant.py:60-134), bit-exact.
+ *   w: (rows, cols) float32
+ *   int8: weight_q int8 (rows, cols);  int4 / nf4: uint8 (rows, (cols+1)/2),
+ *   even element in the high nibble, odd cols padded (int4 code 0 -> nibble 7,
+ *   nf4 index 0).  scale: (rows) float32.
+ * ------------------------------------------------------------------------ */
+int mb2_quantize(int scheme, const float *w, int64_t rows, int64_t cols,
+                 void *weight_q, float *scale, mb2_stream_t stream);
+
+/* dequantize_{int8,int4,nf4} (quant.py:68-69, 90-101, 124-134): w_out (rows, in_dim) f32. */
+int mb2_dequantize(int scheme, const void *weight_q, const float *scale,
+                   int64_t rows, int64_t in_dim, float *w_out,
+                   mb2_stream_t stream);
+
+/* QuantizedLinear.forward (quant.py:188-190): y = x deq(W)^T (+ bias).
+ *   x: (M, ld_x) in dtype; y: (M, ld_y) in dtype; weight_q/scale as above. */
+int mb2_qlinear(int scheme, int dtype, const void *x, int64_t ld_x,
+                const void *weight_q, const float *scale, const void *bias,
+                void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
+                mb2_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Whole block.  Weights follow the mamba_ssm state_dict (_mamba.py:67-84);
+ * a quantised linear passes weight_q/scale instead of weight.
+ * ------------------------------------------------------------------------ */
+typedef struct mb2_linear_w {
+    const void *weight;     /* (out, in) in dtype, or NULL when quantised   */
+    const float *weight_split; /* optional (2, out, in) TF32 halves (F32 path)  */
+    const void *weight_q;   /* quantised codes, or NULL                      */
+    const float *scale;     /* (out) per-channel scale when quantised        */
+    const void *bias;       /* (out) or NULL                                 */
+    int scheme;             /* mb2_scheme                                    */
+} mb2_linear_w;
+
+typedef struct mb2_block {
+    int64_t d_model, d_inner, d_state, d_conv, dt_rank;
+    int dtype;                      /* mb2_dtype of activations and weights */
+    mb2_linear_w in_proj, x_proj, dt_proj, out_proj;
+    const void *conv_w;             /* (d_inner, d_conv) */
+    const void *conv_b;             /* (d_inner) or NULL */
+    const void *A_log;              /* (d_inner, d_state) */
+    const void *D;                  /* (d_inner) */
+} mb2_block;
+
+/* Bytes of workspace mb2_block_forward needs for (batch, seqlen). */
+size_t mb2_block_workspace_bytes(const mb2_block *blk, int64_t batch,
+                                 int64_t seqlen);
+
+/* CPUMamba.forward (_mamba.py:204-265); with h_last / conv_tail non-NULL also
+ * the state of forward_with_final_state (:165-202) from the same pass.
+ *   x, out: (batch, seqlen, d_model) contiguous in dtype. */
+int mb2_block_forward(const mb2_block *blk, const void *x, void *out,
+                      int64_t batch, int64_t seqlen, float *h_last,
+                      void *conv_tail, void *workspace, size_t workspace_bytes,
+                      mb2_stream_t stream);
+
+/* Bytes of workspace mb2_block_step needs for a batch. */
+size_t mb2_step_workspace_bytes(const mb2_block *blk, int64_t batch);
+
+/* CPUMamba.forward_step (_mamba.py:103-163) for one token per sequence.
+ * h (batch, d_inner, d_state) f32 and conv_state (batch, d_inner, d_conv-1)
+ * are updated IN PLACE.  x, out: (batch, d_model). */
+int mb2_block_step(const mb2_block *blk, const void *x, void *out, float *h,
+                   void *conv_state, int64_t batch, void *workspace,
+                   size_t workspace_bytes, mb2_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAMBA_B200_H */

@@ -214,11 +214,14 @@ def _front(p, x, quant):
     return x_pre, z, xc, dt, A, Bm, Cm
 
 
-def block_forward(p, x, quant=None):
-    """CPUMamba.forward (_mamba.py:204-265) with the C-restated scan."""
+def block_forward(p, x, quant=None, scan_op=None):
+    """CPUMamba.forward (_mamba.py:204-265) with the C-restated scan, or with
+    ``scan_op`` = the reference's own compiled op (load_ref_scan_op())."""
     with torch.no_grad():
         _, z, xc, dt, A, Bm, Cm = _front(p, x, quant)
-        y = selective_scan(xc.float(), dt.float(), A, Bm.float(), Cm.float(), p["D"].float())
+        args = (xc.float().contiguous(), dt.float().contiguous(), A.contiguous(),
+                Bm.float().contiguous(), Cm.float().contiguous(), p["D"].float().contiguous())
+        y = scan_op.selective_scan_cpu(*args) if scan_op is not None else selective_scan(*args)
         y = y.to(xc.dtype) * F.silu(z)                         # :263-264
         return linear(p, "out_proj", y, quant)                 # :265
 

@@ -1,0 +1,136 @@
+"""GPU parity of the whole block: forward, forward_with_final_state and
+forward_step against the reference's golden outputs and the pinned oracle.
+
+Bars: fp32 max abs diff <= 1e-5; bf16 mean relative error <= 2e-2 against the
+fp32 reference with the formula of the reference's tests/test_bf16.py:53."""
+import pytest
+import torch
+
+import oracle
+from cpu_mamba_b200 import CPUMamba
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-5
+
+
+def bf16_rel(y_fp, y_bf):
+    y_fp, y_bf = y_fp.float().cpu(), y_bf.float().cpu()
+    rel = (y_fp - y_bf).abs() / (y_fp.abs().clamp(min=1e-3) + 1e-6)
+    return rel.mean().item(), rel.quantile(0.9).item()
+
+
+def make_block(p, d_model, d_state, dtype=torch.float32):
+    m = CPUMamba(d_model=d_model, d_state=d_state).eval()
+    m.load_state_dict({k: v.float() for k, v in p.items()}, strict=True)
+    return m.to(device="cuda", dtype=dtype)
+
+
+def test_forward_fp32_matches_reference_goldens(golden):
+    for case in golden("block.pt")["fp32"]:
+        m = make_block(case["params"], case["d_model"], case["d_state"])
+        with torch.no_grad():
+            y = m(case["x"].cuda()).cpu()
+        assert y.shape == case["x"].shape
+        err = (y - case["y"]).abs().max().item()
+        assert err <= TOL, err
+
+
+def test_forward_bf16_matches_reference(golden):
+    case = golden("block.pt")["bf16"]
+    m = make_block(case["params"], 64, 16, torch.bfloat16)
+    with torch.no_grad():
+        y = m(case["x"].to(torch.bfloat16).cuda())
+    assert y.dtype == torch.bfloat16 and torch.isfinite(y).all()
+    mean, p90 = bf16_rel(case["y_fp32"], y)
+    assert mean <= 2e-2 and p90 <= 0.30, (mean, p90)
+    ref_mean, _ = bf16_rel(case["y_fp32"], case["y_bf16"])
+    assert mean <= max(2e-2, 1.5 * ref_mean)
+
+
+@pytest.mark.parametrize("shape", [(3, 37, 64, 24), (2, 181, 96, 16), (1, 2, 48, 8),
+                                   (2, 65, 128, 64)])
+def test_forward_fp32_matches_oracle(shape):
+    b, T, dm, S = shape
+    p = oracle.make_block_params(dm, S, seed=dm + S)
+    x = torch.randn(b, T, dm, generator=torch.Generator().manual_seed(T))
+    m = make_block(p, dm, S)
+    with torch.no_grad():
+        y = m(x.cuda()).cpu()
+    assert (y - oracle.block_forward(p, x)).abs().max().item() <= TOL
+
+
+def test_forward_with_final_state_matches_reference(golden):
+    c = golden("stateful.pt")
+    m = make_block(c["params"], c["d_model"], c["d_state"])
+    x = c["x"].cuda()
+    Tp = c["T_pref"]
+    with torch.no_grad():
+        y_pref, st = m.forward_with_final_state(x[:, :Tp])
+    assert (y_pref.cpu() - c["y_pref"]).abs().max().item() <= TOL
+    assert (st["h"].cpu() - c["pref_state"]["h"]).abs().max().item() <= TOL
+    assert torch.equal(st["conv_state"].cpu(), c["pref_state"]["conv_state"])
+    ys = []
+    h_obj, conv_obj = st["h"], st["conv_state"]
+    for t in range(Tp, x.shape[1]):
+        with torch.no_grad():
+            y, st = m.forward_step(x[:, t], st)
+        ys.append(y.cpu())
+    assert st["h"] is h_obj and st["conv_state"] is conv_obj      # updated in place
+    assert (torch.stack(ys, 1) - c["y_steps"]).abs().max().item() <= TOL
+    assert (st["h"].cpu() - c["final_state"]["h"]).abs().max().item() <= TOL
+    assert torch.equal(st["conv_state"].cpu(), c["final_state"]["conv_state"])
+    # full forward over the whole sequence agrees with prefill + steps
+    with torch.no_grad():
+        y_full = m(x).cpu()
+    assert (y_full - c["y_full"]).abs().max().item() <= TOL
+
+
+def test_steps_from_init_state_match_reference(golden):
+    c = golden("stateful.pt")
+    m = make_block(c["params"], c["d_model"], c["d_state"])
+    x = c["x"].cuda()
+    st = m.init_state(x.shape[0])
+    ys = []
+    for t in range(4):
+        with torch.no_grad():
+            y, st = m.forward_step(x[:, t].unsqueeze(1), st)       # (B, 1, D) input
+        ys.append(y.cpu())
+    assert (torch.stack(ys, 1) - c["y_init_steps"]).abs().max().item() <= TOL
+    assert (st["h"].cpu() - c["init_steps_state"]["h"]).abs().max().item() <= TOL
+
+
+def test_step_2d_equals_3d_input():
+    p = oracle.make_block_params(64, 8, seed=5)
+    m = make_block(p, 64, 8)
+    x = torch.randn(2, 64, device="cuda")
+    with torch.no_grad():
+        y2, _ = m.forward_step(x, m.init_state(2))
+        y3, _ = m.forward_step(x.unsqueeze(1), m.init_state(2))
+    assert torch.equal(y2, y3)
+
+
+def test_short_prompt_conv_tail_is_left_padded():
+    p = oracle.make_block_params(64, 8, seed=6)
+    m = make_block(p, 64, 8)
+    x = torch.randn(2, 2, 64)
+    with torch.no_grad():
+        _, st = m.forward_with_final_state(x.cuda())
+    _, st_ref = oracle.block_forward_with_final_state(p, x)
+    assert torch.equal(st["conv_state"].cpu(), st_ref["conv_state"])
+    assert (st["h"].cpu() - st_ref["h"]).abs().max().item() <= TOL
+
+
+def test_prefill_plus_steps_bf16_close():
+    p = oracle.make_block_params(64, 16, seed=8)
+    m32 = make_block(p, 64, 16)
+    m16 = make_block(p, 64, 16, torch.bfloat16)
+    x = torch.randn(2, 24, 64, device="cuda")
+    with torch.no_grad():
+        y32 = m32(x)
+        y16, st = m16.forward_with_final_state(x[:, :16].bfloat16())
+        ys = [y16]
+        for t in range(16, 24):
+            y, st = m16.forward_step(x[:, t].bfloat16(), st)
+            ys.append(y.unsqueeze(1))
+    mean, _ = bf16_rel(y32, torch.cat(ys, 1))
+    assert mean <= 2e-2, mean

@@ -1,0 +1,106 @@
+"""Host-side API of the package (no GPU): the reference's module surface,
+state_dict layout (tests/test_parity.py:30-49 of the reference), helpers, and
+the rule that there is no CPU fallback."""
+import pytest
+import torch
+
+from cpu_mamba_b200 import (CPUMamba, QuantConfig, assert_state_dict_compatible,
+                            memory_footprint, selective_scan)
+
+
+def test_state_dict_keys_and_shapes():
+    block = CPUMamba(d_model=384, d_state=24, d_conv=4, expand=2)
+    sd = block.state_dict()
+    assert set(sd) == {"A_log", "D", "in_proj.weight", "conv1d.weight", "conv1d.bias",
+                       "x_proj.weight", "dt_proj.weight", "dt_proj.bias", "out_proj.weight"}
+    assert sd["A_log"].shape == (768, 24)
+    assert sd["D"].shape == (768,)
+    assert sd["in_proj.weight"].shape == (1536, 384)
+    assert sd["conv1d.weight"].shape == (768, 1, 4)
+    assert sd["x_proj.weight"].shape == (24 + 48, 768)
+    assert sd["dt_proj.weight"].shape == (768, 24)
+    assert sd["out_proj.weight"].shape == (384, 768)
+    assert torch.equal(sd["A_log"][0], torch.log(torch.arange(1, 25, dtype=torch.float32)))
+
+
+def test_loads_reference_state_dict(golden):
+    case = golden("block.pt")["fp32"][0]
+    block = CPUMamba(d_model=case["d_model"], d_state=case["d_state"])
+    block.load_state_dict(case["params"], strict=True)
+
+
+def test_state_dict_compatibility_helper():
+    block = CPUMamba(64, 8)
+    sd = block.state_dict()
+    assert_state_dict_compatible(block, sd)
+    bad = dict(sd)
+    bad["A_log"] = torch.zeros(100, 8)
+    with pytest.raises(ValueError, match="shape mismatch"):
+        assert_state_dict_compatible(block, bad)
+    bad = dict(sd)
+    bad["extra_key"] = torch.zeros(1)
+    with pytest.raises(ValueError, match="unexpected keys"):
+        assert_state_dict_compatible(block, bad)
+    bad = dict(sd)
+    del bad["D"]
+    with pytest.raises(ValueError, match="missing keys"):
+        assert_state_dict_compatible(block, bad)
+
+
+def test_quant_config_validation():
+    assert QuantConfig().scheme == "int8"
+    for s in ("int8", "int4", "nf4"):
+        QuantConfig(scheme=s)
+    with pytest.raises(ValueError, match="unknown scheme"):
+        QuantConfig(scheme="fp8")
+
+
+def test_init_state_shapes_and_dtypes():
+    block = CPUMamba(d_model=64, d_state=8, d_conv=4, expand=2)
+    st = block.init_state(batch_size=4)
+    assert st["h"].shape == (4, 128, 8) and st["h"].dtype == torch.float32
+    assert st["conv_state"].shape == (4, 128, 3)
+    st16 = block.to(torch.bfloat16).init_state(2)
+    assert st16["h"].dtype == torch.float32 and st16["conv_state"].dtype == torch.bfloat16
+
+
+def test_no_cpu_fallback():
+    block = CPUMamba(64, 8).eval()
+    x = torch.randn(1, 4, 64)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        block(x)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        block.forward_step(x[:, 0], block.init_state(1))
+    t = torch.zeros(1, 2, 3)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        selective_scan(t, t, torch.zeros(3, 4), torch.zeros(1, 2, 4), torch.zeros(1, 2, 4),
+                       torch.zeros(3))
+
+
+def test_selective_scan_contract_errors():
+    t = torch.zeros(1, 2, 3)
+    A, Bm, D = torch.zeros(3, 4), torch.zeros(1, 2, 4), torch.zeros(3)
+    with pytest.raises(RuntimeError, match="contiguous"):
+        selective_scan(t.transpose(1, 2), t, A, Bm, Bm, D)
+    with pytest.raises(RuntimeError, match="fp32 only"):
+        selective_scan(t.double(), t, A, Bm, Bm, D)
+    with pytest.raises(RuntimeError, match="shape mismatch"):
+        selective_scan(t, t, A, Bm, Bm, D.view(1, 3))
+
+
+def test_bf16_params_half_the_bytes_and_footprint():
+    fp = CPUMamba(128, 16)
+    bf = CPUMamba(128, 16).to(torch.bfloat16)
+    fb = sum(p.numel() * p.element_size() for p in fp.parameters())
+    bb = sum(p.numel() * p.element_size() for p in bf.parameters())
+    assert bb == fb // 2
+    m = memory_footprint(fp)
+    assert m["quant_buffer_bytes"] == 0 and m["total_bytes"] == fb
+
+
+def test_backend_attributes_tolerated():
+    block = CPUMamba(64, 8)
+    block._scan_backend = "assoc"
+    block._assoc_chunk_T = 16
+    block._force_time_loop = True
+    assert set(block.state_dict()) == set(CPUMamba(64, 8).state_dict())
