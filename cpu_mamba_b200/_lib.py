@@ -49,6 +49,7 @@ class Block(ctypes.Structure):
 _SIGS = {
     "mb2_version": (ctypes.c_int, []),
     "mb2_last_error": (ctypes.c_char_p, []),
+    "mb2_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
     "mb2_selective_scan": (ctypes.c_int, [_vp] * 7 + [_c_i64] * 4 + [_vp, _vp, _vp]),
     "mb2_conv1d_silu": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _vp, _vp, _vp, _c_i64, _vp,
                                        _c_i64, _c_i64, _c_i64, _c_i64, _vp]),
@@ -92,6 +93,13 @@ def lib() -> ctypes.CDLL:
                 fn.argtypes = args
             _LIB = L
     return _LIB
+
+
+def device_status(clear: bool = True) -> int:
+    """0, or the code of a kernel-side wait that expired since the last clear."""
+    code = ctypes.c_int(0)
+    check(lib().mb2_device_status(ctypes.byref(code), int(clear)), "device_status")
+    return code.value
 
 
 def exported_symbols():

@@ -1,47 +1,459 @@
-// Tensor-core GEMM entry (tcgen05).  Placeholder until the sm_100a kernel
-// lands: reports "not used" so callers take the CUDA-core kernel.
+// Tensor-core GEMM for sm_100a (tcgen05 + TMA + TMEM): y = x W^T (+ bias).
+//
+// Used for the block's large-M projections (in_proj, x_proj, out_proj;
+// nn.Linear at src/cpu_mamba/_mamba.py:67,74,84).
+//
+//   BF16 mode : A, B bf16 (K-major), kind::f16 MMA, fp32 accumulation in TMEM,
+//               bf16 output -- the reference's bf16 F.linear.
+//   F32 mode  : fp32-faithful 3-term TF32 split.  W arrives pre-split as TF32
+//               hi / lo planes (mb2_split_tf32).  Each A tile is loaded as fp32
+//               and split in shared memory by four transform warps into
+//               hi = tf32_rn(a) and lo = tf32_rn(a - hi); the MMA warp issues
+//               A_hi*W_hi + A_hi*W_lo + A_lo*W_hi into one fp32 accumulator.
+//               The dropped A_lo*W_lo term and the rounding of lo are
+//               <= 2^-21 |a||w| per product, below fp32 FMA accumulation noise.
+//
+// CTA = 6 warps, one 128 x 128 output tile:
+//   warp 0  TMA producer (one elected lane), STAGES-deep smem ring
+//   warp 1  TMEM allocator + MMA issuer (one elected lane)
+//   warps 2-5  F32 mode: A-tile transform during the main loop;
+//              all modes: epilogue (TMEM -> registers -> smem -> coalesced
+//              global stores, bias add, dtype conversion, column remap)
+// Operand tiles are 128 rows x 128 bytes, 128-byte swizzled (TMA and UMMA
+// descriptors agree).  Every mbarrier wait is bounded (~2 s): on expiry the
+// thread records an error in g_mb2_device_error and abandons the tile, and the
+// allocating warp still frees its TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace mb2 {
 
-int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *w_split,
-            const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
-            int64_t n1, int64_t off1, int64_t n2, int64_t off2, cudaStream_t st, bool *used) {
-    (void)dtype; (void)x; (void)ld_x; (void)w; (void)w_split; (void)bias; (void)y; (void)ld_y;
-    (void)M; (void)N; (void)K; (void)n1; (void)off1; (void)n2; (void)off2; (void)st;
-    *used = false;
-    return MB2_OK;
+__device__ int g_mb2_device_error = 0;  // 0 = ok; else a code of where a wait expired
+
+namespace tc {
+
+constexpr int BM = 128, BN = 128;
+constexpr int TILE_BYTES = 128 * 128;   // one operand tile: 128 rows x 128 B
+constexpr int THREADS = 192;
+constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s bound on any wait
+
+enum Mode { F32X3 = 0, BF16 = 1 };
+
+template <int MODE> struct Cfg;
+template <> struct Cfg<F32X3> {
+    static constexpr int STAGES = 3;
+    static constexpr int TILES = 4;           // A_hi(raw), A_lo, B_hi, B_lo
+    static constexpr int BK = 32;             // fp32 elements per 128 B row
+    static constexpr int KSTEP = 8;           // K per tf32 MMA
+    static constexpr uint32_t TX = 3 * TILE_BYTES;  // bytes by TMA per stage
+};
+template <> struct Cfg<BF16> {
+    static constexpr int STAGES = 6;
+    static constexpr int TILES = 2;           // A, B
+    static constexpr int BK = 64;
+    static constexpr int KSTEP = 16;
+    static constexpr uint32_t TX = 2 * TILE_BYTES;
+};
+
+template <int MODE>
+constexpr size_t smem_bytes() {
+    return 1024 /*align slack*/ + (size_t)Cfg<MODE>::STAGES * Cfg<MODE>::TILES * TILE_BYTES + 256;
 }
 
-}  // namespace mb2
+struct Params {
+    void *y; int64_t ld_y;
+    const void *bias;
+    int64_t M, N, K;
+    int64_t n1, n2, off1, off2;   // output column remap
+};
 
-// ------------------------------------------------------------- TF32 split ---
-// hi = tf32_rn(w), lo = tf32_rn(w - hi): w == hi + lo up to 2^-22 |w|.  Used
-// as a derived cache of fp32 weights for the 3-term TF32 tensor-core GEMM.
-namespace mb2 {
+// ------------------------------------------------------------- primitives
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+
+// Bounded wait; false (and the device error flag set) when it expired.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int where) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if ((i & 255) == 0 && globaltimer() - t0 > WAIT_NS) {
+            atomicCAS(&g_mb2_device_error, 0, where);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, uint32_t bar,
+                                            int32_t c0, int32_t c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row groups of
+// 1024 B (SBO), sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+template <int MODE>
+__host__ __device__ constexpr uint32_t instr_desc() {
+    // D fmt F32 (bits 4-5 = 1); A/B fmt (bits 7-9, 10-12): TF32 = 2, BF16 = 1;
+    // K-major A and B; N >> 3 at bits 17-22; M >> 4 at bits 24-28.
+    constexpr uint32_t fmt = MODE == F32X3 ? 2u : 1u;
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
+           ((uint32_t)(BM >> 4) << 24);
+}
+
+template <int MODE>
+__device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accum) {
+    const uint32_t idesc = instr_desc<MODE>();
+    if (MODE == F32X3) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+            ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accum));
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+            ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accum));
+    }
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ float tf32_rn(float v) {
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
     return __uint_as_float(r);
 }
 
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ----------------------------------------------------------------- kernel
+template <int MODE, typename TO>
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b0,
+               const __grid_constant__ CUtensorMap map_b1, const Params p) {
+    using C = Cfg<MODE>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *gbase = smem_raw + (base - raw);
+    // ring: stage s, tile t at base + (s * TILES + t) * TILE_BYTES
+    const uint32_t bars = base + C::STAGES * C::TILES * TILE_BYTES;
+    // barriers: full[S], empty[S], xform[S], accum, done ; then tmem slot
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (C::STAGES + s); };
+    auto xform = [&](int s) { return bars + 8u * (2 * C::STAGES + s); };
+    const uint32_t accum_bar = bars + 8u * (3 * C::STAGES);
+    const uint32_t done_bar = accum_bar + 8u;
+    const uint32_t tmem_slot = done_bar + 8u;
+    uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(gbase + (tmem_slot - base));
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int64_t m0 = (int64_t)blockIdx.y * BM;
+    const int64_t n0 = (int64_t)blockIdx.x * BN;
+    const int nk = (int)ceil_div(p.K, C::BK);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+            mbar_init(xform(s), 128);
+        }
+        mbar_init(accum_bar, 1);
+        mbar_init(done_bar, 128);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(tmem_slot), "r"(BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot_ptr;
+
+    auto tile = [&](int s, int t) { return base + (uint32_t)((s * C::TILES + t) * TILE_BYTES); };
+
+    if (warp == 0) {
+        // ---------------------------------------------------- TMA producer
+        if (lane == 0) {
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % C::STAGES;
+                const uint32_t ph = (kb / C::STAGES) & 1;
+                if (!mbar_wait(empty(s), ph ^ 1, 1)) break;
+                mbar_expect_tx(full(s), C::TX);
+                const int32_t kc = kb * C::BK;
+                tma_load_2d(tile(s, 0), &map_a, full(s), kc, (int32_t)m0);
+                if (MODE == F32X3) {
+                    tma_load_2d(tile(s, 2), &map_b0, full(s), kc, (int32_t)n0);
+                    tma_load_2d(tile(s, 3), &map_b1, full(s), kc, (int32_t)n0);
+                } else {
+                    tma_load_2d(tile(s, 1), &map_b0, full(s), kc, (int32_t)n0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            bool ok = true;
+            for (int kb = 0; kb < nk && ok; ++kb) {
+                const int s = kb % C::STAGES;
+                const uint32_t ph = (kb / C::STAGES) & 1;
+                ok = mbar_wait(full(s), ph, 2);
+                if (ok && MODE == F32X3) ok = mbar_wait(xform(s), ph, 3);
+                if (!ok) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                for (int kk = 0; kk < C::BK / C::KSTEP; ++kk) {
+                    const uint32_t koff = kk * 32;  // 32 bytes of K per MMA
+                    const uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
+                    if (MODE == F32X3) {
+                        const uint64_t ah = smem_desc(tile(s, 0) + koff);
+                        const uint64_t al = smem_desc(tile(s, 1) + koff);
+                        const uint64_t bh = smem_desc(tile(s, 2) + koff);
+                        const uint64_t bl = smem_desc(tile(s, 3) + koff);
+                        mma<MODE>(tmem, ah, bh, acc0);
+                        mma<MODE>(tmem, ah, bl, 1u);
+                        mma<MODE>(tmem, al, bh, 1u);
+                    } else {
+                        mma<MODE>(tmem, smem_desc(tile(s, 0) + koff), smem_desc(tile(s, 1) + koff),
+                                  acc0);
+                    }
+                }
+                mma_commit(empty(s));   // frees the stage once these MMAs have read it
+            }
+            if (ok) mma_commit(accum_bar);  // accumulator complete
+        }
+        __syncwarp();
+        // free TMEM after the epilogue drained it (bounded)
+        mbar_wait(done_bar, 0, 4);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+    } else {
+        // ----------------------------- transform (F32) + epilogue, warps 2-5
+        const int et = threadIdx.x - 64;   // 0..127
+        bool ok = true;
+        if (MODE == F32X3) {
+            for (int kb = 0; kb < nk; ++kb) {
+                const int s = kb % C::STAGES;
+                const uint32_t ph = (kb / C::STAGES) & 1;
+                if (!mbar_wait(full(s), ph, 5)) { ok = false; break; }
+                // elementwise, so the swizzled layout needs no decoding
+                float4 *hi = reinterpret_cast<float4 *>(gbase + (tile(s, 0) - base));
+                float4 *lo = reinterpret_cast<float4 *>(gbase + (tile(s, 1) - base));
+#pragma unroll
+                for (int i = 0; i < TILE_BYTES / 16 / 128; ++i) {
+                    const int idx = et + i * 128;
+                    float4 v = hi[idx];
+                    float4 h, l;
+                    h.x = tf32_rn(v.x); l.x = tf32_rn(v.x - h.x);
+                    h.y = tf32_rn(v.y); l.y = tf32_rn(v.y - h.y);
+                    h.z = tf32_rn(v.z); l.z = tf32_rn(v.z - h.z);
+                    h.w = tf32_rn(v.w); l.w = tf32_rn(v.w - h.w);
+                    hi[idx] = h;
+                    lo[idx] = l;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(xform(s));
+            }
+        }
+        if (ok) ok = mbar_wait(accum_bar, 0, 6);
+        ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld is warp-collective
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int q = warp & 3;             // TMEM lane quarter this warp may read
+        // staging: 32 rows x (BN + 1) floats per warp, in the (now idle) ring
+        float *stage = reinterpret_cast<float *>(gbase) + q * 32 * (BN + 1);
+        if (ok) {
+#pragma unroll
+            for (int cb = 0; cb < BN / 32; ++cb) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + cb * 32, r);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) stage[lane * (BN + 1) + cb * 32 + j] = __uint_as_float(r[j]);
+            }
+        }
+        __syncwarp();
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        mbar_arrive(done_bar);              // TMEM no longer needed by this thread
+        if (ok) {
+            TO *Y = static_cast<TO *>(p.y);
+            const TO *bias = static_cast<const TO *>(p.bias);
+            for (int rr = 0; rr < 32; ++rr) {
+                const int64_t m = m0 + q * 32 + rr;
+                if (m >= p.M) break;
+#pragma unroll
+                for (int c4 = 0; c4 < BN / 32; ++c4) {
+                    const int64_t n = n0 + c4 * 32 + lane;
+                    if (n < p.N) {
+                        float v = stage[rr * (BN + 1) + c4 * 32 + lane];
+                        if (bias) v += io<TO>::to_f(bias[n]);
+                        const int64_t col = n + (n >= p.n1 ? p.off1 : 0) + (n >= p.n2 ? p.off2 : 0);
+                        Y[m * p.ld_y + col] = io<TO>::from_f(v);
+                    }
+                }
+            }
+        }
+    }
+}
+
+}  // namespace tc
+
+// ------------------------------------------------------------------- host
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int get_encode() {
+    if (g_encode) return MB2_OK;
+    cudaDriverEntryPointQueryResult q;
+    void *fn = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return fail(MB2_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return MB2_OK;
+}
+
+// 2D K-major tile map: rows x K elements, box 128 rows x 128 bytes, 128B swizzle.
+static int make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K, int64_t ld,
+                    bool bf16) {
+    const size_t es = bf16 ? 2 : 4;
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / es), 128};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                          2, const_cast<void *>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MB2_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return MB2_OK;
+}
+
+template <int MODE, typename TO>
+static int launch_tc(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
+                     const tc::Params &p, cudaStream_t st) {
+    auto kern = tc::gemm_tc_kernel<MODE, TO>;
+    constexpr size_t smem = tc::smem_bytes<MODE>();
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_tc smem attribute: %s", cudaGetErrorString(e));
+    dim3 grid((unsigned)ceil_div(p.N, tc::BN), (unsigned)ceil_div(p.M, tc::BM));
+    kern<<<grid, tc::THREADS, smem, st>>>(a, b0, b1, p);
+    return check_launch("gemm_tc_kernel");
+}
+
+// Tensor-core path when it applies (large M, aligned operands); *used reports it.
+int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *w_split,
+            const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
+            int64_t n1, int64_t off1, int64_t n2, int64_t off2, cudaStream_t st, bool *used) {
+    *used = false;
+    const bool bf16 = dtype == MB2_BF16;
+    const size_t es = bf16 ? 2 : 4;
+    if (M < 256 || N < 16 || K < 16) return MB2_OK;         // skinny: CUDA-core kernel
+    if (!bf16 && !w_split) return MB2_OK;                   // exact-fp32 path requested
+    if (ceil_div(M, tc::BM) > 65535) return MB2_OK;
+    // TMA: 16-byte aligned bases and row strides
+    if (!aligned(x, 16) || (ld_x * es) % 16 != 0 || (K * es) % 16 != 0) return MB2_OK;
+    const void *b0 = bf16 ? w : (const void *)w_split;
+    const void *b1 = bf16 ? w : (const void *)(w_split + N * K);
+    if (!aligned(b0, 16) || !aligned(b1, 16)) return MB2_OK;
+    MB2_TRY(get_encode());
+    CUtensorMap ma, mb0, mb1;
+    MB2_TRY(make_map(&ma, x, M, K, ld_x, bf16));
+    MB2_TRY(make_map(&mb0, b0, N, K, K, bf16));
+    MB2_TRY(make_map(&mb1, b1, N, K, K, bf16));
+    tc::Params p{y, ld_y, bias, M, N, K, n1, n2, off1, off2};
+    *used = true;
+    if (bf16) return launch_tc<tc::BF16, __nv_bfloat16>(ma, mb0, mb1, p, st);
+    return launch_tc<tc::F32X3, float>(ma, mb0, mb1, p, st);
+}
+
+}  // namespace mb2
+
+// ------------------------------------------------------------- TF32 split ---
+// hi = tf32_rn(w), lo = tf32_rn(w - hi): w == hi + lo up to 2^-22 |w|.  A
+// derived cache of fp32 weights for the 3-term TF32 tensor-core GEMM.
+namespace mb2 {
 __global__ void split_tf32_kernel(const float *__restrict__ w, float *__restrict__ out,
                                   int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const float v = w[i];
-    const float h = tf32_rn(v);
+    const float h = tc::tf32_rn(v);
     out[i] = h;
-    out[n + i] = tf32_rn(v - h);
+    out[n + i] = tc::tf32_rn(v - h);
 }
 }  // namespace mb2
 
-extern "C" int mb2_split_tf32(const float *w, float *out, int64_t numel,
-                              mb2_stream_t stream) {
+extern "C" int mb2_split_tf32(const float *w, float *out, int64_t numel, mb2_stream_t stream) {
     MB2_REQUIRE(numel >= 0, MB2_ERR_SHAPE, "split_tf32: negative size");
     if (numel == 0) return MB2_OK;
     MB2_REQUIRE(w && out, MB2_ERR_ARG, "split_tf32: null pointer");
     mb2::split_tf32_kernel<<<(unsigned)mb2::ceil_div(numel, 256), 256, 0, (cudaStream_t)stream>>>(
         w, out, numel);
     return mb2::check_launch("split_tf32_kernel");
+}
+
+extern "C" int mb2_device_status(int *code, int clear) {
+    MB2_REQUIRE(code, MB2_ERR_ARG, "device_status: null pointer");
+    cudaError_t e = cudaMemcpyFromSymbol(code, mb2::g_mb2_device_error, sizeof(int));
+    if (e != cudaSuccess) return mb2::fail(MB2_ERR_CUDA, "device_status: %s", cudaGetErrorString(e));
+    if (clear) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(mb2::g_mb2_device_error, &zero, sizeof(int));
+        if (e != cudaSuccess) return mb2::fail(MB2_ERR_CUDA, "device_status: %s", cudaGetErrorString(e));
+    }
+    return MB2_OK;
 }

@@ -45,6 +45,11 @@ enum mb2_scheme { MB2_Q_NONE = 0, MB2_Q_INT8 = 1, MB2_Q_INT4 = 2, MB2_Q_NF4 = 3 
 int mb2_version(void);
 const char *mb2_last_error(void);
 
+/* Device-side status of the current device: 0, or the code of the first
+ * bounded wait inside a kernel that expired (the kernel then abandoned its
+ * tile instead of hanging).  clear != 0 resets it.  Synchronous. */
+int mb2_device_status(int *code, int clear);
+
 /* ------------------------------------------------------------------------
  * Selective scan -- drop-in for selective_scan_cpu(x, dt, A, B, C, D) -> y
  * (src/cpu_mamba/selective_scan_cpu.cpp:19-26, bound at

@@ -68,7 +68,8 @@ def test_forward_with_final_state_matches_reference(golden):
         y_pref, st = m.forward_with_final_state(x[:, :Tp])
     assert (y_pref.cpu() - c["y_pref"]).abs().max().item() <= TOL
     assert (st["h"].cpu() - c["pref_state"]["h"]).abs().max().item() <= TOL
-    assert torch.equal(st["conv_state"].cpu(), c["pref_state"]["conv_state"])
+    # the conv tail holds in_proj outputs (GEMM results): compared at the fp32 bar
+    assert (st["conv_state"].cpu() - c["pref_state"]["conv_state"]).abs().max().item() <= TOL
     ys = []
     h_obj, conv_obj = st["h"], st["conv_state"]
     for t in range(Tp, x.shape[1]):
@@ -78,7 +79,7 @@ def test_forward_with_final_state_matches_reference(golden):
     assert st["h"] is h_obj and st["conv_state"] is conv_obj      # updated in place
     assert (torch.stack(ys, 1) - c["y_steps"]).abs().max().item() <= TOL
     assert (st["h"].cpu() - c["final_state"]["h"]).abs().max().item() <= TOL
-    assert torch.equal(st["conv_state"].cpu(), c["final_state"]["conv_state"])
+    assert (st["conv_state"].cpu() - c["final_state"]["conv_state"]).abs().max().item() <= TOL
     # full forward over the whole sequence agrees with prefill + steps
     with torch.no_grad():
         y_full = m(x).cpu()
@@ -116,7 +117,7 @@ def test_short_prompt_conv_tail_is_left_padded():
     with torch.no_grad():
         _, st = m.forward_with_final_state(x.cuda())
     _, st_ref = oracle.block_forward_with_final_state(p, x)
-    assert torch.equal(st["conv_state"].cpu(), st_ref["conv_state"])
+    assert (st["conv_state"].cpu() - st_ref["conv_state"]).abs().max().item() <= TOL
     assert (st["h"].cpu() - st_ref["h"]).abs().max().item() <= TOL
 
 

@@ -1,0 +1,75 @@
+"""The tcgen05 tensor-core GEMM (csrc/gemm_tc.cu) against float64 references.
+
+fp32 mode (3-term TF32 split) must be as accurate as an fp32 FMA GEMM: error
+within a small multiple of the CUDA-core kernel's own error against float64.
+bf16 mode: bf16 operands, fp32 accumulation, bf16 output rounding only."""
+import pytest
+import torch
+
+from cpu_mamba_b200 import _lib, ops
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(256, 128, 32), (1000, 200, 100), (300, 96, 1536), (4096, 3072, 768), (2049, 768, 1536)]
+
+
+def _data(M, N, K, seed):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g)
+    w = (torch.rand(N, K, generator=g) * 2 - 1) / K ** 0.5
+    b = torch.randn(N, generator=g) * 0.1
+    return x, w, b
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_tf32x3_matches_float64(shape):
+    M, N, K = shape
+    x, w, b = _data(M, N, K, sum(shape))
+    ref = (x.double() @ w.double().T + b.double()).float()
+    xd, wd, bd = x.cuda(), w.cuda(), b.cuda()
+    y_tc = ops.linear(xd, wd, bd, weight_split=ops.split_tf32(wd)).cpu()
+    y_fma = ops.linear(xd, wd, bd).cpu()
+    assert _lib.device_status() == 0
+    e_tc = (y_tc - ref).abs().max().item()
+    e_fma = (y_fma - ref).abs().max().item()
+    assert e_tc <= max(4 * e_fma, 2e-6), (e_tc, e_fma)
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_bf16_matches_float64_of_rounded_operands(shape):
+    M, N, K = shape
+    x, w, b = _data(M, N, K, 7 + sum(shape))
+    xb, wb, bb = x.bfloat16(), w.bfloat16(), b.bfloat16()
+    ref = xb.double() @ wb.double().T + bb.double()
+    y = ops.linear(xb.cuda(), wb.cuda(), bb.cuda()).cpu().double()
+    assert _lib.device_status() == 0
+    # only the final bf16 rounding (2^-9 relative) plus fp32 accumulation noise
+    err = ((y - ref).abs() / (ref.abs() + 1e-2)).max().item()
+    assert err <= 2 ** -8, err
+
+
+def test_split_tf32_is_exact_decomposition():
+    w = torch.randn(37, 53, device="cuda")
+    s = ops.split_tf32(w)
+    hi, lo = s[0], s[1]
+    bits = lambda t: t.view(torch.int32) & 0x1FFF
+    assert (bits(hi) == 0).all() and (bits(lo) == 0).all()      # TF32-representable
+    assert ((hi.double() + lo.double() - w.double()).abs() <= w.double().abs() * 2 ** -21).all()
+
+
+def test_column_remap_and_strided_output():
+    """x_proj-style launch: three output segments written at aligned offsets."""
+    M, K, R, S = 512, 256, 12, 16
+    x, w, _ = _data(M, R + 2 * S, K, 3)
+    xd, wd = x.cuda(), w.cuda()
+    ref = ops.linear(xd, wd, None, weight_split=ops.split_tf32(wd))
+    blk = _lib.lib()
+    ldy = 16 + 16 + 16
+    y = torch.full((M, ldy), float("nan"), device="cuda")
+    split = ops.split_tf32(wd)
+    # direct C-ABI call through the internal remap is exercised by the block
+    # forward; here check the plain strided store path (ld_y > N)
+    _lib.check(blk.mb2_linear(0, xd.data_ptr(), K, wd.data_ptr(), split.data_ptr(), None,
+                              y.data_ptr(), ldy, M, R + 2 * S, K, _lib.stream_of(xd)), "linear")
+    assert torch.equal(y[:, :R + 2 * S], ref)
+    assert torch.isnan(y[:, R + 2 * S:]).all()
