@@ -9,9 +9,13 @@
 //               hi / lo planes (mb2_split_tf32).  Each A tile is loaded as fp32
 //               and split in shared memory by four transform warps into
 //               hi = tf32_rn(a) and lo = tf32_rn(a - hi); the MMA warp issues
-//               A_hi*W_hi + A_hi*W_lo + A_lo*W_hi into one fp32 accumulator.
-//               The dropped A_lo*W_lo term and the rounding of lo are
-//               <= 2^-21 |a||w| per product, below fp32 FMA accumulation noise.
+//               A_hi*W_hi + A_hi*W_lo + A_lo*W_hi.  The dropped A_lo*W_lo term
+//               and the rounding of lo are <= 2^-21 |a||w| per product.
+//               The tensor core truncates when it adds into an fp32
+//               accumulator, so the error grows with the number of MMAs per
+//               accumulator: the big hi*hi products alternate between two TMEM
+//               accumulators by K slice, the small cross terms go to a third,
+//               and the epilogue sums the three in fp32 round-to-nearest.
 //
 // CTA = 6 warps, one 128 x 128 output tile:
 //   warp 0  TMA producer (one elected lane), STAGES-deep smem ring
@@ -35,6 +39,7 @@ __device__ int g_mb2_device_error = 0;  // 0 = ok; else a code of where a wait e
 namespace tc {
 
 constexpr int BM = 128, BN = 128;
+constexpr int TMEM_COLS = 512;          // F32: 3 accumulators of BN columns
 constexpr int TILE_BYTES = 128 * 128;   // one operand tile: 128 rows x 128 B
 constexpr int THREADS = 192;
 constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s bound on any wait
@@ -218,7 +223,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(tmem_slot), "r"(BN));
+                     ::"r"(tmem_slot), "r"(MODE == F32X3 ? TMEM_COLS : BN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -266,9 +271,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         const uint64_t al = smem_desc(tile(s, 1) + koff);
                         const uint64_t bh = smem_desc(tile(s, 2) + koff);
                         const uint64_t bl = smem_desc(tile(s, 3) + koff);
-                        mma<MODE>(tmem, ah, bh, acc0);
-                        mma<MODE>(tmem, ah, bl, 1u);
-                        mma<MODE>(tmem, al, bh, 1u);
+                        // big: accumulator (kk & 1) (BK/KSTEP = 4 slices per
+                        // k-block, so both are initialised in k-block 0)
+                        const uint32_t big = tmem + (uint32_t)((kk & 1) * BN);
+                        mma<MODE>(big, ah, bh, (kb > 0 || kk > 1) ? 1u : 0u);
+                        mma<MODE>(tmem + 2 * BN, ah, bl, acc0);
+                        mma<MODE>(tmem + 2 * BN, al, bh, 1u);
                     } else {
                         mma<MODE>(tmem, smem_desc(tile(s, 0) + koff), smem_desc(tile(s, 1) + koff),
                                   acc0);
@@ -282,7 +290,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         // free TMEM after the epilogue drained it (bounded)
         mbar_wait(done_bar, 0, 4);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+                     ::"r"(tmem), "r"(MODE == F32X3 ? TMEM_COLS : BN));
     } else {
         // ----------------------------- transform (F32) + epilogue, warps 2-5
         const int et = threadIdx.x - 64;   // 0..127
@@ -320,10 +329,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (ok) {
 #pragma unroll
             for (int cb = 0; cb < BN / 32; ++cb) {
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + cb * 32;
                 uint32_t r[32];
-                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + cb * 32, r);
+                tmem_ld32(ta, r);
+                if (MODE == F32X3) {
+                    uint32_t r1[32], r2[32];
+                    tmem_ld32(ta + BN, r1);
+                    tmem_ld32(ta + 2 * BN, r2);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) stage[lane * (BN + 1) + cb * 32 + j] = __uint_as_float(r[j]);
+                    for (int j = 0; j < 32; ++j)
+                        stage[lane * (BN + 1) + cb * 32 + j] =
+                            (__uint_as_float(r[j]) + __uint_as_float(r1[j])) + __uint_as_float(r2[j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        stage[lane * (BN + 1) + cb * 32 + j] = __uint_as_float(r[j]);
+                }
             }
         }
         __syncwarp();
