@@ -16,6 +16,7 @@ LIB_PATH = _PKG / "_lib" / "libmamba_b200.so"
 
 MB2_OK = 0
 MB2_F32, MB2_BF16 = 0, 1
+EPI_NONE, EPI_SOFTPLUS = 0, 1
 SCHEMES = {"none": 0, "int8": 1, "int4": 2, "nf4": 3}
 _ERR_NAMES = {1: "bad argument", 2: "bad shape", 3: "misaligned", 4: "unsupported",
               5: "CUDA error", 6: "workspace too small"}
@@ -54,15 +55,15 @@ _SIGS = {
     "mb2_conv1d_silu": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _vp, _vp, _vp, _c_i64, _vp,
                                        _c_i64, _c_i64, _c_i64, _c_i64, _vp]),
     "mb2_scan_fused": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _vp, _c_i64, _vp, _c_i64,
-                                      _vp, _vp, _vp, _vp, _vp, _vp, _vp, _c_i64,
+                                      _vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp,
                                       _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp]),
     "mb2_linear": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _vp, _vp, _vp, _vp, _c_i64,
-                                  _c_i64, _c_i64, _c_i64, _vp]),
+                                  _c_i64, _c_i64, _c_i64, ctypes.c_int, _vp]),
     "mb2_split_tf32": (ctypes.c_int, [_vp, _vp, _c_i64, _vp]),
     "mb2_quantize": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _c_i64, _vp, _vp, _vp]),
     "mb2_dequantize": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _c_i64, _c_i64, _vp, _vp]),
     "mb2_qlinear": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _vp, _c_i64, _vp, _vp, _vp,
-                                   _vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp]),
+                                   _vp, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _vp]),
     "mb2_block_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Block), _c_i64, _c_i64]),
     "mb2_block_forward": (ctypes.c_int, [ctypes.POINTER(Block), _vp, _vp, _c_i64, _c_i64,
                                          _vp, _vp, _vp, ctypes.c_size_t, _vp]),

@@ -2,14 +2,15 @@
 // the forward_with_final_state state outputs (:165-202) and the single-token
 // step (:103-163), plus the linear-layer entry points.
 //
-// Forward pipeline (5 launches, caller-provided workspace, no allocation):
-//   1. in_proj            x (N, dm)       -> xz (N, 2di)
-//   2. conv1d + SiLU      xz[:, :di]      -> xc (N, di)   [+ conv tail]
-//   3. x_proj             xc              -> xdbl (N, ldx) segments dt_low | B | C,
-//                                            each starting on an 8-element boundary
-//   4. fused scan         xc, xdbl, xz[:, di:] -> y (N, di) [+ h_last]
-//      (dt_proj + softplus + exp(dt A) + recurrence + D skip + SiLU(z) gate)
-//   5. out_proj           y               -> out (N, dm)
+// Forward pipeline (6 launches, caller-provided workspace, no allocation):
+//   1. in_proj            x (N, dm)         -> xz (N, 2di)
+//   2. conv1d + SiLU      xz[:, :di]        -> xc (N, di)   [+ conv tail]
+//   3. x_proj             xc                -> xdbl (N, ldx): dt_low | B | C, each
+//                                              segment on an 8-element boundary
+//   4. dt_proj + softplus xdbl[:, :R]       -> dt (N, di)   (GEMM epilogue)
+//   5. scan               xc, dt, B, C, z   -> y (N, di)    [+ h_last]
+//      (exp(dt A) + recurrence + D skip + cast + SiLU(z) gate; y overwrites dt)
+//   6. out_proj           y                 -> out (N, dm)
 #include "common.cuh"
 
 namespace mb2 {
@@ -17,44 +18,44 @@ namespace mb2 {
 int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
               const float *scale, const void *bias, void *y, int64_t ld_y, int64_t M,
               int64_t N, int64_t K, int64_t n1, int64_t off1, int64_t n2, int64_t off2,
-              cudaStream_t st);
+              int epi, cudaStream_t st);
 int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *w_split,
             const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
-            int64_t n1, int64_t off1, int64_t n2, int64_t off2, cudaStream_t st, bool *used);
+            int64_t n1, int64_t off1, int64_t n2, int64_t off2, int epi, cudaStream_t st,
+            bool *used);
 int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const void *bias,
                 void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
                 int64_t d_inner, int64_t d_conv, cudaStream_t st);
-int scan_fused_segments(int dtype, const void *xc, int64_t ld_xc, const void *dl,
-                        const void *bm, const void *cm, int64_t ld_row, const void *z,
-                        int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
-                        const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
-                        int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
-                        int64_t dt_rank, cudaStream_t stream);
+int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t ld_dt,
+               const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
+               int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
+               void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
+               int64_t d_state, cudaStream_t stream);
 
 // Dense linear: tensor-core kernel where it applies, CUDA-core kernel otherwise.
 static int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, void *y,
-                      int64_t ld_y, int64_t M, int64_t N, int64_t K, int64_t n1 = -1,
-                      int64_t off1 = 0, int64_t n2 = -1, int64_t off2 = 0,
-                      cudaStream_t st = nullptr) {
+                      int64_t ld_y, int64_t M, int64_t N, int64_t K, int epi,
+                      cudaStream_t st, int64_t n1 = -1, int64_t off1 = 0, int64_t n2 = -1,
+                      int64_t off2 = 0) {
     if (n1 < 0) n1 = N;
     if (n2 < 0) n2 = N;
     if (L.scheme != MB2_Q_NONE)
         return gemm_simt(dtype, L.scheme, x, ld_x, L.weight_q, L.scale, L.bias, y, ld_y, M, N, K,
-                         n1, off1, n2, off2, st);
+                         n1, off1, n2, off2, epi, st);
     MB2_REQUIRE(L.weight, MB2_ERR_ARG, "linear: null weight");
     bool used = false;
     MB2_TRY(gemm_tc(dtype, x, ld_x, L.weight, L.weight_split, L.bias, y, ld_y, M, N, K, n1, off1,
-                    n2, off2, st, &used));
+                    n2, off2, epi, st, &used));
     if (used) return MB2_OK;
     return gemm_simt(dtype, MB2_Q_NONE, x, ld_x, L.weight, nullptr, L.bias, y, ld_y, M, N, K,
-                     n1, off1, n2, off2, st);
+                     n1, off1, n2, off2, epi, st);
 }
 
 struct Layout {
     int64_t N, di, dm, S, R, K;
     int64_t RB, RC, ldx;   // x_dbl segment offsets and row length
     size_t es;
-    size_t off_xz, off_xc, off_xdbl, off_y, total;
+    size_t off_xz, off_xc, off_xdbl, off_dt, total;   // y reuses the dt buffer
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -71,7 +72,7 @@ static Layout make_layout(const mb2_block *b, int64_t rows) {
     l.off_xz = off; off = align256(off + (size_t)rows * 2 * l.di * l.es);
     l.off_xc = off; off = align256(off + (size_t)rows * l.di * l.es);
     l.off_xdbl = off; off = align256(off + (size_t)rows * l.ldx * l.es);
-    l.off_y = off; off = align256(off + (size_t)rows * l.di * l.es);
+    l.off_dt = off; off = align256(off + (size_t)rows * l.di * l.es);
     l.total = off;
     return l;
 }
@@ -83,9 +84,6 @@ static int check_block(const mb2_block *b) {
                     b->dt_rank >= 1 && b->d_conv >= 2,
                 MB2_ERR_SHAPE, "block: bad dimensions");
     MB2_REQUIRE(b->conv_w && b->A_log, MB2_ERR_ARG, "block: missing conv1d.weight / A_log");
-    // the fused scan keeps dt_proj's weight rows in registers: a quantised
-    // dt_proj passes its dequantised weight here as well
-    MB2_REQUIRE(b->dt_proj.weight, MB2_ERR_ARG, "block: dt_proj.weight (dense) is required");
     if (b->dtype == MB2_BF16)
         MB2_REQUIRE(b->d_inner % 2 == 0 && b->dt_rank % 2 == 0 && b->d_state % 2 == 0,
                     MB2_ERR_UNSUPPORTED, "block(bf16): d_inner, dt_rank, d_state must be even");
@@ -139,22 +137,27 @@ using namespace mb2;
 
 extern "C" int mb2_linear(int dtype, const void *x, int64_t ld_x, const void *w,
                           const float *w_split, const void *bias, void *y, int64_t ld_y,
-                          int64_t M, int64_t N, int64_t K, mb2_stream_t stream) {
+                          int64_t M, int64_t N, int64_t K, int epilogue, mb2_stream_t stream) {
     MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "linear: bad dtype");
+    MB2_REQUIRE(epilogue == MB2_EPI_NONE || epilogue == MB2_EPI_SOFTPLUS, MB2_ERR_ARG,
+                "linear: bad epilogue");
     MB2_REQUIRE(ld_x >= K && ld_y >= N, MB2_ERR_SHAPE, "linear: leading dimension too small");
     mb2_linear_w L{w, w_split, nullptr, nullptr, bias, MB2_Q_NONE};
-    return linear_any(dtype, L, x, ld_x, y, ld_y, M, N, K, -1, 0, -1, 0, (cudaStream_t)stream);
+    return linear_any(dtype, L, x, ld_x, y, ld_y, M, N, K, epilogue, (cudaStream_t)stream);
 }
 
 extern "C" int mb2_qlinear(int scheme, int dtype, const void *x, int64_t ld_x,
                            const void *weight_q, const float *scale, const void *bias, void *y,
-                           int64_t ld_y, int64_t M, int64_t N, int64_t K, mb2_stream_t stream) {
+                           int64_t ld_y, int64_t M, int64_t N, int64_t K, int epilogue,
+                           mb2_stream_t stream) {
     MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "qlinear: bad dtype");
     MB2_REQUIRE(scheme == MB2_Q_INT8 || scheme == MB2_Q_INT4 || scheme == MB2_Q_NF4, MB2_ERR_ARG,
                 "unknown scheme %d", scheme);
     MB2_REQUIRE(ld_x >= K && ld_y >= N, MB2_ERR_SHAPE, "qlinear: leading dimension too small");
+    MB2_REQUIRE(epilogue == MB2_EPI_NONE || epilogue == MB2_EPI_SOFTPLUS, MB2_ERR_ARG,
+                "qlinear: bad epilogue");
     return gemm_simt(dtype, scheme, x, ld_x, weight_q, scale, bias, y, ld_y, M, N, K, N, 0, N, 0,
-                     (cudaStream_t)stream);
+                     epilogue, (cudaStream_t)stream);
 }
 
 extern "C" size_t mb2_block_workspace_bytes(const mb2_block *blk, int64_t batch, int64_t seqlen) {
@@ -174,25 +177,26 @@ extern "C" int mb2_block_forward(const mb2_block *blk, const void *x, void *out,
                 "block: workspace %zu < required %zu", workspace_bytes, l.total);
     if (batch == 0) return MB2_OK;
     char *ws = static_cast<char *>(workspace);
-    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl, *y = ws + l.off_y;
+    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl, *dt = ws + l.off_dt;
     const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
     const size_t es = l.es;
     if (N > 0) {
         MB2_REQUIRE(x && out && workspace, MB2_ERR_ARG, "block: null pointer");
-        MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, N, 2 * di, l.dm, -1, 0, -1, 0, st));
+        MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, N, 2 * di, l.dm, MB2_EPI_NONE,
+                           st));
     }
     MB2_TRY(conv1d_silu(b.dtype, xz, 2 * di, b.conv_w, b.conv_b, xc, di, conv_tail, batch, seqlen,
                         di, b.d_conv, st));
     if (N > 0) {
-        MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, R, l.RB - R,
-                           R + S, l.RC - l.RB - S, st));
+        MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, MB2_EPI_NONE,
+                           st, R, l.RB - R, R + S, l.RC - l.RB - S));
+        MB2_TRY(linear_any(b.dtype, b.dt_proj, xdbl, l.ldx, dt, di, N, di, R, MB2_EPI_SOFTPLUS, st));
     }
-    MB2_TRY(scan_fused_segments(b.dtype, xc, di, xdbl, (char *)xdbl + l.RB * es,
-                                (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
-                                b.dt_proj.weight, b.dt_proj.bias, b.A_log, b.D, nullptr, h_last, y,
-                                di, batch, seqlen, di, S, R, st));
+    MB2_TRY(scan_gated(b.dtype, xc, di, dt, di, (char *)xdbl + l.RB * es, l.ldx,
+                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log, b.D,
+                       nullptr, h_last, dt, di, batch, seqlen, di, S, st));
     if (N > 0)
-        MB2_TRY(linear_any(b.dtype, b.out_proj, y, di, out, l.dm, N, l.dm, di, -1, 0, -1, 0, st));
+        MB2_TRY(linear_any(b.dtype, b.out_proj, dt, di, out, l.dm, N, l.dm, di, MB2_EPI_NONE, st));
     return MB2_OK;
 }
 
@@ -214,22 +218,23 @@ extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, fl
     if (batch == 0) return MB2_OK;
     MB2_REQUIRE(x && out && h && conv_state && workspace, MB2_ERR_ARG, "step: null pointer");
     char *ws = static_cast<char *>(workspace);
-    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl, *y = ws + l.off_y;
+    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl, *dt = ws + l.off_dt;
     const int64_t di = l.di, S = l.S, R = l.R;
     const size_t es = l.es;
-    MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, batch, 2 * di, l.dm, -1, 0, -1, 0, st));
+    MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, batch, 2 * di, l.dm, MB2_EPI_NONE,
+                       st));
     if (b.dtype == MB2_F32)
         MB2_TRY(launch_conv_step<float>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b, conv_state,
                                         xc, batch, di, st));
     else
         MB2_TRY(launch_conv_step<__nv_bfloat16>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b,
                                                 conv_state, xc, batch, di, st));
-    MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, batch, R + 2 * S, di, R, l.RB - R,
-                       R + S, l.RC - l.RB - S, st));
-    // one timestep of the fused scan, h read and written in place
-    MB2_TRY(scan_fused_segments(b.dtype, xc, di, xdbl, (char *)xdbl + l.RB * es,
-                                (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
-                                b.dt_proj.weight, b.dt_proj.bias, b.A_log, b.D, h, h, y, di, batch,
-                                1, di, S, R, st));
-    return linear_any(b.dtype, b.out_proj, y, di, out, l.dm, batch, l.dm, di, -1, 0, -1, 0, st);
+    MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, batch, R + 2 * S, di, MB2_EPI_NONE,
+                       st, R, l.RB - R, R + S, l.RC - l.RB - S));
+    MB2_TRY(linear_any(b.dtype, b.dt_proj, xdbl, l.ldx, dt, di, batch, di, R, MB2_EPI_SOFTPLUS, st));
+    // one timestep of the scan, h read and written in place
+    MB2_TRY(scan_gated(b.dtype, xc, di, dt, di, (char *)xdbl + l.RB * es, l.ldx,
+                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log, b.D,
+                       h, h, dt, di, batch, 1, di, S, st));
+    return linear_any(b.dtype, b.out_proj, dt, di, out, l.dm, batch, l.dm, di, MB2_EPI_NONE, st);
 }

@@ -72,6 +72,7 @@ struct Params {
     const void *bias;
     int64_t M, N, K;
     int64_t n1, n2, off1, off2;   // output column remap
+    int epi;                      // MB2_EPI_NONE / MB2_EPI_SOFTPLUS
 };
 
 // ------------------------------------------------------------- primitives
@@ -362,6 +363,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     if (n < p.N) {
                         float v = stage[rr * (BN + 1) + c4 * 32 + lane];
                         if (bias) v += io<TO>::to_f(bias[n]);
+                        // dt_proj's softplus (_mamba.py:219-220) on the value
+                        // the reference would have stored in its dtype
+                        if (p.epi == MB2_EPI_SOFTPLUS) v = softplus_f(io<TO>::round(v));
                         const int64_t col = n + (n >= p.n1 ? p.off1 : 0) + (n >= p.n2 ? p.off2 : 0);
                         Y[m * p.ld_y + col] = io<TO>::from_f(v);
                     }
@@ -418,7 +422,8 @@ static int launch_tc(const CUtensorMap &a, const CUtensorMap &b0, const CUtensor
 // Tensor-core path when it applies (large M, aligned operands); *used reports it.
 int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *w_split,
             const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
-            int64_t n1, int64_t off1, int64_t n2, int64_t off2, cudaStream_t st, bool *used) {
+            int64_t n1, int64_t off1, int64_t n2, int64_t off2, int epi, cudaStream_t st,
+            bool *used) {
     *used = false;
     const bool bf16 = dtype == MB2_BF16;
     const size_t es = bf16 ? 2 : 4;
@@ -435,7 +440,7 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
     MB2_TRY(make_map(&ma, x, M, K, ld_x, bf16));
     MB2_TRY(make_map(&mb0, b0, N, K, K, bf16));
     MB2_TRY(make_map(&mb1, b1, N, K, K, bf16));
-    tc::Params p{y, ld_y, bias, M, N, K, n1, n2, off1, off2};
+    tc::Params p{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi};
     *used = true;
     if (bf16) return launch_tc<tc::BF16, __nv_bfloat16>(ma, mb0, mb1, p, st);
     return launch_tc<tc::F32X3, float>(ma, mb0, mb1, p, st);

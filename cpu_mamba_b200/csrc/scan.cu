@@ -1,25 +1,30 @@
 // Selective scan kernels (Mamba S6 recurrence) for sm_100a.
 //
 // Reference semantics: src/cpu_mamba/selective_scan_cpu.cpp:56-85 -- for each
-// (batch b, channel d): h[s] = 0; for t: dA = exp(dt*A[d,s]);
+// (batch b, channel d): h[s] = h0 or 0; for t: dA = exp(dt*A[d,s]);
 // dBx = (dt*B[b,t,s])*x; h = dA*h + dBx; y += h*C[b,t,s]; out = y + D[d]*x.
 //
 // Mapping: one CTA owns (batch b, 128/L consecutive channels) for the whole
 // sequence.  Each channel is handled by L adjacent lanes, each holding SPL of
-// the d_state states of h in registers (L*SPL >= d_state, padded states have
-// A = B = C = 0 so they stay 0).  The per-lane partial y is reduced with
-// shuffles.  Time is sequential; inputs for SCAN_TC timesteps are staged in
-// shared memory by asynchronous copies one chunk ahead (double buffer).
+// the d_state states of h in registers (L*SPL >= d_state; padded states have
+// A = B = C = 0 and stay 0); the per-lane partial y is reduced with shuffles.
+// Time is sequential: the recurrence is cheap, the d_state exponentials per
+// token-channel on the MUFU pipe are the bound, and every (b, channel) pair is
+// independent, so the GPU is filled by batch x channels without splitting T.
+// Inputs for SCAN_TC timesteps are staged in shared memory by asynchronous
+// copies one chunk ahead (double buffer): the per-channel x / dt / z rows
+// (coalesced across the CTA's channels) and the B / C rows, which every
+// channel of the CTA reads with vector loads.
 //
-// exp(dt*A) is evaluated as exp2(dt * (A*log2 e)) on the MUFU pipe, which is
-// the bound of this kernel (d_state exponentials per token-channel).
+// exp(dt*A) is evaluated as 2^(dt * (A log2 e)) with ex2.approx.ftz.
 //
 // Two modes:
-//   plain  -- drop-in for selective_scan_cpu: dt given, A given, no gate;
-//   fused  -- dt = softplus(dt_low . W_dt[d] + b_dt) computed in registers
-//             (dt_proj fused: _mamba.py:219-220), A = -exp(A_log) (:222),
-//             output cast to the activation dtype and gated by SiLU(z)
-//             (:263-264).
+//   plain  -- drop-in for selective_scan_cpu: A given, output y + D x in fp32;
+//   gated  -- A = -exp(A_log) from the module's parameter (_mamba.py:222),
+//             output cast to the activation dtype and multiplied by SiLU(z)
+//             (_mamba.py:263-264).
+// dt always arrives precomputed (softplus(dt_proj(.)) is the epilogue of the
+// dt_proj GEMM).
 #include "common.cuh"
 
 namespace mb2 {
@@ -28,56 +33,127 @@ constexpr int SCAN_THREADS = 128;  // threads per CTA; channels per CTA = 128 / 
 constexpr int SCAN_TC = 16;        // timesteps per staged chunk
 
 struct ScanParams {
-    const void *x;    int64_t ld_x;   // (N, ld_x)   x (plain) / conv output (fused)
-    const void *d2;   int64_t ld_d2;  // (N, ld_d2)  dt (plain) / z (fused)
-    const void *bm;   int64_t ld_b;   // rows of B
-    const void *cm;   int64_t ld_c;   // rows of C
-    const void *dl;   int64_t ld_dl;  // rows of dt_low (fused)
-    const void *w_dt; const void *b_dt;  // (di, R), (di)            (fused)
-    const void *A;                    // A (fp32, plain) or A_log (dtype, fused)
-    const void *D;                    // (di) fp32 (plain) / dtype (fused)
-    const float *h0; float *h_last;   // (batch, di, S) or null
-    void *y;          int64_t ld_y;
+    const void *x;  int64_t ld_x;    // (N, ld_x)  x / conv output
+    const void *dt; int64_t ld_dt;   // (N, ld_dt) dt (softplus applied)
+    const void *z;  int64_t ld_z;    // (N, ld_z)  gate input (gated mode)
+    const void *bm; int64_t ld_b;    // rows of B
+    const void *cm; int64_t ld_c;    // rows of C
+    const void *A;                   // A fp32 (plain) or A_log in T (gated)
+    const void *D;                   // (di) fp32 (plain) / T (gated), may be null
+    const float *h0; float *h_last;  // (batch, di, S) or null
+    void *y;        int64_t ld_y;
     int64_t batch, seqlen, d_inner;
-    int d_state, dt_rank, lanes;      // lanes == L
+    int d_state, lanes;              // lanes == L
+    unsigned vec16;                  // bit i: array i rows are 16-byte aligned
 };
 
-// Words (4-byte units) of one staged row segment of `n` elements of T.
+enum { ARR_X = 1, ARR_DT = 2, ARR_Z = 4, ARR_B = 8, ARR_C = 16 };
+
 template <typename T> __host__ __device__ constexpr int epw() { return 4 / (int)sizeof(T); }
 
-// Stage `rows` x `cols_padded` elements (cols valid, rest zero) of a row-major
-// source into shared memory, as 4-byte async copies with zero fill.
+__device__ __forceinline__ float ex2(float v) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+
+// Stage rows x cols_padded elements of a row-major source into shared memory
+// (valid cols copied, the rest zero-filled): 16-byte async copies when the
+// rows are 16-byte aligned, else 4-byte copies with hardware zero fill.
 template <typename T>
-__device__ __forceinline__ void stage_rows(T *dst, int cols_padded, const T *src,
-                                           int64_t ld, int64_t row0, int rows_valid,
-                                           int rows, int cols, int tid, int nthr) {
+__device__ __forceinline__ void stage_rows(T *dst, int cols_padded, const T *src, int64_t ld,
+                                           int64_t row0, int rows_valid, int rows, int cols,
+                                           bool vec16, int tid, int nthr) {
     constexpr int E = epw<T>();
-    const int wpr = cols_padded / E;  // words per row (cols_padded % E == 0)
+    if (vec16) {
+        constexpr int V = 16 / (int)sizeof(T);        // elements per 16-byte chunk
+        const int cpr = cols_padded / V;              // chunks per row
+        const int total = rows * cpr;
+        for (int i = tid; i < total; i += nthr) {
+            const int r = i / cpr;
+            const int c = (i - r * cpr) * V;
+            const uint32_t s = smem_u32(dst + r * cols_padded + c);
+            const bool rv = r < rows_valid;
+            if (rv && c + V <= cols) {
+                cp_async16(dst + r * cols_padded + c, src + (row0 + r) * ld + c);
+            } else {
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    const int cw = c + w * E;
+                    int bytes = 0;
+                    const T *g = src;
+                    if (rv && cw < cols) {
+                        g = src + (row0 + r) * ld + cw;
+                        bytes = (cols - cw >= E) ? 4 : 2;
+                    }
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n"
+                                 ::"r"(s + 4 * w), "l"(g), "r"(bytes));
+                }
+            }
+        }
+        return;
+    }
+    const int wpr = cols_padded / E;  // words per row
     const int total = rows * wpr;
     for (int i = tid; i < total; i += nthr) {
         const int r = i / wpr;
-        const int w = i - r * wpr;
-        const int c = w * E;
+        const int c = (i - r * wpr) * E;
         int bytes = 0;
         const T *g = src;
         if (r < rows_valid && c < cols) {
             g = src + (row0 + r) * ld + c;
             bytes = (cols - c >= E) ? 4 : 2;  // half word only for bf16 tails
         }
-        uint32_t s = smem_u32(dst + r * cols_padded + c);
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(g),
-                     "r"(bytes));
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n"
+                     ::"r"(smem_u32(dst + r * cols_padded + c)), "l"(g), "r"(bytes));
     }
 }
 
-template <typename T, int SPL, int RMAX, bool FUSED>
+// N consecutive values from shared memory as floats, widest aligned loads.
+template <typename T, int N> struct Vec;
+template <int N> struct Vec<float, N> {
+    static __device__ __forceinline__ void load(const float *p, float (&v)[N]) {
+#pragma unroll
+        for (int k = 0; k < N / 4; ++k) {
+            const float4 q = reinterpret_cast<const float4 *>(p)[k];
+            v[4 * k] = q.x; v[4 * k + 1] = q.y; v[4 * k + 2] = q.z; v[4 * k + 3] = q.w;
+        }
+    }
+};
+template <int N> struct Vec<__nv_bfloat16, N> {
+    static __device__ __forceinline__ void load(const __nv_bfloat16 *p, float (&v)[N]) {
+#pragma unroll
+        for (int k = 0; k < N / 4; ++k) {
+            const uint2 q = reinterpret_cast<const uint2 *>(p)[k];
+            v[4 * k] = __uint_as_float(q.x << 16);
+            v[4 * k + 1] = __uint_as_float(q.x & 0xFFFF0000u);
+            v[4 * k + 2] = __uint_as_float(q.y << 16);
+            v[4 * k + 3] = __uint_as_float(q.y & 0xFFFF0000u);
+        }
+    }
+};
+
+// Per-stage layout (elements of T): x | dt | z | B | C, each block a multiple
+// of 16 bytes so every array starts 16-byte aligned.
+struct StageLayout {
+    int CH, SPp, n_x, n_bc, elems;
+    __host__ __device__ StageLayout(int L, int spl, int esize, bool gated) {
+        CH = SCAN_THREADS / L;
+        const int v = 16 / esize;
+        SPp = ((L * spl + v - 1) / v) * v;
+        n_x = SCAN_TC * CH;
+        n_bc = SCAN_TC * SPp;
+        elems = (gated ? 3 : 2) * n_x + 2 * n_bc;
+    }
+};
+
+template <typename T, int SPL, bool GATED>
 __global__ void __launch_bounds__(SCAN_THREADS, 4)
 scan_kernel(const ScanParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    constexpr int E = epw<T>();
     const int L = p.lanes;
-    const int CH = SCAN_THREADS / L;  // channels per CTA
-    const int nthr = SCAN_THREADS;
+    const StageLayout lay(L, SPL, (int)sizeof(T), GATED);
+    const int CH = lay.CH;
     const int tid = threadIdx.x;
     const int c = tid / L;         // channel within CTA
     const int j = tid - c * L;     // lane within channel group
@@ -88,72 +164,51 @@ scan_kernel(const ScanParams p) {
     const int S = p.d_state;
     const int T_ = (int)p.seqlen;
     const int ch_valid = (int)((p.d_inner - d0 < CH) ? p.d_inner - d0 : CH);
-
-    // staged layout (per stage), all row lengths multiples of E elements
-    const int SP = L * SPL;                        // padded states per row
-    const int SPp = ((SP + E - 1) / E) * E;
-    const int RP = FUSED ? L * RMAX : 0;           // padded dt_low per row
-    const int n_x = SCAN_TC * CH;
-    const int n_bc = SCAN_TC * SPp;
-    const int n_dl = SCAN_TC * RP;
-    const int stage_elems = 2 * n_x + 2 * n_bc + n_dl;
     T *stage0 = reinterpret_cast<T *>(smem_raw);
 
-    // per-thread constants
     float A2[SPL], h[SPL];
 #pragma unroll
     for (int i = 0; i < SPL; ++i) {
         const int s = j * SPL + i;
         float a = 0.0f, h_init = 0.0f;
         if (active && s < S) {
-            if (FUSED) {
-                const float alog = io<T>::to_f(static_cast<const T *>(p.A)[d * S + s]);
-                a = -expf(alog);
-            } else {
+            if (GATED)
+                a = -expf(io<T>::to_f(static_cast<const T *>(p.A)[d * S + s]));
+            else
                 a = static_cast<const float *>(p.A)[d * S + s];
-            }
             if (p.h0) h_init = p.h0[((int64_t)b * p.d_inner + d) * S + s];
         }
         A2[i] = a * kLog2e;
         h[i] = h_init;
     }
-    float wdt[FUSED ? RMAX : 1];
-    float bias_dt = 0.0f, Dv = 0.0f;
-    if (FUSED) {
-#pragma unroll
-        for (int r = 0; r < RMAX; ++r) {
-            const int rr = j * RMAX + r;
-            wdt[r] = (active && rr < p.dt_rank)
-                         ? io<T>::to_f(static_cast<const T *>(p.w_dt)[d * p.dt_rank + rr])
-                         : 0.0f;
-        }
-        if (active) {
-            bias_dt = p.b_dt ? io<T>::to_f(static_cast<const T *>(p.b_dt)[d]) : 0.0f;
-            Dv = p.D ? io<T>::to_f(static_cast<const T *>(p.D)[d]) : 0.0f;
-        }
-    } else if (active) {
-        Dv = p.D ? static_cast<const float *>(p.D)[d] : 0.0f;
-    }
+    float Dv = 0.0f;
+    if (active && p.D)
+        Dv = GATED ? io<T>::to_f(static_cast<const T *>(p.D)[d]) : static_cast<const float *>(p.D)[d];
 
     const int64_t row_base = (int64_t)b * p.seqlen;
     const T *xg = static_cast<const T *>(p.x) + d0;
-    const T *d2g = static_cast<const T *>(p.d2) + d0;
+    const T *dtg = static_cast<const T *>(p.dt) + d0;
+    const T *zg = GATED ? static_cast<const T *>(p.z) + d0 : nullptr;
     const T *bg = static_cast<const T *>(p.bm);
     const T *cg = static_cast<const T *>(p.cm);
-    const T *dlg = static_cast<const T *>(p.dl);
+    const int nz = GATED ? 1 : 0;
 
     auto issue = [&](int chunk) {
-        T *st = stage0 + (chunk & 1) * stage_elems;
+        T *st = stage0 + (chunk & 1) * lay.elems;
         const int t0 = chunk * SCAN_TC;
         const int rv = min(SCAN_TC, T_ - t0);
         const int64_t r0 = row_base + t0;
-        stage_rows<T>(st, CH, xg, p.ld_x, r0, rv, SCAN_TC, ch_valid, tid, nthr);
-        stage_rows<T>(st + n_x, CH, d2g, p.ld_d2, r0, rv, SCAN_TC, ch_valid, tid, nthr);
-        stage_rows<T>(st + 2 * n_x, SPp, bg, p.ld_b, r0, rv, SCAN_TC, S, tid, nthr);
-        stage_rows<T>(st + 2 * n_x + n_bc, SPp, cg, p.ld_c, r0, rv, SCAN_TC, S, tid, nthr);
-        if (FUSED)
-            stage_rows<T>(st + 2 * n_x + 2 * n_bc, RP, dlg, p.ld_dl, r0, rv, SCAN_TC,
-                          p.dt_rank, tid, nthr);
+        stage_rows<T>(st, CH, xg, p.ld_x, r0, rv, SCAN_TC, ch_valid, p.vec16 & ARR_X,
+                      tid, SCAN_THREADS);
+        stage_rows<T>(st + lay.n_x, CH, dtg, p.ld_dt, r0, rv, SCAN_TC, ch_valid,
+                      p.vec16 & ARR_DT, tid, SCAN_THREADS);
+        if (GATED)
+            stage_rows<T>(st + 2 * lay.n_x, CH, zg, p.ld_z, r0, rv, SCAN_TC, ch_valid,
+                          p.vec16 & ARR_Z, tid, SCAN_THREADS);
+        stage_rows<T>(st + (2 + nz) * lay.n_x, lay.SPp, bg, p.ld_b, r0, rv, SCAN_TC, S,
+                      p.vec16 & ARR_B, tid, SCAN_THREADS);
+        stage_rows<T>(st + (2 + nz) * lay.n_x + lay.n_bc, lay.SPp, cg, p.ld_c, r0, rv, SCAN_TC,
+                      S, p.vec16 & ARR_C, tid, SCAN_THREADS);
     };
 
     const int nchunks = (T_ + SCAN_TC - 1) / SCAN_TC;
@@ -166,43 +221,34 @@ scan_kernel(const ScanParams p) {
         cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        const T *st = stage0 + (ch & 1) * stage_elems;
-        const T *xs = st;
-        const T *d2s = st + n_x;
-        const T *bs = st + 2 * n_x + j * SPL;
-        const T *cs = st + 2 * n_x + n_bc + j * SPL;
-        const T *dls = st + 2 * n_x + 2 * n_bc + j * RMAX;
+        const T *st = stage0 + (ch & 1) * lay.elems;
+        const T *xs = st + c;
+        const T *dts = st + lay.n_x + c;
+        const T *zs = st + 2 * lay.n_x + c;
+        const T *bs = st + (2 + nz) * lay.n_x + j * SPL;
+        const T *cs = bs + lay.n_bc;
         const int t0 = ch * SCAN_TC;
         const int tn = min(SCAN_TC, T_ - t0);
+#pragma unroll 2
         for (int tt = 0; tt < tn; ++tt) {
-            const float xv = io<T>::to_f(xs[tt * CH + c]);
-            float dtv;
-            if (FUSED) {
-                float part = 0.0f;
-#pragma unroll
-                for (int r = 0; r < RMAX; ++r)
-                    part = fmaf(io<T>::to_f(dls[tt * RP + r]), wdt[r], part);
-                for (int m = 1; m < L; m <<= 1) part += __shfl_xor_sync(0xffffffffu, part, m);
-                const float v = io<T>::round(part + bias_dt);
-                dtv = io<T>::round(softplus_f(v));
-            } else {
-                dtv = io<T>::to_f(d2s[tt * CH + c]);
-            }
+            const float xv = io<T>::to_f(xs[tt * CH]);
+            const float dtv = io<T>::to_f(dts[tt * CH]);
+            float bv[SPL], cv[SPL];
+            Vec<T, SPL>::load(bs + tt * lay.SPp, bv);
+            Vec<T, SPL>::load(cs + tt * lay.SPp, cv);
             float yp = 0.0f;
 #pragma unroll
             for (int i = 0; i < SPL; ++i) {
-                const float bv = io<T>::to_f(bs[tt * SPp + i]);
-                const float cv = io<T>::to_f(cs[tt * SPp + i]);
-                const float dA = exp2f(dtv * A2[i]);
-                const float dBx = (dtv * bv) * xv;
+                const float dA = ex2(dtv * A2[i]);
+                const float dBx = (dtv * bv[i]) * xv;
                 h[i] = fmaf(dA, h[i], dBx);
-                yp = fmaf(h[i], cv, yp);
+                yp = fmaf(h[i], cv[i], yp);
             }
             for (int m = 1; m < L; m <<= 1) yp += __shfl_xor_sync(0xffffffffu, yp, m);
             if (j == 0 && active) {
                 float out = yp + Dv * xv;
-                if (FUSED) {
-                    const float zv = io<T>::to_f(d2s[tt * CH + c]);
+                if (GATED) {
+                    const float zv = io<T>::to_f(zs[tt * CH]);
                     out = io<T>::round(out) * io<T>::round(silu_f(zv));
                 }
                 yg[(row_base + t0 + tt) * p.ld_y + d] = io<T>::from_f(out);
@@ -233,64 +279,88 @@ static ScanShape pick_shape(int S) {
     return {16, 16};
 }
 
-static int pick_rmax(int R, int L) {
-    const int per = (R + L - 1) / L;
-    const int opts[] = {8, 16, 24, 32, 48, 64};
-    for (int o : opts)
-        if (per <= o) return o;
-    return -1;
+static bool rows16(const void *p, int64_t ld, size_t es) {
+    return aligned(p, 16) && (ld * (int64_t)es) % 16 == 0;
 }
 
-template <typename T, int SPL, int RMAX, bool FUSED>
-static int launch_scan(const ScanParams &p, cudaStream_t st) {
-    constexpr int E = epw<T>();
-    const int L = p.lanes;
-    const int SP = L * SPL;
-    const int SPp = ((SP + E - 1) / E) * E;
-    const int RP = FUSED ? L * RMAX : 0;
-    const int CH = SCAN_THREADS / L;
-    const size_t stage = (size_t)(2 * SCAN_TC * CH + 2 * SCAN_TC * SPp + SCAN_TC * RP) * sizeof(T);
-    const size_t smem = 2 * stage;
-    auto kern = scan_kernel<T, SPL, RMAX, FUSED>;
+template <typename T, int SPL, bool GATED>
+static int launch_scan(ScanParams p, cudaStream_t st) {
+    const StageLayout lay(p.lanes, SPL, (int)sizeof(T), GATED);
+    const size_t smem = 2 * (size_t)lay.elems * sizeof(T);
+    auto kern = scan_kernel<T, SPL, GATED>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "scan: smem attribute: %s", cudaGetErrorString(e));
     }
-    dim3 grid((unsigned)ceil_div(p.d_inner, CH), (unsigned)p.batch);
+    const size_t es = sizeof(T);
+    // the x / dt / z tiles start at channel d0 = blockIdx.x * CH
+    const bool ch16 = (lay.CH * es) % 16 == 0;
+    p.vec16 = 0;
+    if (ch16 && rows16(p.x, p.ld_x, es)) p.vec16 |= ARR_X;
+    if (ch16 && rows16(p.dt, p.ld_dt, es)) p.vec16 |= ARR_DT;
+    if (GATED && ch16 && rows16(p.z, p.ld_z, es)) p.vec16 |= ARR_Z;
+    if (rows16(p.bm, p.ld_b, es)) p.vec16 |= ARR_B;
+    if (rows16(p.cm, p.ld_c, es)) p.vec16 |= ARR_C;
+    dim3 grid((unsigned)ceil_div(p.d_inner, lay.CH), (unsigned)p.batch);
     kern<<<grid, SCAN_THREADS, smem, st>>>(p);
     return check_launch("scan_kernel");
 }
 
-template <typename T, bool FUSED, int SPL>
-static int dispatch_rmax(const ScanParams &p, int rmax, cudaStream_t st) {
-    if constexpr (!FUSED) {
-        return launch_scan<T, SPL, 8, false>(p, st);
-    } else {
-    switch (rmax) {
-        case 8: return launch_scan<T, SPL, 8, FUSED>(p, st);
-        case 16: return launch_scan<T, SPL, 16, FUSED>(p, st);
-        case 24: return launch_scan<T, SPL, 24, FUSED>(p, st);
-        case 32: return launch_scan<T, SPL, 32, FUSED>(p, st);
-        case 48: return launch_scan<T, SPL, 48, FUSED>(p, st);
-        case 64: return launch_scan<T, SPL, 64, FUSED>(p, st);
-    }
-    return fail(MB2_ERR_UNSUPPORTED, "scan: dt_rank %d too large for %d lanes", p.dt_rank, p.lanes);
-    }
-}
-
-template <typename T, bool FUSED>
+template <typename T, bool GATED>
 static int dispatch_scan(ScanParams p, cudaStream_t st) {
     const ScanShape sh = pick_shape(p.d_state);
     p.lanes = sh.lanes;
-    const int rmax = FUSED ? pick_rmax(p.dt_rank, sh.lanes) : 8;
-    if (FUSED && rmax < 0)
-        return fail(MB2_ERR_UNSUPPORTED, "scan: dt_rank %d too large (max %d for d_state %d)",
-                    p.dt_rank, 64 * sh.lanes, p.d_state);
     switch (sh.spl) {
-        case 8: return dispatch_rmax<T, FUSED, 8>(p, rmax, st);
-        case 12: return dispatch_rmax<T, FUSED, 12>(p, rmax, st);
-        default: return dispatch_rmax<T, FUSED, 16>(p, rmax, st);
+        case 8: return launch_scan<T, 8, GATED>(p, st);
+        case 12: return launch_scan<T, 12, GATED>(p, st);
+        default: return launch_scan<T, 16, GATED>(p, st);
     }
+}
+
+// Shared argument checks; 4-byte staging copies need 4-byte aligned bf16 rows.
+static int check_rows(int dtype, const void *ptr, int64_t ld, int64_t cols, const char *name) {
+    MB2_REQUIRE(ld >= cols, MB2_ERR_SHAPE, "scan: leading dimension of %s too small", name);
+    if (dtype == MB2_BF16)
+        MB2_REQUIRE(aligned(ptr, 4) && ld % 2 == 0, MB2_ERR_ALIGN,
+                    "scan(bf16): %s rows must start on 4-byte boundaries (even offsets and "
+                    "leading dimension)", name);
+    return MB2_OK;
+}
+
+int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t ld_dt,
+               const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
+               int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
+               void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
+               int64_t d_state, cudaStream_t stream) {
+    MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "scan: bad dtype");
+    MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0, MB2_ERR_SHAPE, "scan: bad sizes");
+    MB2_REQUIRE(d_state >= 1 && d_state <= 256, MB2_ERR_SHAPE,
+                "d_state > 256 not supported (got %lld)", (long long)d_state);
+    MB2_REQUIRE(batch < 65536, MB2_ERR_SHAPE, "scan: batch too large");
+    if (batch == 0 || d_inner == 0) return MB2_OK;
+    MB2_REQUIRE(A_log && (seqlen == 0 || (xc && dt && bm && cm && z && y)), MB2_ERR_ARG,
+                "scan: null pointer");
+    if (dtype == MB2_BF16)
+        MB2_REQUIRE(d_inner % 2 == 0 && d_state % 2 == 0, MB2_ERR_ALIGN,
+                    "scan(bf16): d_inner and d_state must be even");
+    MB2_TRY(check_rows(dtype, xc, ld_xc, d_inner, "x"));
+    MB2_TRY(check_rows(dtype, dt, ld_dt, d_inner, "dt"));
+    MB2_TRY(check_rows(dtype, z, ld_z, d_inner, "z"));
+    MB2_TRY(check_rows(dtype, bm, ld_b, d_state, "B"));
+    MB2_TRY(check_rows(dtype, cm, ld_c, d_state, "C"));
+    MB2_REQUIRE(ld_y >= d_inner, MB2_ERR_SHAPE, "scan: leading dimension of y too small");
+    ScanParams p{};
+    p.x = xc; p.ld_x = ld_xc;
+    p.dt = dt; p.ld_dt = ld_dt;
+    p.z = z; p.ld_z = ld_z;
+    p.bm = bm; p.ld_b = ld_b;
+    p.cm = cm; p.ld_c = ld_c;
+    p.A = A_log; p.D = D; p.h0 = h0; p.h_last = h_last;
+    p.y = y; p.ld_y = ld_y;
+    p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
+    p.d_state = (int)d_state;
+    if (dtype == MB2_F32) return dispatch_scan<float, true>(p, stream);
+    return dispatch_scan<__nv_bfloat16, true>(p, stream);
 }
 
 }  // namespace mb2
@@ -313,82 +383,22 @@ extern "C" int mb2_selective_scan(const float *x, const float *dt, const float *
                 "selective_scan: null pointer");
     ScanParams p{};
     p.x = x; p.ld_x = d_inner;
-    p.d2 = dt; p.ld_d2 = d_inner;
+    p.dt = dt; p.ld_dt = d_inner;
     p.bm = B; p.ld_b = d_state;
     p.cm = C; p.ld_c = d_state;
     p.A = A; p.D = D; p.h0 = h0; p.h_last = h_last;
     p.y = y; p.ld_y = d_inner;
     p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
-    p.d_state = (int)d_state; p.dt_rank = 0;
+    p.d_state = (int)d_state;
     return dispatch_scan<float, false>(p, (cudaStream_t)stream);
 }
 
-extern "C" int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *xdbl,
-                              int64_t ld_xdbl, const void *z, int64_t ld_z,
-                              const void *w_dt, const void *b_dt, const void *A_log,
+extern "C" int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dt,
+                              int64_t ld_dt, const void *B, int64_t ld_b, const void *C,
+                              int64_t ld_c, const void *z, int64_t ld_z, const void *A_log,
                               const void *D, const float *h0, float *h_last, void *y,
                               int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
-                              int64_t d_state, int64_t dt_rank, mb2_stream_t stream) {
-    MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "scan_fused: bad dtype");
-    MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0 && dt_rank >= 1, MB2_ERR_SHAPE,
-                "scan_fused: bad sizes");
-    MB2_REQUIRE(d_state >= 1 && d_state <= 256, MB2_ERR_SHAPE,
-                "d_state > 256 not supported (got %lld)", (long long)d_state);
-    MB2_REQUIRE(batch < 65536, MB2_ERR_SHAPE, "scan_fused: batch too large");
-    if (batch == 0 || d_inner == 0) return MB2_OK;
-    MB2_REQUIRE(w_dt && A_log && (seqlen == 0 || (xc && xdbl && z && y)), MB2_ERR_ARG,
-                "scan_fused: null pointer");
-    MB2_REQUIRE(ld_xc >= d_inner && ld_z >= d_inner && ld_y >= d_inner &&
-                    ld_xdbl >= dt_rank + 2 * d_state,
-                MB2_ERR_SHAPE, "scan_fused: leading dimension too small");
-    const size_t es = dtype_size(dtype);
-    if (dtype == MB2_BF16) {
-        // 4-byte staging copies: every row segment must start on a 4-byte boundary
-        MB2_REQUIRE(aligned(xc, 4) && aligned(z, 4) && aligned(xdbl, 4) && ld_xc % 2 == 0 &&
-                        ld_z % 2 == 0 && ld_xdbl % 2 == 0 && dt_rank % 2 == 0 &&
-                        d_state % 2 == 0 && d_inner % 2 == 0,
-                    MB2_ERR_ALIGN,
-                    "scan_fused(bf16): pointers, leading dims, d_inner, dt_rank and d_state "
-                    "must be even / 4-byte aligned");
-    }
-    (void)es;
-    ScanParams p{};
-    const char *xd = static_cast<const char *>(xdbl);
-    p.x = xc; p.ld_x = ld_xc;
-    p.d2 = z; p.ld_d2 = ld_z;
-    p.dl = xd; p.ld_dl = ld_xdbl;
-    p.bm = xd + dt_rank * es; p.ld_b = ld_xdbl;
-    p.cm = xd + (dt_rank + d_state) * es; p.ld_c = ld_xdbl;
-    p.w_dt = w_dt; p.b_dt = b_dt; p.A = A_log; p.D = D;
-    p.h0 = h0; p.h_last = h_last;
-    p.y = y; p.ld_y = ld_y;
-    p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
-    p.d_state = (int)d_state; p.dt_rank = (int)dt_rank;
-    if (dtype == MB2_F32) return dispatch_scan<float, true>(p, (cudaStream_t)stream);
-    return dispatch_scan<__nv_bfloat16, true>(p, (cudaStream_t)stream);
+                              int64_t d_state, mb2_stream_t stream) {
+    return scan_gated(dtype, xc, ld_xc, dt, ld_dt, B, ld_b, C, ld_c, z, ld_z, A_log, D, h0,
+                      h_last, y, ld_y, batch, seqlen, d_inner, d_state, (cudaStream_t)stream);
 }
-
-// Internal entry for the block forward: x_dbl with separately aligned segments.
-namespace mb2 {
-int scan_fused_segments(int dtype, const void *xc, int64_t ld_xc, const void *dl,
-                        const void *bm, const void *cm, int64_t ld_row, const void *z,
-                        int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
-                        const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
-                        int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
-                        int64_t dt_rank, cudaStream_t stream) {
-    ScanParams p{};
-    p.x = xc; p.ld_x = ld_xc;
-    p.d2 = z; p.ld_d2 = ld_z;
-    p.dl = dl; p.ld_dl = ld_row;
-    p.bm = bm; p.ld_b = ld_row;
-    p.cm = cm; p.ld_c = ld_row;
-    p.w_dt = w_dt; p.b_dt = b_dt; p.A = A_log; p.D = D;
-    p.h0 = h0; p.h_last = h_last;
-    p.y = y; p.ld_y = ld_y;
-    p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
-    p.d_state = (int)d_state; p.dt_rank = (int)dt_rank;
-    if (batch == 0 || d_inner == 0) return MB2_OK;
-    if (dtype == MB2_F32) return dispatch_scan<float, true>(p, stream);
-    return dispatch_scan<__nv_bfloat16, true>(p, stream);
-}
-}  // namespace mb2

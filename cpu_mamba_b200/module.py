@@ -109,11 +109,6 @@ class CPUMamba(nn.Module):
             keep.append(scale)
             d.scale = scale.data_ptr()
             d.scheme = _lib.SCHEMES[mod.scheme]
-            if name == "dt_proj":
-                # the fused scan holds dt_proj rows in registers: pass deq(W)
-                dense = mod.dense_weight(self._param_dtype())
-                keep.append(dense)
-                d.weight = dense.data_ptr()
         elif isinstance(mod, nn.Linear):
             w = mod.weight
             if not w.is_contiguous():
@@ -121,7 +116,7 @@ class CPUMamba(nn.Module):
                 keep.append(w)
             d.weight = w.data_ptr()
             d.scheme = 0
-            if w.dtype == torch.float32 and name != "dt_proj":
+            if w.dtype == torch.float32:
                 d.weight_split = self._tf32_split(name, w).data_ptr()
         else:
             raise TypeError(f"{name} must be nn.Linear or QuantizedLinear, got {type(mod)}")

@@ -72,24 +72,25 @@ def conv1d_silu(x_in: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.T
     return (xc, tail) if return_tail else xc
 
 
-def scan_fused(xc, xdbl, z, w_dt, b_dt, A_log, D, batch, seqlen, h0=None,
-               return_last_state=False):
-    """dt_proj + softplus + selective scan + D skip + SiLU(z) gate in one kernel.
+def scan_fused(xc, dt, Bm, Cm, z, A_log, D, batch, seqlen, h0=None,
+               return_last_state=False, out=None):
+    """Gated selective scan: A = -exp(A_log), recurrence, D skip, cast and
+    SiLU(z) gate in one kernel.
 
-    xc, z: (N, *) row views (N = batch*seqlen); xdbl: (N, dt_rank + 2*d_state)
-    rows; weights as stored by the module.  Returns y (N, d_inner)."""
-    require_cuda(xc, xdbl, z, w_dt, what="scan_fused")
-    di, R = w_dt.shape
-    S = A_log.shape[1]
-    y = torch.empty(batch * seqlen, di, device=xc.device, dtype=xc.dtype)
+    xc, dt, z: (N, d_inner) row views (N = batch*seqlen, any row stride);
+    Bm, Cm: (N, d_state) row views (e.g. column slices of x_proj's output);
+    A_log: (d_inner, d_state); D: (d_inner).  Returns y (N, d_inner)."""
+    require_cuda(xc, dt, Bm, Cm, z, A_log, what="scan_fused")
+    di, S = A_log.shape
+    y = out if out is not None else torch.empty(batch * seqlen, di, device=xc.device, dtype=xc.dtype)
     h_last = (torch.empty(batch, di, S, device=xc.device, dtype=torch.float32)
               if return_last_state else None)
-    w_dt, A_log = w_dt.contiguous(), A_log.contiguous()   # keep alive across the call
+    A_log = A_log.contiguous()                       # keep alive across the call
     h0 = None if h0 is None else h0.contiguous()
-    check(lib().mb2_scan_fused(dtype_code(xc.dtype), ptr(xc), xc.stride(0), ptr(xdbl),
-                               xdbl.stride(0), ptr(z), z.stride(0), ptr(w_dt),
-                               ptr(b_dt), ptr(A_log), ptr(D), ptr(h0), ptr(h_last), ptr(y),
-                               di, batch, seqlen, di, S, R, stream_of(xc)), "scan_fused")
+    check(lib().mb2_scan_fused(dtype_code(xc.dtype), ptr(xc), xc.stride(0), ptr(dt), dt.stride(0),
+                               ptr(Bm), Bm.stride(0), ptr(Cm), Cm.stride(0), ptr(z), z.stride(0),
+                               ptr(A_log), ptr(D), ptr(h0), ptr(h_last), ptr(y), y.stride(0),
+                               batch, seqlen, di, S, stream_of(xc)), "scan_fused")
     return (y, h_last) if return_last_state else y
 
 
@@ -105,8 +106,9 @@ def split_tf32(w: torch.Tensor) -> torch.Tensor:
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
-           weight_split: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """y = x W^T + b over the last dim of x (nn.Linear semantics)."""
+           weight_split: Optional[torch.Tensor] = None, softplus: bool = False) -> torch.Tensor:
+    """y = x W^T + b over the last dim of x (nn.Linear semantics); softplus=True
+    applies F.softplus to the result in the same kernel (dt_proj's epilogue)."""
     require_cuda(x, weight, bias, what="linear")
     N, K = weight.shape
     lead = x.shape[:-1]
@@ -117,7 +119,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
     weight = weight.contiguous()
     check(lib().mb2_linear(dtype_code(x.dtype), ptr(x2), x2.stride(0), ptr(weight),
                            ptr(weight_split), ptr(bias), ptr(y), N, x2.shape[0], N, K,
-                           stream_of(x)), "linear")
+                           _lib.EPI_SOFTPLUS if softplus else _lib.EPI_NONE, stream_of(x)), "linear")
     return y.reshape(*lead, N)
 
 
@@ -148,7 +150,7 @@ def dequantize(scheme: str, weight_q: torch.Tensor, scale: torch.Tensor, in_dim:
 
 
 def qlinear(x: torch.Tensor, scheme: str, weight_q: torch.Tensor, scale: torch.Tensor,
-            bias: Optional[torch.Tensor], in_features: int) -> torch.Tensor:
+            bias: Optional[torch.Tensor], in_features: int, softplus: bool = False) -> torch.Tensor:
     """QuantizedLinear.forward: y = x deq(W)^T + b with W dequantised in-kernel."""
     require_cuda(x, weight_q, scale, bias, what="qlinear")
     N = weight_q.shape[0]
@@ -160,5 +162,7 @@ def qlinear(x: torch.Tensor, scheme: str, weight_q: torch.Tensor, scale: torch.T
     weight_q, scale = weight_q.contiguous(), scale.to(torch.float32).contiguous()
     check(lib().mb2_qlinear(_lib.SCHEMES[scheme], dtype_code(x.dtype), ptr(x2), x2.stride(0),
                             ptr(weight_q), ptr(scale), ptr(bias), ptr(y),
-                            N, x2.shape[0], N, in_features, stream_of(x)), f"qlinear_{scheme}")
+                            N, x2.shape[0], N, in_features,
+                            _lib.EPI_SOFTPLUS if softplus else _lib.EPI_NONE, stream_of(x)),
+          f"qlinear_{scheme}")
     return y.reshape(*lead, N)

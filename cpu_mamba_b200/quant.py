@@ -110,18 +110,9 @@ class QuantizedLinear(nn.Module):
             self.bias = nn.Parameter(bias.detach().clone())
         else:
             self.register_parameter("bias", None)
-        self._dense_cache = None  # (key, dequantised weight in a dtype)
 
     def dequantize_weight(self) -> torch.Tensor:
         return _dequant(self.scheme, self.weight_q, self.scale, self._packed_in_dim)
-
-    def dense_weight(self, dtype: torch.dtype) -> torch.Tensor:
-        """deq(W).to(dtype) on the module's device, cached while the buffers are unchanged."""
-        key = (self.weight_q.data_ptr(), self.weight_q._version, self.scale.data_ptr(),
-               self.scale._version, dtype)
-        if self._dense_cache is None or self._dense_cache[0] != key:
-            self._dense_cache = (key, self.dequantize_weight().to(dtype).contiguous())
-        return self._dense_cache[1]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return ops.qlinear(x, self.scheme, self.weight_q, self.scale, self.bias, self.in_features)

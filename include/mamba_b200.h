@@ -38,6 +38,10 @@ enum mb2_status {
 
 enum mb2_dtype { MB2_F32 = 0, MB2_BF16 = 1 };
 
+/* Linear-layer epilogues: none, or softplus(y) (beta 1, threshold 20) as
+ * dt_proj is followed by in src/cpu_mamba/_mamba.py:219-220. */
+enum mb2_epilogue { MB2_EPI_NONE = 0, MB2_EPI_SOFTPLUS = 1 };
+
 /* Quantisation schemes of src/cpu_mamba/quant.py:47-53 (QuantConfig.scheme). */
 enum mb2_scheme { MB2_Q_NONE = 0, MB2_Q_INT8 = 1, MB2_Q_INT4 = 2, MB2_Q_NF4 = 3 };
 
@@ -83,24 +87,26 @@ int mb2_conv1d_silu(int dtype, const void *x_in, int64_t ld_in,
                     int64_t d_inner, int64_t d_conv, mb2_stream_t stream);
 
 /* ------------------------------------------------------------------------
- * Fused scan stage: dt_proj + softplus (_mamba.py:219-220), A = -exp(A_log)
- * (:222), selective scan + D skip (cpp:68-83), cast and SiLU(z) gate
- * (_mamba.py:263-264).
- *   xc:   (N, ld_xc)   conv+SiLU output
- *   xdbl: (N, ld_xdbl) x_proj output, columns [dt_low (R) | B (S) | C (S)]
- *   z:    (N, ld_z)    gate input (the z half of in_proj's output)
- *   w_dt: (d_inner, R) b_dt: (d_inner)   A_log: (d_inner, S)   D: (d_inner)
- *   (weights in the activation dtype; A_log and D as stored by the module)
- *   y:    (N, ld_y)    gated output
- *   h0 / h_last: optional (batch, d_inner, S) float32 initial / final state.
+ * Gated scan stage of the block: A = -exp(A_log) (_mamba.py:222), selective
+ * scan + D skip (selective_scan_cpu.cpp:68-83), cast to the activation dtype
+ * and SiLU(z) gate (_mamba.py:263-264).
+ *   xc: (N, ld_xc) conv+SiLU output      dt: (N, ld_dt) softplus(dt_proj(.))
+ *   B:  (N, ld_b), C: (N, ld_c) rows of d_state values (x_proj's B, C columns)
+ *   z:  (N, ld_z) gate input (the z half of in_proj's output)
+ *   A_log: (d_inner, d_state), D: (d_inner), both in the activation dtype
+ *   y:  (N, ld_y) gated output; may alias dt (each dt element is read before
+ *       the same y element is written)
+ *   h0 / h_last: optional (batch, d_inner, d_state) float32 initial / final
+ *   state (h0 may alias h_last: the single-token step updates h in place).
+ * bf16 rows must start on 4-byte boundaries.
  * ------------------------------------------------------------------------ */
-int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc,
-                   const void *xdbl, int64_t ld_xdbl, const void *z,
-                   int64_t ld_z, const void *w_dt, const void *b_dt,
+int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dt,
+                   int64_t ld_dt, const void *B, int64_t ld_b, const void *C,
+                   int64_t ld_c, const void *z, int64_t ld_z,
                    const void *A_log, const void *D, const float *h0,
                    float *h_last, void *y, int64_t ld_y, int64_t batch,
                    int64_t seqlen, int64_t d_inner, int64_t d_state,
-                   int64_t dt_rank, mb2_stream_t stream);
+                   mb2_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Linear layer y = x W^T (+ bias): nn.Linear as used by in_proj, x_proj,
@@ -113,7 +119,8 @@ int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc,
  * ------------------------------------------------------------------------ */
 int mb2_linear(int dtype, const void *x, int64_t ld_x, const void *w,
                const float *w_split, const void *bias, void *y, int64_t ld_y,
-               int64_t M, int64_t N, int64_t K, mb2_stream_t stream);
+               int64_t M, int64_t N, int64_t K, int epilogue,
+               mb2_stream_t stream);
 
 /* Split an fp32 tensor of numel elements into its TF32 halves:
  * out[0:numel] = hi = tf32_rn(w), out[numel:2 numel] = lo = tf32_rn(w - hi),
@@ -142,7 +149,7 @@ int mb2_dequantize(int scheme, const void *weight_q, const float *scale,
 int mb2_qlinear(int scheme, int dtype, const void *x, int64_t ld_x,
                 const void *weight_q, const float *scale, const void *bias,
                 void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
-                mb2_stream_t stream);
+                int epilogue, mb2_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Whole block.  Weights follow the mamba_ssm state_dict (_mamba.py:67-84);

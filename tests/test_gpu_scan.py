@@ -84,8 +84,9 @@ def test_scan_empty_sequence():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_fused_scan_matches_composition(dtype):
-    """dt_proj + softplus + scan + D + gate in one kernel == the reference's composition."""
+def test_gated_scan_matches_composition(dtype):
+    """A = -exp(A_log), scan, D skip, cast and SiLU(z) gate in one kernel, reading
+    B and C as column slices of x_proj's output == the reference's composition."""
     p = oracle.make_block_params(96, 16, seed=11, dtype=dtype)
     di, S = p["A_log"].shape
     R = p["dt_proj.weight"].shape[1]
@@ -97,14 +98,27 @@ def test_fused_scan_matches_composition(dtype):
     dt = torch.nn.functional.softplus(
         torch.nn.functional.linear(xdbl[:, :R], p["dt_proj.weight"], p["dt_proj.bias"]))
     A = -torch.exp(p["A_log"].float())
-    y_scan = oracle.selective_scan(xc.float().view(b, T, di), dt.float().view(b, T, di), A,
-                                   xdbl[:, R:R + S].float().view(b, T, S),
-                                   xdbl[:, R + S:].float().view(b, T, S), p["D"].float())
+    y_scan, h_ref = oracle.selective_scan(
+        xc.float().view(b, T, di), dt.float().view(b, T, di), A,
+        xdbl[:, R:R + S].float().view(b, T, S), xdbl[:, R + S:].float().view(b, T, S),
+        p["D"].float(), return_last_state=True)
     y_ref = y_scan.view(b * T, di).to(dtype) * torch.nn.functional.silu(z)
-    y = ops.scan_fused(*_cuda(xc, xdbl, z, p["dt_proj.weight"], p["dt_proj.bias"], p["A_log"],
-                              p["D"]), b, T)
+    xd = xdbl.cuda()
+    y, h = ops.scan_fused(xc.cuda(), dt.cuda(), xd[:, R:R + S], xd[:, R + S:], z.cuda(),
+                          p["A_log"].cuda(), p["D"].cuda(), b, T, return_last_state=True)
+    assert (h.cpu() - h_ref).abs().max().item() <= TOL
     if dtype == torch.float32:
         assert (y.cpu() - y_ref).abs().max().item() <= TOL
     else:
         rel = (y.cpu().float() - y_ref.float()).abs() / (y_ref.float().abs().clamp(min=1e-3) + 1e-6)
         assert rel.mean().item() <= 2e-2
+
+
+def test_gated_scan_rejects_misaligned_bf16_rows():
+    di, S = 64, 16
+    xc = torch.zeros(4, di, device="cuda", dtype=torch.bfloat16)
+    xdbl = torch.zeros(4, 2 * S + 3, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="4-byte"):
+        ops.scan_fused(xc, xc, xdbl[:, 3:3 + S], xdbl[:, 3 + S:], xc,
+                       torch.zeros(di, S, device="cuda", dtype=torch.bfloat16),
+                       torch.ones(di, device="cuda", dtype=torch.bfloat16), 1, 4)
