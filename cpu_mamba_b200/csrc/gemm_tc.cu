@@ -7,10 +7,13 @@
 //               bf16 output -- the reference's bf16 F.linear.
 //   F32 mode  : fp32-faithful 3-term TF32 split.  W arrives pre-split as TF32
 //               hi / lo planes (mb2_split_tf32).  Each A tile is loaded as fp32
-//               and split in shared memory by four transform warps into
-//               hi = tf32_rn(a) and lo = tf32_rn(a - hi); the MMA warp issues
-//               A_hi*W_hi + A_hi*W_lo + A_lo*W_hi.  The dropped A_lo*W_lo term
-//               and the rounding of lo are <= 2^-21 |a||w| per product.
+//               by TMA; four transform warps read it row by row, split it into
+//               hi = tf32_rn(a) and lo = tf32_rn(a - hi) and write both into
+//               tensor memory (tcgen05.st), so the MMAs take A from TMEM and
+//               only W from shared memory (shared-memory bandwidth, not the
+//               tensor pipe, is what a shared-memory A would saturate).  The MMA
+//               warp issues A_hi*W_hi + A_hi*W_lo + A_lo*W_hi.  The dropped
+//               A_lo*W_lo term and the rounding of lo are <= 2^-21 |a||w|.
 //               The tensor core truncates when it adds into an fp32
 //               accumulator, so the error grows with the number of MMAs per
 //               accumulator: the big hi*hi products alternate between two TMEM
@@ -39,7 +42,8 @@ __device__ int g_mb2_device_error = 0;  // 0 = ok; else a code of where a wait e
 namespace tc {
 
 constexpr int BM = 128, BN = 128;
-constexpr int TMEM_COLS = 512;          // F32: 3 accumulators of BN columns
+constexpr int TMEM_COLS = 512;          // F32: 3 accumulators of BN columns + 2 A slots
+constexpr int A_TMEM_COL = 3 * BN;      // F32: split-A slot l at 384 + 64 l (hi), +32 (lo)
 constexpr int TILE_BYTES = 128 * 128;   // one operand tile: 128 rows x 128 B
 constexpr int THREADS = 192;
 constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s bound on any wait
@@ -47,9 +51,12 @@ constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s bound on any wait
 enum Mode { F32X3 = 0, BF16 = 1 };
 
 template <int MODE> struct Cfg;
+// F32X3: a 4-deep TMA ring of (A raw, W_hi, W_lo) tiles (192 KB); the split
+// A (hi, lo) lives in two TMEM slots of 64 columns next to the accumulators.
 template <> struct Cfg<F32X3> {
-    static constexpr int STAGES = 3;
-    static constexpr int TILES = 4;           // A_hi(raw), A_lo, B_hi, B_lo
+    static constexpr int STAGES = 4;
+    static constexpr int TILES = 3;           // A raw, B_hi, B_lo
+    static constexpr int LO = 2;              // TMEM slots for the split A
     static constexpr int BK = 32;             // fp32 elements per 128 B row
     static constexpr int KSTEP = 8;           // K per tf32 MMA
     static constexpr uint32_t TX = 3 * TILE_BYTES;  // bytes by TMA per stage
@@ -57,6 +64,7 @@ template <> struct Cfg<F32X3> {
 template <> struct Cfg<BF16> {
     static constexpr int STAGES = 6;
     static constexpr int TILES = 2;           // A, B
+    static constexpr int LO = 0;
     static constexpr int BK = 64;
     static constexpr int KSTEP = 16;
     static constexpr uint32_t TX = 2 * TILE_BYTES;
@@ -159,6 +167,30 @@ __device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t da, uint64_t db, u
     }
 }
 
+// tf32 MMA with A (128 x 8) read from tensor memory, B from shared memory.
+__device__ __forceinline__ void mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db,
+                                       uint32_t accum) {
+    const uint32_t idesc = instr_desc<F32X3>();
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accum));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]),
+          "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]),
+          "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+          "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+          "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]),
+          "r"(r[31])
+        : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                  ::"r"(bar) : "memory");
@@ -197,11 +229,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     uint8_t *gbase = smem_raw + (base - raw);
     // ring: stage s, tile t at base + (s * TILES + t) * TILE_BYTES
     const uint32_t bars = base + C::STAGES * C::TILES * TILE_BYTES;
-    // barriers: full[S], empty[S], xform[S], accum, done ; then tmem slot
+    // barriers: full[S], empty[S], xform[S], a_empty[LO], accum, done; tmem slot
     auto full = [&](int s) { return bars + 8u * s; };
     auto empty = [&](int s) { return bars + 8u * (C::STAGES + s); };
     auto xform = [&](int s) { return bars + 8u * (2 * C::STAGES + s); };
-    const uint32_t accum_bar = bars + 8u * (3 * C::STAGES);
+    auto lo_empty = [&](int l) { return bars + 8u * (3 * C::STAGES + l); };
+    const uint32_t accum_bar = bars + 8u * (3 * C::STAGES + C::LO);
     const uint32_t done_bar = accum_bar + 8u;
     const uint32_t tmem_slot = done_bar + 8u;
     uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(gbase + (tmem_slot - base));
@@ -218,6 +251,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             mbar_init(empty(s), 1);
             mbar_init(xform(s), 128);
         }
+        for (int l = 0; l < C::LO; ++l) mbar_init(lo_empty(l), 1);
         mbar_init(accum_bar, 1);
         mbar_init(done_bar, 128);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -245,8 +279,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 const int32_t kc = kb * C::BK;
                 tma_load_2d(tile(s, 0), &map_a, full(s), kc, (int32_t)m0);
                 if (MODE == F32X3) {
-                    tma_load_2d(tile(s, 2), &map_b0, full(s), kc, (int32_t)n0);
-                    tma_load_2d(tile(s, 3), &map_b1, full(s), kc, (int32_t)n0);
+                    tma_load_2d(tile(s, 1), &map_b0, full(s), kc, (int32_t)n0);
+                    tma_load_2d(tile(s, 2), &map_b1, full(s), kc, (int32_t)n0);
                 } else {
                     tma_load_2d(tile(s, 1), &map_b0, full(s), kc, (int32_t)n0);
                 }
@@ -268,22 +302,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     const uint32_t koff = kk * 32;  // 32 bytes of K per MMA
                     const uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
                     if (MODE == F32X3) {
-                        const uint64_t ah = smem_desc(tile(s, 0) + koff);
-                        const uint64_t al = smem_desc(tile(s, 1) + koff);
-                        const uint64_t bh = smem_desc(tile(s, 2) + koff);
-                        const uint64_t bl = smem_desc(tile(s, 3) + koff);
+                        // split A of this k-block in TMEM: hi at +0, lo at +32 columns
+                        const uint32_t ah = tmem + A_TMEM_COL + (uint32_t)((kb % C::LO) * 64 + kk * C::KSTEP);
+                        const uint32_t al = ah + 32;
+                        const uint64_t bh = smem_desc(tile(s, 1) + koff);
+                        const uint64_t bl = smem_desc(tile(s, 2) + koff);
                         // big: accumulator (kk & 1) (BK/KSTEP = 4 slices per
                         // k-block, so both are initialised in k-block 0)
                         const uint32_t big = tmem + (uint32_t)((kk & 1) * BN);
-                        mma<MODE>(big, ah, bh, (kb > 0 || kk > 1) ? 1u : 0u);
-                        mma<MODE>(tmem + 2 * BN, ah, bl, acc0);
-                        mma<MODE>(tmem + 2 * BN, al, bh, 1u);
+                        mma_ts(big, ah, bh, (kb > 0 || kk > 1) ? 1u : 0u);
+                        mma_ts(tmem + 2 * BN, ah, bl, acc0);
+                        mma_ts(tmem + 2 * BN, al, bh, 1u);
                     } else {
                         mma<MODE>(tmem, smem_desc(tile(s, 0) + koff), smem_desc(tile(s, 1) + koff),
                                   acc0);
                     }
                 }
                 mma_commit(empty(s));   // frees the stage once these MMAs have read it
+                if (MODE == F32X3) mma_commit(lo_empty(kb % C::LO));
             }
             if (ok) mma_commit(accum_bar);  // accumulator complete
         }
@@ -295,29 +331,37 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                      ::"r"(tmem), "r"(MODE == F32X3 ? TMEM_COLS : BN));
     } else {
         // ----------------------------- transform (F32) + epilogue, warps 2-5
-        const int et = threadIdx.x - 64;   // 0..127
         bool ok = true;
         if (MODE == F32X3) {
             for (int kb = 0; kb < nk; ++kb) {
                 const int s = kb % C::STAGES;
                 const uint32_t ph = (kb / C::STAGES) & 1;
-                if (!mbar_wait(full(s), ph, 5)) { ok = false; break; }
-                // elementwise, so the swizzled layout needs no decoding
-                float4 *hi = reinterpret_cast<float4 *>(gbase + (tile(s, 0) - base));
-                float4 *lo = reinterpret_cast<float4 *>(gbase + (tile(s, 1) - base));
+                const int l = kb % C::LO;
+                bool w = mbar_wait(full(s), ph, 5);
+                w = w && mbar_wait(lo_empty(l), ((kb / C::LO) & 1) ^ 1, 7);
+                if (!__all_sync(0xffffffffu, w)) { ok = false; break; }  // tcgen05.st is warp-wide
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                // this thread's row of the 128B-swizzled A tile: logical 16-byte
+                // chunk c sits at physical chunk c ^ (row & 7)
+                const int row = (warp & 3) * 32 + lane;
+                const uint8_t *arow = gbase + (tile(s, 0) - base) + row * 128;
+                uint32_t hi[32], lo[32];
 #pragma unroll
-                for (int i = 0; i < TILE_BYTES / 16 / 128; ++i) {
-                    const int idx = et + i * 128;
-                    float4 v = hi[idx];
-                    float4 h, l;
-                    h.x = tf32_rn(v.x); l.x = tf32_rn(v.x - h.x);
-                    h.y = tf32_rn(v.y); l.y = tf32_rn(v.y - h.y);
-                    h.z = tf32_rn(v.z); l.z = tf32_rn(v.z - h.z);
-                    h.w = tf32_rn(v.w); l.w = tf32_rn(v.w - h.w);
-                    hi[idx] = h;
-                    lo[idx] = l;
+                for (int c = 0; c < 8; ++c) {
+                    const float4 v = *reinterpret_cast<const float4 *>(arow + ((c ^ (row & 7)) << 4));
+                    const float a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float h = tf32_rn(a[e]);
+                        hi[4 * c + e] = __float_as_uint(h);
+                        lo[4 * c + e] = __float_as_uint(tf32_rn(a[e] - h));
+                    }
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                const uint32_t ta = tmem + ((uint32_t)((warp & 3) * 32) << 16) + A_TMEM_COL + l * 64;
+                tmem_st32(ta, hi);
+                tmem_st32(ta + 32, lo);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 mbar_arrive(xform(s));
             }
         }

@@ -7,7 +7,10 @@
 // Mapping: one CTA owns (batch b, 128/L consecutive channels) for the whole
 // sequence.  Each channel is handled by L adjacent lanes, each holding SPL of
 // the d_state states of h in registers (L*SPL >= d_state; padded states have
-// A = B = C = 0 and stay 0); the per-lane partial y is reduced with shuffles.
+// A = B = C = 0 and stay 0).  The per-step loop does only the state update and
+// writes each lane's partial y to shared memory; after each chunk a read-out
+// pass sums the lane partials, adds D x, applies the gate and stores the
+// chunk's rows with coalesced writes.
 // Time is sequential: the recurrence is cheap, the d_state exponentials per
 // token-channel on the MUFU pipe are the bound, and every (b, channel) pair is
 // independent, so the GPU is filled by batch x channels without splitting T.
@@ -134,7 +137,8 @@ template <int N> struct Vec<__nv_bfloat16, N> {
 };
 
 // Per-stage layout (elements of T): x | dt | z | B | C, each block a multiple
-// of 16 bytes so every array starts 16-byte aligned.
+// of 16 bytes so every array starts 16-byte aligned.  After the two stages
+// comes one float block of SCAN_TC x 128 per-lane partial sums of y.
 struct StageLayout {
     int CH, SPp, n_x, n_bc, elems;
     __host__ __device__ StageLayout(int L, int spl, int esize, bool gated) {
@@ -145,10 +149,13 @@ struct StageLayout {
         n_bc = SCAN_TC * SPp;
         elems = (gated ? 3 : 2) * n_x + 2 * n_bc;
     }
+    __host__ __device__ size_t bytes(int esize) const {
+        return 2 * (size_t)elems * esize + (size_t)SCAN_TC * SCAN_THREADS * sizeof(float);
+    }
 };
 
 template <typename T, int SPL, bool GATED>
-__global__ void __launch_bounds__(SCAN_THREADS, 4)
+__global__ void __launch_bounds__(SCAN_THREADS, 5)
 scan_kernel(const ScanParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int L = p.lanes;
@@ -165,6 +172,8 @@ scan_kernel(const ScanParams p) {
     const int T_ = (int)p.seqlen;
     const int ch_valid = (int)((p.d_inner - d0 < CH) ? p.d_inner - d0 : CH);
     T *stage0 = reinterpret_cast<T *>(smem_raw);
+    // per-lane partial y of the current chunk: ys[tt][tid]
+    float *ys = reinterpret_cast<float *>(smem_raw + 2 * (size_t)lay.elems * sizeof(T));
 
     float A2[SPL], h[SPL];
 #pragma unroll
@@ -181,9 +190,6 @@ scan_kernel(const ScanParams p) {
         A2[i] = a * kLog2e;
         h[i] = h_init;
     }
-    float Dv = 0.0f;
-    if (active && p.D)
-        Dv = GATED ? io<T>::to_f(static_cast<const T *>(p.D)[d]) : static_cast<const float *>(p.D)[d];
 
     const int64_t row_base = (int64_t)b * p.seqlen;
     const T *xg = static_cast<const T *>(p.x) + d0;
@@ -224,35 +230,50 @@ scan_kernel(const ScanParams p) {
         const T *st = stage0 + (ch & 1) * lay.elems;
         const T *xs = st + c;
         const T *dts = st + lay.n_x + c;
-        const T *zs = st + 2 * lay.n_x + c;
         const T *bs = st + (2 + nz) * lay.n_x + j * SPL;
         const T *cs = bs + lay.n_bc;
         const int t0 = ch * SCAN_TC;
         const int tn = min(SCAN_TC, T_ - t0);
+        // recurrence: per step only the state update and this lane's partial y
 #pragma unroll 2
         for (int tt = 0; tt < tn; ++tt) {
             const float xv = io<T>::to_f(xs[tt * CH]);
             const float dtv = io<T>::to_f(dts[tt * CH]);
+            const float dtx = dtv * xv;
             float bv[SPL], cv[SPL];
             Vec<T, SPL>::load(bs + tt * lay.SPp, bv);
             Vec<T, SPL>::load(cs + tt * lay.SPp, cv);
-            float yp = 0.0f;
+            float y0 = 0.0f, y1 = 0.0f, y2 = 0.0f;
 #pragma unroll
             for (int i = 0; i < SPL; ++i) {
                 const float dA = ex2(dtv * A2[i]);
-                const float dBx = (dtv * bv[i]) * xv;
-                h[i] = fmaf(dA, h[i], dBx);
-                yp = fmaf(h[i], cv[i], yp);
+                h[i] = fmaf(dA, h[i], dtx * bv[i]);
+                if (i % 3 == 0) y0 = fmaf(h[i], cv[i], y0);
+                else if (i % 3 == 1) y1 = fmaf(h[i], cv[i], y1);
+                else y2 = fmaf(h[i], cv[i], y2);
             }
-            for (int m = 1; m < L; m <<= 1) yp += __shfl_xor_sync(0xffffffffu, yp, m);
-            if (j == 0 && active) {
-                float out = yp + Dv * xv;
-                if (GATED) {
-                    const float zv = io<T>::to_f(zs[tt * CH]);
-                    out = io<T>::round(out) * io<T>::round(silu_f(zv));
-                }
-                yg[(row_base + t0 + tt) * p.ld_y + d] = io<T>::from_f(out);
+            ys[tt * SCAN_THREADS + tid] = (y0 + y1) + y2;
+        }
+        __syncthreads();
+        // read-out: y = sum of lane partials + D x, then (gated) cast and
+        // SiLU(z) gate; coalesced row segments of CH channels
+        const T *xrow = st;
+        const T *zrow = st + 2 * lay.n_x;
+        for (int e = tid; e < tn * CH; e += SCAN_THREADS) {
+            const int tt = e / CH, cc = e - tt * CH;
+            const int64_t dd = d0 + cc;
+            if (dd >= p.d_inner) continue;
+            float yv = 0.0f;
+            for (int l = 0; l < L; ++l) yv += ys[tt * SCAN_THREADS + cc * L + l];
+            const float xv = io<T>::to_f(xrow[tt * CH + cc]);
+            const float dd_v = GATED ? io<T>::to_f(static_cast<const T *>(p.D)[dd])
+                                     : static_cast<const float *>(p.D)[dd];
+            float out = yv + (p.D ? dd_v : 0.0f) * xv;
+            if (GATED) {
+                const float zv = io<T>::to_f(zrow[tt * CH + cc]);
+                out = io<T>::round(out) * io<T>::round(silu_f(zv));
             }
+            yg[(row_base + t0 + tt) * p.ld_y + dd] = io<T>::from_f(out);
         }
         __syncthreads();
     }
@@ -286,7 +307,7 @@ static bool rows16(const void *p, int64_t ld, size_t es) {
 template <typename T, int SPL, bool GATED>
 static int launch_scan(ScanParams p, cudaStream_t st) {
     const StageLayout lay(p.lanes, SPL, (int)sizeof(T), GATED);
-    const size_t smem = 2 * (size_t)lay.elems * sizeof(T);
+    const size_t smem = lay.bytes((int)sizeof(T));
     auto kern = scan_kernel<T, SPL, GATED>;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
