@@ -245,7 +245,7 @@ def run_ours(args, cfg):
     if rank == 0:
         hbm, bf16, bf16_s, src = peaks()
         roof = roofline(stages, cfg, hbm, bf16, src)
-        launches_per_step = 6 if not step_mode else 6
+        launches_per_step = 5
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -273,12 +273,12 @@ def step_e2e(m, xd, state, step_mode):
         return m(xd)
 
 
-STAGES = ("in_proj", "conv1d_silu", "x_proj", "dt_proj", "scan", "out_proj")
+STAGES = ("in_proj", "conv1d_silu", "x_proj", "scan", "out_proj")
 
 
 def profile_stages(m, x, cfg, dtype, steps):
     """Per-stage CUDA-event durations (same stream, averaged over up to 20 runs)
-    of the six launches of one forward, issued through the stage entry points."""
+    of the five launches of one forward, issued through the stage entry points."""
     from cpu_mamba_b200 import ops
     from cpu_mamba_b200.quant import QuantizedLinear
     if any(isinstance(getattr(m, n), QuantizedLinear) for n in ("in_proj", "x_proj", "dt_proj", "out_proj")):
@@ -288,7 +288,7 @@ def profile_stages(m, x, cfg, dtype, steps):
     di, S, R = m.d_inner, m.d_state, m.dt_rank
     stream = torch.cuda.current_stream(dev)
     split = {n: (m._tf32_split(n, getattr(m, n).weight) if dtype == torch.float32 else None)
-             for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
+             for n in ("in_proj", "x_proj", "out_proj")}
     x2 = x.reshape(B * T, dm)
     times = {k: [] for k in STAGES}
     n = max(3, min(steps, 20))
@@ -302,14 +302,11 @@ def profile_stages(m, x, cfg, dtype, steps):
             ev[2].record(stream)
             xdbl = ops.linear(xc, m.x_proj.weight, None, split["x_proj"])
             ev[3].record(stream)
-            dt = ops.linear(xdbl[:, :R], m.dt_proj.weight, m.dt_proj.bias, split["dt_proj"],
-                            softplus=True)
+            y = ops.scan_fused(xc, xdbl[:, :R], xdbl[:, R:R + S], xdbl[:, R + S:], xz[:, di:],
+                               m.dt_proj.weight, m.dt_proj.bias, m.A_log, m.D, B, T, out=xc)
             ev[4].record(stream)
-            y = ops.scan_fused(xc, dt, xdbl[:, R:R + S], xdbl[:, R + S:], xz[:, di:], m.A_log,
-                               m.D, B, T, out=dt)
-            ev[5].record(stream)
             ops.linear(y, m.out_proj.weight, None, split["out_proj"])
-            ev[6].record(stream)
+            ev[5].record(stream)
         torch.cuda.synchronize(dev)
         if it > 0:
             for i, k in enumerate(times):
@@ -326,10 +323,10 @@ def roofline(stages, cfg, hbm_gbs, bf16_tflops, src):
     es = 4 if cfg["dtype"] == "f32" else 2
     N = B * T
     flops = {"in_proj": 2 * N * dm * 2 * di, "x_proj": 2 * N * di * (R + 2 * S),
-             "dt_proj": 2 * N * R * di, "out_proj": 2 * N * di * dm}
+             "out_proj": 2 * N * di * dm}
     # algorithmic bytes of the HBM-bound stages (each tensor read / written once)
     nbytes = {"conv1d_silu": N * di * es * 2,
-              "scan": N * es * (4 * di + 2 * S)}      # x, dt, z, B, C in; y out
+              "scan": N * es * (3 * di + R + 2 * S)}      # x, z, dt_low, B, C in; y out
     top = max(stages, key=stages.get)
     t = stages[top] / 1e3
     if top in flops:

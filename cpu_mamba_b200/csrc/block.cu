@@ -2,15 +2,15 @@
 // the forward_with_final_state state outputs (:165-202) and the single-token
 // step (:103-163), plus the linear-layer entry points.
 //
-// Forward pipeline (6 launches, caller-provided workspace, no allocation):
-//   1. in_proj            x (N, dm)         -> xz (N, 2di)
-//   2. conv1d + SiLU      xz[:, :di]        -> xc (N, di)   [+ conv tail]
-//   3. x_proj             xc                -> xdbl (N, ldx): dt_low | B | C, each
-//                                              segment on an 8-element boundary
-//   4. dt_proj + softplus xdbl[:, :R]       -> dt (N, di)   (GEMM epilogue)
-//   5. scan               xc, dt, B, C, z   -> y (N, di)    [+ h_last]
-//      (exp(dt A) + recurrence + D skip + cast + SiLU(z) gate; y overwrites dt)
-//   6. out_proj           y                 -> out (N, dm)
+// Forward pipeline (5 launches, caller-provided workspace, no allocation):
+//   1. in_proj            x (N, dm)          -> xz (N, 2di)
+//   2. conv1d + SiLU      xz[:, :di]         -> xc (N, di)   [+ conv tail]
+//   3. x_proj             xc                 -> xdbl (N, ldx): dt_low | B | C, each
+//                                               segment on an 8-element boundary
+//   4. fused scan         xc, xdbl, xz[:, di:] -> y (N, di)  [+ h_last]
+//      (dt_proj + softplus + exp(dt A) + recurrence + D skip + cast + SiLU(z)
+//       gate; y overwrites xc in place)
+//   5. out_proj           y                  -> out (N, dm)
 #include "common.cuh"
 
 namespace mb2 {
@@ -26,11 +26,12 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
 int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const void *bias,
                 void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
                 int64_t d_inner, int64_t d_conv, cudaStream_t st);
-int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t ld_dt,
+int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t ld_dl,
                const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
-               int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
-               void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
-               int64_t d_state, cudaStream_t stream);
+               int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
+               const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
+               int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, int64_t dt_rank,
+               cudaStream_t stream);
 
 // Dense linear: tensor-core kernel where it applies, CUDA-core kernel otherwise.
 static int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, void *y,
@@ -55,7 +56,7 @@ struct Layout {
     int64_t N, di, dm, S, R, K;
     int64_t RB, RC, ldx;   // x_dbl segment offsets and row length
     size_t es;
-    size_t off_xz, off_xc, off_xdbl, off_dt, total;   // y reuses the dt buffer
+    size_t off_xz, off_xc, off_xdbl, total;   // y reuses the xc buffer
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -72,10 +73,13 @@ static Layout make_layout(const mb2_block *b, int64_t rows) {
     l.off_xz = off; off = align256(off + (size_t)rows * 2 * l.di * l.es);
     l.off_xc = off; off = align256(off + (size_t)rows * l.di * l.es);
     l.off_xdbl = off; off = align256(off + (size_t)rows * l.ldx * l.es);
-    l.off_dt = off; off = align256(off + (size_t)rows * l.di * l.es);
     l.total = off;
     return l;
 }
+
+// dt_proj's weight as the fused scan reads it: dense rows in the activation
+// dtype (a quantised dt_proj supplies its dequantised weight in .weight).
+static const void *dt_weight(const mb2_block &b) { return b.dt_proj.weight; }
 
 static int check_block(const mb2_block *b) {
     MB2_REQUIRE(b, MB2_ERR_ARG, "block: null descriptor");
@@ -84,6 +88,8 @@ static int check_block(const mb2_block *b) {
                     b->dt_rank >= 1 && b->d_conv >= 2,
                 MB2_ERR_SHAPE, "block: bad dimensions");
     MB2_REQUIRE(b->conv_w && b->A_log, MB2_ERR_ARG, "block: missing conv1d.weight / A_log");
+    MB2_REQUIRE(b->dt_proj.weight, MB2_ERR_ARG,
+                "block: dt_proj.weight (dense; the dequantised weight when quantised) is required");
     if (b->dtype == MB2_BF16)
         MB2_REQUIRE(b->d_inner % 2 == 0 && b->dt_rank % 2 == 0 && b->d_state % 2 == 0,
                     MB2_ERR_UNSUPPORTED, "block(bf16): d_inner, dt_rank, d_state must be even");
@@ -177,7 +183,7 @@ extern "C" int mb2_block_forward(const mb2_block *blk, const void *x, void *out,
                 "block: workspace %zu < required %zu", workspace_bytes, l.total);
     if (batch == 0) return MB2_OK;
     char *ws = static_cast<char *>(workspace);
-    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl, *dt = ws + l.off_dt;
+    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
     const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
     const size_t es = l.es;
     if (N > 0) {
@@ -187,16 +193,15 @@ extern "C" int mb2_block_forward(const mb2_block *blk, const void *x, void *out,
     }
     MB2_TRY(conv1d_silu(b.dtype, xz, 2 * di, b.conv_w, b.conv_b, xc, di, conv_tail, batch, seqlen,
                         di, b.d_conv, st));
-    if (N > 0) {
+    if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, MB2_EPI_NONE,
                            st, R, l.RB - R, R + S, l.RC - l.RB - S));
-        MB2_TRY(linear_any(b.dtype, b.dt_proj, xdbl, l.ldx, dt, di, N, di, R, MB2_EPI_SOFTPLUS, st));
-    }
-    MB2_TRY(scan_gated(b.dtype, xc, di, dt, di, (char *)xdbl + l.RB * es, l.ldx,
-                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log, b.D,
-                       nullptr, h_last, dt, di, batch, seqlen, di, S, st));
+    MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
+                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
+                       dt_weight(b), b.dt_proj.bias, b.A_log, b.D, nullptr, h_last, xc, di, batch,
+                       seqlen, di, S, R, st));
     if (N > 0)
-        MB2_TRY(linear_any(b.dtype, b.out_proj, dt, di, out, l.dm, N, l.dm, di, MB2_EPI_NONE, st));
+        MB2_TRY(linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, N, l.dm, di, MB2_EPI_NONE, st));
     return MB2_OK;
 }
 
@@ -218,7 +223,7 @@ extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, fl
     if (batch == 0) return MB2_OK;
     MB2_REQUIRE(x && out && h && conv_state && workspace, MB2_ERR_ARG, "step: null pointer");
     char *ws = static_cast<char *>(workspace);
-    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl, *dt = ws + l.off_dt;
+    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
     const int64_t di = l.di, S = l.S, R = l.R;
     const size_t es = l.es;
     MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, batch, 2 * di, l.dm, MB2_EPI_NONE,
@@ -231,10 +236,10 @@ extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, fl
                                                 conv_state, xc, batch, di, st));
     MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, batch, R + 2 * S, di, MB2_EPI_NONE,
                        st, R, l.RB - R, R + S, l.RC - l.RB - S));
-    MB2_TRY(linear_any(b.dtype, b.dt_proj, xdbl, l.ldx, dt, di, batch, di, R, MB2_EPI_SOFTPLUS, st));
-    // one timestep of the scan, h read and written in place
-    MB2_TRY(scan_gated(b.dtype, xc, di, dt, di, (char *)xdbl + l.RB * es, l.ldx,
-                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log, b.D,
-                       h, h, dt, di, batch, 1, di, S, st));
-    return linear_any(b.dtype, b.out_proj, dt, di, out, l.dm, batch, l.dm, di, MB2_EPI_NONE, st);
+    // one timestep of the fused scan, h read and written in place
+    MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
+                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
+                       dt_weight(b), b.dt_proj.bias, b.A_log, b.D, h, h, xc, di, batch, 1, di, S,
+                       R, st));
+    return linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, batch, l.dm, di, MB2_EPI_NONE, st);
 }

@@ -4,53 +4,57 @@
 // (batch b, channel d): h[s] = h0 or 0; for t: dA = exp(dt*A[d,s]);
 // dBx = (dt*B[b,t,s])*x; h = dA*h + dBx; y += h*C[b,t,s]; out = y + D[d]*x.
 //
-// Mapping: one CTA owns (batch b, 128/L consecutive channels) for the whole
-// sequence.  Each channel is handled by L adjacent lanes, each holding SPL of
-// the d_state states of h in registers (L*SPL >= d_state; padded states have
-// A = B = C = 0 and stay 0).  The per-step loop does only the state update and
-// writes each lane's partial y to shared memory; after each chunk a read-out
-// pass sums the lane partials, adds D x, applies the gate and stores the
-// chunk's rows with coalesced writes.
-// Time is sequential: the recurrence is cheap, the d_state exponentials per
-// token-channel on the MUFU pipe are the bound, and every (b, channel) pair is
-// independent, so the GPU is filled by batch x channels without splitting T.
-// Inputs for SCAN_TC timesteps are staged in shared memory by asynchronous
-// copies one chunk ahead (double buffer): the per-channel x / dt / z rows
-// (coalesced across the CTA's channels) and the B / C rows, which every
-// channel of the CTA reads with vector loads.
+// Mapping: one CTA owns (batch b, CH = 128/L consecutive channels) for the
+// whole sequence.  Each channel is handled by L adjacent lanes, each holding
+// SPL of the d_state states of h in registers (L*SPL >= d_state; padded
+// states have A = B = C = 0 and stay 0).  Time is sequential: the recurrence
+// is cheap, the d_state exponentials per token-channel on the MUFU pipe are
+// the bound, and (batch x channel) pairs fill the GPU without splitting T.
 //
+// Per chunk of SCAN_TC timesteps, inputs are staged in shared memory by
+// asynchronous copies one chunk ahead (double buffer): the per-channel x and
+// z rows and the per-token rows of B, C (and dt_low) that all channels read.
+// The per-step loop only updates the states and writes each lane's partial y
+// to shared memory; a read-out pass per chunk sums the L partials, adds D x,
+// applies the gate and writes the chunk's rows with coalesced stores.
+//
+// Modes:
+//   PLAIN -- drop-in for selective_scan_cpu: dt, A given; out = y + D x (fp32)
+//   FUSED -- the block's stage: dt = softplus(dt_low . W_dt[d] + b_dt) with
+//            W_dt's row in registers (dt_proj + softplus, _mamba.py:219-220;
+//            exact fp32 FMA dot products, the softplus of each token-channel
+//            computed once: lane j of a channel's group evaluates step j of
+//            every group of G steps and shares it by shuffle),
+//            A = -exp(A_log) (:222), output cast to the activation dtype and
+//            multiplied by SiLU(z) (:263-264).
 // exp(dt*A) is evaluated as 2^(dt * (A log2 e)) with ex2.approx.ftz.
-//
-// Two modes:
-//   plain  -- drop-in for selective_scan_cpu: A given, output y + D x in fp32;
-//   gated  -- A = -exp(A_log) from the module's parameter (_mamba.py:222),
-//             output cast to the activation dtype and multiplied by SiLU(z)
-//             (_mamba.py:263-264).
-// dt always arrives precomputed (softplus(dt_proj(.)) is the epilogue of the
-// dt_proj GEMM).
 #include "common.cuh"
 
 namespace mb2 {
 
-constexpr int SCAN_THREADS = 128;  // threads per CTA; channels per CTA = 128 / L
+constexpr int SCAN_THREADS = 128;  // threads per CTA
 constexpr int SCAN_TC = 16;        // timesteps per staged chunk
+
+enum ScanMode { PLAIN = 0, FUSED = 1 };
 
 struct ScanParams {
     const void *x;  int64_t ld_x;    // (N, ld_x)  x / conv output
-    const void *dt; int64_t ld_dt;   // (N, ld_dt) dt (softplus applied)
-    const void *z;  int64_t ld_z;    // (N, ld_z)  gate input (gated mode)
+    const void *dt; int64_t ld_dt;   // PLAIN: (N, ld_dt) dt
+    const void *z;  int64_t ld_z;    // FUSED: (N, ld_z) gate input
     const void *bm; int64_t ld_b;    // rows of B
     const void *cm; int64_t ld_c;    // rows of C
-    const void *A;                   // A fp32 (plain) or A_log in T (gated)
-    const void *D;                   // (di) fp32 (plain) / T (gated), may be null
+    const void *dl; int64_t ld_dl;   // FUSED: rows of dt_low (R values)
+    const void *w_dt; const void *b_dt;  // FUSED: (di, R), (di)
+    const void *A;                   // PLAIN: A fp32; FUSED: A_log in T
+    const void *D;                   // (di) fp32 (PLAIN) / T (FUSED), may be null
     const float *h0; float *h_last;  // (batch, di, S) or null
     void *y;        int64_t ld_y;
     int64_t batch, seqlen, d_inner;
-    int d_state, lanes;              // lanes == L
+    int d_state, dt_rank;
     unsigned vec16;                  // bit i: array i rows are 16-byte aligned
 };
 
-enum { ARR_X = 1, ARR_DT = 2, ARR_Z = 4, ARR_B = 8, ARR_C = 16 };
+enum { ARR_X = 1, ARR_D2 = 2, ARR_B = 4, ARR_C = 8, ARR_DL = 16 };
 
 template <typename T> __host__ __device__ constexpr int epw() { return 4 / (int)sizeof(T); }
 
@@ -60,35 +64,33 @@ __device__ __forceinline__ float ex2(float v) {
     return r;
 }
 
-// Stage rows x cols_padded elements of a row-major source into shared memory
-// (valid cols copied, the rest zero-filled): 16-byte async copies when the
-// rows are 16-byte aligned, else 4-byte copies with hardware zero fill.
-template <typename T>
-__device__ __forceinline__ void stage_rows(T *dst, int cols_padded, const T *src, int64_t ld,
-                                           int64_t row0, int rows_valid, int rows, int cols,
-                                           bool vec16, int tid, int nthr) {
+// Stage ROWS x COLS_P elements of a row-major source into shared memory
+// (`cols` valid, the rest zero-filled).  16-byte async copies when the rows
+// are 16-byte aligned, else 4-byte copies with hardware zero fill.
+template <typename T, int ROWS, int COLS_P>
+__device__ __forceinline__ void stage_rows(T *dst, const T *src, int64_t ld, int rows_valid,
+                                           int cols, bool vec16, int tid) {
     constexpr int E = epw<T>();
     if (vec16) {
-        constexpr int V = 16 / (int)sizeof(T);        // elements per 16-byte chunk
-        const int cpr = cols_padded / V;              // chunks per row
-        const int total = rows * cpr;
-        for (int i = tid; i < total; i += nthr) {
-            const int r = i / cpr;
-            const int c = (i - r * cpr) * V;
-            const uint32_t s = smem_u32(dst + r * cols_padded + c);
+        constexpr int V = 16 / (int)sizeof(T);       // elements per 16-byte chunk
+        constexpr int CPR = COLS_P / V;              // chunks per row
+        static_assert(COLS_P % V == 0, "row not a multiple of 16 bytes");
+#pragma unroll 1
+        for (int i = tid; i < ROWS * CPR; i += SCAN_THREADS) {
+            const int r = i / CPR;
+            const int c = (i - r * CPR) * V;
+            T *d = dst + r * COLS_P + c;
             const bool rv = r < rows_valid;
             if (rv && c + V <= cols) {
-                cp_async16(dst + r * cols_padded + c, src + (row0 + r) * ld + c);
+                cp_async16(d, src + r * ld + c);
             } else {
+                const uint32_t s = smem_u32(d);
 #pragma unroll
                 for (int w = 0; w < 4; ++w) {
                     const int cw = c + w * E;
-                    int bytes = 0;
-                    const T *g = src;
-                    if (rv && cw < cols) {
-                        g = src + (row0 + r) * ld + cw;
-                        bytes = (cols - cw >= E) ? 4 : 2;
-                    }
+                    const bool ok = rv && cw < cols;
+                    const T *g = ok ? src + r * ld + cw : src;
+                    const int bytes = ok ? ((cols - cw >= E) ? 4 : 2) : 0;
                     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n"
                                  ::"r"(s + 4 * w), "l"(g), "r"(bytes));
                 }
@@ -96,19 +98,17 @@ __device__ __forceinline__ void stage_rows(T *dst, int cols_padded, const T *src
         }
         return;
     }
-    const int wpr = cols_padded / E;  // words per row
-    const int total = rows * wpr;
-    for (int i = tid; i < total; i += nthr) {
-        const int r = i / wpr;
-        const int c = (i - r * wpr) * E;
-        int bytes = 0;
-        const T *g = src;
-        if (r < rows_valid && c < cols) {
-            g = src + (row0 + r) * ld + c;
-            bytes = (cols - c >= E) ? 4 : 2;  // half word only for bf16 tails
-        }
+    constexpr int WPR = COLS_P / E;
+    static_assert(COLS_P % E == 0, "row not a multiple of 4 bytes");
+#pragma unroll 1
+    for (int i = tid; i < ROWS * WPR; i += SCAN_THREADS) {
+        const int r = i / WPR;
+        const int c = (i - r * WPR) * E;
+        const bool ok = r < rows_valid && c < cols;
+        const T *g = ok ? src + r * ld + c : src;
+        const int bytes = ok ? ((cols - c >= E) ? 4 : 2) : 0;
         asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n"
-                     ::"r"(smem_u32(dst + r * cols_padded + c)), "l"(g), "r"(bytes));
+                     ::"r"(smem_u32(dst + r * COLS_P + c)), "l"(g), "r"(bytes));
     }
 }
 
@@ -136,34 +136,34 @@ template <int N> struct Vec<__nv_bfloat16, N> {
     }
 };
 
-// Per-stage layout (elements of T): x | dt | z | B | C, each block a multiple
-// of 16 bytes so every array starts 16-byte aligned.  After the two stages
-// comes one float block of SCAN_TC x 128 per-lane partial sums of y.
-struct StageLayout {
-    int CH, SPp, n_x, n_bc, elems;
-    __host__ __device__ StageLayout(int L, int spl, int esize, bool gated) {
-        CH = SCAN_THREADS / L;
-        const int v = 16 / esize;
-        SPp = ((L * spl + v - 1) / v) * v;
-        n_x = SCAN_TC * CH;
-        n_bc = SCAN_TC * SPp;
-        elems = (gated ? 3 : 2) * n_x + 2 * n_bc;
-    }
-    __host__ __device__ size_t bytes(int esize) const {
-        return 2 * (size_t)elems * esize + (size_t)SCAN_TC * SCAN_THREADS * sizeof(float);
-    }
+// Compile-time geometry of one instantiation.
+template <typename T, int SPL, int L, int MODE, int RL>
+struct Geo {
+    static constexpr int CH = SCAN_THREADS / L;              // channels per CTA
+    static constexpr int V = 16 / (int)sizeof(T);            // elements per 16 B
+    static constexpr int SPP = ((L * SPL + V - 1) / V) * V;  // padded B/C row
+    static constexpr int RP = ((L * RL + V - 1) / V) * V;    // padded dt_low row
+    static constexpr int NX = SCAN_TC * CH;
+    static constexpr int NBC = SCAN_TC * SPP;
+    static constexpr int NDL = MODE == FUSED ? SCAN_TC * RP : 0;
+    static constexpr int ELEMS = 2 * NX + 2 * NBC + NDL;     // x | dt-or-z | B | C | dt_low
+    static constexpr int G = L < 4 ? L : 4;                  // steps per softplus group
+    static constexpr size_t BYTES = 2 * (size_t)ELEMS * sizeof(T) +
+                                    (size_t)SCAN_TC * SCAN_THREADS * sizeof(float);
 };
 
-template <typename T, int SPL, bool GATED>
-__global__ void __launch_bounds__(SCAN_THREADS, 5)
+template <typename T, int SPL, int L, int MODE, int RL>
+__global__ void __launch_bounds__(SCAN_THREADS, 4)
 scan_kernel(const ScanParams p) {
+    using Gm = Geo<T, SPL, L, MODE, RL>;
+    constexpr int CH = Gm::CH;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int L = p.lanes;
-    const StageLayout lay(L, SPL, (int)sizeof(T), GATED);
-    const int CH = lay.CH;
+    T *stage0 = reinterpret_cast<T *>(smem_raw);
+    float *ys = reinterpret_cast<float *>(smem_raw + 2 * (size_t)Gm::ELEMS * sizeof(T));
+
     const int tid = threadIdx.x;
-    const int c = tid / L;         // channel within CTA
-    const int j = tid - c * L;     // lane within channel group
+    const int c = tid / L;          // channel within CTA
+    const int j = tid % L;          // lane within the channel's group
     const int b = blockIdx.y;
     const int64_t d0 = (int64_t)blockIdx.x * CH;
     const int64_t d = d0 + c;
@@ -171,9 +171,6 @@ scan_kernel(const ScanParams p) {
     const int S = p.d_state;
     const int T_ = (int)p.seqlen;
     const int ch_valid = (int)((p.d_inner - d0 < CH) ? p.d_inner - d0 : CH);
-    T *stage0 = reinterpret_cast<T *>(smem_raw);
-    // per-lane partial y of the current chunk: ys[tt][tid]
-    float *ys = reinterpret_cast<float *>(smem_raw + 2 * (size_t)lay.elems * sizeof(T));
 
     float A2[SPL], h[SPL];
 #pragma unroll
@@ -181,7 +178,7 @@ scan_kernel(const ScanParams p) {
         const int s = j * SPL + i;
         float a = 0.0f, h_init = 0.0f;
         if (active && s < S) {
-            if (GATED)
+            if (MODE == FUSED)
                 a = -expf(io<T>::to_f(static_cast<const T *>(p.A)[d * S + s]));
             else
                 a = static_cast<const float *>(p.A)[d * S + s];
@@ -190,90 +187,144 @@ scan_kernel(const ScanParams p) {
         A2[i] = a * kLog2e;
         h[i] = h_init;
     }
+    // FUSED: this lane's slice of W_dt[d, :] and the bias
+    float wdt[MODE == FUSED ? RL : 1];
+    float bias_dt = 0.0f;
+    if (MODE == FUSED) {
+#pragma unroll
+        for (int r = 0; r < RL; ++r) {
+            const int rr = j * RL + r;
+            wdt[r] = (active && rr < p.dt_rank)
+                         ? io<T>::to_f(static_cast<const T *>(p.w_dt)[d * p.dt_rank + rr]) : 0.0f;
+        }
+        if (active && p.b_dt) bias_dt = io<T>::to_f(static_cast<const T *>(p.b_dt)[d]);
+    }
 
     const int64_t row_base = (int64_t)b * p.seqlen;
-    const T *xg = static_cast<const T *>(p.x) + d0;
-    const T *dtg = static_cast<const T *>(p.dt) + d0;
-    const T *zg = GATED ? static_cast<const T *>(p.z) + d0 : nullptr;
-    const T *bg = static_cast<const T *>(p.bm);
-    const T *cg = static_cast<const T *>(p.cm);
-    const int nz = GATED ? 1 : 0;
+    const T *xg = static_cast<const T *>(p.x) + row_base * p.ld_x + d0;
+    const T *d2g = MODE == FUSED ? static_cast<const T *>(p.z) + row_base * p.ld_z + d0
+                                 : static_cast<const T *>(p.dt) + row_base * p.ld_dt + d0;
+    const int64_t ld_d2 = MODE == FUSED ? p.ld_z : p.ld_dt;
+    const T *bg = static_cast<const T *>(p.bm) + row_base * p.ld_b;
+    const T *cg = static_cast<const T *>(p.cm) + row_base * p.ld_c;
+    const T *dlg = MODE == FUSED ? static_cast<const T *>(p.dl) + row_base * p.ld_dl : nullptr;
 
     auto issue = [&](int chunk) {
-        T *st = stage0 + (chunk & 1) * lay.elems;
-        const int t0 = chunk * SCAN_TC;
-        const int rv = min(SCAN_TC, T_ - t0);
-        const int64_t r0 = row_base + t0;
-        stage_rows<T>(st, CH, xg, p.ld_x, r0, rv, SCAN_TC, ch_valid, p.vec16 & ARR_X,
-                      tid, SCAN_THREADS);
-        stage_rows<T>(st + lay.n_x, CH, dtg, p.ld_dt, r0, rv, SCAN_TC, ch_valid,
-                      p.vec16 & ARR_DT, tid, SCAN_THREADS);
-        if (GATED)
-            stage_rows<T>(st + 2 * lay.n_x, CH, zg, p.ld_z, r0, rv, SCAN_TC, ch_valid,
-                          p.vec16 & ARR_Z, tid, SCAN_THREADS);
-        stage_rows<T>(st + (2 + nz) * lay.n_x, lay.SPp, bg, p.ld_b, r0, rv, SCAN_TC, S,
-                      p.vec16 & ARR_B, tid, SCAN_THREADS);
-        stage_rows<T>(st + (2 + nz) * lay.n_x + lay.n_bc, lay.SPp, cg, p.ld_c, r0, rv, SCAN_TC,
-                      S, p.vec16 & ARR_C, tid, SCAN_THREADS);
+        T *st = stage0 + (chunk & 1) * Gm::ELEMS;
+        const int64_t t0 = (int64_t)chunk * SCAN_TC;
+        const int rv = min(SCAN_TC, T_ - (int)t0);
+        stage_rows<T, SCAN_TC, CH>(st, xg + t0 * p.ld_x, p.ld_x, rv, ch_valid,
+                                   p.vec16 & ARR_X, tid);
+        stage_rows<T, SCAN_TC, CH>(st + Gm::NX, d2g + t0 * ld_d2, ld_d2, rv, ch_valid,
+                                   p.vec16 & ARR_D2, tid);
+        stage_rows<T, SCAN_TC, Gm::SPP>(st + 2 * Gm::NX, bg + t0 * p.ld_b, p.ld_b, rv, S,
+                                        p.vec16 & ARR_B, tid);
+        stage_rows<T, SCAN_TC, Gm::SPP>(st + 2 * Gm::NX + Gm::NBC, cg + t0 * p.ld_c, p.ld_c, rv,
+                                        S, p.vec16 & ARR_C, tid);
+        if (MODE == FUSED)
+            stage_rows<T, SCAN_TC, Gm::RP>(st + 2 * Gm::NX + 2 * Gm::NBC, dlg + t0 * p.ld_dl,
+                                           p.ld_dl, rv, p.dt_rank, p.vec16 & ARR_DL, tid);
     };
+
+    // read-out geometry: thread owns column cc of rows rr0, rr0 + 128/CH, ...
+    constexpr int RSTEP = SCAN_THREADS / CH;
+    const int cc = tid % CH, rr0 = tid / CH;
+    const bool col_ok = cc < ch_valid;
+    float d_skip = 0.0f;
+    if (col_ok && p.D)
+        d_skip = MODE == FUSED ? io<T>::to_f(static_cast<const T *>(p.D)[d0 + cc])
+                               : static_cast<const float *>(p.D)[d0 + cc];
+    T *yg = static_cast<T *>(p.y) + row_base * p.ld_y + d0 + cc;
 
     const int nchunks = (T_ + SCAN_TC - 1) / SCAN_TC;
     if (nchunks > 0) issue(0);
     cp_async_commit();
-    T *yg = static_cast<T *>(p.y);
 
     for (int ch = 0; ch < nchunks; ++ch) {
         if (ch + 1 < nchunks) issue(ch + 1);
         cp_async_commit();
         cp_async_wait<1>();
         __syncthreads();
-        const T *st = stage0 + (ch & 1) * lay.elems;
+        const T *st = stage0 + (ch & 1) * Gm::ELEMS;
         const T *xs = st + c;
-        const T *dts = st + lay.n_x + c;
-        const T *bs = st + (2 + nz) * lay.n_x + j * SPL;
-        const T *cs = bs + lay.n_bc;
-        const int t0 = ch * SCAN_TC;
-        const int tn = min(SCAN_TC, T_ - t0);
-        // recurrence: per step only the state update and this lane's partial y
-#pragma unroll 2
-        for (int tt = 0; tt < tn; ++tt) {
-            const float xv = io<T>::to_f(xs[tt * CH]);
-            const float dtv = io<T>::to_f(dts[tt * CH]);
-            const float dtx = dtv * xv;
-            float bv[SPL], cv[SPL];
-            Vec<T, SPL>::load(bs + tt * lay.SPp, bv);
-            Vec<T, SPL>::load(cs + tt * lay.SPp, cv);
-            float y0 = 0.0f, y1 = 0.0f, y2 = 0.0f;
+        const T *d2s = st + Gm::NX + c;
+        const T *bs = st + 2 * Gm::NX + j * SPL;
+        const T *cs = bs + Gm::NBC;
+        const T *dls = st + 2 * Gm::NX + 2 * Gm::NBC + j * RL;
+        const int tn = min(SCAN_TC, T_ - ch * SCAN_TC);
+
+#pragma unroll 1
+        for (int g0 = 0; g0 < tn; g0 += Gm::G) {
+            // ---- dt for the G steps of this group (rows >= tn are zero-filled)
+            float dtg[Gm::G];
+            if (MODE == FUSED) {
+                float v[Gm::G];
 #pragma unroll
-            for (int i = 0; i < SPL; ++i) {
-                const float dA = ex2(dtv * A2[i]);
-                h[i] = fmaf(dA, h[i], dtx * bv[i]);
-                if (i % 3 == 0) y0 = fmaf(h[i], cv[i], y0);
-                else if (i % 3 == 1) y1 = fmaf(h[i], cv[i], y1);
-                else y2 = fmaf(h[i], cv[i], y2);
+                for (int g = 0; g < Gm::G; ++g) {
+                    float part = 0.0f;
+                    if (RL % 4 == 0) {
+                        float dlv[RL];
+                        Vec<T, RL>::load(dls + (g0 + g) * Gm::RP, dlv);
+#pragma unroll
+                        for (int r = 0; r < RL; ++r) part = fmaf(dlv[r], wdt[r], part);
+                    } else {
+#pragma unroll
+                        for (int r = 0; r < RL; ++r)
+                            part = fmaf(io<T>::to_f(dls[(g0 + g) * Gm::RP + r]), wdt[r], part);
+                    }
+#pragma unroll
+                    for (int m = 1; m < L; m <<= 1) part += __shfl_xor_sync(0xffffffffu, part, m);
+                    v[g] = part;
+                }
+                // lane j (< G) evaluates step j of the group, then shares it
+                float mine = v[0];
+#pragma unroll
+                for (int g = 1; g < Gm::G; ++g) mine = (j == g) ? v[g] : mine;
+                const float sp = io<T>::round(softplus_f(io<T>::round(mine + bias_dt)));
+                const int lane0 = (threadIdx.x & 31) & ~(L - 1);
+#pragma unroll
+                for (int g = 0; g < Gm::G; ++g) dtg[g] = __shfl_sync(0xffffffffu, sp, lane0 + g);
+            } else {
+#pragma unroll
+                for (int g = 0; g < Gm::G; ++g) dtg[g] = io<T>::to_f(d2s[(g0 + g) * CH]);
             }
-            ys[tt * SCAN_THREADS + tid] = (y0 + y1) + y2;
+            // ---- recurrence for the G steps (tn is CTA-uniform: no divergence)
+#pragma unroll
+            for (int g = 0; g < Gm::G; ++g) {
+                const int tt = g0 + g;
+                if (tt >= tn) break;          // padded steps must not touch h
+                const float dtv = dtg[g];
+                const float dtx = dtv * io<T>::to_f(xs[tt * CH]);
+                float bv[SPL], cv[SPL];
+                Vec<T, SPL>::load(bs + tt * Gm::SPP, bv);
+                Vec<T, SPL>::load(cs + tt * Gm::SPP, cv);
+                float y0 = 0.0f, y1 = 0.0f, y2 = 0.0f;
+#pragma unroll
+                for (int i = 0; i < SPL; ++i) {
+                    const float dA = ex2(dtv * A2[i]);
+                    h[i] = fmaf(dA, h[i], dtx * bv[i]);
+                    if (i % 3 == 0) y0 = fmaf(h[i], cv[i], y0);
+                    else if (i % 3 == 1) y1 = fmaf(h[i], cv[i], y1);
+                    else y2 = fmaf(h[i], cv[i], y2);
+                }
+                ys[tt * SCAN_THREADS + tid] = (y0 + y1) + y2;
+            }
         }
         __syncthreads();
-        // read-out: y = sum of lane partials + D x, then (gated) cast and
-        // SiLU(z) gate; coalesced row segments of CH channels
-        const T *xrow = st;
-        const T *zrow = st + 2 * lay.n_x;
-        for (int e = tid; e < tn * CH; e += SCAN_THREADS) {
-            const int tt = e / CH, cc = e - tt * CH;
-            const int64_t dd = d0 + cc;
-            if (dd >= p.d_inner) continue;
-            float yv = 0.0f;
-            for (int l = 0; l < L; ++l) yv += ys[tt * SCAN_THREADS + cc * L + l];
-            const float xv = io<T>::to_f(xrow[tt * CH + cc]);
-            const float dd_v = GATED ? io<T>::to_f(static_cast<const T *>(p.D)[dd])
-                                     : static_cast<const float *>(p.D)[dd];
-            float out = yv + (p.D ? dd_v : 0.0f) * xv;
-            if (GATED) {
-                const float zv = io<T>::to_f(zrow[tt * CH + cc]);
-                out = io<T>::round(out) * io<T>::round(silu_f(zv));
+        // ---- read-out: sum lane partials, D skip, (FUSED) cast + SiLU(z) gate
+        const T *xrow = st + cc;
+        const T *zrow = st + Gm::NX + cc;
+        if (col_ok) {
+#pragma unroll 4
+            for (int tt = rr0; tt < tn; tt += RSTEP) {
+                float yv = 0.0f;
+#pragma unroll
+                for (int l = 0; l < L; ++l) yv += ys[tt * SCAN_THREADS + cc * L + l];
+                float out = yv + d_skip * io<T>::to_f(xrow[tt * CH]);
+                if (MODE == FUSED)
+                    out = io<T>::round(out) * io<T>::round(silu_f(io<T>::to_f(zrow[tt * CH])));
+                yg[((int64_t)ch * SCAN_TC + tt) * p.ld_y] = io<T>::from_f(out);
             }
-            yg[(row_base + t0 + tt) * p.ld_y + dd] = io<T>::from_f(out);
         }
         __syncthreads();
     }
@@ -288,57 +339,64 @@ scan_kernel(const ScanParams p) {
 }
 
 // -------------------------------------------------------------- dispatch ---
-struct ScanShape { int spl, lanes; };
-
-static ScanShape pick_shape(int S) {
-    if (S <= 8) return {8, 1};
-    if (S <= 16) return {8, 2};
-    if (S <= 24) return {12, 2};
-    if (S <= 32) return {16, 2};
-    if (S <= 64) return {16, 4};
-    if (S <= 128) return {16, 8};
-    return {16, 16};
-}
-
 static bool rows16(const void *p, int64_t ld, size_t es) {
     return aligned(p, 16) && (ld * (int64_t)es) % 16 == 0;
 }
 
-template <typename T, int SPL, bool GATED>
+template <typename T, int SPL, int L, int MODE, int RL>
 static int launch_scan(ScanParams p, cudaStream_t st) {
-    const StageLayout lay(p.lanes, SPL, (int)sizeof(T), GATED);
-    const size_t smem = lay.bytes((int)sizeof(T));
-    auto kern = scan_kernel<T, SPL, GATED>;
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    using Gm = Geo<T, SPL, L, MODE, RL>;
+    auto kern = scan_kernel<T, SPL, L, MODE, RL>;
+    if (Gm::BYTES > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)Gm::BYTES);
         if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "scan: smem attribute: %s", cudaGetErrorString(e));
     }
     const size_t es = sizeof(T);
-    // the x / dt / z tiles start at channel d0 = blockIdx.x * CH
-    const bool ch16 = (lay.CH * es) % 16 == 0;
+    const bool ch16 = (Gm::CH * es) % 16 == 0;     // x / z tiles start at d0 = k * CH
     p.vec16 = 0;
     if (ch16 && rows16(p.x, p.ld_x, es)) p.vec16 |= ARR_X;
-    if (ch16 && rows16(p.dt, p.ld_dt, es)) p.vec16 |= ARR_DT;
-    if (GATED && ch16 && rows16(p.z, p.ld_z, es)) p.vec16 |= ARR_Z;
+    if (MODE == FUSED ? (ch16 && rows16(p.z, p.ld_z, es)) : (ch16 && rows16(p.dt, p.ld_dt, es)))
+        p.vec16 |= ARR_D2;
     if (rows16(p.bm, p.ld_b, es)) p.vec16 |= ARR_B;
     if (rows16(p.cm, p.ld_c, es)) p.vec16 |= ARR_C;
-    dim3 grid((unsigned)ceil_div(p.d_inner, lay.CH), (unsigned)p.batch);
-    kern<<<grid, SCAN_THREADS, smem, st>>>(p);
+    if (MODE == FUSED && rows16(p.dl, p.ld_dl, es)) p.vec16 |= ARR_DL;
+    dim3 grid((unsigned)ceil_div(p.d_inner, Gm::CH), (unsigned)p.batch);
+    kern<<<grid, SCAN_THREADS, Gm::BYTES, st>>>(p);
     return check_launch("scan_kernel");
 }
 
-template <typename T, bool GATED>
-static int dispatch_scan(ScanParams p, cudaStream_t st) {
-    const ScanShape sh = pick_shape(p.d_state);
-    p.lanes = sh.lanes;
-    switch (sh.spl) {
-        case 8: return launch_scan<T, 8, GATED>(p, st);
-        case 12: return launch_scan<T, 12, GATED>(p, st);
-        default: return launch_scan<T, 16, GATED>(p, st);
+// (SPL, L) by d_state; RL (dt_rank slice per lane, FUSED only) by dt_rank.
+template <typename T, int MODE, int SPL, int L>
+static int dispatch_rl(const ScanParams &p, cudaStream_t st) {
+    if constexpr (MODE == PLAIN) {
+        return launch_scan<T, SPL, L, PLAIN, 1>(p, st);
+    } else {
+        const int per = (p.dt_rank + L - 1) / L;
+        if (per <= 8) return launch_scan<T, SPL, L, FUSED, 8>(p, st);
+        if (per <= 16) return launch_scan<T, SPL, L, FUSED, 16>(p, st);
+        if (per <= 24) return launch_scan<T, SPL, L, FUSED, 24>(p, st);
+        if (per <= 32) return launch_scan<T, SPL, L, FUSED, 32>(p, st);
+        if (per <= 48) return launch_scan<T, SPL, L, FUSED, 48>(p, st);
+        if (per <= 64) return launch_scan<T, SPL, L, FUSED, 64>(p, st);
+        return fail(MB2_ERR_UNSUPPORTED, "scan: dt_rank %d too large for d_state %d (max %d)",
+                    p.dt_rank, p.d_state, 64 * L);
     }
 }
 
-// Shared argument checks; 4-byte staging copies need 4-byte aligned bf16 rows.
+template <typename T, int MODE>
+static int dispatch_scan(const ScanParams &p, cudaStream_t st) {
+    const int S = p.d_state;
+    if (S <= 8) return dispatch_rl<T, MODE, 8, 1>(p, st);
+    if (S <= 16) return dispatch_rl<T, MODE, 8, 2>(p, st);
+    if (S <= 24) return dispatch_rl<T, MODE, 12, 2>(p, st);
+    if (S <= 32) return dispatch_rl<T, MODE, 16, 2>(p, st);
+    if (S <= 64) return dispatch_rl<T, MODE, 16, 4>(p, st);
+    if (S <= 128) return dispatch_rl<T, MODE, 16, 8>(p, st);
+    return dispatch_rl<T, MODE, 16, 16>(p, st);
+}
+
+// bf16 staging copies 4-byte words: every row must start on a 4-byte boundary.
 static int check_rows(int dtype, const void *ptr, int64_t ld, int64_t cols, const char *name) {
     MB2_REQUIRE(ld >= cols, MB2_ERR_SHAPE, "scan: leading dimension of %s too small", name);
     if (dtype == MB2_BF16)
@@ -348,40 +406,42 @@ static int check_rows(int dtype, const void *ptr, int64_t ld, int64_t cols, cons
     return MB2_OK;
 }
 
-int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t ld_dt,
+int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t ld_dl,
                const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
-               int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
-               void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
-               int64_t d_state, cudaStream_t stream) {
+               int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
+               const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
+               int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, int64_t dt_rank,
+               cudaStream_t stream) {
     MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "scan: bad dtype");
-    MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0, MB2_ERR_SHAPE, "scan: bad sizes");
+    MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0 && dt_rank >= 1, MB2_ERR_SHAPE,
+                "scan: bad sizes");
     MB2_REQUIRE(d_state >= 1 && d_state <= 256, MB2_ERR_SHAPE,
                 "d_state > 256 not supported (got %lld)", (long long)d_state);
     MB2_REQUIRE(batch < 65536, MB2_ERR_SHAPE, "scan: batch too large");
     if (batch == 0 || d_inner == 0) return MB2_OK;
-    MB2_REQUIRE(A_log && (seqlen == 0 || (xc && dt && bm && cm && z && y)), MB2_ERR_ARG,
+    MB2_REQUIRE(A_log && w_dt && (seqlen == 0 || (xc && dl && bm && cm && z && y)), MB2_ERR_ARG,
                 "scan: null pointer");
     if (dtype == MB2_BF16)
-        MB2_REQUIRE(d_inner % 2 == 0 && d_state % 2 == 0, MB2_ERR_ALIGN,
-                    "scan(bf16): d_inner and d_state must be even");
+        MB2_REQUIRE(d_inner % 2 == 0, MB2_ERR_ALIGN, "scan(bf16): d_inner must be even");
     MB2_TRY(check_rows(dtype, xc, ld_xc, d_inner, "x"));
-    MB2_TRY(check_rows(dtype, dt, ld_dt, d_inner, "dt"));
     MB2_TRY(check_rows(dtype, z, ld_z, d_inner, "z"));
     MB2_TRY(check_rows(dtype, bm, ld_b, d_state, "B"));
     MB2_TRY(check_rows(dtype, cm, ld_c, d_state, "C"));
+    MB2_TRY(check_rows(dtype, dl, ld_dl, dt_rank, "dt_low"));
     MB2_REQUIRE(ld_y >= d_inner, MB2_ERR_SHAPE, "scan: leading dimension of y too small");
     ScanParams p{};
     p.x = xc; p.ld_x = ld_xc;
-    p.dt = dt; p.ld_dt = ld_dt;
     p.z = z; p.ld_z = ld_z;
     p.bm = bm; p.ld_b = ld_b;
     p.cm = cm; p.ld_c = ld_c;
+    p.dl = dl; p.ld_dl = ld_dl;
+    p.w_dt = w_dt; p.b_dt = b_dt;
     p.A = A_log; p.D = D; p.h0 = h0; p.h_last = h_last;
     p.y = y; p.ld_y = ld_y;
     p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
-    p.d_state = (int)d_state;
-    if (dtype == MB2_F32) return dispatch_scan<float, true>(p, stream);
-    return dispatch_scan<__nv_bfloat16, true>(p, stream);
+    p.d_state = (int)d_state; p.dt_rank = (int)dt_rank;
+    if (dtype == MB2_F32) return dispatch_scan<float, FUSED>(p, stream);
+    return dispatch_scan<__nv_bfloat16, FUSED>(p, stream);
 }
 
 }  // namespace mb2
@@ -411,15 +471,17 @@ extern "C" int mb2_selective_scan(const float *x, const float *dt, const float *
     p.y = y; p.ld_y = d_inner;
     p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
     p.d_state = (int)d_state;
-    return dispatch_scan<float, false>(p, (cudaStream_t)stream);
+    return dispatch_scan<float, PLAIN>(p, (cudaStream_t)stream);
 }
 
-extern "C" int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dt,
-                              int64_t ld_dt, const void *B, int64_t ld_b, const void *C,
-                              int64_t ld_c, const void *z, int64_t ld_z, const void *A_log,
-                              const void *D, const float *h0, float *h_last, void *y,
-                              int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
-                              int64_t d_state, mb2_stream_t stream) {
-    return scan_gated(dtype, xc, ld_xc, dt, ld_dt, B, ld_b, C, ld_c, z, ld_z, A_log, D, h0,
-                      h_last, y, ld_y, batch, seqlen, d_inner, d_state, (cudaStream_t)stream);
+extern "C" int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dt_low,
+                              int64_t ld_dl, const void *B, int64_t ld_b, const void *C,
+                              int64_t ld_c, const void *z, int64_t ld_z, const void *w_dt,
+                              const void *b_dt, const void *A_log, const void *D,
+                              const float *h0, float *h_last, void *y, int64_t ld_y,
+                              int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state,
+                              int64_t dt_rank, mb2_stream_t stream) {
+    return scan_fused(dtype, xc, ld_xc, dt_low, ld_dl, B, ld_b, C, ld_c, z, ld_z, w_dt, b_dt,
+                      A_log, D, h0, h_last, y, ld_y, batch, seqlen, d_inner, d_state, dt_rank,
+                      (cudaStream_t)stream);
 }

@@ -109,6 +109,11 @@ class CPUMamba(nn.Module):
             keep.append(scale)
             d.scale = scale.data_ptr()
             d.scheme = _lib.SCHEMES[mod.scheme]
+            if name == "dt_proj":
+                # the fused scan reads dt_proj's rows densely: pass deq(W)
+                dense = mod.dense_weight(self._param_dtype())
+                keep.append(dense)
+                d.weight = dense.data_ptr()
         elif isinstance(mod, nn.Linear):
             w = mod.weight
             if not w.is_contiguous():
@@ -116,7 +121,7 @@ class CPUMamba(nn.Module):
                 keep.append(w)
             d.weight = w.data_ptr()
             d.scheme = 0
-            if w.dtype == torch.float32:
+            if w.dtype == torch.float32 and name != "dt_proj":
                 d.weight_split = self._tf32_split(name, w).data_ptr()
         else:
             raise TypeError(f"{name} must be nn.Linear or QuantizedLinear, got {type(mod)}")

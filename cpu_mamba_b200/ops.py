@@ -72,25 +72,27 @@ def conv1d_silu(x_in: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.T
     return (xc, tail) if return_tail else xc
 
 
-def scan_fused(xc, dt, Bm, Cm, z, A_log, D, batch, seqlen, h0=None,
+def scan_fused(xc, dt_low, Bm, Cm, z, w_dt, b_dt, A_log, D, batch, seqlen, h0=None,
                return_last_state=False, out=None):
-    """Gated selective scan: A = -exp(A_log), recurrence, D skip, cast and
-    SiLU(z) gate in one kernel.
+    """The block's scan stage in one kernel: dt = softplus(dt_low W_dt^T + b_dt),
+    A = -exp(A_log), selective scan, D skip, cast and SiLU(z) gate.
 
-    xc, dt, z: (N, d_inner) row views (N = batch*seqlen, any row stride);
-    Bm, Cm: (N, d_state) row views (e.g. column slices of x_proj's output);
-    A_log: (d_inner, d_state); D: (d_inner).  Returns y (N, d_inner)."""
-    require_cuda(xc, dt, Bm, Cm, z, A_log, what="scan_fused")
+    xc, z: (N, d_inner) row views (N = batch*seqlen, any row stride);
+    dt_low, Bm, Cm: (N, dt_rank) / (N, d_state) row views (e.g. the column
+    slices of x_proj's output); w_dt: (d_inner, dt_rank).  Returns y (N, d_inner)."""
+    require_cuda(xc, dt_low, Bm, Cm, z, w_dt, A_log, what="scan_fused")
     di, S = A_log.shape
+    R = w_dt.shape[1]
     y = out if out is not None else torch.empty(batch * seqlen, di, device=xc.device, dtype=xc.dtype)
     h_last = (torch.empty(batch, di, S, device=xc.device, dtype=torch.float32)
               if return_last_state else None)
-    A_log = A_log.contiguous()                       # keep alive across the call
+    A_log, w_dt = A_log.contiguous(), w_dt.contiguous()   # keep alive across the call
     h0 = None if h0 is None else h0.contiguous()
-    check(lib().mb2_scan_fused(dtype_code(xc.dtype), ptr(xc), xc.stride(0), ptr(dt), dt.stride(0),
-                               ptr(Bm), Bm.stride(0), ptr(Cm), Cm.stride(0), ptr(z), z.stride(0),
-                               ptr(A_log), ptr(D), ptr(h0), ptr(h_last), ptr(y), y.stride(0),
-                               batch, seqlen, di, S, stream_of(xc)), "scan_fused")
+    check(lib().mb2_scan_fused(dtype_code(xc.dtype), ptr(xc), xc.stride(0), ptr(dt_low),
+                               dt_low.stride(0), ptr(Bm), Bm.stride(0), ptr(Cm), Cm.stride(0),
+                               ptr(z), z.stride(0), ptr(w_dt), ptr(b_dt), ptr(A_log), ptr(D),
+                               ptr(h0), ptr(h_last), ptr(y), y.stride(0), batch, seqlen, di, S, R,
+                               stream_of(xc)), "scan_fused")
     return (y, h_last) if return_last_state else y
 
 

@@ -114,6 +114,18 @@ class QuantizedLinear(nn.Module):
     def dequantize_weight(self) -> torch.Tensor:
         return _dequant(self.scheme, self.weight_q, self.scale, self._packed_in_dim)
 
+    def dense_weight(self, dtype: torch.dtype) -> torch.Tensor:
+        """deq(W).to(dtype), cached while the buffers are unchanged.  The block's
+        fused scan keeps dt_proj's rows in registers and reads this (a derived
+        cache of d_inner x dt_rank values, not module state)."""
+        key = (self.weight_q.data_ptr(), self.weight_q._version, self.scale.data_ptr(),
+               self.scale._version, dtype)
+        cache = getattr(self, "_dense_cache", None)
+        if cache is None or cache[0] != key:
+            cache = (key, self.dequantize_weight().to(dtype).contiguous())
+            self._dense_cache = cache
+        return cache[1]
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return ops.qlinear(x, self.scheme, self.weight_q, self.scale, self.bias, self.in_features)
 

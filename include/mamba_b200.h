@@ -87,26 +87,30 @@ int mb2_conv1d_silu(int dtype, const void *x_in, int64_t ld_in,
                     int64_t d_inner, int64_t d_conv, mb2_stream_t stream);
 
 /* ------------------------------------------------------------------------
- * Gated scan stage of the block: A = -exp(A_log) (_mamba.py:222), selective
- * scan + D skip (selective_scan_cpu.cpp:68-83), cast to the activation dtype
- * and SiLU(z) gate (_mamba.py:263-264).
- *   xc: (N, ld_xc) conv+SiLU output      dt: (N, ld_dt) softplus(dt_proj(.))
- *   B:  (N, ld_b), C: (N, ld_c) rows of d_state values (x_proj's B, C columns)
- *   z:  (N, ld_z) gate input (the z half of in_proj's output)
- *   A_log: (d_inner, d_state), D: (d_inner), both in the activation dtype
- *   y:  (N, ld_y) gated output; may alias dt (each dt element is read before
- *       the same y element is written)
+ * Fused scan stage of the block, one kernel: dt = softplus(dt_low W_dt^T +
+ * b_dt) (dt_proj, _mamba.py:219-220), A = -exp(A_log) (:222), selective scan
+ * + D skip (selective_scan_cpu.cpp:68-83), cast to the activation dtype and
+ * SiLU(z) gate (_mamba.py:263-264).
+ *   xc:     (N, ld_xc) conv+SiLU output
+ *   dt_low, B, C: (N, ld_*) rows of dt_rank / d_state / d_state values
+ *           (the three column segments of x_proj's output)
+ *   z:      (N, ld_z) gate input (the z half of in_proj's output)
+ *   w_dt:   (d_inner, dt_rank), b_dt: (d_inner), A_log: (d_inner, d_state),
+ *   D: (d_inner) -- all in the activation dtype
+ *   y:      (N, ld_y) gated output; may alias xc (each element of xc is read
+ *           before the same element of y is written)
  *   h0 / h_last: optional (batch, d_inner, d_state) float32 initial / final
  *   state (h0 may alias h_last: the single-token step updates h in place).
  * bf16 rows must start on 4-byte boundaries.
  * ------------------------------------------------------------------------ */
-int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dt,
-                   int64_t ld_dt, const void *B, int64_t ld_b, const void *C,
-                   int64_t ld_c, const void *z, int64_t ld_z,
+int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc,
+                   const void *dt_low, int64_t ld_dl, const void *B,
+                   int64_t ld_b, const void *C, int64_t ld_c, const void *z,
+                   int64_t ld_z, const void *w_dt, const void *b_dt,
                    const void *A_log, const void *D, const float *h0,
                    float *h_last, void *y, int64_t ld_y, int64_t batch,
                    int64_t seqlen, int64_t d_inner, int64_t d_state,
-                   mb2_stream_t stream);
+                   int64_t dt_rank, mb2_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Linear layer y = x W^T (+ bias): nn.Linear as used by in_proj, x_proj,

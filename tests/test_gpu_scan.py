@@ -85,8 +85,9 @@ def test_scan_empty_sequence():
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_gated_scan_matches_composition(dtype):
-    """A = -exp(A_log), scan, D skip, cast and SiLU(z) gate in one kernel, reading
-    B and C as column slices of x_proj's output == the reference's composition."""
+    """dt_proj + softplus, A = -exp(A_log), scan, D skip, cast and SiLU(z) gate in
+    one kernel, reading dt_low, B and C as column slices of x_proj's output ==
+    the reference's composition."""
     p = oracle.make_block_params(96, 16, seed=11, dtype=dtype)
     di, S = p["A_log"].shape
     R = p["dt_proj.weight"].shape[1]
@@ -104,7 +105,8 @@ def test_gated_scan_matches_composition(dtype):
         p["D"].float(), return_last_state=True)
     y_ref = y_scan.view(b * T, di).to(dtype) * torch.nn.functional.silu(z)
     xd = xdbl.cuda()
-    y, h = ops.scan_fused(xc.cuda(), dt.cuda(), xd[:, R:R + S], xd[:, R + S:], z.cuda(),
+    y, h = ops.scan_fused(xc.cuda(), xd[:, :R], xd[:, R:R + S], xd[:, R + S:], z.cuda(),
+                          p["dt_proj.weight"].cuda(), p["dt_proj.bias"].cuda(),
                           p["A_log"].cuda(), p["D"].cuda(), b, T, return_last_state=True)
     assert (h.cpu() - h_ref).abs().max().item() <= TOL
     if dtype == torch.float32:
@@ -115,10 +117,35 @@ def test_gated_scan_matches_composition(dtype):
 
 
 def test_gated_scan_rejects_misaligned_bf16_rows():
-    di, S = 64, 16
+    di, S, R = 64, 16, 3
     xc = torch.zeros(4, di, device="cuda", dtype=torch.bfloat16)
-    xdbl = torch.zeros(4, 2 * S + 3, device="cuda", dtype=torch.bfloat16)
+    xdbl = torch.zeros(4, 2 * S + R, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="4-byte"):
-        ops.scan_fused(xc, xc, xdbl[:, 3:3 + S], xdbl[:, 3 + S:], xc,
+        ops.scan_fused(xc, xdbl[:, :R], xdbl[:, R:R + S], xdbl[:, R + S:], xc,
+                       torch.zeros(di, R, device="cuda", dtype=torch.bfloat16), None,
                        torch.zeros(di, S, device="cuda", dtype=torch.bfloat16),
                        torch.ones(di, device="cuda", dtype=torch.bfloat16), 1, 4)
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 5, 17, 33])
+def test_gated_scan_ragged_lengths_state(T):
+    """Final state after sequence lengths that end inside a chunk / step group."""
+    p = oracle.make_block_params(64, 24, seed=T)
+    di, S = p["A_log"].shape
+    R = p["dt_proj.weight"].shape[1]
+    b = 3
+    g = torch.Generator().manual_seed(100 + T)
+    xc = torch.randn(b * T, di, generator=g)
+    xdbl = torch.randn(b * T, R + 2 * S, generator=g) * 0.5
+    z = torch.randn(b * T, di, generator=g)
+    dt = torch.nn.functional.softplus(
+        torch.nn.functional.linear(xdbl[:, :R], p["dt_proj.weight"], p["dt_proj.bias"]))
+    _, h_ref = oracle.selective_scan(xc.view(b, T, di), dt.view(b, T, di),
+                                     -torch.exp(p["A_log"]), xdbl[:, R:R + S].reshape(b, T, S),
+                                     xdbl[:, R + S:].reshape(b, T, S), p["D"],
+                                     return_last_state=True)
+    xd = xdbl.cuda()
+    _, h = ops.scan_fused(xc.cuda(), xd[:, :R], xd[:, R:R + S], xd[:, R + S:], z.cuda(),
+                          p["dt_proj.weight"].cuda(), p["dt_proj.bias"].cuda(), p["A_log"].cuda(),
+                          p["D"].cuda(), b, T, return_last_state=True)
+    assert (h.cpu() - h_ref).abs().max().item() <= TOL
