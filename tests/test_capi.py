@@ -57,7 +57,7 @@ def test_block_descriptor_validation():
     rc = lib.mb2_block_forward(ctypes.byref(blk), None, None, 1, 1, None, None, None, 0, None)
     assert rc == 1
     need = lib.mb2_block_workspace_bytes(ctypes.byref(blk), 2, 16)
-    assert need > 2 * 16 * (2 * 128 + 128 + 128) * 4
+    assert need >= 2 * 16 * (2 * 128 + 128) * 4      # xz + xc (y overwrites xc)
     blk.conv_w = blk.A_log = 1  # non-null sentinels; validation stops before any use
     blk.dt_proj.weight = 1
     rc = lib.mb2_block_forward(ctypes.byref(blk), None, None, 2, 16, None, None, None, 0, None)
