@@ -22,9 +22,9 @@
 //   PLAIN -- drop-in for selective_scan_cpu: dt, A given; out = y + D x (fp32)
 //   FUSED -- the block's stage: dt = softplus(dt_low . W_dt[d] + b_dt) with
 //            W_dt's row in registers (dt_proj + softplus, _mamba.py:219-220;
-//            exact fp32 FMA dot products, the softplus of each token-channel
-//            computed once: lane j of a channel's group evaluates step j of
-//            every group of G steps and shares it by shuffle),
+//            exact fp32 FMA dot products for a whole chunk at a time, the
+//            softplus of each token-channel computed once, by one of the
+//            channel's lanes, into a shared-memory dt tile),
 //            A = -exp(A_log) (:222), output cast to the activation dtype and
 //            multiplied by SiLU(z) (:263-264).
 // exp(dt*A) is evaluated as 2^(dt * (A log2 e)) with ex2.approx.ftz.
@@ -62,6 +62,29 @@ __device__ __forceinline__ float ex2(float v) {
     float r;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
     return r;
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE fp32 round-to-nearest
+// lanes per instruction, halving the FMA-pipe instruction count of the state
+// update).  A pair lives in a 64-bit register.
+using f2 = unsigned long long;
+__device__ __forceinline__ f2 pk(float a, float b) {
+    f2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk(f2 v, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+    f2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+    f2 d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
 }
 
 // Stage ROWS x COLS_P elements of a row-major source into shared memory
@@ -147,9 +170,11 @@ struct Geo {
     static constexpr int NBC = SCAN_TC * SPP;
     static constexpr int NDL = MODE == FUSED ? SCAN_TC * RP : 0;
     static constexpr int ELEMS = 2 * NX + 2 * NBC + NDL;     // x | dt-or-z | B | C | dt_low
-    static constexpr int G = L < 4 ? L : 4;                  // steps per softplus group
+    // after the two stages: per-lane partial y (SCAN_TC x 128 floats) and, in
+    // FUSED mode, the chunk's dt tile (SCAN_TC x CH floats)
     static constexpr size_t BYTES = 2 * (size_t)ELEMS * sizeof(T) +
-                                    (size_t)SCAN_TC * SCAN_THREADS * sizeof(float);
+                                    (size_t)SCAN_TC * SCAN_THREADS * sizeof(float) +
+                                    (MODE == FUSED ? (size_t)SCAN_TC * CH * sizeof(float) : 0);
 };
 
 template <typename T, int SPL, int L, int MODE, int RL>
@@ -160,6 +185,7 @@ scan_kernel(const ScanParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *stage0 = reinterpret_cast<T *>(smem_raw);
     float *ys = reinterpret_cast<float *>(smem_raw + 2 * (size_t)Gm::ELEMS * sizeof(T));
+    float *dts = ys + SCAN_TC * SCAN_THREADS;   // FUSED: dt of the chunk, [tt][channel]
 
     const int tid = threadIdx.x;
     const int c = tid / L;          // channel within CTA
@@ -172,30 +198,41 @@ scan_kernel(const ScanParams p) {
     const int T_ = (int)p.seqlen;
     const int ch_valid = (int)((p.d_inner - d0 < CH) ? p.d_inner - d0 : CH);
 
-    float A2[SPL], h[SPL];
+    static_assert(SPL % 2 == 0 && (RL % 2 == 0 || RL == 1), "states / dt_rank slices come in pairs");
+    constexpr int NP = SPL / 2;
+    f2 A2[NP], h[NP];
 #pragma unroll
-    for (int i = 0; i < SPL; ++i) {
-        const int s = j * SPL + i;
-        float a = 0.0f, h_init = 0.0f;
-        if (active && s < S) {
-            if (MODE == FUSED)
-                a = -expf(io<T>::to_f(static_cast<const T *>(p.A)[d * S + s]));
-            else
-                a = static_cast<const float *>(p.A)[d * S + s];
-            if (p.h0) h_init = p.h0[((int64_t)b * p.d_inner + d) * S + s];
+    for (int q = 0; q < NP; ++q) {
+        float a[2] = {0.0f, 0.0f}, hi[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int s = j * SPL + 2 * q + e;
+            if (active && s < S) {
+                if (MODE == FUSED)
+                    a[e] = -expf(io<T>::to_f(static_cast<const T *>(p.A)[d * S + s]));
+                else
+                    a[e] = static_cast<const float *>(p.A)[d * S + s];
+                if (p.h0) hi[e] = p.h0[((int64_t)b * p.d_inner + d) * S + s];
+            }
         }
-        A2[i] = a * kLog2e;
-        h[i] = h_init;
+        A2[q] = pk(a[0] * kLog2e, a[1] * kLog2e);
+        h[q] = pk(hi[0], hi[1]);
     }
-    // FUSED: this lane's slice of W_dt[d, :] and the bias
-    float wdt[MODE == FUSED ? RL : 1];
+    // FUSED: this lane's slice of W_dt[d, :] (as pairs) and the bias
+    constexpr int RP2 = MODE == FUSED ? RL / 2 : 1;
+    f2 wdt[RP2];
     float bias_dt = 0.0f;
     if (MODE == FUSED) {
 #pragma unroll
-        for (int r = 0; r < RL; ++r) {
-            const int rr = j * RL + r;
-            wdt[r] = (active && rr < p.dt_rank)
-                         ? io<T>::to_f(static_cast<const T *>(p.w_dt)[d * p.dt_rank + rr]) : 0.0f;
+        for (int q = 0; q < RP2; ++q) {
+            float w[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int rr = j * RL + 2 * q + e;
+                w[e] = (active && rr < p.dt_rank)
+                           ? io<T>::to_f(static_cast<const T *>(p.w_dt)[d * p.dt_rank + rr]) : 0.0f;
+            }
+            wdt[q] = pk(w[0], w[1]);
         }
         if (active && p.b_dt) bias_dt = io<T>::to_f(static_cast<const T *>(p.b_dt)[d]);
     }
@@ -253,62 +290,66 @@ scan_kernel(const ScanParams p) {
         const T *dls = st + 2 * Gm::NX + 2 * Gm::NBC + j * RL;
         const int tn = min(SCAN_TC, T_ - ch * SCAN_TC);
 
+        if (MODE == FUSED) {
+            // ---- dt of the whole chunk: 16 independent dot products per lane
+            // (rows >= tn are zero-filled and never used), shuffle-reduced over
+            // the channel's L lanes; lane j finishes steps j, j + L, ... with
+            // bias + softplus, so each token-channel's softplus runs once.
+            constexpr int HALF = SCAN_TC / 2;     // two passes of 8 independent chains
 #pragma unroll 1
-        for (int g0 = 0; g0 < tn; g0 += Gm::G) {
-            // ---- dt for the G steps of this group (rows >= tn are zero-filled)
-            float dtg[Gm::G];
-            if (MODE == FUSED) {
-                float v[Gm::G];
+            for (int t0 = 0; t0 < SCAN_TC; t0 += HALF) {
+                float part[HALF];
 #pragma unroll
-                for (int g = 0; g < Gm::G; ++g) {
-                    float part = 0.0f;
-                    if (RL % 4 == 0) {
-                        float dlv[RL];
-                        Vec<T, RL>::load(dls + (g0 + g) * Gm::RP, dlv);
+                for (int u = 0; u < HALF; ++u) {
+                    float dlv[RL > 1 ? RL : 4];
+                    Vec<T, (RL > 1 ? RL : 4)>::load(dls + (t0 + u) * Gm::RP, dlv);
+                    f2 acc = pk(0.0f, 0.0f);
 #pragma unroll
-                        for (int r = 0; r < RL; ++r) part = fmaf(dlv[r], wdt[r], part);
-                    } else {
-#pragma unroll
-                        for (int r = 0; r < RL; ++r)
-                            part = fmaf(io<T>::to_f(dls[(g0 + g) * Gm::RP + r]), wdt[r], part);
-                    }
-#pragma unroll
-                    for (int m = 1; m < L; m <<= 1) part += __shfl_xor_sync(0xffffffffu, part, m);
-                    v[g] = part;
+                    for (int q = 0; q < RP2; ++q)
+                        acc = fma2(pk(dlv[2 * q], dlv[2 * q + 1]), wdt[q], acc);
+                    float pa, pb;
+                    upk(acc, pa, pb);
+                    part[u] = pa + pb;
                 }
-                // lane j (< G) evaluates step j of the group, then shares it
-                float mine = v[0];
 #pragma unroll
-                for (int g = 1; g < Gm::G; ++g) mine = (j == g) ? v[g] : mine;
-                const float sp = io<T>::round(softplus_f(io<T>::round(mine + bias_dt)));
-                const int lane0 = (threadIdx.x & 31) & ~(L - 1);
+                for (int u = 0; u < HALF; ++u)
 #pragma unroll
-                for (int g = 0; g < Gm::G; ++g) dtg[g] = __shfl_sync(0xffffffffu, sp, lane0 + g);
-            } else {
+                    for (int m = 1; m < L; m <<= 1)
+                        part[u] += __shfl_xor_sync(0xffffffffu, part[u], m);
 #pragma unroll
-                for (int g = 0; g < Gm::G; ++g) dtg[g] = io<T>::to_f(d2s[(g0 + g) * CH]);
-            }
-            // ---- recurrence for the G steps (tn is CTA-uniform: no divergence)
+                for (int k = 0; k < HALF; k += (L < HALF ? L : HALF)) {
+                    float v = part[k];
 #pragma unroll
-            for (int g = 0; g < Gm::G; ++g) {
-                const int tt = g0 + g;
-                if (tt >= tn) break;          // padded steps must not touch h
-                const float dtv = dtg[g];
-                const float dtx = dtv * io<T>::to_f(xs[tt * CH]);
-                float bv[SPL], cv[SPL];
-                Vec<T, SPL>::load(bs + tt * Gm::SPP, bv);
-                Vec<T, SPL>::load(cs + tt * Gm::SPP, cv);
-                float y0 = 0.0f, y1 = 0.0f, y2 = 0.0f;
-#pragma unroll
-                for (int i = 0; i < SPL; ++i) {
-                    const float dA = ex2(dtv * A2[i]);
-                    h[i] = fmaf(dA, h[i], dtx * bv[i]);
-                    if (i % 3 == 0) y0 = fmaf(h[i], cv[i], y0);
-                    else if (i % 3 == 1) y1 = fmaf(h[i], cv[i], y1);
-                    else y2 = fmaf(h[i], cv[i], y2);
+                    for (int l = 1; l < L && k + l < HALF; ++l) v = (j == l) ? part[k + l] : v;
+                    if (L <= HALF || j < HALF)
+                        dts[(t0 + k + j) * CH + c] = io<T>::round(softplus_f(io<T>::round(v + bias_dt)));
                 }
-                ys[tt * SCAN_THREADS + tid] = (y0 + y1) + y2;
             }
+            __syncwarp();   // a channel's L lanes share one warp
+        }
+        // ---- recurrence (tn is CTA-uniform)
+#pragma unroll 2
+        for (int tt = 0; tt < tn; ++tt) {
+            const float dtv = MODE == FUSED ? dts[tt * CH + c] : io<T>::to_f(d2s[tt * CH]);
+            const float dtx = dtv * io<T>::to_f(xs[tt * CH]);
+            const f2 dt2 = pk(dtv, dtv), dtx2 = pk(dtx, dtx);
+            float bv[SPL], cv[SPL];
+            Vec<T, SPL>::load(bs + tt * Gm::SPP, bv);
+            Vec<T, SPL>::load(cs + tt * Gm::SPP, cv);
+            f2 ya = pk(0.0f, 0.0f), yb = ya;
+#pragma unroll
+            for (int q = 0; q < NP; ++q) {
+                float e0, e1;
+                upk(mul2(dt2, A2[q]), e0, e1);
+                const f2 dA = pk(ex2(e0), ex2(e1));
+                h[q] = fma2(dA, h[q], mul2(dtx2, pk(bv[2 * q], bv[2 * q + 1])));
+                if (q & 1) yb = fma2(h[q], pk(cv[2 * q], cv[2 * q + 1]), yb);
+                else ya = fma2(h[q], pk(cv[2 * q], cv[2 * q + 1]), ya);
+            }
+            float y0, y1, y2, y3;
+            upk(ya, y0, y1);
+            upk(yb, y2, y3);
+            ys[tt * SCAN_THREADS + tid] = (y0 + y1) + (y2 + y3);
         }
         __syncthreads();
         // ---- read-out: sum lane partials, D skip, (FUSED) cast + SiLU(z) gate
@@ -331,9 +372,14 @@ scan_kernel(const ScanParams p) {
     cp_async_wait<0>();
     if (p.h_last && active) {
 #pragma unroll
-        for (int i = 0; i < SPL; ++i) {
-            const int s = j * SPL + i;
-            if (s < S) p.h_last[((int64_t)b * p.d_inner + d) * S + s] = h[i];
+        for (int q = 0; q < NP; ++q) {
+            float hv[2];
+            upk(h[q], hv[0], hv[1]);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int s = j * SPL + 2 * q + e;
+                if (s < S) p.h_last[((int64_t)b * p.d_inner + d) * S + s] = hv[e];
+            }
         }
     }
 }
