@@ -10,26 +10,31 @@
 //               by TMA; four transform warps read it row by row, split it into
 //               hi = tf32_rn(a) and lo = tf32_rn(a - hi) and write both into
 //               tensor memory (tcgen05.st), so the MMAs take A from TMEM and
-//               only W from shared memory (shared-memory bandwidth, not the
-//               tensor pipe, is what a shared-memory A would saturate).  The MMA
-//               warp issues A_hi*W_hi + A_hi*W_lo + A_lo*W_hi.  The dropped
-//               A_lo*W_lo term and the rounding of lo are <= 2^-21 |a||w|.
-//               The tensor core truncates when it adds into an fp32
-//               accumulator, so the error grows with the number of MMAs per
-//               accumulator: the big hi*hi products alternate between two TMEM
-//               accumulators by K slice, the small cross terms go to a third,
-//               and the epilogue sums the three in fp32 round-to-nearest.
+//               only W from shared memory.  The MMA warp issues
+//               A_hi*W_hi + A_hi*W_lo + A_lo*W_hi.  The dropped A_lo*W_lo term
+//               and the rounding of lo are <= 2^-21 |a||w|.  The tensor core
+//               truncates when it adds into an fp32 accumulator, so the error
+//               grows with the number of MMAs per accumulator: the big hi*hi
+//               products alternate between two TMEM accumulators by K slice,
+//               the small cross terms go to a third, and the epilogue sums the
+//               three in fp32 round-to-nearest.
 //
-// CTA = 6 warps, one 128 x 128 output tile:
-//   warp 0  TMA producer (one elected lane), STAGES-deep smem ring
-//   warp 1  TMEM allocator + MMA issuer (one elected lane)
-//   warps 2-5  F32 mode: A-tile transform during the main loop;
-//              all modes: epilogue (TMEM -> registers -> smem -> coalesced
-//              global stores, bias add, dtype conversion, column remap)
+// Persistent, warp-specialised: one CTA per SM walks the 128 x 128 output
+// tiles (n fastest, so co-resident CTAs share A rows in L2):
+//   warp 0      TMA producer (one lane), STAGES-deep shared-memory ring that
+//               runs ahead across tile boundaries
+//   warp 1      TMEM allocator + MMA issuer (one lane)
+//   warps 2-5   F32 mode: A split into TMEM (two k-block slots)
+//   last 4      epilogue: drain the accumulator(s) from TMEM, hand TMEM back
+//               to the MMA warp, then bias / softplus / dtype conversion into
+//               a 128B-swizzled staging tile in shared memory and TMA bulk
+//               tensor stores to global memory, overlapping the next tile's
+//               main loop.  (A column remap or an unaligned output falls back
+//               to plain stores.)
 // Operand tiles are 128 rows x 128 bytes, 128-byte swizzled (TMA and UMMA
 // descriptors agree).  Every mbarrier wait is bounded (~2 s): on expiry the
-// thread records an error in g_mb2_device_error and abandons the tile, and the
-// allocating warp still frees its TMEM.
+// thread records an error in g_mb2_device_error and stops, and the allocating
+// warp still frees its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -42,37 +47,50 @@ __device__ int g_mb2_device_error = 0;  // 0 = ok; else a code of where a wait e
 namespace tc {
 
 constexpr int BM = 128, BN = 128;
-constexpr int TMEM_COLS = 512;          // F32: 3 accumulators of BN columns + 2 A slots
-constexpr int A_TMEM_COL = 3 * BN;      // F32: split-A slot l at 384 + 64 l (hi), +32 (lo)
 constexpr int TILE_BYTES = 128 * 128;   // one operand tile: 128 rows x 128 B
-constexpr int THREADS = 192;
 constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s bound on any wait
 
 enum Mode { F32X3 = 0, BF16 = 1 };
 
 template <int MODE> struct Cfg;
-// F32X3: a 4-deep TMA ring of (A raw, W_hi, W_lo) tiles (192 KB); the split
-// A (hi, lo) lives in two TMEM slots of 64 columns next to the accumulators.
+// F32X3: 3-deep TMA ring of (A raw, W_hi, W_lo) tiles; the split A (hi, lo)
+// lives in two TMEM slots of 64 columns next to the three accumulators.
 template <> struct Cfg<F32X3> {
-    static constexpr int STAGES = 4;
+    static constexpr int STAGES = 3;
     static constexpr int TILES = 3;           // A raw, B_hi, B_lo
     static constexpr int LO = 2;              // TMEM slots for the split A
     static constexpr int BK = 32;             // fp32 elements per 128 B row
     static constexpr int KSTEP = 8;           // K per tf32 MMA
     static constexpr uint32_t TX = 3 * TILE_BYTES;  // bytes by TMA per stage
+    static constexpr int NACC = 1;            // accumulator sets (3 x BN columns)
+    static constexpr int ACC_COLS = 3 * BN;
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int A_COL = 3 * BN;      // split-A slot l at 384 + 64 l (hi), +32 (lo)
+    static constexpr int WARPS = 10;
+    static constexpr int EPI0 = 6;            // first epilogue warp
 };
+// BF16: 5-deep ring of (A, W) tiles, two accumulators so the MMAs of the next
+// tile overlap the epilogue of the previous one.
 template <> struct Cfg<BF16> {
-    static constexpr int STAGES = 6;
+    static constexpr int STAGES = 5;
     static constexpr int TILES = 2;           // A, B
-    static constexpr int LO = 0;
+    static constexpr int LO = 1;              // (no split A; one unused barrier)
     static constexpr int BK = 64;
     static constexpr int KSTEP = 16;
     static constexpr uint32_t TX = 2 * TILE_BYTES;
+    static constexpr int NACC = 2;
+    static constexpr int ACC_COLS = BN;
+    static constexpr int TMEM_COLS = 256;
+    static constexpr int A_COL = 0;
+    static constexpr int WARPS = 6;
+    static constexpr int EPI0 = 2;
 };
 
-template <int MODE>
+// shared memory: ring | output staging (BM x BN of TO) | barriers
+template <int MODE, typename TO>
 constexpr size_t smem_bytes() {
-    return 1024 /*align slack*/ + (size_t)Cfg<MODE>::STAGES * Cfg<MODE>::TILES * TILE_BYTES + 256;
+    return 1024 /*align slack*/ + (size_t)Cfg<MODE>::STAGES * Cfg<MODE>::TILES * TILE_BYTES +
+           (size_t)BM * BN * sizeof(TO) + 256;
 }
 
 struct Params {
@@ -81,6 +99,7 @@ struct Params {
     int64_t M, N, K;
     int64_t n1, n2, off1, off2;   // output column remap
     int epi;                      // MB2_EPI_NONE / MB2_EPI_SOFTPLUS
+    int tma_store;                // 1: store through map_y
 };
 
 // ------------------------------------------------------------- primitives
@@ -217,32 +236,45 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t src, int32_t c0,
+                                             int32_t c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(c0), "r"(c1) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;"); }
+__device__ __forceinline__ void bulk_wait_read0() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // ----------------------------------------------------------------- kernel
 template <int MODE, typename TO>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(Cfg<MODE>::WARPS * 32, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b0,
-               const __grid_constant__ CUtensorMap map_b1, const Params p) {
+               const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_y,
+               const Params p) {
     using C = Cfg<MODE>;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *gbase = smem_raw + (base - raw);
-    // ring: stage s, tile t at base + (s * TILES + t) * TILE_BYTES
-    const uint32_t bars = base + C::STAGES * C::TILES * TILE_BYTES;
-    // barriers: full[S], empty[S], xform[S], a_empty[LO], accum, done; tmem slot
+    const uint32_t out_base = base + C::STAGES * C::TILES * TILE_BYTES;   // 1024-aligned
+    const uint32_t bars = out_base + BM * BN * (uint32_t)sizeof(TO);
+    // barriers: full[S] empty[S] xform[S] a_empty[LO] acc_full[NACC] acc_empty[NACC]; tmem slot
     auto full = [&](int s) { return bars + 8u * s; };
     auto empty = [&](int s) { return bars + 8u * (C::STAGES + s); };
     auto xform = [&](int s) { return bars + 8u * (2 * C::STAGES + s); };
-    auto lo_empty = [&](int l) { return bars + 8u * (3 * C::STAGES + l); };
-    const uint32_t accum_bar = bars + 8u * (3 * C::STAGES + C::LO);
-    const uint32_t done_bar = accum_bar + 8u;
-    const uint32_t tmem_slot = done_bar + 8u;
+    auto a_empty = [&](int l) { return bars + 8u * (3 * C::STAGES + l); };
+    auto acc_full = [&](int b) { return bars + 8u * (3 * C::STAGES + C::LO + b); };
+    auto acc_empty = [&](int b) { return bars + 8u * (3 * C::STAGES + C::LO + C::NACC + b); };
+    const uint32_t tmem_slot = bars + 8u * (3 * C::STAGES + C::LO + 2 * C::NACC);
     uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(gbase + (tmem_slot - base));
+    auto tile = [&](int s, int t) { return base + (uint32_t)((s * C::TILES + t) * TILE_BYTES); };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int64_t m0 = (int64_t)blockIdx.y * BM;
-    const int64_t n0 = (int64_t)blockIdx.x * BN;
+    const int num_n = (int)ceil_div(p.N, BN);
+    const int num_tiles = (int)ceil_div(p.M, BM) * num_n;
     const int nk = (int)ceil_div(p.K, C::BK);
 
     if (threadIdx.x == 0) {
@@ -251,14 +283,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             mbar_init(empty(s), 1);
             mbar_init(xform(s), 128);
         }
-        for (int l = 0; l < C::LO; ++l) mbar_init(lo_empty(l), 1);
-        mbar_init(accum_bar, 1);
-        mbar_init(done_bar, 128);
+        for (int l = 0; l < C::LO; ++l) mbar_init(a_empty(l), 1);
+        for (int b = 0; b < C::NACC; ++b) {
+            mbar_init(acc_full(b), 1);
+            mbar_init(acc_empty(b), 128);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(tmem_slot), "r"(MODE == F32X3 ? TMEM_COLS : BN));
+                     ::"r"(tmem_slot), "r"(C::TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -266,84 +300,96 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot_ptr;
 
-    auto tile = [&](int s, int t) { return base + (uint32_t)((s * C::TILES + t) * TILE_BYTES); };
-
     if (warp == 0) {
         // ---------------------------------------------------- TMA producer
         if (lane == 0) {
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % C::STAGES;
-                const uint32_t ph = (kb / C::STAGES) & 1;
-                if (!mbar_wait(empty(s), ph ^ 1, 1)) break;
-                mbar_expect_tx(full(s), C::TX);
-                const int32_t kc = kb * C::BK;
-                tma_load_2d(tile(s, 0), &map_a, full(s), kc, (int32_t)m0);
-                if (MODE == F32X3) {
-                    tma_load_2d(tile(s, 1), &map_b0, full(s), kc, (int32_t)n0);
-                    tma_load_2d(tile(s, 2), &map_b1, full(s), kc, (int32_t)n0);
-                } else {
-                    tma_load_2d(tile(s, 1), &map_b0, full(s), kc, (int32_t)n0);
+            uint32_t g = 0;  // k-blocks issued by this CTA
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                const int32_t m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % C::STAGES;
+                    const uint32_t ph = (g / C::STAGES) & 1;
+                    if (!mbar_wait(empty(s), ph ^ 1, 1)) { ok = false; break; }
+                    mbar_expect_tx(full(s), C::TX);
+                    const int32_t kc = kb * C::BK;
+                    tma_load_2d(tile(s, 0), &map_a, full(s), kc, m0);
+                    tma_load_2d(tile(s, 1), &map_b0, full(s), kc, n0);
+                    if (MODE == F32X3) tma_load_2d(tile(s, 2), &map_b1, full(s), kc, n0);
                 }
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------ MMA issuer
+        uint32_t g = 0;
+        int it = 0;
+        bool ok = true;
         if (lane == 0) {
-            bool ok = true;
-            for (int kb = 0; kb < nk && ok; ++kb) {
-                const int s = kb % C::STAGES;
-                const uint32_t ph = (kb / C::STAGES) & 1;
-                ok = mbar_wait(full(s), ph, 2);
-                if (ok && MODE == F32X3) ok = mbar_wait(xform(s), ph, 3);
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+                const int b = it % C::NACC;
+                ok = mbar_wait(acc_empty(b), ((it / C::NACC) & 1) ^ 1, 8);
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t acc = tmem + (uint32_t)(b * C::ACC_COLS);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % C::STAGES;
+                    const uint32_t ph = (g / C::STAGES) & 1;
+                    ok = mbar_wait(full(s), ph, 2);
+                    if (ok && MODE == F32X3) ok = mbar_wait(xform(s), ph, 3);
+                    if (!ok) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
-                for (int kk = 0; kk < C::BK / C::KSTEP; ++kk) {
-                    const uint32_t koff = kk * 32;  // 32 bytes of K per MMA
-                    const uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
-                    if (MODE == F32X3) {
-                        // split A of this k-block in TMEM: hi at +0, lo at +32 columns
-                        const uint32_t ah = tmem + A_TMEM_COL + (uint32_t)((kb % C::LO) * 64 + kk * C::KSTEP);
-                        const uint32_t al = ah + 32;
-                        const uint64_t bh = smem_desc(tile(s, 1) + koff);
-                        const uint64_t bl = smem_desc(tile(s, 2) + koff);
-                        // big: accumulator (kk & 1) (BK/KSTEP = 4 slices per
-                        // k-block, so both are initialised in k-block 0)
-                        const uint32_t big = tmem + (uint32_t)((kk & 1) * BN);
-                        mma_ts(big, ah, bh, (kb > 0 || kk > 1) ? 1u : 0u);
-                        mma_ts(tmem + 2 * BN, ah, bl, acc0);
-                        mma_ts(tmem + 2 * BN, al, bh, 1u);
-                    } else {
-                        mma<MODE>(tmem, smem_desc(tile(s, 0) + koff), smem_desc(tile(s, 1) + koff),
-                                  acc0);
+                    for (int kk = 0; kk < C::BK / C::KSTEP; ++kk) {
+                        const uint32_t koff = kk * 32;  // 32 bytes of K per MMA
+                        const uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
+                        if (MODE == F32X3) {
+                            const uint32_t ah = tmem + C::A_COL + (uint32_t)((g % C::LO) * 64 + kk * C::KSTEP);
+                            const uint32_t al = ah + 32;
+                            const uint64_t bh = smem_desc(tile(s, 1) + koff);
+                            const uint64_t bl = smem_desc(tile(s, 2) + koff);
+                            // big: accumulator (kk & 1) (4 K slices per k-block,
+                            // so both are initialised in k-block 0)
+                            mma_ts(acc + (uint32_t)((kk & 1) * BN), ah, bh, (kb > 0 || kk > 1) ? 1u : 0u);
+                            mma_ts(acc + 2 * BN, ah, bl, acc0);
+                            mma_ts(acc + 2 * BN, al, bh, 1u);
+                        } else {
+                            mma<MODE>(acc, smem_desc(tile(s, 0) + koff), smem_desc(tile(s, 1) + koff),
+                                      acc0);
+                        }
                     }
+                    mma_commit(empty(s));   // frees the stage once these MMAs have read it
+                    if (MODE == F32X3) mma_commit(a_empty(g % C::LO));
                 }
-                mma_commit(empty(s));   // frees the stage once these MMAs have read it
-                if (MODE == F32X3) mma_commit(lo_empty(kb % C::LO));
+                if (ok) mma_commit(acc_full(b));  // this tile's accumulator is complete
             }
-            if (ok) mma_commit(accum_bar);  // accumulator complete
         }
         __syncwarp();
-        // free TMEM after the epilogue drained it (bounded)
-        mbar_wait(done_bar, 0, 4);
+        // free TMEM after the epilogue drained the last tile (bounded)
+        const int it_all = __shfl_sync(0xffffffffu, it, 0);
+        if (it_all > 0) {
+            const int last = it_all - 1;
+            mbar_wait(acc_empty(last % C::NACC), (last / C::NACC) & 1, 4);
+        }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
-                     ::"r"(tmem), "r"(MODE == F32X3 ? TMEM_COLS : BN));
-    } else {
-        // ----------------------------- transform (F32) + epilogue, warps 2-5
+                     ::"r"(tmem), "r"(C::TMEM_COLS));
+    } else if (MODE == F32X3 && warp < C::EPI0) {
+        // ------------------------------------------- A split into TMEM, F32
+        const int q = warp & 3;                // TMEM lane quarter of this warp
+        const int row = q * 32 + lane;
+        uint32_t g = 0;
         bool ok = true;
-        if (MODE == F32X3) {
-            for (int kb = 0; kb < nk; ++kb) {
-                const int s = kb % C::STAGES;
-                const uint32_t ph = (kb / C::STAGES) & 1;
-                const int l = kb % C::LO;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const int s = g % C::STAGES;
+                const uint32_t ph = (g / C::STAGES) & 1;
+                const int l = g % C::LO;
                 bool w = mbar_wait(full(s), ph, 5);
-                w = w && mbar_wait(lo_empty(l), ((kb / C::LO) & 1) ^ 1, 7);
+                w = w && mbar_wait(a_empty(l), ((g / C::LO) & 1) ^ 1, 7);
                 if (!__all_sync(0xffffffffu, w)) { ok = false; break; }  // tcgen05.st is warp-wide
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 // this thread's row of the 128B-swizzled A tile: logical 16-byte
                 // chunk c sits at physical chunk c ^ (row & 7)
-                const int row = (warp & 3) * 32 + lane;
                 const uint8_t *arow = gbase + (tile(s, 0) - base) + row * 128;
                 uint32_t hi[32], lo[32];
 #pragma unroll
@@ -357,7 +403,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         lo[4 * c + e] = __float_as_uint(tf32_rn(a[e] - h));
                     }
                 }
-                const uint32_t ta = tmem + ((uint32_t)((warp & 3) * 32) << 16) + A_TMEM_COL + l * 64;
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + C::A_COL + l * 64;
                 tmem_st32(ta, hi);
                 tmem_st32(ta + 32, lo);
                 asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
@@ -365,57 +411,109 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 mbar_arrive(xform(s));
             }
         }
-        if (ok) ok = mbar_wait(accum_bar, 0, 6);
-        ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld is warp-collective
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int q = warp & 3;             // TMEM lane quarter this warp may read
-        // staging: 32 rows x (BN + 1) floats per warp, in the (now idle) ring
-        float *stage = reinterpret_cast<float *>(gbase) + q * 32 * (BN + 1);
-        if (ok) {
-#pragma unroll
+    } else if (warp >= C::EPI0) {
+        // ---------------------------------------------------------- epilogue
+        const int q = warp & 3;                 // TMEM lane quarter this warp may read
+        constexpr int VEC = 16 / (int)sizeof(TO);     // outputs per 16-byte chunk
+        constexpr int BOXC = 128 / (int)sizeof(TO);   // columns per 128-byte staging row
+        // this warp's staging: BN / BOXC boxes of 32 rows x 128 B, 128B-swizzled
+        const uint32_t wst = out_base + (uint32_t)(q * 32 * BN * sizeof(TO));
+        uint8_t *wst_g = gbase + (wst - base);
+        TO *Y = static_cast<TO *>(p.y);
+        const TO *bias = static_cast<const TO *>(p.bias);
+        int it = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+            const int64_t m0 = (int64_t)(t / num_n) * BM, n0 = (int64_t)(t % num_n) * BN;
+            const int b = it % C::NACC;
+            bool w = mbar_wait(acc_full(b), (it / C::NACC) & 1, 6);
+            if (!__all_sync(0xffffffffu, w)) break;   // tcgen05.ld is warp-collective
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            // the previous tile's stores must have read the staging tile
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
+            const uint32_t acc = tmem + (uint32_t)(b * C::ACC_COLS) + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
             for (int cb = 0; cb < BN / 32; ++cb) {
-                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + cb * 32;
                 uint32_t r[32];
-                tmem_ld32(ta, r);
+                tmem_ld32(acc + cb * 32, r);
+                float v[32];
                 if (MODE == F32X3) {
                     uint32_t r1[32], r2[32];
-                    tmem_ld32(ta + BN, r1);
-                    tmem_ld32(ta + 2 * BN, r2);
+                    tmem_ld32(acc + BN + cb * 32, r1);
+                    tmem_ld32(acc + 2 * BN + cb * 32, r2);
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        stage[lane * (BN + 1) + cb * 32 + j] =
-                            (__uint_as_float(r[j]) + __uint_as_float(r1[j])) + __uint_as_float(r2[j]);
+                        v[j] = (__uint_as_float(r[j]) + __uint_as_float(r1[j])) + __uint_as_float(r2[j]);
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        stage[lane * (BN + 1) + cb * 32 + j] = __uint_as_float(r[j]);
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int64_t n = n0 + cb * 32 + j;
+                    if (bias) v[j] += (n < p.N) ? io<TO>::to_f(bias[n]) : 0.0f;
+                    // dt_proj's softplus (_mamba.py:219-220) on the value the
+                    // reference would have stored in its dtype
+                    if (p.epi == MB2_EPI_SOFTPLUS) v[j] = softplus_f(io<TO>::round(v[j]));
+                }
+                // row `lane` of box cb*32/BOXC: its 16-byte chunks at c ^ (row & 7)
+                const int box = (cb * 32) / BOXC;
+                const int col0 = (cb * 32) % BOXC;          // element offset in the box row
+                uint8_t *rowp = wst_g + box * (32 * 128) + lane * 128;
+#pragma unroll
+                for (int c = 0; c < 32 / VEC; ++c) {
+                    const int chunk = (col0 / VEC) + c;
+                    uint4 pk4;
+                    uint32_t *pw = reinterpret_cast<uint32_t *>(&pk4);
+                    if (sizeof(TO) == 4) {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) pw[e] = __float_as_uint(v[c * VEC + e]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const __nv_bfloat162 h2 = __floats2bfloat162_rn(v[c * VEC + 2 * e],
+                                                                            v[c * VEC + 2 * e + 1]);
+                            pw[e] = *reinterpret_cast<const uint32_t *>(&h2);
+                        }
+                    }
+                    *reinterpret_cast<uint4 *>(rowp + ((chunk ^ (lane & 7)) << 4)) = pk4;
                 }
             }
-        }
-        __syncwarp();
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        mbar_arrive(done_bar);              // TMEM no longer needed by this thread
-        if (ok) {
-            TO *Y = static_cast<TO *>(p.y);
-            const TO *bias = static_cast<const TO *>(p.bias);
-            for (int rr = 0; rr < 32; ++rr) {
-                const int64_t m = m0 + q * 32 + rr;
-                if (m >= p.M) break;
+            // TMEM drained: the MMA warp may start the next tile in this buffer
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            mbar_arrive(acc_empty(b));
+            if (p.tma_store) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
 #pragma unroll
-                for (int c4 = 0; c4 < BN / 32; ++c4) {
-                    const int64_t n = n0 + c4 * 32 + lane;
-                    if (n < p.N) {
-                        float v = stage[rr * (BN + 1) + c4 * 32 + lane];
-                        if (bias) v += io<TO>::to_f(bias[n]);
-                        // dt_proj's softplus (_mamba.py:219-220) on the value
-                        // the reference would have stored in its dtype
-                        if (p.epi == MB2_EPI_SOFTPLUS) v = softplus_f(io<TO>::round(v));
-                        const int64_t col = n + (n >= p.n1 ? p.off1 : 0) + (n >= p.n2 ? p.off2 : 0);
-                        Y[m * p.ld_y + col] = io<TO>::from_f(v);
+                    for (int bx = 0; bx < BN / BOXC; ++bx)
+                        tma_store_2d(&map_y, wst + bx * 32 * 128, (int32_t)(n0 + bx * BOXC),
+                                     (int32_t)(m0 + q * 32));
+                    bulk_commit();
+                }
+            } else {
+                // plain stores with the column remap: row rr of this warp's slab
+                __syncwarp();
+                for (int rr = 0; rr < 32; ++rr) {
+                    const int64_t m = m0 + q * 32 + rr;
+                    if (m >= p.M) break;
+#pragma unroll
+                    for (int c4 = 0; c4 < BN / 32; ++c4) {
+                        const int col = c4 * 32 + lane;
+                        const int64_t n = n0 + col;
+                        if (n >= p.N) continue;
+                        const int box = col / BOXC, ce = col % BOXC;
+                        const uint8_t *src = wst_g + box * (32 * 128) + rr * 128 +
+                                             (((ce / VEC) ^ (rr & 7)) << 4) + (ce % VEC) * sizeof(TO);
+                        const int64_t dst = n + (n >= p.n1 ? p.off1 : 0) + (n >= p.n2 ? p.off2 : 0);
+                        Y[m * p.ld_y + dst] = *reinterpret_cast<const TO *>(src);
                     }
                 }
+                __syncwarp();
             }
         }
+        if (lane == 0) bulk_wait0();   // stores complete before the CTA exits
     }
 }
 
@@ -423,6 +521,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 
 // ------------------------------------------------------------------- host
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static int g_num_sms = 0;
 
 static int get_encode() {
     if (g_encode) return MB2_OK;
@@ -435,13 +534,13 @@ static int get_encode() {
     return MB2_OK;
 }
 
-// 2D K-major tile map: rows x K elements, box 128 rows x 128 bytes, 128B swizzle.
-static int make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K, int64_t ld,
-                    bool bf16) {
+// 2D row-major map: rows x cols elements, box (box_rows x 128 bytes), 128B swizzle.
+static int make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols, int64_t ld,
+                    bool bf16, int box_rows) {
     const size_t es = bf16 ? 2 : 4;
-    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
-    cuuint32_t box[2] = {(cuuint32_t)(128 / es), 128};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                           2, const_cast<void *>(ptr), dims, strides, box, estr,
@@ -453,13 +552,20 @@ static int make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t K, 
 
 template <int MODE, typename TO>
 static int launch_tc(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
-                     const tc::Params &p, cudaStream_t st) {
+                     const CUtensorMap &ym, const tc::Params &p, cudaStream_t st) {
     auto kern = tc::gemm_tc_kernel<MODE, TO>;
-    constexpr size_t smem = tc::smem_bytes<MODE>();
+    constexpr size_t smem = tc::smem_bytes<MODE, TO>();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_tc smem attribute: %s", cudaGetErrorString(e));
-    dim3 grid((unsigned)ceil_div(p.N, tc::BN), (unsigned)ceil_div(p.M, tc::BM));
-    kern<<<grid, tc::THREADS, smem, st>>>(a, b0, b1, p);
+    if (g_num_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    const int64_t tiles = ceil_div(p.M, tc::BM) * ceil_div(p.N, tc::BN);
+    const unsigned grid = (unsigned)(tiles < g_num_sms ? tiles : g_num_sms);
+    kern<<<grid, tc::Cfg<MODE>::WARPS * 32, smem, st>>>(a, b0, b1, ym, p);
     return check_launch("gemm_tc_kernel");
 }
 
@@ -473,21 +579,24 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
     const size_t es = bf16 ? 2 : 4;
     if (M < 256 || N < 16 || K < 16) return MB2_OK;         // skinny: CUDA-core kernel
     if (!bf16 && !w_split) return MB2_OK;                   // exact-fp32 path requested
-    if (ceil_div(M, tc::BM) > 65535) return MB2_OK;
     // TMA: 16-byte aligned bases and row strides
     if (!aligned(x, 16) || (ld_x * es) % 16 != 0 || (K * es) % 16 != 0) return MB2_OK;
     const void *b0 = bf16 ? w : (const void *)w_split;
     const void *b1 = bf16 ? w : (const void *)(w_split + N * K);
     if (!aligned(b0, 16) || !aligned(b1, 16)) return MB2_OK;
     MB2_TRY(get_encode());
-    CUtensorMap ma, mb0, mb1;
-    MB2_TRY(make_map(&ma, x, M, K, ld_x, bf16));
-    MB2_TRY(make_map(&mb0, b0, N, K, K, bf16));
-    MB2_TRY(make_map(&mb1, b1, N, K, K, bf16));
-    tc::Params p{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi};
+    CUtensorMap ma, mb0, mb1, my;
+    MB2_TRY(make_map(&ma, x, M, K, ld_x, bf16, 128));
+    MB2_TRY(make_map(&mb0, b0, N, K, K, bf16, 128));
+    MB2_TRY(make_map(&mb1, b1, N, K, K, bf16, 128));
+    const bool remap = (n1 < N && off1 != 0) || (n2 < N && off2 != 0);
+    const bool tma_store = !remap && aligned(y, 16) && (ld_y * es) % 16 == 0;
+    if (tma_store) MB2_TRY(make_map(&my, y, M, N, ld_y, bf16, 32));
+    else my = mb0;  // unused
+    tc::Params p{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0};
     *used = true;
-    if (bf16) return launch_tc<tc::BF16, __nv_bfloat16>(ma, mb0, mb1, p, st);
-    return launch_tc<tc::F32X3, float>(ma, mb0, mb1, p, st);
+    if (bf16) return launch_tc<tc::BF16, __nv_bfloat16>(ma, mb0, mb1, my, p, st);
+    return launch_tc<tc::F32X3, float>(ma, mb0, mb1, my, p, st);
 }
 
 }  // namespace mb2

@@ -54,7 +54,8 @@ def selective_scan(x, dt, A, B, C, D, h0: Optional[torch.Tensor] = None,
 
 
 def conv1d_silu(x_in: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor],
-                batch: int, seqlen: int, d_inner: int, return_tail: bool = False):
+                batch: int, seqlen: int, d_inner: int, return_tail: bool = False,
+                out: Optional[torch.Tensor] = None):
     """silu(causal depthwise conv1d(x) + bias) over rows of x_in (token-major,
     first d_inner columns; row stride = x_in.stride(0)).  weight: (d_inner, 1, K)
     or (d_inner, K)."""
@@ -63,12 +64,13 @@ def conv1d_silu(x_in: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.T
         raise RuntimeError("conv1d_silu: rows must be contiguous")
     K = weight.shape[-1]
     w = weight.reshape(d_inner, K).contiguous()
-    xc = torch.empty(batch * seqlen, d_inner, device=x_in.device, dtype=x_in.dtype)
+    xc = out if out is not None else torch.empty(batch * seqlen, d_inner, device=x_in.device,
+                                                 dtype=x_in.dtype)
     tail = (torch.empty(batch, d_inner, K - 1, device=x_in.device, dtype=x_in.dtype)
             if return_tail else None)
     check(lib().mb2_conv1d_silu(dtype_code(x_in.dtype), ptr(x_in), x_in.stride(0), ptr(w),
-                                ptr(bias), ptr(xc), d_inner, ptr(tail), batch, seqlen, d_inner,
-                                K, stream_of(x_in)), "conv1d_silu")
+                                ptr(bias), ptr(xc), xc.stride(0), ptr(tail), batch, seqlen,
+                                d_inner, K, stream_of(x_in)), "conv1d_silu")
     return (xc, tail) if return_tail else xc
 
 
@@ -108,7 +110,8 @@ def split_tf32(w: torch.Tensor) -> torch.Tensor:
 
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
-           weight_split: Optional[torch.Tensor] = None, softplus: bool = False) -> torch.Tensor:
+           weight_split: Optional[torch.Tensor] = None, softplus: bool = False,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = x W^T + b over the last dim of x (nn.Linear semantics); softplus=True
     applies F.softplus to the result in the same kernel (dt_proj's epilogue)."""
     require_cuda(x, weight, bias, what="linear")
@@ -117,12 +120,12 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
     x2 = x.reshape(-1, K)
     if x2.stride(-1) != 1:
         x2 = x2.contiguous()
-    y = torch.empty(x2.shape[0], N, device=x.device, dtype=x.dtype)
+    y = out if out is not None else torch.empty(x2.shape[0], N, device=x.device, dtype=x.dtype)
     weight = weight.contiguous()
     check(lib().mb2_linear(dtype_code(x.dtype), ptr(x2), x2.stride(0), ptr(weight),
-                           ptr(weight_split), ptr(bias), ptr(y), N, x2.shape[0], N, K,
+                           ptr(weight_split), ptr(bias), ptr(y), y.stride(0), x2.shape[0], N, K,
                            _lib.EPI_SOFTPLUS if softplus else _lib.EPI_NONE, stream_of(x)), "linear")
-    return y.reshape(*lead, N)
+    return y if out is not None else y.reshape(*lead, N)
 
 
 def quantize(scheme: str, w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, int]:
