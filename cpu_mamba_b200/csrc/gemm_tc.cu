@@ -221,7 +221,8 @@ __device__ __forceinline__ float tf32_rn(float v) {
     return __uint_as_float(r);
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 32 lanes x 32 columns from TMEM; the load is asynchronous until tmem_wait_ld()
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -233,6 +234,8 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
           "=r"(r[31])
         : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
@@ -432,21 +435,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             if (lane == 0) bulk_wait_read0();
             __syncwarp();
             const uint32_t acc = tmem + (uint32_t)(b * C::ACC_COLS) + ((uint32_t)(q * 32) << 16);
+            // BF16: the whole 128-column accumulator in one round trip
+            uint32_t ra[32], rb[32], rc[32];
+            static_assert(BN == 128, "epilogue assumes 4 column blocks");
 #pragma unroll 1
             for (int cb = 0; cb < BN / 32; ++cb) {
-                uint32_t r[32];
-                tmem_ld32(acc + cb * 32, r);
                 float v[32];
                 if (MODE == F32X3) {
-                    uint32_t r1[32], r2[32];
-                    tmem_ld32(acc + BN + cb * 32, r1);
-                    tmem_ld32(acc + 2 * BN + cb * 32, r2);
+                    // the three accumulators of this 32-column block in one round trip
+                    tmem_ld32_async(acc + cb * 32, ra);
+                    tmem_ld32_async(acc + BN + cb * 32, rb);
+                    tmem_ld32_async(acc + 2 * BN + cb * 32, rc);
+                    tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
-                        v[j] = (__uint_as_float(r[j]) + __uint_as_float(r1[j])) + __uint_as_float(r2[j]);
+                        v[j] = (__uint_as_float(ra[j]) + __uint_as_float(rb[j])) + __uint_as_float(rc[j]);
                 } else {
+                    tmem_ld32_async(acc + cb * 32, ra);
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+                    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(ra[j]);
                 }
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
