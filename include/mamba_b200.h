@@ -200,6 +200,23 @@ int mb2_block_step(const mb2_block *blk, const void *x, void *out, float *h,
                    void *conv_state, int64_t batch, void *workspace,
                    size_t workspace_bytes, mb2_stream_t stream);
 
+/* Size of the device array mb2_block_step_static uses as its workspace. */
+#define MB2_STEP_STATIC_SCRATCH_BYTES (8u << 20)
+
+/* mb2_block_step for callers that cannot allocate device memory (a plugin
+ * whose host application owns the device memory budget, or a serving loop
+ * that must not allocate once running).  No counterpart in the reference: its
+ * forward_step allocates host tensors freely.  Same arguments and results as
+ * mb2_block_step, but the workspace is a fixed MB2_STEP_STATIC_SCRATCH_BYTES
+ * (8 MiB) array inside the library, held on every GPU that loads the library
+ * until exit; a batch whose mb2_step_workspace_bytes exceeds it returns
+ * MB2_ERR_WORKSPACE.  Allocates nothing.  The first call on a device looks the
+ * array's address up (cudaGetSymbolAddress) with that device current, so make
+ * it before any stream capture.  All calls on a device share the array: calls
+ * whose GPU work overlaps race and must be ordered by the caller. */
+int mb2_block_step_static(const mb2_block *blk, const void *x, void *out, float *h,
+                          void *conv_state, int64_t batch, mb2_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
