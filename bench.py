@@ -244,7 +244,7 @@ def run_ours(args, cfg):
     result = None
     if rank == 0:
         hbm, bf16, bf16_s, src = peaks()
-        roof = roofline(stages, cfg, hbm, bf16, src)
+        roof = roofline(stages, cfg, hbm, bf16, src, ms / args.steps)
         launches_per_step = 5
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
@@ -319,7 +319,37 @@ def profile_stages(m, x, cfg, dtype, steps):
     return {k: statistics.mean(v) for k, v in times.items()}
 
 
-def roofline(stages, cfg, hbm_gbs, bf16_tflops, src):
+# DRAM bytes (read + write) per token of each launch, from ncu captures of the
+# config-0 shapes at batch 64 (profiles/gemm_tc_f32x3_b64_t180.md,
+# profiles/scan_fused_f32_b64_t180.md, profiles/conv1d_silu_f32_b64_t180.md);
+# every tensor these kernels touch grows with the token count, so a full-size
+# launch moves (bytes per token) x N.
+TRAFFIC_PER_TOKEN = {
+    ("f32", 768, 24, "in_proj"): (54.325248e6 + 98.165504e6) / 11520,
+    ("f32", 768, 24, "x_proj"): (72.015104e6 + 1.871104e6) / 11520,
+    ("f32", 768, 24, "out_proj"): (80.273664e6 + 12.322816e6) / 11520,
+    ("f32", 768, 24, "scan"): (146.500096e6 + 33.24544e6) / 11520,
+    ("f32", 768, 24, "conv1d_silu"): (71.217152e6 + 26.989824e6) / 11520,
+}
+
+
+def realistic_block_bytes(cfg):
+    """HBM bytes of one block forward for a four-stage fused design (in_proj |
+    conv + x_proj | dt_proj + scan + gate | out_proj), each stage reading and
+    writing its tensors once: es x (2 d_model + 7 d_inner + 2 (R + 2S)) per
+    token, plus the weights once (config 0: 49,920 B per token, 1.372 GB)."""
+    B, T, dm, S = cfg["batch"], cfg["seqlen"], cfg["d_model"], cfg["d_state"]
+    di = 2 * dm
+    R = cfg.get("dt_rank", math.ceil(dm / 16))
+    es = 4 if cfg["dtype"] == "f32" else 2
+    N = B * T
+    xd = R + 2 * S
+    act = N * es * (2 * dm + 7 * di + 2 * xd)
+    w = es * (2 * di * dm + xd * di + di * R + dm * di)
+    return act + w
+
+
+def roofline(stages, cfg, hbm_gbs, bf16_tflops, src, ms_per_step):
     if not stages:
         return None
     B, T, dm, S = cfg["batch"], cfg["seqlen"], cfg["d_model"], cfg["d_state"]
@@ -334,14 +364,31 @@ def roofline(stages, cfg, hbm_gbs, bf16_tflops, src):
               "scan": N * es * (3 * di + R + 2 * S)}      # x, z, dt_low, B, C in; y out
     top = max(stages, key=stages.get)
     t = stages[top] / 1e3
+    tpt = TRAFFIC_PER_TOKEN.get((cfg["dtype"], dm, S, top))
+    traffic = tpt * N if tpt else None
+    blk_bytes = realistic_block_bytes(cfg)
+    blk_gbs = blk_bytes / (ms_per_step / 1e3) / 1e9
+    block = {"bytes": blk_bytes, "achieved": blk_gbs, "peak": hbm_gbs, "unit": "GB/s",
+             "frac": blk_gbs / hbm_gbs,
+             "note": "whole block vs HBM, each stage reading and writing its tensors once"}
     if top in flops:
         ach = flops[top] / t / 1e12
-        return {"kernel": top, "bound": "tensor", "achieved": ach, "peak": bf16_tflops,
-                "unit": "TFLOP/s", "frac": ach / bf16_tflops, "traffic": None,
-                "peak_source": f"{src} bf16 dense"}
+        r = {"kernel": top, "bound": "tensor", "achieved": ach, "peak": bf16_tflops,
+             "unit": "TFLOP/s", "frac": ach / bf16_tflops, "traffic": traffic,
+             "peak_source": f"{src} bf16 dense"}
+        if cfg["dtype"] == "f32":
+            # fp32-faithful path: three TF32 MMAs per multiply-add; the dense TF32
+            # rate of the tensor core is half its bf16 rate
+            ex = 3 * flops[top] / t / 1e12
+            r["tensor_pipe"] = {"tf32_tflops_executed": ex, "tf32_peak": bf16_tflops / 2,
+                                "frac": ex / (bf16_tflops / 2),
+                                "peak_source": f"{src} bf16 dense / 2"}
+        r["block"] = block
+        return r
     ach = nbytes[top] / t / 1e9
     return {"kernel": top, "bound": "hbm", "achieved": ach, "peak": hbm_gbs, "unit": "GB/s",
-            "frac": ach / hbm_gbs, "traffic": None, "peak_source": f"{src} HBM copy"}
+            "frac": ach / hbm_gbs, "traffic": traffic, "peak_source": f"{src} HBM copy",
+            "block": block}
 
 
 # ------------------------------------------------------- reference arm / CPU
