@@ -10,7 +10,9 @@ x ~ N(0,1); Kaiming-uniform linear weights; conv ~ U(-0.5, 0.5);
 A_log = log(1..S); D = 1; dt_proj.bias = softplus^-1(log-uniform[1e-3, 0.1]).
 Other configs are measurement aids: 1 = bf16 B=8 T=8192 (S=16); 2 = stateful
 decode B=64 (d_model 1024): metric over forward_step calls; 3 = int8 weights,
-d_model 1536, B=32 T=2048.
+d_model 1536, B=32 T=2048; 4 = 24-layer RMSNorm pre-norm residual stack in
+bf16 (d_model 768, S=16), B=1024 x T=2048 split across the ranks (strong
+scaling; tokens/s counts tokens through all 24 layers).
 
 Multi-GPU: one process per GPU (torchrun); each rank runs its own batch
 (weak scaling, no data-path collective); time = max over ranks of the
@@ -51,6 +53,8 @@ CONFIGS = {
             seqlen=512, dtype="f32", mode="step", dt_rank=64),
     3: dict(workload="mamba_block_fwd_int8_b32_t2048_dm1536", d_model=1536, d_state=16,
             batch=32, seqlen=2048, dtype="f32", mode="forward", quant="int8", dt_rank=96),
+    4: dict(workload="mamba_stack24_rmsnorm_fwd_bf16_b1024_t2048", d_model=768, d_state=16,
+            batch=1024, seqlen=2048, dtype="bf16", mode="stack", n_layers=24),
 }
 
 
@@ -161,6 +165,34 @@ def make_params(cfg, seed):
     return p, R
 
 
+def make_stack(cfg):
+    """The residual stack with every layer's block drawn as make_params draws
+    one (seed = layer index) and RMSNorm weights of one (their init)."""
+    from cpu_mamba_b200 import MambaStack
+    n, dm = cfg["n_layers"], cfg["d_model"]
+    sd = {}
+    for i in range(n):
+        p, R = make_params(cfg, seed=i)
+        sd[f"layers.{i}.norm.weight"] = torch.ones(dm)
+        sd.update({f"layers.{i}.mixer.{k}": v for k, v in p.items()})
+    m = MambaStack(n, dm, d_state=cfg["d_state"], dt_rank=R, eps=1e-5).eval()
+    m.load_state_dict(sd, strict=True)
+    return m, R
+
+
+def stack_roofline(cfg, batch, hbm_gbs, src, ms_per_step):
+    """Whole-stack HBM fraction: per layer the four-stage block bytes plus the
+    norm pass (x read) and the residual (x read in out_proj's epilogue)."""
+    c = dict(cfg, batch=batch)
+    es = 4 if cfg["dtype"] == "f32" else 2
+    per_layer = realistic_block_bytes(c) + 2 * batch * cfg["seqlen"] * cfg["d_model"] * es
+    nbytes = per_layer * cfg["n_layers"]
+    ach = nbytes / (ms_per_step / 1e3) / 1e9
+    return {"kernel": f"stack of {cfg['n_layers']} layers (6 launches each)", "bound": "hbm",
+            "achieved": ach, "peak": hbm_gbs, "unit": "GB/s", "frac": ach / hbm_gbs,
+            "traffic": None, "bytes_per_step": nbytes, "peak_source": f"{src} HBM copy"}
+
+
 # ------------------------------------------------------------- our arm
 def run_ours(args, cfg):
     from cpu_mamba_b200 import CPUMamba, QuantConfig, quantize_block
@@ -172,18 +204,27 @@ def run_ours(args, cfg):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     dtype = torch.float32 if cfg["dtype"] == "f32" else torch.bfloat16
-    p, R = make_params(cfg, seed=0)
-    m = CPUMamba(cfg["d_model"], d_state=cfg["d_state"], dt_rank=R).eval()
-    m.load_state_dict(p, strict=True)
-    m = m.to(device=dev, dtype=dtype)
-    if cfg.get("quant"):
-        quantize_block(m, QuantConfig(cfg["quant"]))
-    B, T, dm = cfg["batch"], cfg["seqlen"], cfg["d_model"]
+    stack_mode = cfg["mode"] == "stack"
+    if stack_mode:
+        m, R = make_stack(cfg)
+        m = m.to(device=dev, dtype=dtype)
+        if cfg["batch"] % ws:
+            raise SystemExit(f"batch {cfg['batch']} does not split over {ws} ranks")
+        B = cfg["batch"] // ws                 # strong scaling: the batch is sharded
+    else:
+        p, R = make_params(cfg, seed=0)
+        m = CPUMamba(cfg["d_model"], d_state=cfg["d_state"], dt_rank=R).eval()
+        m.load_state_dict(p, strict=True)
+        m = m.to(device=dev, dtype=dtype)
+        if cfg.get("quant"):
+            quantize_block(m, QuantConfig(cfg["quant"]))
+        B = cfg["batch"]
+    T, dm = cfg["seqlen"], cfg["d_model"]
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     step_mode = cfg["mode"] == "step"
     in_shape = (B, dm) if step_mode else (B, T, dm)
     in_bytes = math.prod(in_shape) * (4 if dtype == torch.float32 else 2)
-    nbuf = max(4, math.ceil(2 * L2_BYTES / in_bytes)) if not step_mode else 8
+    nbuf = 8 if step_mode else max(2 if stack_mode else 4, math.ceil(2 * L2_BYTES / in_bytes))
     xs = [torch.randn(in_shape, generator=g, device=dev).to(dtype) for _ in range(nbuf)]
     state = None
     if step_mode:
@@ -229,9 +270,7 @@ def run_ours(args, cfg):
     for i in range(max(3, min(args.steps, 10)) + 1):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        xd = host_in.to(dev, non_blocking=True)
-        y = step_e2e(m, xd, state, step_mode)
-        host_out.copy_(y, non_blocking=True)
+        step_e2e(m, host_in, host_out, state, step_mode, dev)
         b.record(stream)
         torch.cuda.synchronize(dev)
         if i > 0:
@@ -240,21 +279,27 @@ def run_ours(args, cfg):
     e2e = {"value": ws * tokens_per_step / (e2e_t / 1e3), "unit": "tokens/s",
            "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": in_bytes}
 
-    stages = profile_stages(m, xs[0], cfg, dtype, args.steps) if not step_mode else {}
+    stages = profile_stages(m, xs[0], cfg, dtype, args.steps) if cfg["mode"] == "forward" else {}
     result = None
     if rank == 0:
         hbm, bf16, bf16_s, src = peaks()
-        roof = roofline(stages, cfg, hbm, bf16, src, ms / args.steps)
-        launches_per_step = 5
+        if stack_mode:
+            roof = stack_roofline(cfg, B, hbm, src, ms / args.steps)
+            launches_per_step = 6 * cfg["n_layers"]
+        else:
+            roof = roofline(stages, cfg, hbm, bf16, src, ms / args.steps)
+            launches_per_step = 5
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if stack_mode else "weak",
+            "vs_baseline": None,
             "dtype": cfg["dtype"], "data": "synthetic (seeded; shapes of the configuration)",
             "config": {"workload": cfg["workload"], "batch_per_gpu": B, "global_batch": B * ws,
                        "seq_len": T if not step_mode else 1, "d_model": dm,
                        "d_inner": 2 * dm, "d_state": cfg["d_state"], "dt_rank": R,
                        "quant": cfg.get("quant"), "parallelism": f"batch-sharded x{ws}",
+                       "layers": cfg.get("n_layers", 1),
                        "l2": f"inputs rotated over {nbuf} buffers ({nbuf * in_bytes / 2**20:.0f} MB > L2)"},
             "roofline": roof, "stages_ms": stages, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
@@ -266,11 +311,16 @@ def run_ours(args, cfg):
     return result
 
 
-def step_e2e(m, xd, state, step_mode):
+def step_e2e(m, host_in, host_out, state, step_mode, dev):
+    """One step through the public API from pinned host memory to pinned host
+    memory.  A forward streams batch slices with the copies overlapping the
+    kernels (CPUMamba.forward_host); a decode step is too small to split."""
     with torch.no_grad():
         if step_mode:
-            return m.forward_step(xd, state)[0]
-        return m(xd)
+            y = m.forward_step(host_in.to(dev, non_blocking=True), state)[0]
+            host_out.copy_(y, non_blocking=True)
+        else:
+            m.forward_host(host_in, out=host_out)
 
 
 STAGES = ("in_proj", "conv1d_silu", "x_proj", "scan", "out_proj")
@@ -412,8 +462,33 @@ def cpu_cores():
         return os.cpu_count() or 1
 
 
+def cpu_baseline_stack(cfg, min_seconds=10.0, max_runs=5):
+    """The stack composed from the reference's CPU block (its compiled scan op)
+    and torch RMSNorm, in float32, on one sequence of the workload."""
+    import oracle
+    cores = cpu_cores()
+    torch.set_num_threads(cores)
+    op = oracle.load_ref_scan_op()
+    layers = []
+    for i in range(cfg["n_layers"]):
+        p, _ = make_params(cfg, seed=i)
+        layers.append((p, torch.ones(cfg["d_model"])))
+    x = torch.randn(1, cfg["seqlen"], cfg["d_model"], generator=torch.Generator().manual_seed(1))
+    ts, t_start = [], time.perf_counter()
+    while len(ts) < 2 or (time.perf_counter() - t_start < min_seconds and len(ts) < max_runs):
+        t0 = time.perf_counter()
+        oracle.stack_forward(layers, x, 1e-5, scan_op=op)
+        ts.append(time.perf_counter() - t0)
+    return {"value": cfg["seqlen"] / statistics.median(ts), "unit": "tokens/s", "cores": cores,
+            "kind": "reference" if op is not None else "port",
+            "sample": f"1 x {cfg['seqlen']} tokens through {cfg['n_layers']} layers, float32, "
+                      f"median of {len(ts)}"}
+
+
 def cpu_baseline(cfg, min_seconds=10.0, max_runs=10):
     """The reference's CPU block forward on a bounded sample of the workload."""
+    if cfg["mode"] == "stack":
+        return cpu_baseline_stack(cfg)
     if cfg["mode"] != "forward" or cfg.get("quant"):
         return None
     cores = cpu_cores()

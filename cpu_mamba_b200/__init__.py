@@ -11,6 +11,7 @@ from .module import CPUMamba, assert_state_dict_compatible
 from .quant import QuantConfig, QuantizedLinear, memory_footprint, quantize_block
 from .ops import selective_scan
 from .scan_assoc import selective_scan_assoc, selective_scan_assoc_chunked
+from .stack import MambaLayer, MambaStack
 
 B200Mamba = CPUMamba
 
@@ -18,5 +19,6 @@ __version__ = "0.4.0+b200"
 __all__ = [
     "CPUMamba", "B200Mamba", "assert_state_dict_compatible", "QuantConfig",
     "QuantizedLinear", "quantize_block", "memory_footprint", "selective_scan",
-    "selective_scan_assoc", "selective_scan_assoc_chunked", "__version__",
+    "selective_scan_assoc", "selective_scan_assoc_chunked", "MambaLayer", "MambaStack",
+    "__version__",
 ]

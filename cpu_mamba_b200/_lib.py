@@ -72,6 +72,11 @@ _SIGS = {
                                       _vp, ctypes.c_size_t, _vp]),
     "mb2_block_step_static": (ctypes.c_int, [ctypes.POINTER(Block), _vp, _vp, _vp, _vp, _c_i64,
                                              _vp]),
+    "mb2_fold_norm": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _c_i64, _c_i64, _vp]),
+    "mb2_stack_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Block), _c_i64, _c_i64,
+                                                    _c_i64]),
+    "mb2_stack_forward": (ctypes.c_int, [ctypes.POINTER(Block), _c_i64, ctypes.c_float, _vp,
+                                         _c_i64, _c_i64, _vp, ctypes.c_size_t, _vp]),
 }
 
 _LIB = None

@@ -11,45 +11,25 @@
 //      (dt_proj + softplus + exp(dt A) + recurrence + D skip + cast + SiLU(z)
 //       gate; y overwrites xc in place)
 //   5. out_proj           y                  -> out (N, dm)
-#include "common.cuh"
+#include "internal.cuh"
 
 namespace mb2 {
 
-int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
-              const float *scale, const void *bias, void *y, int64_t ld_y, int64_t M,
-              int64_t N, int64_t K, int64_t n1, int64_t off1, int64_t n2, int64_t off2,
-              int epi, cudaStream_t st);
-int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *w_split,
-            const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
-            int64_t n1, int64_t off1, int64_t n2, int64_t off2, int epi, cudaStream_t st,
-            bool *used);
-int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const void *bias,
-                void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
-                int64_t d_inner, int64_t d_conv, cudaStream_t st);
-int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t ld_dl,
-               const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
-               int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
-               const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
-               int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, int64_t dt_rank,
-               cudaStream_t stream);
-
-// Dense linear: tensor-core kernel where it applies, CUDA-core kernel otherwise.
-static int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, void *y,
-                      int64_t ld_y, int64_t M, int64_t N, int64_t K, int epi,
-                      cudaStream_t st, int64_t n1 = -1, int64_t off1 = 0, int64_t n2 = -1,
-                      int64_t off2 = 0) {
+int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, void *y,
+               int64_t ld_y, int64_t M, int64_t N, int64_t K, int epi, cudaStream_t st,
+               int64_t n1, int64_t off1, int64_t n2, int64_t off2, const EpiExtra &ex) {
     if (n1 < 0) n1 = N;
     if (n2 < 0) n2 = N;
     if (L.scheme != MB2_Q_NONE)
         return gemm_simt(dtype, L.scheme, x, ld_x, L.weight_q, L.scale, L.bias, y, ld_y, M, N, K,
-                         n1, off1, n2, off2, epi, st);
+                         n1, off1, n2, off2, epi, st, ex);
     MB2_REQUIRE(L.weight, MB2_ERR_ARG, "linear: null weight");
     bool used = false;
     MB2_TRY(gemm_tc(dtype, x, ld_x, L.weight, L.weight_split, L.bias, y, ld_y, M, N, K, n1, off1,
-                    n2, off2, epi, st, &used));
+                    n2, off2, epi, st, &used, ex));
     if (used) return MB2_OK;
     return gemm_simt(dtype, MB2_Q_NONE, x, ld_x, L.weight, nullptr, L.bias, y, ld_y, M, N, K,
-                     n1, off1, n2, off2, epi, st);
+                     n1, off1, n2, off2, epi, st, ex);
 }
 
 struct Layout {
@@ -166,6 +146,38 @@ extern "C" int mb2_qlinear(int scheme, int dtype, const void *x, int64_t ld_x,
                      epilogue, (cudaStream_t)stream);
 }
 
+// The five launches of one block forward over N = batch * seqlen rows.
+// row_scale (N floats) scales in_proj's output rows (a pre-norm folded into
+// in_proj); resid (N, d_model) is added to out_proj's output (may alias out).
+static int block_pipeline(const mb2_block &b, const Layout &l, const void *x, void *out,
+                          int64_t batch, int64_t seqlen, float *h_last, void *conv_tail,
+                          char *ws, cudaStream_t st, const float *row_scale,
+                          const void *resid) {
+    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
+    const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
+    const size_t es = l.es;
+    EpiExtra in_ex, out_ex;
+    in_ex.row_scale = row_scale;
+    out_ex.resid = resid;
+    out_ex.ld_r = l.dm;
+    if (N > 0)
+        MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, N, 2 * di, l.dm, MB2_EPI_NONE,
+                           st, -1, 0, -1, 0, in_ex));
+    MB2_TRY(conv1d_silu(b.dtype, xz, 2 * di, b.conv_w, b.conv_b, xc, di, conv_tail, batch, seqlen,
+                        di, b.d_conv, st));
+    if (N > 0)
+        MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, MB2_EPI_NONE,
+                           st, R, l.RB - R, R + S, l.RC - l.RB - S));
+    MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
+                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
+                       dt_weight(b), b.dt_proj.bias, b.A_log, b.D, nullptr, h_last, xc, di, batch,
+                       seqlen, di, S, R, st));
+    if (N > 0)
+        MB2_TRY(linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, N, l.dm, di, MB2_EPI_NONE, st,
+                           -1, 0, -1, 0, out_ex));
+    return MB2_OK;
+}
+
 extern "C" size_t mb2_block_workspace_bytes(const mb2_block *blk, int64_t batch, int64_t seqlen) {
     if (!blk || batch < 0 || seqlen < 0) return 0;
     return make_layout(blk, batch * seqlen).total;
@@ -182,27 +194,9 @@ extern "C" int mb2_block_forward(const mb2_block *blk, const void *x, void *out,
     MB2_REQUIRE(workspace_bytes >= l.total, MB2_ERR_WORKSPACE,
                 "block: workspace %zu < required %zu", workspace_bytes, l.total);
     if (batch == 0) return MB2_OK;
-    char *ws = static_cast<char *>(workspace);
-    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
-    const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
-    const size_t es = l.es;
-    if (N > 0) {
-        MB2_REQUIRE(x && out && workspace, MB2_ERR_ARG, "block: null pointer");
-        MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, N, 2 * di, l.dm, MB2_EPI_NONE,
-                           st));
-    }
-    MB2_TRY(conv1d_silu(b.dtype, xz, 2 * di, b.conv_w, b.conv_b, xc, di, conv_tail, batch, seqlen,
-                        di, b.d_conv, st));
-    if (N > 0)
-        MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, MB2_EPI_NONE,
-                           st, R, l.RB - R, R + S, l.RC - l.RB - S));
-    MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
-                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
-                       dt_weight(b), b.dt_proj.bias, b.A_log, b.D, nullptr, h_last, xc, di, batch,
-                       seqlen, di, S, R, st));
-    if (N > 0)
-        MB2_TRY(linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, N, l.dm, di, MB2_EPI_NONE, st));
-    return MB2_OK;
+    if (l.N > 0) MB2_REQUIRE(x && out && workspace, MB2_ERR_ARG, "block: null pointer");
+    return block_pipeline(b, l, x, out, batch, seqlen, h_last, conv_tail,
+                          static_cast<char *>(workspace), st, nullptr, nullptr);
 }
 
 extern "C" size_t mb2_step_workspace_bytes(const mb2_block *blk, int64_t batch) {
@@ -242,4 +236,137 @@ extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, fl
                        dt_weight(b), b.dt_proj.bias, b.A_log, b.D, h, h, xc, di, batch, 1, di, S,
                        R, st));
     return linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, batch, l.dm, di, MB2_EPI_NONE, st);
+}
+
+// ------------------------------------------------------------------ stack ---
+// A residual stack of pre-norm blocks, x <- x + block(RMSNorm(x)) per layer
+// (the Mamba-130M-style composition; the reference has no stack: its block is
+// composed with torch.nn.RMSNorm around CPUMamba.forward).  RMSNorm(x) =
+// x / rms(x) * g with rms(x) = sqrt(mean(x^2) + eps).  Its weight g is folded
+// into in_proj's columns once (mb2_fold_norm), and 1 / rms(x_m) is one float
+// per token that in_proj's epilogue multiplies in, so the normalised
+// activations are never written.  out_proj's epilogue adds the residual and
+// writes the stream in place.  Per layer: row-rms pass + the block's five
+// launches.
+
+// one warp per row: r[m] = 1 / sqrt(mean(x[m, :]^2) + eps), fp32 accumulation
+template <typename T>
+__global__ void rms_scale_kernel(const T *__restrict__ x, int64_t ld, int64_t rows, int64_t D,
+                                 float eps, float *__restrict__ r, int vec) {
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const T *xr = x + row * ld;
+    float ss = 0.0f;
+    if (vec) {
+        constexpr int V = 16 / (int)sizeof(T);
+        for (int64_t c = (int64_t)lane * V; c < D; c += 32 * V) {
+            const uint4 u = *reinterpret_cast<const uint4 *>(xr + c);
+            const T *e = reinterpret_cast<const T *>(&u);
+#pragma unroll
+            for (int k = 0; k < V; ++k) {
+                const float f = io<T>::to_f(e[k]);
+                ss = fmaf(f, f, ss);
+            }
+        }
+    } else {
+        for (int64_t c = lane; c < D; c += 32) {
+            const float f = io<T>::to_f(xr[c]);
+            ss = fmaf(f, f, ss);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) r[row] = 1.0f / sqrtf(ss / (float)D + eps);
+}
+
+static int rms_scale(int dtype, const void *x, int64_t rows, int64_t D, float eps, float *r,
+                     cudaStream_t st) {
+    if (rows == 0) return MB2_OK;
+    const size_t es = dtype_size(dtype);
+    const int vec = aligned(x, 16) && (D * (int64_t)es) % 16 == 0;
+    const unsigned grid = (unsigned)ceil_div(rows, (int64_t)8);
+    if (dtype == MB2_F32)
+        rms_scale_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float *>(x), D, rows, D,
+                                                      eps, r, vec);
+    else
+        rms_scale_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16 *>(x), D, rows, D, eps, r, vec);
+    return check_launch("rms_scale_kernel");
+}
+
+template <typename T>
+__global__ void fold_norm_kernel(const T *__restrict__ w, const T *__restrict__ g,
+                                 T *__restrict__ out, int64_t rows, int64_t cols) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * cols) return;
+    out[i] = io<T>::from_f(io<T>::to_f(w[i]) * io<T>::to_f(g[i % cols]));
+}
+
+extern "C" int mb2_fold_norm(int dtype, const void *w, const void *norm_weight, void *out,
+                             int64_t rows, int64_t cols, mb2_stream_t stream) {
+    MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "fold_norm: bad dtype");
+    MB2_REQUIRE(rows >= 0 && cols >= 0, MB2_ERR_SHAPE, "fold_norm: negative size");
+    if (rows * cols == 0) return MB2_OK;
+    MB2_REQUIRE(w && norm_weight && out, MB2_ERR_ARG, "fold_norm: null pointer");
+    const unsigned grid = (unsigned)ceil_div(rows * cols, (int64_t)256);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (dtype == MB2_F32)
+        fold_norm_kernel<float><<<grid, 256, 0, st>>>(
+            static_cast<const float *>(w), static_cast<const float *>(norm_weight),
+            static_cast<float *>(out), rows, cols);
+    else
+        fold_norm_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16 *>(w), static_cast<const __nv_bfloat16 *>(norm_weight),
+            static_cast<__nv_bfloat16 *>(out), rows, cols);
+    return check_launch("fold_norm_kernel");
+}
+
+static size_t stack_bytes(const mb2_block *layers, int64_t n_layers, int64_t rows,
+                          size_t *off_r) {
+    size_t ws = 0;
+    for (int64_t i = 0; i < n_layers; ++i) {
+        const size_t t = make_layout(&layers[i], rows).total;
+        ws = t > ws ? t : ws;
+    }
+    *off_r = ws;
+    return ws + align256((size_t)rows * sizeof(float));
+}
+
+extern "C" size_t mb2_stack_workspace_bytes(const mb2_block *layers, int64_t n_layers,
+                                            int64_t batch, int64_t seqlen) {
+    if (!layers || n_layers <= 0 || batch < 0 || seqlen < 0) return 0;
+    size_t off_r;
+    return stack_bytes(layers, n_layers, batch * seqlen, &off_r);
+}
+
+extern "C" int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, float eps, void *x,
+                                 int64_t batch, int64_t seqlen, void *workspace,
+                                 size_t workspace_bytes, mb2_stream_t stream) {
+    MB2_REQUIRE(layers && n_layers > 0, MB2_ERR_ARG, "stack: no layers");
+    MB2_REQUIRE(batch >= 0 && seqlen >= 0, MB2_ERR_SHAPE, "stack: negative size");
+    MB2_REQUIRE(eps >= 0.0f, MB2_ERR_ARG, "stack: negative eps");
+    for (int64_t i = 0; i < n_layers; ++i) {
+        MB2_TRY(check_block(&layers[i]));
+        MB2_REQUIRE(layers[i].d_model == layers[0].d_model && layers[i].dtype == layers[0].dtype,
+                    MB2_ERR_SHAPE, "stack: layer %lld differs in d_model or dtype",
+                    (long long)i);
+    }
+    const int64_t N = batch * seqlen;
+    size_t off_r;
+    const size_t need = stack_bytes(layers, n_layers, N, &off_r);
+    MB2_REQUIRE(workspace_bytes >= need, MB2_ERR_WORKSPACE,
+                "stack: workspace %zu < required %zu", workspace_bytes, need);
+    if (N == 0) return MB2_OK;
+    MB2_REQUIRE(x && workspace, MB2_ERR_ARG, "stack: null pointer");
+    cudaStream_t st = (cudaStream_t)stream;
+    char *ws = static_cast<char *>(workspace);
+    float *r = reinterpret_cast<float *>(ws + off_r);
+    for (int64_t i = 0; i < n_layers; ++i) {
+        const mb2_block &b = layers[i];
+        const Layout l = make_layout(&b, N);
+        MB2_TRY(rms_scale(b.dtype, x, N, b.d_model, eps, r, st));
+        MB2_TRY(block_pipeline(b, l, x, x, batch, seqlen, nullptr, nullptr, ws, st, r, x));
+    }
+    return MB2_OK;
 }

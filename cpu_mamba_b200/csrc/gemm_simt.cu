@@ -11,7 +11,7 @@
 // Tile 128 x 64 x 16, 256 threads, 8 x 4 outputs per thread, register-prefetch
 // double buffer.  An optional column remap writes x_proj's three output
 // segments (dt_low | B | C) to separately aligned column offsets.
-#include "common.cuh"
+#include "internal.cuh"
 
 namespace mb2 {
 
@@ -29,6 +29,8 @@ struct GemmArgs {
     int64_t n1, n2, off1, off2;    // output column remap
     int epi;                       // MB2_EPI_NONE / MB2_EPI_SOFTPLUS
     float lut[16];                 // nf4 code book (quant.py:35-40), by value
+    const float *row_scale;        // EpiExtra terms
+    const void *resid; int64_t ld_r;
 };
 
 // quant.py:35-40: a tuple of Python floats turned into a float32 tensor, i.e.
@@ -135,8 +137,11 @@ gemm_simt_kernel(const GemmArgs a) {
         for (int i = 0; i < 8; ++i) {
             const int64_t m = m0 + ty * 8 + i;
             if (m < a.M) {
-                float v = acc[i][jj] + bv;
+                float v = acc[i][jj];
+                if (a.row_scale) v *= a.row_scale[m];
+                v += bv;
                 if (a.epi == MB2_EPI_SOFTPLUS) v = softplus_f(io<T>::round(v));
+                if (a.resid) v += io<T>::to_f(static_cast<const T *>(a.resid)[m * a.ld_r + n]);
                 Y[m * a.ld_y + col] = io<T>::from_f(v);
             }
         }
@@ -154,13 +159,14 @@ static int launch_simt(const GemmArgs &a, cudaStream_t st) {
 int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
               const float *scale, const void *bias, void *y, int64_t ld_y, int64_t M,
               int64_t N, int64_t K, int64_t n1, int64_t off1, int64_t n2, int64_t off2,
-              int epi, cudaStream_t st) {
+              int epi, cudaStream_t st, const EpiExtra &ex) {
     MB2_REQUIRE(M >= 0 && N >= 0 && K >= 0, MB2_ERR_SHAPE, "linear: negative size");
     MB2_REQUIRE(ceil_div(M, SG_BM) <= 65535, MB2_ERR_SHAPE, "linear: M too large");
     if (M == 0 || N == 0) return MB2_OK;
     MB2_REQUIRE(x && w && y, MB2_ERR_ARG, "linear: null pointer");
     MB2_REQUIRE(scheme == MB2_Q_NONE || scale, MB2_ERR_ARG, "linear: quantised weight needs scale");
-    GemmArgs a{x, ld_x, w, scale, bias, y, ld_y, M, N, K, n1, n2, off1, off2, epi, {}};
+    GemmArgs a{x, ld_x, w, scale, bias, y, ld_y, M, N, K, n1, n2, off1, off2, epi, {},
+               ex.row_scale, ex.resid, ex.ld_r};
     nf4_lut(a.lut);
     const bool f32 = dtype == MB2_F32;
     switch (scheme) {

@@ -38,7 +38,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include "common.cuh"
+#include "internal.cuh"
 
 namespace mb2 {
 
@@ -100,6 +100,8 @@ struct Params {
     int64_t n1, n2, off1, off2;   // output column remap
     int epi;                      // MB2_EPI_NONE / MB2_EPI_SOFTPLUS
     int tma_store;                // 1: store through map_y
+    const float *row_scale;       // EpiExtra terms (internal.cuh)
+    const void *resid; int64_t ld_r;
 };
 
 // ------------------------------------------------------------- primitives
@@ -251,7 +253,9 @@ __device__ __forceinline__ void bulk_wait_read0() {
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ----------------------------------------------------------------- kernel
-template <int MODE, typename TO>
+// EXTRA: the epilogue applies EpiExtra's row scale / residual (a separate
+// instantiation, so the plain projections carry none of its code)
+template <int MODE, typename TO, bool EXTRA>
 __global__ void __launch_bounds__(Cfg<MODE>::WARPS * 32, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b0,
                const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_y,
@@ -435,6 +439,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             if (lane == 0) bulk_wait_read0();
             __syncwarp();
             const uint32_t acc = tmem + (uint32_t)(b * C::ACC_COLS) + ((uint32_t)(q * 32) << 16);
+            const int64_t m_row = m0 + q * 32 + lane;     // the output row this thread drains
+            const bool row_ok = m_row < p.M;
+            const float rscale = (p.row_scale && row_ok) ? p.row_scale[m_row] : 1.0f;
+            const TO *rrow = static_cast<const TO *>(p.resid) + (row_ok ? m_row : 0) * p.ld_r;
             // BF16: the whole 128-column accumulator in one round trip
             uint32_t ra[32], rb[32], rc[32];
             static_assert(BN == 128, "epilogue assumes 4 column blocks");
@@ -459,10 +467,25 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int64_t n = n0 + cb * 32 + j;
+                    if (EXTRA && p.row_scale) v[j] *= rscale;
                     if (bias) v[j] += (n < p.N) ? io<TO>::to_f(bias[n]) : 0.0f;
                     // dt_proj's softplus (_mamba.py:219-220) on the value the
                     // reference would have stored in its dtype
                     if (p.epi == MB2_EPI_SOFTPLUS) v[j] = softplus_f(io<TO>::round(v[j]));
+                }
+                if (EXTRA && p.resid && row_ok) {
+                    // residual add: this row's 32 columns, 16 bytes at a time
+                    // (the host guarantees 16-byte rows and N % VEC == 0)
+#pragma unroll
+                    for (int c = 0; c < 32 / VEC; ++c) {
+                        const int64_t nb = n0 + cb * 32 + c * VEC;
+                        if (nb < p.N) {
+                            const uint4 u = *reinterpret_cast<const uint4 *>(rrow + nb);
+                            const TO *e = reinterpret_cast<const TO *>(&u);
+#pragma unroll
+                            for (int k = 0; k < VEC; ++k) v[c * VEC + k] += io<TO>::to_f(e[k]);
+                        }
+                    }
                 }
                 // row `lane` of box cb*32/BOXC: its 16-byte chunks at c ^ (row & 7)
                 const int box = (cb * 32) / BOXC;
@@ -558,10 +581,10 @@ static int make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t col
     return MB2_OK;
 }
 
-template <int MODE, typename TO>
+template <int MODE, typename TO, bool EXTRA>
 static int launch_tc(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
                      const CUtensorMap &ym, const tc::Params &p, cudaStream_t st) {
-    auto kern = tc::gemm_tc_kernel<MODE, TO>;
+    auto kern = tc::gemm_tc_kernel<MODE, TO, EXTRA>;
     constexpr size_t smem = tc::smem_bytes<MODE, TO>();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_tc smem attribute: %s", cudaGetErrorString(e));
@@ -581,7 +604,7 @@ static int launch_tc(const CUtensorMap &a, const CUtensorMap &b0, const CUtensor
 int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *w_split,
             const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
             int64_t n1, int64_t off1, int64_t n2, int64_t off2, int epi, cudaStream_t st,
-            bool *used) {
+            bool *used, const EpiExtra &ex) {
     *used = false;
     const bool bf16 = dtype == MB2_BF16;
     const size_t es = bf16 ? 2 : 4;
@@ -589,6 +612,9 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
     if (!bf16 && !w_split) return MB2_OK;                   // exact-fp32 path requested
     // TMA: 16-byte aligned bases and row strides
     if (!aligned(x, 16) || (ld_x * es) % 16 != 0 || (K * es) % 16 != 0) return MB2_OK;
+    // the residual is read in 16-byte pieces
+    if (ex.resid && (!aligned(ex.resid, 16) || (ex.ld_r * es) % 16 != 0 || (N * es) % 16 != 0))
+        return MB2_OK;
     const void *b0 = bf16 ? w : (const void *)w_split;
     const void *b1 = bf16 ? w : (const void *)(w_split + N * K);
     if (!aligned(b0, 16) || !aligned(b1, 16)) return MB2_OK;
@@ -601,10 +627,15 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
     const bool tma_store = !remap && aligned(y, 16) && (ld_y * es) % 16 == 0;
     if (tma_store) MB2_TRY(make_map(&my, y, M, N, ld_y, bf16, 32));
     else my = mb0;  // unused
-    tc::Params p{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0};
+    tc::Params p{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0,
+                 ex.row_scale, ex.resid, ex.ld_r};
     *used = true;
-    if (bf16) return launch_tc<tc::BF16, __nv_bfloat16>(ma, mb0, mb1, my, p, st);
-    return launch_tc<tc::F32X3, float>(ma, mb0, mb1, my, p, st);
+    const bool extra = ex.row_scale || ex.resid;
+    if (bf16)
+        return extra ? launch_tc<tc::BF16, __nv_bfloat16, true>(ma, mb0, mb1, my, p, st)
+                     : launch_tc<tc::BF16, __nv_bfloat16, false>(ma, mb0, mb1, my, p, st);
+    return extra ? launch_tc<tc::F32X3, float, true>(ma, mb0, mb1, my, p, st)
+                 : launch_tc<tc::F32X3, float, false>(ma, mb0, mb1, my, p, st);
 }
 
 }  // namespace mb2

@@ -1,0 +1,48 @@
+// Internal launchers shared between the library's translation units (not part
+// of the C ABI).
+#pragma once
+
+#include "common.cuh"
+
+namespace mb2 {
+
+// Optional terms of a projection's epilogue, applied to each output element
+// y[m, n] in this order:
+//   v  = acc * row_scale[m]          (pre-norm folded into the projection:
+//                                     row_scale = 1 / rms(x_m), the norm weight
+//                                     folded into W's columns)
+//   v += bias[n];  softplus if asked
+//   v += resid[m * ld_r + n]          (residual add; resid may alias y)
+struct EpiExtra {
+    const float *row_scale = nullptr;
+    const void *resid = nullptr;
+    int64_t ld_r = 0;
+};
+
+int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
+              const float *scale, const void *bias, void *y, int64_t ld_y, int64_t M,
+              int64_t N, int64_t K, int64_t n1, int64_t off1, int64_t n2, int64_t off2,
+              int epi, cudaStream_t st, const EpiExtra &ex = EpiExtra{});
+int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *w_split,
+            const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
+            int64_t n1, int64_t off1, int64_t n2, int64_t off2, int epi, cudaStream_t st,
+            bool *used, const EpiExtra &ex = EpiExtra{});
+int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const void *bias,
+                void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
+                int64_t d_inner, int64_t d_conv, cudaStream_t st);
+int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t ld_dl,
+               const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
+               int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
+               const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
+               int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, int64_t dt_rank,
+               cudaStream_t stream);
+
+// Dense or quantised linear y = x W^T (+ bias, + extras): the tensor-core
+// kernel where it applies, the CUDA-core kernel otherwise.  n1/off1/n2/off2
+// remap output columns (column n is written at n + off1 [n >= n1] + off2 [n >= n2]).
+int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, void *y,
+               int64_t ld_y, int64_t M, int64_t N, int64_t K, int epi, cudaStream_t st,
+               int64_t n1 = -1, int64_t off1 = 0, int64_t n2 = -1, int64_t off2 = 0,
+               const EpiExtra &ex = EpiExtra{});
+
+}  // namespace mb2

@@ -31,10 +31,17 @@ import torch.nn as nn
 from . import _lib, ops
 from ._lib import Block, LinearW, check, dtype_code, lib, stream_of
 from .quant import QuantizedLinear
+from .streaming import run_streamed
 
 
 class CPUMamba(nn.Module):
     """Mamba S6 block, state_dict-compatible with mamba_ssm.Mamba 2.3.x."""
+
+    # device buffers (input + output slice) forward_host keeps in flight
+    _host_slots = 3
+    # relative size of forward_host's first and last slices: the first slice's
+    # upload and the last one's download overlap no compute, so they are small
+    _host_edge = 0.5
 
     def __init__(self, d_model: int, d_state: int = 16, d_conv: int = 4,
                  expand: int = 2, dt_rank="auto",
@@ -147,17 +154,20 @@ class CPUMamba(nn.Module):
         return b
 
     # ---------------------------------------------------------------- forward
-    def _run(self, x: torch.Tensor, want_state: bool):
+    def _run(self, x: torch.Tensor, want_state: bool, out: torch.Tensor | None = None,
+             blk: Block | None = None):
         B, T, D = x.shape
         if D != self.d_model:
             raise RuntimeError(f"expected d_model={self.d_model}, got input of shape {tuple(x.shape)}")
         self._check_io(x, "forward")
         x = x.contiguous()
         keep = []
-        blk = self._descriptor(keep)
+        if blk is None:
+            blk = self._descriptor(keep)
         ws_bytes = lib().mb2_block_workspace_bytes(ctypes.byref(blk), B, T)
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
-        out = torch.empty_like(x)
+        if out is None:
+            out = torch.empty_like(x)
         h = conv = None
         if want_state:
             h = torch.empty(B, self.d_inner, self.d_state, device=x.device, dtype=torch.float32)
@@ -171,6 +181,38 @@ class CPUMamba(nn.Module):
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
         """hidden_states: (B, T, d_model) -> (B, T, d_model) (_mamba.py:204-265)."""
         return self._run(hidden_states, False)[0]
+
+    def forward_host(self, hidden_states: torch.Tensor, out: torch.Tensor | None = None,
+                     chunks: int | None = None) -> torch.Tensor:
+        """forward() for a batch held in host memory; returns a host tensor.
+
+        The batch is cut into ``chunks`` slices along B.  Each slice is copied
+        to the GPU on one stream, run through the block on one of two compute
+        streams and copied back on another, so PCIe transfers in both
+        directions overlap the block's kernels (pinned host memory is needed for the
+        copies to be asynchronous).  Batch rows are independent, so the result
+        is ``forward`` on the whole batch: bit for bit when the slices and the
+        whole batch use the same projection kernel (the tensor-core GEMM takes
+        256 rows and more, the CUDA-core GEMM fewer), else to within the two
+        kernels' rounding.  ``out`` (host, same shape and
+        dtype) receives the result if given.  Returns once the result is in
+        host memory."""
+        x = hidden_states
+        if x.is_cuda:
+            raise RuntimeError("forward_host: hidden_states must be a host tensor; use forward()")
+        B, T, D = x.shape
+        dev = self.conv1d.weight.device
+        if out is None:
+            out = torch.empty(x.shape, dtype=x.dtype, pin_memory=x.is_pinned())
+        if out.shape != x.shape or out.dtype != x.dtype or out.is_cuda:
+            raise RuntimeError("forward_host: out must be a host tensor shaped like the input")
+        x = x.contiguous()
+        n = chunks if chunks is not None else max(1, min(8, B * T // 4096))
+        keep = []
+        blk = self._descriptor(keep)
+        return run_streamed(x, out, dev,
+                            lambda xd, yd: self._run(xd, False, out=yd, blk=blk),
+                            n, self._host_slots, self._host_edge)
 
     def forward_with_final_state(self, hidden_states: torch.Tensor) -> tuple:
         """(y, {"h": (B, d_inner, d_state) f32, "conv_state": (B, d_inner, d_conv-1)})

@@ -109,6 +109,20 @@ def split_tf32(w: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def fold_norm(weight: torch.Tensor, norm_weight: torch.Tensor) -> torch.Tensor:
+    """weight * norm_weight[None, :] rounded to weight's dtype: an RMSNorm
+    weight folded into the columns of the projection that follows it."""
+    require_cuda(weight, norm_weight, what="fold_norm")
+    w = weight.detach().contiguous()
+    g = norm_weight.detach().to(w.dtype).contiguous()
+    if g.shape != (w.shape[-1],):
+        raise RuntimeError(f"fold_norm: norm weight {tuple(g.shape)} vs weight {tuple(w.shape)}")
+    out = torch.empty_like(w)
+    check(lib().mb2_fold_norm(dtype_code(w.dtype), ptr(w), ptr(g), ptr(out), w.shape[0],
+                              w.shape[-1], stream_of(w)), "fold_norm")
+    return out
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
            weight_split: Optional[torch.Tensor] = None, softplus: bool = False,
            out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -200,6 +200,30 @@ int mb2_block_step(const mb2_block *blk, const void *x, void *out, float *h,
                    void *conv_state, int64_t batch, void *workspace,
                    size_t workspace_bytes, mb2_stream_t stream);
 
+/* ---- residual stack: x <- x + block(RMSNorm(x)) per layer ----------------
+ * No single counterpart in the reference (it has no stack); each layer is
+ * CPUMamba.forward (_mamba.py:204-265) applied to torch.nn.RMSNorm(x), the
+ * composition a Mamba-130M-style model makes around the block. */
+
+/* out = w * norm_weight[col] (rows, cols), rounded to dtype: RMSNorm's weight
+ * folded into the columns of the in_proj weight that follows it. */
+int mb2_fold_norm(int dtype, const void *w, const void *norm_weight, void *out,
+                  int64_t rows, int64_t cols, mb2_stream_t stream);
+
+/* Bytes of workspace mb2_stack_forward needs. */
+size_t mb2_stack_workspace_bytes(const mb2_block *layers, int64_t n_layers,
+                                 int64_t batch, int64_t seqlen);
+
+/* n_layers pre-norm residual blocks over x (batch, seqlen, d_model), updated
+ * IN PLACE: per layer x = x + block(x / sqrt(mean(x^2) + eps) * g).  Each
+ * layer's in_proj weight (and its TF32 split for f32) must be the folded
+ * weight mb2_fold_norm(W_in, g) of that layer's norm weight g.  The 1/rms
+ * factor is applied in in_proj's epilogue and the residual add in out_proj's,
+ * so the normalised activations are never materialised. */
+int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, float eps, void *x,
+                      int64_t batch, int64_t seqlen, void *workspace,
+                      size_t workspace_bytes, mb2_stream_t stream);
+
 /* Size of the device array mb2_block_step_static uses as its workspace. */
 #define MB2_STEP_STATIC_SCRATCH_BYTES (8u << 20)
 

@@ -28,7 +28,7 @@ __all__ = [
     "block_forward_with_final_state", "block_step", "init_state",
     "quant_int8", "quant_int4", "quant_nf4", "dequant_int8", "dequant_int4",
     "dequant_nf4", "nf4_lut", "linear", "dequant", "load_ref_scan_op",
-    "make_block_params",
+    "make_block_params", "stack_forward",
 ]
 
 _HERE = pathlib.Path(__file__).resolve().parent
@@ -224,6 +224,20 @@ def block_forward(p, x, quant=None, scan_op=None):
         y = scan_op.selective_scan_cpu(*args) if scan_op is not None else selective_scan(*args)
         y = y.to(xc.dtype) * F.silu(z)                         # :263-264
         return linear(p, "out_proj", y, quant)                 # :265
+
+
+def stack_forward(layers, x, eps=1e-5, scan_op=None):
+    """A residual pre-norm stack, x <- x + block(RMSNorm(x)) per layer, in
+    float32: torch.nn.RMSNorm (F.rms_norm, weight g, ``eps``) composed with
+    CPUMamba.forward (_mamba.py:204-265).  The reference has no stack; this is
+    how a model built on it composes the block.  layers: [(block params, g)]."""
+    with torch.no_grad():
+        x = _cpu_f32(x)
+        for p, g in layers:
+            pf = {k: v.float() for k, v in p.items()}
+            xn = F.rms_norm(x, (x.shape[-1],), g.float(), eps)
+            x = x + block_forward(pf, xn, scan_op=scan_op)
+        return x
 
 
 def block_forward_with_final_state(p, x, quant=None):

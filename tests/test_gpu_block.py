@@ -135,3 +135,24 @@ def test_prefill_plus_steps_bf16_close():
             ys.append(y.unsqueeze(1))
     mean, _ = bf16_rel(y32, torch.cat(ys, 1))
     assert mean <= 2e-2, mean
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("chunks,pinned", [(None, True), (1, True), (3, False), (7, True)])
+def test_forward_host_equals_forward(dtype, chunks, pinned):
+    """Streaming host->GPU->host in batch slices gives exactly forward()'s result
+    (batch rows are independent), whatever the slice count."""
+    torch.manual_seed(3)
+    m = CPUMamba(d_model=64, d_state=16).cuda().to(dtype).eval()
+    x = torch.randn(7, 33, 64).to(dtype)
+    if pinned:
+        x = x.pin_memory()
+    with torch.no_grad():
+        ref = m(x.cuda()).cpu()
+        y = m.forward_host(x, chunks=chunks)
+    assert not y.is_cuda and y.shape == x.shape
+    assert torch.equal(y, ref)
+    out = torch.empty_like(x)
+    with torch.no_grad():
+        assert m.forward_host(x, out=out, chunks=chunks) is out
+    assert torch.equal(out, ref)

@@ -104,3 +104,24 @@ def test_backend_attributes_tolerated():
     block._assoc_chunk_T = 16
     block._force_time_loop = True
     assert set(block.state_dict()) == set(CPUMamba(64, 8).state_dict())
+
+
+def test_stack_state_dict_layout_and_slices():
+    """MambaStack keeps mamba_ssm's MixerModel names; forward_host's slices
+    cover the batch with small end slices."""
+    from cpu_mamba_b200 import MambaStack
+    from cpu_mamba_b200.streaming import slice_bounds
+    st = MambaStack(3, 64, d_state=16)
+    sd = st.state_dict()
+    assert sd["layers.2.norm.weight"].shape == (64,)
+    assert sd["layers.0.mixer.in_proj.weight"].shape == (256, 64)
+    assert len([k for k in sd if k.startswith("layers.1.")]) == 10
+    with pytest.raises(RuntimeError, match="CUDA"):
+        st(torch.randn(1, 4, 64))
+    for B, n in [(151, 6), (7, 7), (10, 9), (5, 2), (1, 1), (151, 3)]:
+        b = slice_bounds(B, n, 0.5)
+        assert len(b) == n and b[0][0] == 0 and b[-1][1] == B
+        assert all(lo < hi for lo, hi in b)
+        assert all(b[i][1] == b[i + 1][0] for i in range(n - 1))
+    b = slice_bounds(151, 6, 0.5)
+    assert b[0][1] - b[0][0] < b[2][1] - b[2][0]
