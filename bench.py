@@ -70,10 +70,8 @@ def peaks():
 
 # ----------------------------------------------------------------- helpers
 def dist_env():
-    ws = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    return ws, rank, local
+    from cpu_mamba_b200 import dist
+    return dist.env()
 
 
 class ClockSampler:
@@ -199,18 +197,15 @@ def run_ours(args, cfg):
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if ws > 1:
-        import torch.distributed as dist
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    from cpu_mamba_b200 import dist
+    dist.init("nccl", dev)
     dtype = torch.float32 if cfg["dtype"] == "f32" else torch.bfloat16
     stack_mode = cfg["mode"] == "stack"
     if stack_mode:
         m, R = make_stack(cfg)
         m = m.to(device=dev, dtype=dtype)
-        if cfg["batch"] % ws:
-            raise SystemExit(f"batch {cfg['batch']} does not split over {ws} ranks")
-        B = cfg["batch"] // ws                 # strong scaling: the batch is sharded
+        lo, hi = dist.shard(cfg["batch"], ws, rank)
+        B = hi - lo                            # strong scaling: the batch is sharded
     else:
         p, R = make_params(cfg, seed=0)
         m = CPUMamba(cfg["d_model"], d_state=cfg["d_state"], dt_rank=R).eval()
@@ -242,8 +237,7 @@ def run_ours(args, cfg):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
-    if ws > 1:
-        torch.distributed.barrier()
+    dist.barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(dev) as clk:
@@ -252,15 +246,11 @@ def run_ours(args, cfg):
             step(i)
         e1.record(stream)
         torch.cuda.synchronize(dev)
-    if ws > 1:
-        torch.distributed.barrier()
-    ms = e0.elapsed_time(e1)
-    if ws > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = t.item()
+    dist.barrier()
+    ms = dist.max_over_ranks(e0.elapsed_time(e1), dev)      # the slowest rank's time
     tokens_per_step = B * (1 if step_mode else T)
-    value = ws * tokens_per_step * args.steps / (ms / 1e3)
+    tokens_all = dist.sum_over_ranks(tokens_per_step, dev)  # whole job, all shards
+    value = tokens_all * args.steps / (ms / 1e3)
 
     # end to end through the public API from pinned host buffers
     host_in = torch.empty(in_shape, dtype=dtype, pin_memory=True)
@@ -275,8 +265,8 @@ def run_ours(args, cfg):
         torch.cuda.synchronize(dev)
         if i > 0:
             e2e_ms.append(a.elapsed_time(b))
-    e2e_t = statistics.median(e2e_ms)
-    e2e = {"value": ws * tokens_per_step / (e2e_t / 1e3), "unit": "tokens/s",
+    e2e_t = dist.max_over_ranks(statistics.median(e2e_ms), dev)
+    e2e = {"value": tokens_all / (e2e_t / 1e3), "unit": "tokens/s",
            "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": in_bytes}
 
     stages = profile_stages(m, xs[0], cfg, dtype, args.steps) if cfg["mode"] == "forward" else {}
@@ -295,7 +285,8 @@ def run_ours(args, cfg):
             "higher_is_better": True, "scaling": "strong" if stack_mode else "weak",
             "vs_baseline": None,
             "dtype": cfg["dtype"], "data": "synthetic (seeded; shapes of the configuration)",
-            "config": {"workload": cfg["workload"], "batch_per_gpu": B, "global_batch": B * ws,
+            "config": {"workload": cfg["workload"], "batch_per_gpu": B,
+                       "global_batch": int(tokens_all) // (1 if step_mode else T),
                        "seq_len": T if not step_mode else 1, "d_model": dm,
                        "d_inner": 2 * dm, "d_state": cfg["d_state"], "dt_rank": R,
                        "quant": cfg.get("quant"), "parallelism": f"batch-sharded x{ws}",
@@ -305,9 +296,7 @@ def run_ours(args, cfg):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
-    if ws > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+    dist.shutdown()
     return result
 
 
