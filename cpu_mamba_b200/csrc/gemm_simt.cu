@@ -127,23 +127,54 @@ gemm_simt_kernel(const GemmArgs a) {
 
     T *Y = static_cast<T *>(a.y);
     const T *bias = static_cast<const T *>(a.bias);
+    // optional terms, each behind one branch for the whole 8 x 4 block (a
+    // per-element test of the softplus would spread its inlined body over
+    // 32 instruction-cache lines)
+    if (a.row_scale) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int64_t m = m0 + ty * 8 + i;
+            const float rs = m < a.M ? a.row_scale[m] : 1.0f;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) acc[i][jj] *= rs;
+        }
+    }
+    if (bias) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const int64_t n = n0 + tx * 4 + jj;
+            const float bv = n < a.N ? io<T>::to_f(bias[n]) : 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i][jj] += bv;
+        }
+    }
+    if (a.epi == MB2_EPI_SOFTPLUS) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) acc[i][jj] = softplus_f(io<T>::round(acc[i][jj]));
+    }
+    if (a.resid) {
+        const T *R = static_cast<const T *>(a.resid);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int64_t m = m0 + ty * 8 + i;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int64_t n = n0 + tx * 4 + jj;
+                if (m < a.M && n < a.N) acc[i][jj] += io<T>::to_f(R[m * a.ld_r + n]);
+            }
+        }
+    }
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
         const int64_t n = n0 + tx * 4 + jj;
         if (n >= a.N) continue;
-        const float bv = bias ? io<T>::to_f(bias[n]) : 0.0f;
         const int64_t col = n + (n >= a.n1 ? a.off1 : 0) + (n >= a.n2 ? a.off2 : 0);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int64_t m = m0 + ty * 8 + i;
-            if (m < a.M) {
-                float v = acc[i][jj];
-                if (a.row_scale) v *= a.row_scale[m];
-                v += bv;
-                if (a.epi == MB2_EPI_SOFTPLUS) v = softplus_f(io<T>::round(v));
-                if (a.resid) v += io<T>::to_f(static_cast<const T *>(a.resid)[m * a.ld_r + n]);
-                Y[m * a.ld_y + col] = io<T>::from_f(v);
-            }
+            if (m < a.M) Y[m * a.ld_y + col] = io<T>::from_f(acc[i][jj]);
         }
     }
 }

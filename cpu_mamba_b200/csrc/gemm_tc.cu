@@ -253,8 +253,9 @@ __device__ __forceinline__ void bulk_wait_read0() {
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ----------------------------------------------------------------- kernel
-// EXTRA: the epilogue applies EpiExtra's row scale / residual (a separate
-// instantiation, so the plain projections carry none of its code)
+// EXTRA: the epilogue applies EpiExtra's row scale / residual and the softplus
+// epilogue (a separate instantiation, so the plain projections carry none of
+// its code: the kernel is sensitive to instruction-cache misses)
 template <int MODE, typename TO, bool EXTRA>
 __global__ void __launch_bounds__(Cfg<MODE>::WARPS * 32, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b0,
@@ -464,14 +465,26 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(ra[j]);
                 }
+                // each optional term behind ONE branch per column block: a
+                // per-element test would make every not-taken softplus body a
+                // jump into a new instruction-cache line (measured: 6.7 us of
+                // drain per tile instead of 0.8)
+                if (EXTRA && p.row_scale) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int64_t n = n0 + cb * 32 + j;
-                    if (EXTRA && p.row_scale) v[j] *= rscale;
-                    if (bias) v[j] += (n < p.N) ? io<TO>::to_f(bias[n]) : 0.0f;
+                    for (int j = 0; j < 32; ++j) v[j] *= rscale;
+                }
+                if (bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int64_t n = n0 + cb * 32 + j;
+                        v[j] += (n < p.N) ? io<TO>::to_f(bias[n]) : 0.0f;
+                    }
+                }
+                if (EXTRA && p.epi == MB2_EPI_SOFTPLUS) {
                     // dt_proj's softplus (_mamba.py:219-220) on the value the
                     // reference would have stored in its dtype
-                    if (p.epi == MB2_EPI_SOFTPLUS) v[j] = softplus_f(io<TO>::round(v[j]));
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = softplus_f(io<TO>::round(v[j]));
                 }
                 if (EXTRA && p.resid && row_ok) {
                     // residual add: this row's 32 columns, 16 bytes at a time
@@ -630,7 +643,7 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
     tc::Params p{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0,
                  ex.row_scale, ex.resid, ex.ld_r};
     *used = true;
-    const bool extra = ex.row_scale || ex.resid;
+    const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS;
     if (bf16)
         return extra ? launch_tc<tc::BF16, __nv_bfloat16, true>(ma, mb0, mb1, my, p, st)
                      : launch_tc<tc::BF16, __nv_bfloat16, false>(ma, mb0, mb1, my, p, st);
