@@ -186,7 +186,7 @@ def stack_roofline(cfg, batch, hbm_gbs, src, ms_per_step):
     per_layer = realistic_block_bytes(c) + 2 * batch * cfg["seqlen"] * cfg["d_model"] * es
     nbytes = per_layer * cfg["n_layers"]
     ach = nbytes / (ms_per_step / 1e3) / 1e9
-    return {"kernel": f"stack of {cfg['n_layers']} layers (6 launches each)", "bound": "hbm",
+    return {"kernel": f"stack of {cfg['n_layers']} layers (7 launches each)", "bound": "hbm",
             "achieved": ach, "peak": hbm_gbs, "unit": "GB/s", "frac": ach / hbm_gbs,
             "traffic": None, "bytes_per_step": nbytes, "peak_source": f"{src} HBM copy"}
 
@@ -275,10 +275,10 @@ def run_ours(args, cfg):
         hbm, bf16, bf16_s, src = peaks()
         if stack_mode:
             roof = stack_roofline(cfg, B, hbm, src, ms / args.steps)
-            launches_per_step = 6 * cfg["n_layers"]
+            launches_per_step = 7 * cfg["n_layers"]
         else:
             roof = roofline(stages, cfg, hbm, bf16, src, ms / args.steps)
-            launches_per_step = 5
+            launches_per_step = 6 if cfg["mode"] == "forward" else 5
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -312,12 +312,12 @@ def step_e2e(m, host_in, host_out, state, step_mode, dev):
             m.forward_host(host_in, out=host_out)
 
 
-STAGES = ("in_proj", "conv1d_silu", "x_proj", "scan", "out_proj")
+STAGES = ("in_proj", "conv1d_silu", "x_proj", "dt_proj", "scan", "out_proj")
 
 
 def profile_stages(m, x, cfg, dtype, steps):
     """Per-stage CUDA-event durations (same stream, averaged over up to 20 runs)
-    of the five launches of one forward, issued through the stage entry points."""
+    of the six launches of one forward, issued through the stage entry points."""
     from cpu_mamba_b200 import ops
     from cpu_mamba_b200.quant import QuantizedLinear
     if any(isinstance(getattr(m, n), QuantizedLinear) for n in ("in_proj", "x_proj", "dt_proj", "out_proj")):
@@ -327,7 +327,7 @@ def profile_stages(m, x, cfg, dtype, steps):
     di, S, R = m.d_inner, m.d_state, m.dt_rank
     stream = torch.cuda.current_stream(dev)
     split = {n: (m._tf32_split(n, getattr(m, n).weight) if dtype == torch.float32 else None)
-             for n in ("in_proj", "x_proj", "out_proj")}
+             for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
     x2 = x.reshape(B * T, dm)
     times = {k: [] for k in STAGES}
     # outputs allocated once: the timed region holds only the launches
@@ -346,11 +346,14 @@ def profile_stages(m, x, cfg, dtype, steps):
             ev[2].record(stream)
             ops.linear(xc, m.x_proj.weight, None, split["x_proj"], out=xdbl)
             ev[3].record(stream)
-            y = ops.scan_fused(xc, xdbl[:, :R], xdbl[:, R:R + S], xdbl[:, R + S:], xz[:, di:],
-                               m.dt_proj.weight, m.dt_proj.bias, m.A_log, m.D, B, T, out=xc)
+            ops.linear(xdbl[:, :R], m.dt_proj.weight, m.dt_proj.bias, split["dt_proj"],
+                       out=xz[:, :di])
             ev[4].record(stream)
-            ops.linear(y, m.out_proj.weight, None, split["out_proj"], out=out)
+            y = ops.scan_gated(xc, xz[:, :di], xdbl[:, R:R + S], xdbl[:, R + S:], xz[:, di:],
+                               m.A_log, m.D, B, T, out=xc)
             ev[5].record(stream)
+            ops.linear(y, m.out_proj.weight, None, split["out_proj"], out=out)
+            ev[6].record(stream)
         torch.cuda.synchronize(dev)
         if it > 0:
             for i, k in enumerate(times):
@@ -400,7 +403,8 @@ def roofline(stages, cfg, hbm_gbs, bf16_tflops, src, ms_per_step):
              "out_proj": 2 * N * di * dm}
     # algorithmic bytes of the HBM-bound stages (each tensor read / written once)
     nbytes = {"conv1d_silu": N * di * es * 2,
-              "scan": N * es * (3 * di + R + 2 * S)}      # x, z, dt_low, B, C in; y out
+              "dt_proj": N * es * (R + di),                # dt_low in, dt out
+              "scan": N * es * (4 * di + 2 * S)}           # x, dt, z, B, C in; y out
     top = max(stages, key=stages.get)
     t = stages[top] / 1e3
     tpt = TRAFFIC_PER_TOKEN.get((cfg["dtype"], dm, S, top))

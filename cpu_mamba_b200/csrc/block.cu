@@ -2,15 +2,18 @@
 // the forward_with_final_state state outputs (:165-202) and the single-token
 // step (:103-163), plus the linear-layer entry points.
 //
-// Forward pipeline (5 launches, caller-provided workspace, no allocation):
+// Forward pipeline (6 launches, caller-provided workspace, no allocation):
 //   1. in_proj            x (N, dm)          -> xz (N, 2di)
 //   2. conv1d + SiLU      xz[:, :di]         -> xc (N, di)   [+ conv tail]
 //   3. x_proj             xc                 -> xdbl (N, ldx): dt_low | B | C, each
 //                                               segment on an 8-element boundary
-//   4. fused scan         xc, xdbl, xz[:, di:] -> y (N, di)  [+ h_last]
-//      (dt_proj + softplus + exp(dt A) + recurrence + D skip + cast + SiLU(z)
-//       gate; y overwrites xc in place)
-//   5. out_proj           y                  -> out (N, dm)
+//   4. dt_proj            xdbl[:, :R]        -> over xz[:, :di] (the conv's
+//                                               input, dead by now)
+//   5. gated scan         xc, dt_proj out, xdbl, xz[:, di:] -> y (N, di)
+//      [+ h_last] (softplus + exp(dt A) + recurrence + D skip + cast + SiLU(z)
+//       gate; y overwrites xc in place).  Where the dt GEMM cannot run on the tensor cores, steps 4
+//       and 5 are one fused scan that also computes dt.
+//   6. out_proj           y                  -> out (N, dm)
 #include "internal.cuh"
 
 namespace mb2 {
@@ -168,10 +171,25 @@ static int block_pipeline(const mb2_block &b, const Layout &l, const void *x, vo
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, MB2_EPI_NONE,
                            st, R, l.RB - R, R + S, l.RC - l.RB - S));
-    MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
-                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
-                       dt_weight(b), b.dt_proj.bias, b.A_log, b.D, nullptr, h_last, xc, di, batch,
-                       seqlen, di, S, R, st));
+    // dt_proj (_mamba.py:219) on the tensor cores, bias in the epilogue,
+    // written over the x half of xz (dead once the conv has run); the gated
+    // scan applies the softplus (:220) as it stages the rows.  Where that GEMM
+    // does not apply (a quantised or unsplit fp32 dt_proj, fewer than 256
+    // rows) the fused scan computes dt itself from W_dt's rows in registers.
+    bool dt_done = false;
+    if (N > 0 && b.dt_proj.scheme == MB2_Q_NONE)
+        MB2_TRY(gemm_tc(b.dtype, xdbl, l.ldx, b.dt_proj.weight, b.dt_proj.weight_split,
+                        b.dt_proj.bias, xz, 2 * di, N, di, R, di, 0, di, 0, MB2_EPI_NONE, st,
+                        &dt_done));
+    if (dt_done)
+        MB2_TRY(scan_gated(b.dtype, xc, di, xz, 2 * di, (char *)xdbl + l.RB * es, l.ldx,
+                           (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log,
+                           b.D, nullptr, h_last, xc, di, batch, seqlen, di, S, st));
+    else
+        MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
+                           (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
+                           dt_weight(b), b.dt_proj.bias, b.A_log, b.D, nullptr, h_last, xc, di,
+                           batch, seqlen, di, S, R, st));
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, N, l.dm, di, MB2_EPI_NONE, st,
                            -1, 0, -1, 0, out_ex));

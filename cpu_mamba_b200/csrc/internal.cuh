@@ -37,6 +37,12 @@ int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t
                int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, int64_t dt_rank,
                cudaStream_t stream);
 
+int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t ld_dt,
+               const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
+               int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
+               void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
+               int64_t d_state, cudaStream_t stream);
+
 // Dense or quantised linear y = x W^T (+ bias, + extras): the tensor-core
 // kernel where it applies, the CUDA-core kernel otherwise.  n1/off1/n2/off2
 // remap output columns (column n is written at n + off1 [n >= n1] + off2 [n >= n2]).

@@ -27,26 +27,30 @@
 //            channel's lanes, into a shared-memory dt tile),
 //            A = -exp(A_log) (:222), output cast to the activation dtype and
 //            multiplied by SiLU(z) (:263-264).
+//   GATED -- FUSED with dt_proj's output given: the block's forward runs the
+//            dt_proj GEMM on the tensor cores (bias in its epilogue); the scan
+//            stages its rows like x and z and applies the softplus once per
+//            token-channel per chunk into the shared-memory dt tile.
 // exp(dt*A) is evaluated as 2^(dt * (A log2 e)) with ex2.approx.ftz.
-#include "common.cuh"
+#include "internal.cuh"
 
 namespace mb2 {
 
 constexpr int SCAN_THREADS = 128;  // threads per CTA
 constexpr int SCAN_TC = 16;        // timesteps per staged chunk
 
-enum ScanMode { PLAIN = 0, FUSED = 1 };
+enum ScanMode { PLAIN = 0, FUSED = 1, GATED = 2 };
 
 struct ScanParams {
     const void *x;  int64_t ld_x;    // (N, ld_x)  x / conv output
-    const void *dt; int64_t ld_dt;   // PLAIN: (N, ld_dt) dt
-    const void *z;  int64_t ld_z;    // FUSED: (N, ld_z) gate input
+    const void *dt; int64_t ld_dt;   // PLAIN, GATED: (N, ld_dt) dt
+    const void *z;  int64_t ld_z;    // FUSED, GATED: (N, ld_z) gate input
     const void *bm; int64_t ld_b;    // rows of B
     const void *cm; int64_t ld_c;    // rows of C
     const void *dl; int64_t ld_dl;   // FUSED: rows of dt_low (R values)
     const void *w_dt; const void *b_dt;  // FUSED: (di, R), (di)
-    const void *A;                   // PLAIN: A fp32; FUSED: A_log in T
-    const void *D;                   // (di) fp32 (PLAIN) / T (FUSED), may be null
+    const void *A;                   // PLAIN: A fp32; FUSED, GATED: A_log in T
+    const void *D;                   // (di) fp32 (PLAIN) / T (FUSED, GATED), may be null
     const float *h0; float *h_last;  // (batch, di, S) or null
     void *y;        int64_t ld_y;
     int64_t batch, seqlen, d_inner;
@@ -54,7 +58,7 @@ struct ScanParams {
     unsigned vec16;                  // bit i: array i rows are 16-byte aligned
 };
 
-enum { ARR_X = 1, ARR_D2 = 2, ARR_B = 4, ARR_C = 8, ARR_DL = 16 };
+enum { ARR_X = 1, ARR_D2 = 2, ARR_B = 4, ARR_C = 8, ARR_DL = 16, ARR_Z = 32 };
 
 template <typename T> __host__ __device__ constexpr int epw() { return 4 / (int)sizeof(T); }
 
@@ -198,12 +202,14 @@ struct Geo {
     static constexpr int NX = SCAN_TC * CH;
     static constexpr int NBC = SCAN_TC * SPP;
     static constexpr int NDL = MODE == FUSED ? SCAN_TC * RP : 0;
-    static constexpr int ELEMS = 2 * NX + 2 * NBC + NDL;     // x | dt-or-z | B | C | dt_low
+    static constexpr int NZ = MODE == GATED ? NX : 0;
+    // x | dt (PLAIN, GATED) or z (FUSED) | B | C | dt_low (FUSED) or z (GATED)
+    static constexpr int ELEMS = 2 * NX + 2 * NBC + NDL + NZ;
     // after the two stages: per-lane partial y (SCAN_TC x 128 floats) and, in
     // FUSED mode, the chunk's dt tile (SCAN_TC x CH floats)
     static constexpr size_t BYTES = 2 * (size_t)ELEMS * sizeof(T) +
                                     (size_t)SCAN_TC * SCAN_THREADS * sizeof(float) +
-                                    (MODE == FUSED ? (size_t)SCAN_TC * CH * sizeof(float) : 0);
+                                    (MODE != PLAIN ? (size_t)SCAN_TC * CH * sizeof(float) : 0);
 };
 
 template <typename T, int SPL, int L, int MODE, int RL>
@@ -214,7 +220,7 @@ scan_kernel(const ScanParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T *stage0 = reinterpret_cast<T *>(smem_raw);
     float *ys = reinterpret_cast<float *>(smem_raw + 2 * (size_t)Gm::ELEMS * sizeof(T));
-    float *dts = ys + SCAN_TC * SCAN_THREADS;   // FUSED: dt of the chunk, [tt][channel]
+    float *dts = ys + SCAN_TC * SCAN_THREADS;   // FUSED, GATED: dt of the chunk, [tt][channel]
 
     const int tid = threadIdx.x;
     const int c = tid / L;          // channel within CTA
@@ -237,7 +243,7 @@ scan_kernel(const ScanParams p) {
         for (int e = 0; e < 2; ++e) {
             const int s = j * SPL + 2 * q + e;
             if (active && s < S) {
-                if (MODE == FUSED)
+                if (MODE != PLAIN)
                     a[e] = -expf(io<T>::to_f(static_cast<const T *>(p.A)[d * S + s]));
                 else
                     a[e] = static_cast<const float *>(p.A)[d * S + s];
@@ -274,6 +280,7 @@ scan_kernel(const ScanParams p) {
     const T *bg = static_cast<const T *>(p.bm) + row_base * p.ld_b;
     const T *cg = static_cast<const T *>(p.cm) + row_base * p.ld_c;
     const T *dlg = MODE == FUSED ? static_cast<const T *>(p.dl) + row_base * p.ld_dl : nullptr;
+    const T *zg = MODE == GATED ? static_cast<const T *>(p.z) + row_base * p.ld_z + d0 : nullptr;
 
     auto issue = [&](int chunk) {
         T *st = stage0 + (chunk & 1) * Gm::ELEMS;
@@ -290,6 +297,9 @@ scan_kernel(const ScanParams p) {
         if (MODE == FUSED)
             stage_rows<T, SCAN_TC, Gm::RP>(st + 2 * Gm::NX + 2 * Gm::NBC, dlg + t0 * p.ld_dl,
                                            p.ld_dl, rv, p.dt_rank, p.vec16 & ARR_DL, tid);
+        if (MODE == GATED)
+            stage_rows<T, SCAN_TC, CH>(st + 2 * Gm::NX + 2 * Gm::NBC, zg + t0 * p.ld_z, p.ld_z,
+                                       rv, ch_valid, p.vec16 & ARR_Z, tid);
     };
 
     // read-out geometry: thread owns column cc of rows rr0, rr0 + 128/CH, ...
@@ -298,7 +308,7 @@ scan_kernel(const ScanParams p) {
     const bool col_ok = cc < ch_valid;
     float d_skip = 0.0f;
     if (col_ok && p.D)
-        d_skip = MODE == FUSED ? io<T>::to_f(static_cast<const T *>(p.D)[d0 + cc])
+        d_skip = MODE != PLAIN ? io<T>::to_f(static_cast<const T *>(p.D)[d0 + cc])
                                : static_cast<const float *>(p.D)[d0 + cc];
     T *yg = static_cast<T *>(p.y) + row_base * p.ld_y + d0 + cc;
 
@@ -356,10 +366,18 @@ scan_kernel(const ScanParams p) {
             }
             __syncwarp();   // a channel's L lanes share one warp
         }
+        if (MODE == GATED) {
+            // ---- dt = softplus(dt_proj output) once per token-channel: lane j
+            // takes steps j, j + L, ... (rows >= tn are zero-filled, unused)
+#pragma unroll
+            for (int tt = j; tt < SCAN_TC; tt += L)
+                dts[tt * CH + c] = io<T>::round(softplus_fast(io<T>::to_f(d2s[tt * CH])));
+            __syncwarp();   // a channel's L lanes share one warp
+        }
         // ---- recurrence (tn is CTA-uniform)
 #pragma unroll 2
         for (int tt = 0; tt < tn; ++tt) {
-            const float dtv = MODE == FUSED ? dts[tt * CH + c] : io<T>::to_f(d2s[tt * CH]);
+            const float dtv = MODE != PLAIN ? dts[tt * CH + c] : io<T>::to_f(d2s[tt * CH]);
             const float dtx = dtv * io<T>::to_f(xs[tt * CH]);
             const f2 dt2 = pk(dtv, dtv), dtx2 = pk(dtx, dtx);
             float bv[SPL], cv[SPL];
@@ -383,7 +401,7 @@ scan_kernel(const ScanParams p) {
         __syncthreads();
         // ---- read-out: sum lane partials, D skip, (FUSED) cast + SiLU(z) gate
         const T *xrow = st + cc;
-        const T *zrow = st + Gm::NX + cc;
+        const T *zrow = st + (MODE == FUSED ? Gm::NX : 2 * Gm::NX + 2 * Gm::NBC) + cc;
         if (col_ok) {
 #pragma unroll 4
             for (int tt = rr0; tt < tn; tt += RSTEP) {
@@ -391,7 +409,7 @@ scan_kernel(const ScanParams p) {
 #pragma unroll
                 for (int l = 0; l < L; ++l) yv += ys[tt * SCAN_THREADS + cc * L + l];
                 float out = yv + d_skip * io<T>::to_f(xrow[tt * CH]);
-                if (MODE == FUSED)
+                if (MODE != PLAIN)
                     out = io<T>::round(out) * io<T>::round(silu_f(io<T>::to_f(zrow[tt * CH])));
                 yg[((int64_t)ch * SCAN_TC + tt) * p.ld_y] = io<T>::from_f(out);
             }
@@ -433,6 +451,7 @@ static int launch_scan(ScanParams p, cudaStream_t st) {
     if (ch16 && rows16(p.x, p.ld_x, es)) p.vec16 |= ARR_X;
     if (MODE == FUSED ? (ch16 && rows16(p.z, p.ld_z, es)) : (ch16 && rows16(p.dt, p.ld_dt, es)))
         p.vec16 |= ARR_D2;
+    if (MODE == GATED && ch16 && rows16(p.z, p.ld_z, es)) p.vec16 |= ARR_Z;
     if (rows16(p.bm, p.ld_b, es)) p.vec16 |= ARR_B;
     if (rows16(p.cm, p.ld_c, es)) p.vec16 |= ARR_C;
     if (MODE == FUSED && rows16(p.dl, p.ld_dl, es)) p.vec16 |= ARR_DL;
@@ -444,8 +463,8 @@ static int launch_scan(ScanParams p, cudaStream_t st) {
 // (SPL, L) by d_state; RL (dt_rank slice per lane, FUSED only) by dt_rank.
 template <typename T, int MODE, int SPL, int L>
 static int dispatch_rl(const ScanParams &p, cudaStream_t st) {
-    if constexpr (MODE == PLAIN) {
-        return launch_scan<T, SPL, L, PLAIN, 1>(p, st);
+    if constexpr (MODE != FUSED) {
+        return launch_scan<T, SPL, L, MODE, 1>(p, st);
     } else {
         const int per = (p.dt_rank + L - 1) / L;
         if (per <= 8) return launch_scan<T, SPL, L, FUSED, 8>(p, st);
@@ -519,6 +538,44 @@ int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t
     return dispatch_scan<__nv_bfloat16, FUSED>(p, stream);
 }
 
+// The block forward's scan stage given dt_proj's output (dt_low W_dt^T + b_dt,
+// from the tensor-core GEMM): dt = softplus(.), A = -exp(A_log), recurrence,
+// D skip, cast and SiLU(z) gate.
+int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t ld_dt,
+               const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
+               int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
+               void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
+               int64_t d_state, cudaStream_t stream) {
+    MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "scan: bad dtype");
+    MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0, MB2_ERR_SHAPE, "scan: bad sizes");
+    MB2_REQUIRE(d_state >= 1 && d_state <= 256, MB2_ERR_SHAPE,
+                "d_state > 256 not supported (got %lld)", (long long)d_state);
+    MB2_REQUIRE(batch < 65536, MB2_ERR_SHAPE, "scan: batch too large");
+    if (batch == 0 || d_inner == 0) return MB2_OK;
+    MB2_REQUIRE(A_log && (seqlen == 0 || (xc && dt && bm && cm && z && y)), MB2_ERR_ARG,
+                "scan: null pointer");
+    if (dtype == MB2_BF16)
+        MB2_REQUIRE(d_inner % 2 == 0, MB2_ERR_ALIGN, "scan(bf16): d_inner must be even");
+    MB2_TRY(check_rows(dtype, xc, ld_xc, d_inner, "x"));
+    MB2_TRY(check_rows(dtype, dt, ld_dt, d_inner, "dt"));
+    MB2_TRY(check_rows(dtype, z, ld_z, d_inner, "z"));
+    MB2_TRY(check_rows(dtype, bm, ld_b, d_state, "B"));
+    MB2_TRY(check_rows(dtype, cm, ld_c, d_state, "C"));
+    MB2_REQUIRE(ld_y >= d_inner, MB2_ERR_SHAPE, "scan: leading dimension of y too small");
+    ScanParams p{};
+    p.x = xc; p.ld_x = ld_xc;
+    p.dt = dt; p.ld_dt = ld_dt;
+    p.z = z; p.ld_z = ld_z;
+    p.bm = bm; p.ld_b = ld_b;
+    p.cm = cm; p.ld_c = ld_c;
+    p.A = A_log; p.D = D; p.h0 = h0; p.h_last = h_last;
+    p.y = y; p.ld_y = ld_y;
+    p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
+    p.d_state = (int)d_state;
+    if (dtype == MB2_F32) return dispatch_scan<float, GATED>(p, stream);
+    return dispatch_scan<__nv_bfloat16, GATED>(p, stream);
+}
+
 }  // namespace mb2
 
 using namespace mb2;
@@ -559,4 +616,14 @@ extern "C" int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc, const vo
     return scan_fused(dtype, xc, ld_xc, dt_low, ld_dl, B, ld_b, C, ld_c, z, ld_z, w_dt, b_dt,
                       A_log, D, h0, h_last, y, ld_y, batch, seqlen, d_inner, d_state, dt_rank,
                       (cudaStream_t)stream);
+}
+
+extern "C" int mb2_scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt,
+                              int64_t ld_dt, const void *B, int64_t ld_b, const void *C,
+                              int64_t ld_c, const void *z, int64_t ld_z, const void *A_log,
+                              const void *D, const float *h0, float *h_last, void *y,
+                              int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
+                              int64_t d_state, mb2_stream_t stream) {
+    return scan_gated(dtype, xc, ld_xc, dt, ld_dt, B, ld_b, C, ld_c, z, ld_z, A_log, D, h0,
+                      h_last, y, ld_y, batch, seqlen, d_inner, d_state, (cudaStream_t)stream);
 }

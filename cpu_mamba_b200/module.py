@@ -128,7 +128,7 @@ class CPUMamba(nn.Module):
                 keep.append(w)
             d.weight = w.data_ptr()
             d.scheme = 0
-            if w.dtype == torch.float32 and name != "dt_proj":
+            if w.dtype == torch.float32:
                 d.weight_split = self._tf32_split(name, w).data_ptr()
         else:
             raise TypeError(f"{name} must be nn.Linear or QuantizedLinear, got {type(mod)}")

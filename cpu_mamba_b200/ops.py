@@ -98,6 +98,26 @@ def scan_fused(xc, dt_low, Bm, Cm, z, w_dt, b_dt, A_log, D, batch, seqlen, h0=No
     return (y, h_last) if return_last_state else y
 
 
+def scan_gated(xc, dt, Bm, Cm, z, A_log, D, batch, seqlen, h0=None, return_last_state=False,
+               out=None):
+    """scan_fused given dt_proj's output dt = linear(dt_low, W_dt, b_dt) (before
+    the softplus, which this kernel applies): A = -exp(A_log), selective scan,
+    D skip, cast and SiLU(z) gate.
+    xc, dt, z: (N, d_inner) row views; Bm, Cm: (N, d_state) row views."""
+    require_cuda(xc, dt, Bm, Cm, z, A_log, what="scan_gated")
+    di, S = A_log.shape
+    y = out if out is not None else torch.empty(batch * seqlen, di, device=xc.device, dtype=xc.dtype)
+    h_last = (torch.empty(batch, di, S, device=xc.device, dtype=torch.float32)
+              if return_last_state else None)
+    A_log = A_log.contiguous()
+    h0 = None if h0 is None else h0.contiguous()
+    check(lib().mb2_scan_gated(dtype_code(xc.dtype), ptr(xc), xc.stride(0), ptr(dt), dt.stride(0),
+                               ptr(Bm), Bm.stride(0), ptr(Cm), Cm.stride(0), ptr(z), z.stride(0),
+                               ptr(A_log), ptr(D), ptr(h0), ptr(h_last), ptr(y), y.stride(0),
+                               batch, seqlen, di, S, stream_of(xc)), "scan_gated")
+    return (y, h_last) if return_last_state else y
+
+
 def split_tf32(w: torch.Tensor) -> torch.Tensor:
     """(2, *w.shape) float32: TF32 hi and lo halves of w (a derived cache)."""
     require_cuda(w, what="split_tf32")

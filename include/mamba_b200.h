@@ -112,6 +112,17 @@ int mb2_scan_fused(int dtype, const void *xc, int64_t ld_xc,
                    int64_t seqlen, int64_t d_inner, int64_t d_state,
                    int64_t dt_rank, mb2_stream_t stream);
 
+/* The same stage given dt_proj's output (dt_low W_dt^T + b_dt, e.g. from
+ * mb2_linear, which the block forward runs on the tensor cores): the kernel
+ * applies the softplus.  dt_pre (N, ld_dt) in the activation dtype; the other
+ * arguments as mb2_scan_fused.  y may alias xc. */
+int mb2_scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt_pre,
+                   int64_t ld_dt, const void *B, int64_t ld_b, const void *C,
+                   int64_t ld_c, const void *z, int64_t ld_z, const void *A_log,
+                   const void *D, const float *h0, float *h_last, void *y,
+                   int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
+                   int64_t d_state, mb2_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Linear layer y = x W^T (+ bias): nn.Linear as used by in_proj, x_proj,
  * dt_proj, out_proj (_mamba.py:67,74-75,84).
@@ -184,7 +195,10 @@ size_t mb2_block_workspace_bytes(const mb2_block *blk, int64_t batch,
 
 /* CPUMamba.forward (_mamba.py:204-265); with h_last / conv_tail non-NULL also
  * the state of forward_with_final_state (:165-202) from the same pass.
- *   x, out: (batch, seqlen, d_model) contiguous in dtype. */
+ *   x, out: (batch, seqlen, d_model) contiguous in dtype.
+ * dt_proj runs as a tensor-core GEMM when it can (dense weight; F32 also
+ * needs its weight_split; batch*seqlen >= 256), otherwise inside the scan
+ * kernel from W_dt's rows. */
 int mb2_block_forward(const mb2_block *blk, const void *x, void *out,
                       int64_t batch, int64_t seqlen, float *h_last,
                       void *conv_tail, void *workspace, size_t workspace_bytes,

@@ -149,3 +149,38 @@ def test_gated_scan_ragged_lengths_state(T):
                           p["dt_proj.weight"].cuda(), p["dt_proj.bias"].cuda(), p["A_log"].cuda(),
                           p["D"].cuda(), b, T, return_last_state=True)
     assert (h.cpu() - h_ref).abs().max().item() <= TOL
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("b,T,S", [(3, 45, 16), (4, 100, 24), (2, 17, 8)])
+def test_scan_with_given_dt_matches_composition(dtype, b, T, S):
+    """The block forward's split form: dt_proj from the projection kernel
+    (tensor cores from 256 rows, with the TF32 halves in fp32), then the scan
+    applying the softplus to it == the reference composition."""
+    p = oracle.make_block_params(96, S, seed=21 + T, dtype=dtype)
+    di = p["A_log"].shape[0]
+    R = p["dt_proj.weight"].shape[1]
+    g = torch.Generator().manual_seed(22 + b)
+    xc = torch.nn.functional.silu(torch.randn(b * T, di, generator=g)).to(dtype)
+    xdbl = (torch.randn(b * T, R + 2 * S, generator=g) * 0.5).to(dtype)
+    z = torch.randn(b * T, di, generator=g).to(dtype)
+    dt_ref = torch.nn.functional.softplus(
+        torch.nn.functional.linear(xdbl[:, :R], p["dt_proj.weight"], p["dt_proj.bias"]))
+    A = -torch.exp(p["A_log"].float())
+    y_scan, h_ref = oracle.selective_scan(
+        xc.float().view(b, T, di), dt_ref.float().view(b, T, di), A,
+        xdbl[:, R:R + S].float().view(b, T, S), xdbl[:, R + S:].float().view(b, T, S),
+        p["D"].float(), return_last_state=True)
+    y_ref = y_scan.view(b * T, di).to(dtype) * torch.nn.functional.silu(z)
+    xd = xdbl.cuda()
+    w_dt = p["dt_proj.weight"].cuda()
+    split = ops.split_tf32(w_dt) if dtype == torch.float32 else None
+    dt = ops.linear(xd[:, :R], w_dt, p["dt_proj.bias"].cuda(), split)
+    y, h = ops.scan_gated(xc.cuda(), dt, xd[:, R:R + S], xd[:, R + S:], z.cuda(),
+                          p["A_log"].cuda(), p["D"].cuda(), b, T, return_last_state=True)
+    assert (h.cpu() - h_ref).abs().max().item() <= TOL
+    if dtype == torch.float32:
+        assert (y.cpu() - y_ref).abs().max().item() <= TOL
+    else:
+        rel = (y.cpu().float() - y_ref.float()).abs() / (y_ref.float().abs().clamp(min=1e-3) + 1e-6)
+        assert rel.mean().item() <= 2e-2
