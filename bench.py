@@ -227,10 +227,12 @@ def run_ours(args, cfg):
             prompt = torch.randn(B, T, dm, generator=g, device=dev).to(dtype)
             _, state = m.forward_with_final_state(prompt)
 
+    graph = m.capture_step(state, xs[0]) if step_mode else None   # decode: one graph per step
+
     def step(i):
         with torch.no_grad():
             if step_mode:
-                return m.forward_step(xs[i % nbuf], state)[0]
+                return graph(xs[i % nbuf])
             return m(xs[i % nbuf])
 
     stream = torch.cuda.current_stream(dev)
@@ -260,7 +262,7 @@ def run_ours(args, cfg):
     for i in range(max(3, min(args.steps, 10)) + 1):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        step_e2e(m, host_in, host_out, state, step_mode, dev)
+        step_e2e(m, host_in, host_out, graph, step_mode, dev)
         b.record(stream)
         torch.cuda.synchronize(dev)
         if i > 0:
@@ -291,6 +293,7 @@ def run_ours(args, cfg):
                        "d_inner": 2 * dm, "d_state": cfg["d_state"], "dt_rank": R,
                        "quant": cfg.get("quant"), "parallelism": f"batch-sharded x{ws}",
                        "layers": cfg.get("n_layers", 1),
+                       "decode": "forward_step captured as one CUDA graph" if step_mode else None,
                        "l2": f"inputs rotated over {nbuf} buffers ({nbuf * in_bytes / 2**20:.0f} MB > L2)"},
             "roofline": roof, "stages_ms": stages, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
@@ -300,13 +303,15 @@ def run_ours(args, cfg):
     return result
 
 
-def step_e2e(m, host_in, host_out, state, step_mode, dev):
+def step_e2e(m, host_in, host_out, graph, step_mode, dev):
     """One step through the public API from pinned host memory to pinned host
     memory.  A forward streams batch slices with the copies overlapping the
-    kernels (CPUMamba.forward_host); a decode step is too small to split."""
+    kernels (CPUMamba.forward_host); a decode step copies the token in,
+    replays the captured step (CPUMamba.capture_step) and copies the output
+    out."""
     with torch.no_grad():
         if step_mode:
-            y = m.forward_step(host_in.to(dev, non_blocking=True), state)[0]
+            y = graph(host_in.to(dev, non_blocking=True))
             host_out.copy_(y, non_blocking=True)
         else:
             m.forward_host(host_in, out=host_out)

@@ -40,11 +40,15 @@ struct Layout {
     int64_t RB, RC, ldx;   // x_dbl segment offsets and row length
     size_t es;
     size_t off_xz, off_xc, off_xdbl, total;   // y reuses the xc buffer
+    size_t off_part, part_bytes;              // step: split-K partial sums
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
-static Layout make_layout(const mb2_block *b, int64_t rows) {
+// Workspace of a forward over `rows` tokens, or (step) of a decode step: the
+// step's projections have few rows and split K, so it adds room for four
+// splits' partial sums of its widest projection.
+static Layout make_layout(const mb2_block *b, int64_t rows, bool step = false) {
     Layout l{};
     l.N = rows;
     l.di = b->d_inner; l.dm = b->d_model; l.S = b->d_state; l.R = b->dt_rank; l.K = b->d_conv;
@@ -56,6 +60,14 @@ static Layout make_layout(const mb2_block *b, int64_t rows) {
     l.off_xz = off; off = align256(off + (size_t)rows * 2 * l.di * l.es);
     l.off_xc = off; off = align256(off + (size_t)rows * l.di * l.es);
     l.off_xdbl = off; off = align256(off + (size_t)rows * l.ldx * l.es);
+    l.off_part = off;
+    l.part_bytes = 0;
+    if (step) {
+        int64_t wide = 2 * l.di > l.dm ? 2 * l.di : l.dm;
+        wide = wide > l.R + 2 * l.S ? wide : l.R + 2 * l.S;
+        l.part_bytes = (size_t)rows * wide * sizeof(float) * 4;
+        off = align256(off + l.part_bytes);
+    }
     l.total = off;
     return l;
 }
@@ -219,7 +231,7 @@ extern "C" int mb2_block_forward(const mb2_block *blk, const void *x, void *out,
 
 extern "C" size_t mb2_step_workspace_bytes(const mb2_block *blk, int64_t batch) {
     if (!blk || batch < 0) return 0;
-    return make_layout(blk, batch).total;
+    return make_layout(blk, batch, true).total;
 }
 
 extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, float *h,
@@ -229,7 +241,7 @@ extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, fl
     MB2_REQUIRE(batch >= 0, MB2_ERR_SHAPE, "step: negative batch");
     const mb2_block &b = *blk;
     cudaStream_t st = (cudaStream_t)stream;
-    const Layout l = make_layout(blk, batch);
+    const Layout l = make_layout(blk, batch, true);
     MB2_REQUIRE(workspace_bytes >= l.total, MB2_ERR_WORKSPACE,
                 "step: workspace %zu < required %zu", workspace_bytes, l.total);
     if (batch == 0) return MB2_OK;
@@ -238,8 +250,11 @@ extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, fl
     void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
     const int64_t di = l.di, S = l.S, R = l.R;
     const size_t es = l.es;
+    EpiExtra sk;                    // split-K scratch for the few-row projections
+    sk.scratch = reinterpret_cast<float *>(ws + l.off_part);
+    sk.scratch_bytes = l.part_bytes;
     MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, batch, 2 * di, l.dm, MB2_EPI_NONE,
-                       st));
+                       st, -1, 0, -1, 0, sk));
     if (b.dtype == MB2_F32)
         MB2_TRY(launch_conv_step<float>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b, conv_state,
                                         xc, batch, di, st));
@@ -247,13 +262,16 @@ extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, fl
         MB2_TRY(launch_conv_step<__nv_bfloat16>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b,
                                                 conv_state, xc, batch, di, st));
     MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, batch, R + 2 * S, di, MB2_EPI_NONE,
-                       st, R, l.RB - R, R + S, l.RC - l.RB - S));
-    // one timestep of the fused scan, h read and written in place
-    MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
-                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
-                       dt_weight(b), b.dt_proj.bias, b.A_log, b.D, h, h, xc, di, batch, 1, di, S,
-                       R, st));
-    return linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, batch, l.dm, di, MB2_EPI_NONE, st);
+                       st, R, l.RB - R, R + S, l.RC - l.RB - S, sk));
+    // dt_proj (bias in the epilogue) over the x half of xz, dead after the conv
+    MB2_TRY(linear_any(b.dtype, b.dt_proj, xdbl, l.ldx, xz, 2 * di, batch, di, R, MB2_EPI_NONE,
+                       st, -1, 0, -1, 0, sk));
+    // one timestep: softplus, exp(dt A), h updated in place, y = C.h + D x, gate
+    MB2_TRY(scan_step(b.dtype, xc, di, xz, 2 * di, (char *)xdbl + l.RB * es,
+                      (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log, b.D,
+                      h, xc, di, batch, di, S, st));
+    return linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, batch, l.dm, di, MB2_EPI_NONE, st,
+                      -1, 0, -1, 0, sk);
 }
 
 // ------------------------------------------------------------------ stack ---

@@ -17,6 +17,10 @@ struct EpiExtra {
     const float *row_scale = nullptr;
     const void *resid = nullptr;
     int64_t ld_r = 0;
+    // not an epilogue term: device scratch the CUDA-core GEMM may use for
+    // split-K partial sums (few-row GEMMs of the decode step), or null
+    float *scratch = nullptr;
+    size_t scratch_bytes = 0;
 };
 
 int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
@@ -42,6 +46,11 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
                int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
                void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
                int64_t d_state, cudaStream_t stream);
+
+int scan_step(int dtype, const void *xc, int64_t ld_x, const void *dt_pre, int64_t ld_dt,
+              const void *bm, const void *cm, int64_t ld_bc, const void *z, int64_t ld_z,
+              const void *A_log, const void *D, float *h, void *y, int64_t ld_y, int64_t batch,
+              int64_t d_inner, int64_t d_state, cudaStream_t st);
 
 // Dense or quantised linear y = x W^T (+ bias, + extras): the tensor-core
 // kernel where it applies, the CUDA-core kernel otherwise.  n1/off1/n2/off2

@@ -576,6 +576,135 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
     return dispatch_scan<__nv_bfloat16, GATED>(p, stream);
 }
 
+// ------------------------------------------------------ single-token step ---
+// forward_step's scan (_mamba.py:140-164): one thread per (sequence b,
+// channel d), channels fastest so the per-channel rows are read coalesced;
+// the channel's state row h[b, d, :] is read, advanced one step and written
+// back in place, 16 states at a time in registers.  dt = softplus(dt_proj
+// output), A = -exp(A_log), dA = 2^(dt * A log2 e) (as the sequence kernel),
+// h = dA h + (dt B) x, y = C.h + D x, out = cast(y) * SiLU(z).
+template <typename T>
+__global__ void __launch_bounds__(256)
+step_scan_kernel(const T *__restrict__ xc, int64_t ld_x, const T *__restrict__ dtp,
+                 int64_t ld_dt, const T *__restrict__ bm, const T *__restrict__ cm,
+                 int64_t ld_bc, const T *__restrict__ z, int64_t ld_z,
+                 const T *__restrict__ A_log, const T *__restrict__ D, float *__restrict__ h,
+                 T *__restrict__ y, int64_t ld_y, int64_t batch, int64_t di, int S) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch * di) return;
+    const int64_t b = i / di, d = i - b * di;
+    const float dt = io<T>::round(softplus_fast(io<T>::to_f(dtp[b * ld_dt + d])));
+    const float x = io<T>::to_f(xc[b * ld_x + d]);
+    const T *Br = bm + b * ld_bc;
+    const T *Cr = cm + b * ld_bc;
+    float *hr = h + (b * di + d) * S;
+    const T *ar = A_log + d * S;
+    float yv = 0.0f;
+    for (int s0 = 0; s0 < S; s0 += 16) {
+        float hv[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) hv[k] = (s0 + k < S) ? hr[s0 + k] : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (s0 + k < S) {
+                const float a = -expf(io<T>::to_f(ar[s0 + k])) * kLog2e;
+                const float dA = ex2(dt * a);
+                hv[k] = fmaf(dA, hv[k], (dt * io<T>::to_f(Br[s0 + k])) * x);
+                yv = fmaf(hv[k], io<T>::to_f(Cr[s0 + k]), yv);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+            if (s0 + k < S) hr[s0 + k] = hv[k];
+    }
+    float out = yv + (D ? io<T>::to_f(D[d]) : 0.0f) * x;
+    out = io<T>::round(out) * io<T>::round(silu_f(io<T>::to_f(z[b * ld_z + d])));
+    y[b * ld_y + d] = io<T>::from_f(out);
+}
+
+// The same step with QS = S/4 threads per channel, each owning 4 consecutive
+// states (one 16-byte load and store of h), so a warp moves 32 x 16 contiguous
+// bytes of the state; y is summed over the channel's QS lanes with shuffles.
+// For S in {4, 8, 16, 32, 64, 128}.
+template <typename T, int QS>
+__global__ void __launch_bounds__(256)
+step_scan_q_kernel(const T *__restrict__ xc, int64_t ld_x, const T *__restrict__ dtp,
+                   int64_t ld_dt, const T *__restrict__ bm, const T *__restrict__ cm,
+                   int64_t ld_bc, const T *__restrict__ z, int64_t ld_z,
+                   const T *__restrict__ A_log, const T *__restrict__ D, float *__restrict__ h,
+                   T *__restrict__ y, int64_t ld_y, int64_t batch, int64_t di) {
+    constexpr int S = 4 * QS;
+    const int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t i = gi / QS;                 // (b, d)
+    const int q = (int)(gi - i * QS);
+    const bool ok = i < batch * di;            // every lane joins the shuffles below
+    const int64_t ii = ok ? i : 0;
+    const int64_t b = ii / di, d = ii - b * di;
+    float yv = 0.0f, x = 0.0f;
+    if (ok) {
+        const float dt = io<T>::round(softplus_fast(io<T>::to_f(dtp[b * ld_dt + d])));
+        x = io<T>::to_f(xc[b * ld_x + d]);
+        const int s0 = 4 * q;
+        float4 *hp = reinterpret_cast<float4 *>(h + (b * di + d) * S + s0);
+        float4 h4 = *hp;
+        float hv[4] = {h4.x, h4.y, h4.z, h4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float a = -expf(io<T>::to_f(A_log[d * S + s0 + k])) * kLog2e;
+            const float dA = ex2(dt * a);
+            hv[k] = fmaf(dA, hv[k], (dt * io<T>::to_f(bm[b * ld_bc + s0 + k])) * x);
+            yv = fmaf(hv[k], io<T>::to_f(cm[b * ld_bc + s0 + k]), yv);
+        }
+        *hp = make_float4(hv[0], hv[1], hv[2], hv[3]);
+    }
+#pragma unroll
+    for (int o = QS / 2; o > 0; o >>= 1) yv += __shfl_xor_sync(0xffffffffu, yv, o);
+    if (ok && q == 0) {
+        float out = yv + (D ? io<T>::to_f(D[d]) : 0.0f) * x;
+        out = io<T>::round(out) * io<T>::round(silu_f(io<T>::to_f(z[b * ld_z + d])));
+        y[b * ld_y + d] = io<T>::from_f(out);
+    }
+}
+
+template <typename T>
+static int launch_step(const void *xc, int64_t ld_x, const void *dt_pre, int64_t ld_dt,
+                       const void *bm, const void *cm, int64_t ld_bc, const void *z,
+                       int64_t ld_z, const void *A_log, const void *D, float *h, void *y,
+                       int64_t ld_y, int64_t batch, int64_t di, int S, cudaStream_t st) {
+    const T *X = static_cast<const T *>(xc), *DT = static_cast<const T *>(dt_pre);
+    const T *Bp = static_cast<const T *>(bm), *Cp = static_cast<const T *>(cm);
+    const T *Z = static_cast<const T *>(z), *AL = static_cast<const T *>(A_log);
+    const T *Dp = static_cast<const T *>(D);
+    T *Y = static_cast<T *>(y);
+    const int64_t n = batch * di;
+    const bool h16 = aligned(h, 16);
+#define MB2_STEP_Q(QSV)                                                                        \
+    if (h16 && S == 4 * QSV) {                                                                 \
+        step_scan_q_kernel<T, QSV><<<(unsigned)ceil_div(n * QSV, (int64_t)256), 256, 0, st>>>( \
+            X, ld_x, DT, ld_dt, Bp, Cp, ld_bc, Z, ld_z, AL, Dp, h, Y, ld_y, batch, di);       \
+        return check_launch("step_scan_q_kernel");                                             \
+    }
+    MB2_STEP_Q(1) MB2_STEP_Q(2) MB2_STEP_Q(4) MB2_STEP_Q(8) MB2_STEP_Q(16) MB2_STEP_Q(32)
+#undef MB2_STEP_Q
+    step_scan_kernel<T><<<(unsigned)ceil_div(n, (int64_t)256), 256, 0, st>>>(
+        X, ld_x, DT, ld_dt, Bp, Cp, ld_bc, Z, ld_z, AL, Dp, h, Y, ld_y, batch, di, S);
+    return check_launch("step_scan_kernel");
+}
+
+int scan_step(int dtype, const void *xc, int64_t ld_x, const void *dt_pre, int64_t ld_dt,
+              const void *bm, const void *cm, int64_t ld_bc, const void *z, int64_t ld_z,
+              const void *A_log, const void *D, float *h, void *y, int64_t ld_y, int64_t batch,
+              int64_t d_inner, int64_t d_state, cudaStream_t st) {
+    MB2_REQUIRE(d_state >= 1 && d_state <= 256, MB2_ERR_SHAPE,
+                "d_state > 256 not supported (got %lld)", (long long)d_state);
+    if (batch == 0 || d_inner == 0) return MB2_OK;
+    if (dtype == MB2_F32)
+        return launch_step<float>(xc, ld_x, dt_pre, ld_dt, bm, cm, ld_bc, z, ld_z, A_log, D, h, y,
+                                  ld_y, batch, d_inner, (int)d_state, st);
+    return launch_step<__nv_bfloat16>(xc, ld_x, dt_pre, ld_dt, bm, cm, ld_bc, z, ld_z, A_log, D,
+                                      h, y, ld_y, batch, d_inner, (int)d_state, st);
+}
+
 }  // namespace mb2
 
 using namespace mb2;

@@ -214,6 +214,11 @@ class CPUMamba(nn.Module):
                             lambda xd, yd: self._run(xd, False, out=yd, blk=blk),
                             n, self._host_slots, self._host_edge)
 
+    def capture_step(self, state: dict, example: torch.Tensor) -> "StepGraph":
+        """A CUDA graph of forward_step for this state dict and batch size
+        (see StepGraph): call it with each token's (B, d_model) input."""
+        return StepGraph(self, state, example)
+
     def forward_with_final_state(self, hidden_states: torch.Tensor) -> tuple:
         """(y, {"h": (B, d_inner, d_state) f32, "conv_state": (B, d_inner, d_conv-1)})
         from one pass (_mamba.py:165-202)."""
@@ -253,6 +258,44 @@ class CPUMamba(nn.Module):
                                    h.data_ptr(), conv.data_ptr(), B, ws.data_ptr(), ws_bytes,
                                    stream_of(x_step)), "forward_step")
         return out, state
+
+
+class StepGraph:
+    """``forward_step`` captured once as a CUDA graph for a fixed batch size and
+    a fixed state dict, then replayed per token: one graph launch instead of
+    the step's host work and kernel launches.
+
+    ``state["h"]`` and ``state["conv_state"]`` are advanced in place by every
+    call, exactly as ``forward_step`` does.  The returned output tensor is a
+    buffer owned by the graph, overwritten by the next call.  Capture runs one
+    warm-up step on a copy of the state first (library set-up happens outside
+    the capture); the captured state is not modified by the capture itself.
+    Rebuild the graph after changing the module's parameters."""
+
+    def __init__(self, block: "CPUMamba", state: dict, example: torch.Tensor):
+        if example.dim() == 3:
+            example = example.squeeze(1)
+        h, conv = state["h"], state["conv_state"]
+        if (h.dtype != torch.float32 or not h.is_contiguous() or not conv.is_contiguous()
+                or conv.dtype != example.dtype or h.device != example.device):
+            raise RuntimeError("StepGraph: state must be contiguous on the input's device, "
+                               "h float32 and conv_state in the input dtype (init_state)")
+        self.block, self.state = block, state
+        self.x = example.detach().clone().contiguous()
+        dev = self.x.device
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.no_grad():
+            block.forward_step(self.x, {k: v.clone() for k, v in state.items()})
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(self.graph):
+            self.y, _ = block.forward_step(self.x, state)
+
+    def __call__(self, x_step: torch.Tensor) -> torch.Tensor:
+        self.x.copy_(x_step.reshape(self.x.shape), non_blocking=True)
+        self.graph.replay()
+        return self.y
 
 
 def assert_state_dict_compatible(cpu_mamba: CPUMamba, sd: dict):

@@ -156,3 +156,43 @@ def test_forward_host_equals_forward(dtype, chunks, pinned):
     with torch.no_grad():
         assert m.forward_host(x, out=out, chunks=chunks) is out
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_step_graph_equals_forward_step(dtype):
+    """forward_step captured as a CUDA graph and replayed gives forward_step's
+    outputs and state bit for bit."""
+    torch.manual_seed(5)
+    m = CPUMamba(d_model=64, d_state=16).cuda().to(dtype).eval()
+    prompt = torch.randn(3, 9, 64, device="cuda").to(dtype)
+    with torch.no_grad():
+        _, st_a = m.forward_with_final_state(prompt)
+    st_b = {k: v.clone() for k, v in st_a.items()}
+    xs = [torch.randn(3, 64, device="cuda").to(dtype) for _ in range(5)]
+    g = m.capture_step(st_b, xs[0])
+    for x in xs:
+        with torch.no_grad():
+            y_a, _ = m.forward_step(x, st_a)
+        y_b = g(x)
+        assert torch.equal(y_a, y_b)
+    assert torch.equal(st_a["h"], st_b["h"])
+    assert torch.equal(st_a["conv_state"], st_b["conv_state"])
+
+
+@pytest.mark.parametrize("d_state", [8, 12, 24, 64])
+def test_prefill_plus_steps_equals_forward(d_state):
+    """forward over T tokens == forward_with_final_state over the first T - 4
+    and four forward_step calls (fp32, 1e-5), for state sizes that take the
+    4-states-per-thread step kernel (8, 64) and the one-thread-per-channel one
+    (12, 24)."""
+    torch.manual_seed(d_state)
+    m = CPUMamba(d_model=64, d_state=d_state).cuda().eval()
+    with torch.no_grad():
+        m.dt_proj.bias.uniform_(-4.0, -2.0)
+    x = torch.randn(3, 20, 64, device="cuda")
+    with torch.no_grad():
+        y_full = m(x)
+        y_pre, st = m.forward_with_final_state(x[:, :16])
+        steps = [m.forward_step(x[:, 16 + k], st)[0] for k in range(4)]
+    y = torch.cat([y_pre, torch.stack(steps, 1)], 1)
+    assert (y - y_full).abs().max().item() <= TOL
