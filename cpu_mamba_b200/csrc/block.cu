@@ -41,6 +41,7 @@ struct Layout {
     size_t es;
     size_t off_xz, off_xc, off_xdbl, total;   // y reuses the xc buffer
     size_t off_part, part_bytes;              // step: split-K partial sums
+    size_t off_seg, seg_bytes;                // forward: scan T-segment state
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -48,7 +49,8 @@ static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 // Workspace of a forward over `rows` tokens, or (step) of a decode step: the
 // step's projections have few rows and split K, so it adds room for four
 // splits' partial sums of its widest projection.
-static Layout make_layout(const mb2_block *b, int64_t rows, bool step = false) {
+static Layout make_layout(const mb2_block *b, int64_t rows, bool step = false,
+                          int64_t batch = 0, int64_t seqlen = 0) {
     Layout l{};
     l.N = rows;
     l.di = b->d_inner; l.dm = b->d_model; l.S = b->d_state; l.R = b->dt_rank; l.K = b->d_conv;
@@ -68,6 +70,9 @@ static Layout make_layout(const mb2_block *b, int64_t rows, bool step = false) {
         l.part_bytes = (size_t)rows * wide * sizeof(float) * 4;
         off = align256(off + l.part_bytes);
     }
+    l.off_seg = off;
+    l.seg_bytes = step ? 0 : scan_segment_bytes(batch, l.di, seqlen, l.S);
+    off = align256(off + l.seg_bytes);
     l.total = off;
     return l;
 }
@@ -196,7 +201,8 @@ static int block_pipeline(const mb2_block &b, const Layout &l, const void *x, vo
     if (dt_done)
         MB2_TRY(scan_gated(b.dtype, xc, di, xz, 2 * di, (char *)xdbl + l.RB * es, l.ldx,
                            (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log,
-                           b.D, nullptr, h_last, xc, di, batch, seqlen, di, S, st));
+                           b.D, nullptr, h_last, xc, di, batch, seqlen, di, S, st,
+                           reinterpret_cast<float *>(ws + l.off_seg), l.seg_bytes));
     else
         MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
                            (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
@@ -210,7 +216,7 @@ static int block_pipeline(const mb2_block &b, const Layout &l, const void *x, vo
 
 extern "C" size_t mb2_block_workspace_bytes(const mb2_block *blk, int64_t batch, int64_t seqlen) {
     if (!blk || batch < 0 || seqlen < 0) return 0;
-    return make_layout(blk, batch * seqlen).total;
+    return make_layout(blk, batch * seqlen, false, batch, seqlen).total;
 }
 
 extern "C" int mb2_block_forward(const mb2_block *blk, const void *x, void *out, int64_t batch,
@@ -220,7 +226,7 @@ extern "C" int mb2_block_forward(const mb2_block *blk, const void *x, void *out,
     MB2_REQUIRE(batch >= 0 && seqlen >= 0, MB2_ERR_SHAPE, "block: negative size");
     const mb2_block &b = *blk;
     cudaStream_t st = (cudaStream_t)stream;
-    const Layout l = make_layout(blk, batch * seqlen);
+    const Layout l = make_layout(blk, batch * seqlen, false, batch, seqlen);
     MB2_REQUIRE(workspace_bytes >= l.total, MB2_ERR_WORKSPACE,
                 "block: workspace %zu < required %zu", workspace_bytes, l.total);
     if (batch == 0) return MB2_OK;
@@ -358,11 +364,12 @@ extern "C" int mb2_fold_norm(int dtype, const void *w, const void *norm_weight, 
     return check_launch("fold_norm_kernel");
 }
 
-static size_t stack_bytes(const mb2_block *layers, int64_t n_layers, int64_t rows,
-                          size_t *off_r) {
+static size_t stack_bytes(const mb2_block *layers, int64_t n_layers, int64_t batch,
+                          int64_t seqlen, size_t *off_r) {
     size_t ws = 0;
+    const int64_t rows = batch * seqlen;
     for (int64_t i = 0; i < n_layers; ++i) {
-        const size_t t = make_layout(&layers[i], rows).total;
+        const size_t t = make_layout(&layers[i], rows, false, batch, seqlen).total;
         ws = t > ws ? t : ws;
     }
     *off_r = ws;
@@ -373,7 +380,7 @@ extern "C" size_t mb2_stack_workspace_bytes(const mb2_block *layers, int64_t n_l
                                             int64_t batch, int64_t seqlen) {
     if (!layers || n_layers <= 0 || batch < 0 || seqlen < 0) return 0;
     size_t off_r;
-    return stack_bytes(layers, n_layers, batch * seqlen, &off_r);
+    return stack_bytes(layers, n_layers, batch, seqlen, &off_r);
 }
 
 extern "C" int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, float eps, void *x,
@@ -390,7 +397,7 @@ extern "C" int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, floa
     }
     const int64_t N = batch * seqlen;
     size_t off_r;
-    const size_t need = stack_bytes(layers, n_layers, N, &off_r);
+    const size_t need = stack_bytes(layers, n_layers, batch, seqlen, &off_r);
     MB2_REQUIRE(workspace_bytes >= need, MB2_ERR_WORKSPACE,
                 "stack: workspace %zu < required %zu", workspace_bytes, need);
     if (N == 0) return MB2_OK;
@@ -400,7 +407,7 @@ extern "C" int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, floa
     float *r = reinterpret_cast<float *>(ws + off_r);
     for (int64_t i = 0; i < n_layers; ++i) {
         const mb2_block &b = layers[i];
-        const Layout l = make_layout(&b, N);
+        const Layout l = make_layout(&b, N, false, batch, seqlen);
         MB2_TRY(rms_scale(b.dtype, x, N, b.d_model, eps, r, st));
         MB2_TRY(block_pipeline(b, l, x, x, batch, seqlen, nullptr, nullptr, ws, st, r, x));
     }

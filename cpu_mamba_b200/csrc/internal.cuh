@@ -45,7 +45,12 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
                const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
                int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
                void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
-               int64_t d_state, cudaStream_t stream);
+               int64_t d_state, cudaStream_t stream, float *seg_ws = nullptr,
+               size_t seg_bytes = 0);
+// Long sequences over few (batch, channel) chains: the number of T segments
+// scan_gated runs in parallel (1 = none) and the scratch it needs for them.
+int scan_segments(int64_t batch, int64_t d_inner, int64_t seqlen, int64_t d_state);
+size_t scan_segment_bytes(int64_t batch, int64_t d_inner, int64_t seqlen, int64_t d_state);
 
 int scan_step(int dtype, const void *xc, int64_t ld_x, const void *dt_pre, int64_t ld_dt,
               const void *bm, const void *cm, int64_t ld_bc, const void *z, int64_t ld_z,

@@ -56,6 +56,14 @@ struct ScanParams {
     int64_t batch, seqlen, d_inner;
     int d_state, dt_rank;
     unsigned vec16;                  // bit i: array i rows are 16-byte aligned
+    // T segments (few independent chains, long sequences): blockIdx.y =
+    // b * nseg + g runs steps [g * seg_len, (g + 1) * seg_len) of sequence b
+    int nseg;                        // <= 1: no segments
+    int64_t seg_len;
+    int summary;                     // 1: pass 1 -- h from 0, writes h_end and sum(dt), no y
+    float *seg_hend;                 // (batch, nseg, d_inner, S)
+    float *seg_sdt;                  // (batch, nseg, d_inner)
+    const float *seg_hstart;         // pass 3: (batch, nseg, d_inner, S) starting states
 };
 
 enum { ARR_X = 1, ARR_D2 = 2, ARR_B = 4, ARR_C = 8, ARR_DL = 16, ARR_Z = 32 };
@@ -169,25 +177,47 @@ __device__ __forceinline__ void stage_rows(T *dst, const T *src, int64_t ld, int
 }
 
 // N consecutive values from shared memory as floats, widest aligned loads.
+// N consecutive elements of a staged row.  N % 4 == 0: 16-byte (fp32) or
+// 8-byte (bf16) loads; otherwise pairs (8 / 4 bytes).  Callers keep the start
+// a multiple of 4 elements (of 2 when N % 4 != 0), so every load is aligned.
 template <typename T, int N> struct Vec;
 template <int N> struct Vec<float, N> {
     static __device__ __forceinline__ void load(const float *p, float (&v)[N]) {
+        static_assert(N % 2 == 0, "pairs");
+        if constexpr (N % 4 == 0) {
 #pragma unroll
-        for (int k = 0; k < N / 4; ++k) {
-            const float4 q = reinterpret_cast<const float4 *>(p)[k];
-            v[4 * k] = q.x; v[4 * k + 1] = q.y; v[4 * k + 2] = q.z; v[4 * k + 3] = q.w;
+            for (int k = 0; k < N / 4; ++k) {
+                const float4 q = reinterpret_cast<const float4 *>(p)[k];
+                v[4 * k] = q.x; v[4 * k + 1] = q.y; v[4 * k + 2] = q.z; v[4 * k + 3] = q.w;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < N / 2; ++k) {
+                const float2 q = reinterpret_cast<const float2 *>(p)[k];
+                v[2 * k] = q.x; v[2 * k + 1] = q.y;
+            }
         }
     }
 };
 template <int N> struct Vec<__nv_bfloat16, N> {
     static __device__ __forceinline__ void load(const __nv_bfloat16 *p, float (&v)[N]) {
+        static_assert(N % 2 == 0, "pairs");
+        if constexpr (N % 4 == 0) {
 #pragma unroll
-        for (int k = 0; k < N / 4; ++k) {
-            const uint2 q = reinterpret_cast<const uint2 *>(p)[k];
-            v[4 * k] = __uint_as_float(q.x << 16);
-            v[4 * k + 1] = __uint_as_float(q.x & 0xFFFF0000u);
-            v[4 * k + 2] = __uint_as_float(q.y << 16);
-            v[4 * k + 3] = __uint_as_float(q.y & 0xFFFF0000u);
+            for (int k = 0; k < N / 4; ++k) {
+                const uint2 q = reinterpret_cast<const uint2 *>(p)[k];
+                v[4 * k] = __uint_as_float(q.x << 16);
+                v[4 * k + 1] = __uint_as_float(q.x & 0xFFFF0000u);
+                v[4 * k + 2] = __uint_as_float(q.y << 16);
+                v[4 * k + 3] = __uint_as_float(q.y & 0xFFFF0000u);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < N / 2; ++k) {
+                const uint32_t q = reinterpret_cast<const uint32_t *>(p)[k];
+                v[2 * k] = __uint_as_float(q << 16);
+                v[2 * k + 1] = __uint_as_float(q & 0xFFFF0000u);
+            }
         }
     }
 };
@@ -212,8 +242,10 @@ struct Geo {
                                     (MODE != PLAIN ? (size_t)SCAN_TC * CH * sizeof(float) : 0);
 };
 
+// 6 CTAs per SM (registers <= 80) where dt is given; the fused kernel keeps
+// W_dt's row slice in registers and needs the 128 of 4 CTAs per SM
 template <typename T, int SPL, int L, int MODE, int RL>
-__global__ void __launch_bounds__(SCAN_THREADS, 4)
+__global__ void __launch_bounds__(SCAN_THREADS, MODE == FUSED ? 4 : 6)
 scan_kernel(const ScanParams p) {
     using Gm = Geo<T, SPL, L, MODE, RL>;
     constexpr int CH = Gm::CH;
@@ -225,12 +257,19 @@ scan_kernel(const ScanParams p) {
     const int tid = threadIdx.x;
     const int c = tid / L;          // channel within CTA
     const int j = tid % L;          // lane within the channel's group
-    const int b = blockIdx.y;
+    const int nseg = p.nseg > 1 ? p.nseg : 1;
+    const int b = blockIdx.y / nseg;
+    const int g = blockIdx.y - b * nseg;              // T segment
+    const int64_t tb = (int64_t)g * p.seg_len;        // first step of the segment
+    int64_t tl = nseg > 1 ? p.seqlen - tb : p.seqlen;
+    if (nseg > 1 && tl > p.seg_len) tl = p.seg_len;
+    if (tl < 0) tl = 0;
+    const int64_t segidx = (int64_t)b * nseg + g;
     const int64_t d0 = (int64_t)blockIdx.x * CH;
     const int64_t d = d0 + c;
     const bool active = d < p.d_inner;
     const int S = p.d_state;
-    const int T_ = (int)p.seqlen;
+    const int T_ = (int)tl;
     const int ch_valid = (int)((p.d_inner - d0 < CH) ? p.d_inner - d0 : CH);
 
     static_assert(SPL % 2 == 0 && (RL % 2 == 0 || RL == 1), "states / dt_rank slices come in pairs");
@@ -247,7 +286,10 @@ scan_kernel(const ScanParams p) {
                     a[e] = -expf(io<T>::to_f(static_cast<const T *>(p.A)[d * S + s]));
                 else
                     a[e] = static_cast<const float *>(p.A)[d * S + s];
-                if (p.h0) hi[e] = p.h0[((int64_t)b * p.d_inner + d) * S + s];
+                if (p.seg_hstart)
+                    hi[e] = p.seg_hstart[(segidx * p.d_inner + d) * S + s];
+                else if (p.h0 && !p.summary)
+                    hi[e] = p.h0[((int64_t)b * p.d_inner + d) * S + s];
             }
         }
         A2[q] = pk(a[0] * kLog2e, a[1] * kLog2e);
@@ -272,7 +314,7 @@ scan_kernel(const ScanParams p) {
         if (active && p.b_dt) bias_dt = io<T>::to_f(static_cast<const T *>(p.b_dt)[d]);
     }
 
-    const int64_t row_base = (int64_t)b * p.seqlen;
+    const int64_t row_base = (int64_t)b * p.seqlen + tb;
     const T *xg = static_cast<const T *>(p.x) + row_base * p.ld_x + d0;
     const T *d2g = MODE == FUSED ? static_cast<const T *>(p.z) + row_base * p.ld_z + d0
                                  : static_cast<const T *>(p.dt) + row_base * p.ld_dt + d0;
@@ -313,6 +355,7 @@ scan_kernel(const ScanParams p) {
     T *yg = static_cast<T *>(p.y) + row_base * p.ld_y + d0 + cc;
 
     const int nchunks = (T_ + SCAN_TC - 1) / SCAN_TC;
+    float sdt = 0.0f;                                  // sum of this channel's dt (pass 1)
     if (nchunks > 0) issue(0);
     cp_async_commit();
 
@@ -375,9 +418,10 @@ scan_kernel(const ScanParams p) {
             __syncwarp();   // a channel's L lanes share one warp
         }
         // ---- recurrence (tn is CTA-uniform)
-#pragma unroll 2
+#pragma unroll 8
         for (int tt = 0; tt < tn; ++tt) {
             const float dtv = MODE != PLAIN ? dts[tt * CH + c] : io<T>::to_f(d2s[tt * CH]);
+            sdt += dtv;
             const float dtx = dtv * io<T>::to_f(xs[tt * CH]);
             const f2 dt2 = pk(dtv, dtv), dtx2 = pk(dtx, dtx);
             float bv[SPL], cv[SPL];
@@ -402,7 +446,7 @@ scan_kernel(const ScanParams p) {
         // ---- read-out: sum lane partials, D skip, (FUSED) cast + SiLU(z) gate
         const T *xrow = st + cc;
         const T *zrow = st + (MODE == FUSED ? Gm::NX : 2 * Gm::NX + 2 * Gm::NBC) + cc;
-        if (col_ok) {
+        if (col_ok && !p.summary) {
 #pragma unroll 4
             for (int tt = rr0; tt < tn; tt += RSTEP) {
                 float yv = 0.0f;
@@ -417,7 +461,12 @@ scan_kernel(const ScanParams p) {
         __syncthreads();
     }
     cp_async_wait<0>();
-    if (p.h_last && active) {
+    // final state: of the sequence (no segments), or of the segment (pass 1);
+    // with segments the carry kernel produces the sequence's final state
+    float *hout = p.summary ? p.seg_hend + segidx * p.d_inner * S
+                            : ((nseg == 1 && p.h_last) ? p.h_last + (int64_t)b * p.d_inner * S
+                                                       : nullptr);
+    if (hout && active) {
 #pragma unroll
         for (int q = 0; q < NP; ++q) {
             float hv[2];
@@ -425,10 +474,37 @@ scan_kernel(const ScanParams p) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const int s = j * SPL + 2 * q + e;
-                if (s < S) p.h_last[((int64_t)b * p.d_inner + d) * S + s] = hv[e];
+                if (s < S) hout[d * S + s] = hv[e];
             }
         }
+        if (p.summary && j == 0) p.seg_sdt[segidx * p.d_inner + d] = sdt;
     }
+}
+
+// Segments' carry (between pass 1 and pass 3): per (b, d, s), in segment
+// order, start(g) = h, then h = exp(A sum(dt_g)) h + h_end(g) -- the product of
+// the segment's per-step decays exp(dt_t A) is the exponential of A times the
+// sum of its dt.  The state after the last segment is the sequence's final
+// state.  A: fp32 (PLAIN) or A_log in T (A = -exp(A_log)).
+template <typename T, bool A_F32>
+__global__ void seg_carry_kernel(const void *A, const float *__restrict__ h0,
+                                 const float *__restrict__ hend, const float *__restrict__ sdt,
+                                 float *__restrict__ hstart, float *__restrict__ h_last,
+                                 int64_t batch, int64_t di, int S, int nseg) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch * di * S) return;
+    const int64_t s = i % S, bd = i / S;
+    const int64_t d = bd % di, b = bd / di;
+    const float a = A_F32 ? static_cast<const float *>(A)[d * S + s]
+                          : -expf(io<T>::to_f(static_cast<const T *>(A)[d * S + s]));
+    const float a2 = a * kLog2e;
+    float hv = h0 ? h0[i] : 0.0f;
+    for (int g = 0; g < nseg; ++g) {
+        const int64_t idx = (b * nseg + g) * di + d;
+        hstart[idx * S + s] = hv;
+        hv = fmaf(ex2(a2 * sdt[idx]), hv, hend[idx * S + s]);
+    }
+    if (h_last) h_last[i] = hv;
 }
 
 // -------------------------------------------------------------- dispatch ---
@@ -455,7 +531,8 @@ static int launch_scan(ScanParams p, cudaStream_t st) {
     if (rows16(p.bm, p.ld_b, es)) p.vec16 |= ARR_B;
     if (rows16(p.cm, p.ld_c, es)) p.vec16 |= ARR_C;
     if (MODE == FUSED && rows16(p.dl, p.ld_dl, es)) p.vec16 |= ARR_DL;
-    dim3 grid((unsigned)ceil_div(p.d_inner, Gm::CH), (unsigned)p.batch);
+    dim3 grid((unsigned)ceil_div(p.d_inner, Gm::CH),
+              (unsigned)(p.batch * (p.nseg > 1 ? p.nseg : 1)));
     kern<<<grid, SCAN_THREADS, Gm::BYTES, st>>>(p);
     return check_launch("scan_kernel");
 }
@@ -478,6 +555,7 @@ static int dispatch_rl(const ScanParams &p, cudaStream_t st) {
     }
 }
 
+// (SPL, L) by d_state.
 template <typename T, int MODE>
 static int dispatch_scan(const ScanParams &p, cudaStream_t st) {
     const int S = p.d_state;
@@ -538,6 +616,49 @@ int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t
     return dispatch_scan<__nv_bfloat16, FUSED>(p, stream);
 }
 
+// ------------------------------------------------------- T segments (host) --
+// Lanes per channel of the dispatch above.
+static int lanes_for(int S) { return S <= 8 ? 1 : S <= 32 ? 2 : S <= 64 ? 4 : S <= 128 ? 8 : 16; }
+
+int scan_segments(int64_t batch, int64_t d_inner, int64_t seqlen, int64_t d_state) {
+    // few independent (batch, channel) chains leave most SMs idle while each
+    // walks a long sequence: cut T into segments until about 148 x 1024
+    // threads (8 CTAs per SM on a B200) are busy, segments >= 256 steps
+    const int64_t threads = batch * d_inner * lanes_for((int)d_state);
+    const int64_t target = (int64_t)148 * 1024;
+    if (threads <= 0 || threads * 2 > target) return 1;
+    int64_t g = ceil_div(target, threads);
+    const int64_t gmax = seqlen / 256;
+    g = g < gmax ? g : gmax;
+    g = g < 64 ? g : 64;
+    return g >= 2 ? (int)g : 1;
+}
+
+size_t scan_segment_bytes(int64_t batch, int64_t d_inner, int64_t seqlen, int64_t d_state) {
+    const int nseg = scan_segments(batch, d_inner, seqlen, d_state);
+    if (nseg <= 1) return 0;
+    return (size_t)batch * nseg * d_inner * (2 * d_state + 1) * sizeof(float);
+}
+
+// Pass 1 (segment summaries), carry, pass 3 (outputs).
+template <typename T, int MODE>
+static int run_segmented(ScanParams p, int nseg, float *ws, cudaStream_t st) {
+    const int64_t S = p.d_state;
+    p.seg_len = round_up(ceil_div(p.seqlen, (int64_t)nseg), (int64_t)SCAN_TC);
+    p.nseg = (int)ceil_div(p.seqlen, p.seg_len);
+    const int64_t nstates = p.batch * p.nseg * p.d_inner * S;
+    float *hend = ws, *hstart = ws + nstates, *sdt = ws + 2 * nstates;
+    float *h_last = p.h_last;
+    p.summary = 1; p.seg_hend = hend; p.seg_sdt = sdt; p.seg_hstart = nullptr;
+    MB2_TRY((dispatch_scan<T, MODE>(p, st)));
+    const int64_t n = p.batch * p.d_inner * S;
+    seg_carry_kernel<T, MODE == PLAIN><<<(unsigned)ceil_div(n, (int64_t)256), 256, 0, st>>>(
+        p.A, p.h0, hend, sdt, hstart, h_last, p.batch, p.d_inner, (int)S, p.nseg);
+    MB2_TRY(check_launch("seg_carry_kernel"));
+    p.summary = 0; p.seg_hstart = hstart;
+    return dispatch_scan<T, MODE>(p, st);
+}
+
 // The block forward's scan stage given dt_proj's output (dt_low W_dt^T + b_dt,
 // from the tensor-core GEMM): dt = softplus(.), A = -exp(A_log), recurrence,
 // D skip, cast and SiLU(z) gate.
@@ -545,7 +666,7 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
                const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
                int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
                void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
-               int64_t d_state, cudaStream_t stream) {
+               int64_t d_state, cudaStream_t stream, float *seg_ws, size_t seg_bytes) {
     MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "scan: bad dtype");
     MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0, MB2_ERR_SHAPE, "scan: bad sizes");
     MB2_REQUIRE(d_state >= 1 && d_state <= 256, MB2_ERR_SHAPE,
@@ -572,6 +693,11 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
     p.y = y; p.ld_y = ld_y;
     p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
     p.d_state = (int)d_state;
+    const int nseg = scan_segments(batch, d_inner, seqlen, d_state);
+    if (nseg > 1 && seg_ws && seg_bytes >= scan_segment_bytes(batch, d_inner, seqlen, d_state)) {
+        if (dtype == MB2_F32) return run_segmented<float, GATED>(p, nseg, seg_ws, stream);
+        return run_segmented<__nv_bfloat16, GATED>(p, nseg, seg_ws, stream);
+    }
     if (dtype == MB2_F32) return dispatch_scan<float, GATED>(p, stream);
     return dispatch_scan<__nv_bfloat16, GATED>(p, stream);
 }
@@ -754,5 +880,6 @@ extern "C" int mb2_scan_gated(int dtype, const void *xc, int64_t ld_xc, const vo
                               int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
                               int64_t d_state, mb2_stream_t stream) {
     return scan_gated(dtype, xc, ld_xc, dt, ld_dt, B, ld_b, C, ld_c, z, ld_z, A_log, D, h0,
-                      h_last, y, ld_y, batch, seqlen, d_inner, d_state, (cudaStream_t)stream);
+                      h_last, y, ld_y, batch, seqlen, d_inner, d_state, (cudaStream_t)stream,
+                      nullptr, 0);
 }

@@ -152,7 +152,8 @@ def test_gated_scan_ragged_lengths_state(T):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("b,T,S", [(3, 45, 16), (4, 100, 24), (2, 17, 8)])
+@pytest.mark.parametrize("b,T,S", [(3, 45, 16), (4, 100, 24), (2, 17, 8), (2, 33, 32),
+                                   (1, 20, 12)])
 def test_scan_with_given_dt_matches_composition(dtype, b, T, S):
     """The block forward's split form: dt_proj from the projection kernel
     (tensor cores from 256 rows, with the TF32 halves in fp32), then the scan
