@@ -23,9 +23,27 @@ int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, vo
                int64_t n1, int64_t off1, int64_t n2, int64_t off2, const EpiExtra &ex) {
     if (n1 < 0) n1 = N;
     if (n2 < 0) n2 = N;
-    if (L.scheme != MB2_Q_NONE)
+    if (L.scheme != MB2_Q_NONE) {
+        // many rows: dequantise the weight into scratch as the tensor-core
+        // operand (bit-exact values, as QuantizedLinear.forward forms them on
+        // every call) and run the tensor-core GEMM; else the CUDA-core GEMM
+        // dequantises tile by tile in its loader
+        if (M >= 256 && ex.scratch &&
+            ex.scratch_bytes >= dequant_operand_bytes(dtype, N, K)) {
+            MB2_TRY(dequant_operand(dtype, L.scheme, L.weight_q, L.scale, N, K, ex.scratch, st));
+            const bool bf = dtype == MB2_BF16;
+            bool used = false;
+            EpiExtra ex2 = ex;
+            ex2.scratch = nullptr;
+            ex2.scratch_bytes = 0;
+            MB2_TRY(gemm_tc(dtype, x, ld_x, bf ? (const void *)ex.scratch : nullptr,
+                            bf ? nullptr : ex.scratch, L.bias, y, ld_y, M, N, K, n1, off1, n2,
+                            off2, epi, st, &used, ex2));
+            if (used) return MB2_OK;
+        }
         return gemm_simt(dtype, L.scheme, x, ld_x, L.weight_q, L.scale, L.bias, y, ld_y, M, N, K,
                          n1, off1, n2, off2, epi, st, ex);
+    }
     MB2_REQUIRE(L.weight, MB2_ERR_ARG, "linear: null weight");
     bool used = false;
     MB2_TRY(gemm_tc(dtype, x, ld_x, L.weight, L.weight_split, L.bias, y, ld_y, M, N, K, n1, off1,
@@ -42,6 +60,7 @@ struct Layout {
     size_t off_xz, off_xc, off_xdbl, total;   // y reuses the xc buffer
     size_t off_part, part_bytes;              // step: split-K partial sums
     size_t off_seg, seg_bytes;                // forward: scan T-segment state
+    size_t off_deq, deq_bytes;                // forward: a quantised weight, dequantised
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -73,6 +92,18 @@ static Layout make_layout(const mb2_block *b, int64_t rows, bool step = false,
     l.off_seg = off;
     l.seg_bytes = step ? 0 : scan_segment_bytes(batch, l.di, seqlen, l.S);
     off = align256(off + l.seg_bytes);
+    l.off_deq = off;
+    l.deq_bytes = 0;
+    if (!step && rows >= 256) {   // the tensor-core path of quantised projections
+        auto need = [&](const mb2_linear_w &w, int64_t n, int64_t k) {
+            const size_t v = w.scheme != MB2_Q_NONE ? dequant_operand_bytes(b->dtype, n, k) : 0;
+            l.deq_bytes = v > l.deq_bytes ? v : l.deq_bytes;
+        };
+        need(b->in_proj, 2 * l.di, l.dm);
+        need(b->x_proj, l.R + 2 * l.S, l.di);
+        need(b->out_proj, l.dm, l.di);
+        off = align256(off + l.deq_bytes);
+    }
     l.total = off;
     return l;
 }
@@ -176,10 +207,15 @@ static int block_pipeline(const mb2_block &b, const Layout &l, const void *x, vo
     void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
     const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
     const size_t es = l.es;
-    EpiExtra in_ex, out_ex;
+    EpiExtra in_ex, out_ex, mid_ex;
     in_ex.row_scale = row_scale;
     out_ex.resid = resid;
     out_ex.ld_r = l.dm;
+    // scratch for dequantised weights (quantised projections)
+    for (EpiExtra *e : {&in_ex, &out_ex, &mid_ex}) {
+        e->scratch = l.deq_bytes ? reinterpret_cast<float *>(ws + l.off_deq) : nullptr;
+        e->scratch_bytes = l.deq_bytes;
+    }
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, N, 2 * di, l.dm, MB2_EPI_NONE,
                            st, -1, 0, -1, 0, in_ex));
@@ -187,14 +223,16 @@ static int block_pipeline(const mb2_block &b, const Layout &l, const void *x, vo
                         di, b.d_conv, st));
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, MB2_EPI_NONE,
-                           st, R, l.RB - R, R + S, l.RC - l.RB - S));
+                           st, R, l.RB - R, R + S, l.RC - l.RB - S, mid_ex));
     // dt_proj (_mamba.py:219) on the tensor cores, bias in the epilogue,
     // written over the x half of xz (dead once the conv has run); the gated
-    // scan applies the softplus (:220) as it stages the rows.  Where that GEMM
-    // does not apply (a quantised or unsplit fp32 dt_proj, fewer than 256
-    // rows) the fused scan computes dt itself from W_dt's rows in registers.
+    // scan applies the softplus (:220) as it stages the rows.  A quantised
+    // dt_proj passes its dequantised weight in .weight (as the fused scan
+    // needs it anyway).  Where that GEMM does not apply (an unsplit fp32
+    // weight, fewer than 256 rows) the fused scan computes dt itself from
+    // W_dt's rows in registers.
     bool dt_done = false;
-    if (N > 0 && b.dt_proj.scheme == MB2_Q_NONE)
+    if (N > 0)
         MB2_TRY(gemm_tc(b.dtype, xdbl, l.ldx, b.dt_proj.weight, b.dt_proj.weight_split,
                         b.dt_proj.bias, xz, 2 * di, N, di, R, di, 0, di, 0, MB2_EPI_NONE, st,
                         &dt_done));

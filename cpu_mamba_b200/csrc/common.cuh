@@ -94,6 +94,13 @@ __device__ __forceinline__ float softplus_f(float v) {
     return v > 20.0f ? v : log1pf(expf(v));
 }
 // SiLU v * sigmoid(v) as v / (1 + e^-v).
+// fp32 -> TF32 (10 explicit mantissa bits), rounded to nearest, ties away
+__device__ __forceinline__ float tf32_round(float v) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(v));
+    return __uint_as_float(r);
+}
+
 __device__ __forceinline__ float silu_f(float v) {
     return __fdividef(v, 1.0f + __expf(-v));
 }

@@ -17,8 +17,9 @@ struct EpiExtra {
     const float *row_scale = nullptr;
     const void *resid = nullptr;
     int64_t ld_r = 0;
-    // not an epilogue term: device scratch the CUDA-core GEMM may use for
-    // split-K partial sums (few-row GEMMs of the decode step), or null
+    // not an epilogue term: device scratch for the projection -- the
+    // dequantised operand of a quantised weight on the tensor-core path, or
+    // the CUDA-core GEMM's split-K partial sums (few-row GEMMs) -- or null
     float *scratch = nullptr;
     size_t scratch_bytes = 0;
 };
@@ -56,6 +57,12 @@ int scan_step(int dtype, const void *xc, int64_t ld_x, const void *dt_pre, int64
               const void *bm, const void *cm, int64_t ld_bc, const void *z, int64_t ld_z,
               const void *A_log, const void *D, float *h, void *y, int64_t ld_y, int64_t batch,
               int64_t d_inner, int64_t d_state, cudaStream_t st);
+
+// Quantised weights as the tensor-core GEMM's operand (bit-exact dequantised
+// values; fp32: TF32 hi / lo planes, bf16: rounded) and its size in bytes.
+size_t dequant_operand_bytes(int dtype, int64_t rows, int64_t in_dim);
+int dequant_operand(int dtype, int scheme, const void *wq, const float *scale, int64_t rows,
+                    int64_t in_dim, void *out, cudaStream_t st);
 
 // Dense or quantised linear y = x W^T (+ bias, + extras): the tensor-core
 // kernel where it applies, the CUDA-core kernel otherwise.  n1/off1/n2/off2

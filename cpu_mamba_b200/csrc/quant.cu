@@ -11,7 +11,7 @@
 // This file is compiled WITHOUT fast-math: w / scale is an IEEE
 // round-to-nearest division (__fdiv_rn) as in torch, rintf rounds half to
 // even as torch.round does.
-#include "common.cuh"
+#include "internal.cuh"
 
 namespace mb2 {
 
@@ -115,6 +115,63 @@ __global__ void dequantize_kernel(const void *__restrict__ wq, const float *__re
         const int nib = (j & 1) ? (byte & 0x0F) : (byte >> 4);
         out[i] = SCHEME == MB2_Q_INT4 ? (float)(nib - 7) * s : lut.v[nib] * s;
     }
+}
+
+// The tensor-core GEMM's weight operand from quantised codes: deq(W) formed
+// exactly as dequantize_kernel (q.float() * scale, quant.py:68-69, :90-101,
+// :124-134) and as QuantizedLinear.forward casts it (.to(x.dtype), :188-190),
+// then, for fp32, split into TF32 planes out[0:n] = hi, out[n:2n] = lo (as
+// mb2_split_tf32), for bf16 rounded to bf16.
+template <int SCHEME, bool BF16>
+__global__ void dequant_operand_kernel(const void *__restrict__ wq,
+                                       const float *__restrict__ scale, int64_t rows,
+                                       int64_t in_dim, void *__restrict__ out, const Lut16 lut) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t n = rows * in_dim;
+    if (i >= n) return;
+    const int64_t r = i / in_dim, j = i - r * in_dim;
+    const float s = scale[r];
+    float w;
+    if (SCHEME == MB2_Q_INT8) {
+        w = (float)static_cast<const int8_t *>(wq)[i] * s;
+    } else {
+        const int64_t pcols = (in_dim + 1) >> 1;
+        const uint8_t byte = static_cast<const uint8_t *>(wq)[r * pcols + (j >> 1)];
+        const int nib = (j & 1) ? (byte & 0x0F) : (byte >> 4);
+        w = SCHEME == MB2_Q_INT4 ? (float)(nib - 7) * s : lut.v[nib] * s;
+    }
+    if (BF16) {
+        static_cast<__nv_bfloat16 *>(out)[i] = __float2bfloat16_rn(w);
+    } else {
+        const float hi = tf32_round(w);
+        static_cast<float *>(out)[i] = hi;
+        static_cast<float *>(out)[n + i] = tf32_round(w - hi);
+    }
+}
+
+size_t dequant_operand_bytes(int dtype, int64_t rows, int64_t in_dim) {
+    return (size_t)rows * in_dim * (dtype == MB2_BF16 ? 2 : 8);
+}
+
+int dequant_operand(int dtype, int scheme, const void *wq, const float *scale, int64_t rows,
+                    int64_t in_dim, void *out, cudaStream_t st) {
+    const int64_t n = rows * in_dim;
+    if (n == 0) return MB2_OK;
+    Lut16 lut;
+    nf4_lut(lut.v);
+    const unsigned grid = (unsigned)ceil_div(n, (int64_t)256);
+    const bool bf = dtype == MB2_BF16;
+#define MB2_DQ(S)                                                                              \
+    (bf ? (dequant_operand_kernel<S, true><<<grid, 256, 0, st>>>(wq, scale, rows, in_dim, out, lut), 0) \
+        : (dequant_operand_kernel<S, false><<<grid, 256, 0, st>>>(wq, scale, rows, in_dim, out, lut), 0))
+    switch (scheme) {
+        case MB2_Q_INT8: MB2_DQ(MB2_Q_INT8); break;
+        case MB2_Q_INT4: MB2_DQ(MB2_Q_INT4); break;
+        case MB2_Q_NF4: MB2_DQ(MB2_Q_NF4); break;
+        default: return fail(MB2_ERR_ARG, "unknown scheme %d", scheme);
+    }
+#undef MB2_DQ
+    return check_launch("dequant_operand_kernel");
 }
 
 }  // namespace mb2

@@ -117,10 +117,13 @@ class CPUMamba(nn.Module):
             d.scale = scale.data_ptr()
             d.scheme = _lib.SCHEMES[mod.scheme]
             if name == "dt_proj":
-                # the fused scan reads dt_proj's rows densely: pass deq(W)
+                # dt_proj runs densely (the tensor-core dt GEMM, or W_dt's rows
+                # in the fused scan): pass deq(W) and, in fp32, its TF32 halves
                 dense = mod.dense_weight(self._param_dtype())
                 keep.append(dense)
                 d.weight = dense.data_ptr()
+                if dense.dtype == torch.float32:
+                    d.weight_split = self._tf32_split("dt_proj_deq", dense).data_ptr()
         elif isinstance(mod, nn.Linear):
             w = mod.weight
             if not w.is_contiguous():

@@ -101,3 +101,38 @@ def test_quantized_step_matches_oracle():
             y_ref, st_ref = oracle.block_step(pq, x, st_ref, quant)
             assert (y.cpu() - y_ref).abs().max().item() <= TOL
         assert (st["h"].cpu() - st_ref["h"]).abs().max().item() <= TOL
+
+
+@pytest.mark.parametrize("scheme", ["int8", "int4", "nf4"])
+def test_quantized_block_many_rows_on_tensor_cores(scheme):
+    """400 rows: each quantised projection is dequantised into the workspace
+    (bit-exact values) and run on the tensor cores; matches the oracle's
+    QuantizedLinear composition within the fp32 bar."""
+    p = oracle.make_block_params(64, 16, seed=41, weight_std=0.02, outlier_frac=0.01)
+    m = CPUMamba(64, 16).eval()
+    m.load_state_dict(p, strict=True)
+    m = m.cuda()
+    quantize_block(m, QuantConfig(scheme))
+    pq = {k: v.cpu() for k, v in m.state_dict().items()}
+    quant = {n: (scheme, getattr(m, n).in_features) for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
+    x = torch.randn(2, 200, 64, generator=torch.Generator().manual_seed(42))
+    y_ref = oracle.block_forward(pq, x, quant=quant)
+    with torch.no_grad():
+        y = m(x.cuda()).cpu()
+    assert (y - y_ref).abs().max().item() <= TOL
+
+
+def test_quantized_block_many_rows_bf16():
+    p = oracle.make_block_params(64, 16, seed=43, weight_std=0.02, outlier_frac=0.01)
+    m = CPUMamba(64, 16).eval()
+    m.load_state_dict(p, strict=True)
+    m = m.cuda().to(torch.bfloat16)
+    quantize_block(m, QuantConfig("int8"))
+    pq = {k: v.cpu().float() if v.is_floating_point() else v.cpu() for k, v in m.state_dict().items()}
+    quant = {n: ("int8", getattr(m, n).in_features) for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
+    x = torch.randn(2, 200, 64, generator=torch.Generator().manual_seed(44))
+    y_ref = oracle.block_forward(pq, x, quant=quant)
+    with torch.no_grad():
+        y = m(x.cuda().to(torch.bfloat16)).float().cpu()
+    rel = ((y - y_ref).abs() / (y_ref.abs().clamp(min=1e-3) + 1e-6)).mean().item()
+    assert rel <= 2e-2
