@@ -75,8 +75,13 @@ def dist_env():
 
 
 class ClockSampler:
-    """nvidia-smi samples (200 ms) of the GPU's clocks during the timed region."""
+    """nvidia-smi samples (every 25 ms) of the GPU's clocks and throttle
+    reasons.  Started before the warm-up so that it is already sampling when
+    the timed region begins; summary() keeps the samples whose arrival time
+    lies in the timed region (widened by one interval on each side, so that a
+    region shorter than the interval still has its nearest samples)."""
 
+    PERIOD_MS = 25
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -88,12 +93,13 @@ class ClockSampler:
             self.index = str(device.index or 0)
         self.proc = None
         self.lines = []
+        self.t0 = self.t1 = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", str(self.PERIOD_MS)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -103,9 +109,15 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.perf_counter(), line.strip()))
 
-    def __exit__(self, *exc):
+    def begin(self):
+        self.t0 = time.perf_counter()
+
+    def end(self):
+        self.t1 = time.perf_counter()
+
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -116,7 +128,10 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        pad = self.PERIOD_MS / 1e3
+        for t, ln in list(self.lines):
+            if self.t0 is None or self.t1 is None or not (self.t0 - pad <= t <= self.t1 + pad):
+                continue
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -131,7 +146,7 @@ class ClockSampler:
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "period_ms": self.PERIOD_MS}
 
 
 def make_params(cfg, seed):
@@ -236,18 +251,21 @@ def run_ours(args, cfg):
             return m(xs[i % nbuf])
 
     stream = torch.cuda.current_stream(dev)
+    clk = ClockSampler(dev).start()          # sampling before the timed region starts
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
     dist.barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev) as clk:
-        e0.record(stream)
-        for i in range(args.steps):
-            step(i)
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
+    clk.begin()
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clk.end()
+    clk.stop()
     dist.barrier()
     ms = dist.max_over_ranks(e0.elapsed_time(e1), dev)      # the slowest rank's time
     tokens_per_step = B * (1 if step_mode else T)
@@ -368,14 +386,16 @@ def profile_stages(m, x, cfg, dtype, steps):
 
 # DRAM bytes (read + write) per token of each launch, from ncu captures of the
 # config-0 shapes at batch 64 (profiles/gemm_tc_f32x3_b64_t180.md,
-# profiles/scan_fused_f32_b64_t180.md, profiles/conv1d_silu_f32_b64_t180.md);
+# profiles/scan_gated_f32_b64_t180.md, profiles/conv1d_silu_f32_b64_t180.md);
 # every tensor these kernels touch grows with the token count, so a full-size
-# launch moves (bytes per token) x N.
+# launch moves (bytes per token) x N.  (dt_proj's output mostly stays in L2
+# at batch 64, so its figure under-counts a full-size launch.)
 TRAFFIC_PER_TOKEN = {
-    ("f32", 768, 24, "in_proj"): (54.325248e6 + 98.165504e6) / 11520,
-    ("f32", 768, 24, "x_proj"): (72.015104e6 + 1.871104e6) / 11520,
-    ("f32", 768, 24, "out_proj"): (80.273664e6 + 12.322816e6) / 11520,
-    ("f32", 768, 24, "scan"): (146.500096e6 + 33.24544e6) / 11520,
+    ("f32", 768, 24, "in_proj"): (54.38208e6 + 96.968192e6) / 11520,
+    ("f32", 768, 24, "x_proj"): (71.99104e6 + 1.200896e6) / 11520,
+    ("f32", 768, 24, "dt_proj"): (4.326656e6 + 15.051264e6) / 11520,
+    ("f32", 768, 24, "out_proj"): (80.250624e6 + 14.976e6) / 11520,
+    ("f32", 768, 24, "scan"): (215.583232e6 + 42.584064e6) / 11520,
     ("f32", 768, 24, "conv1d_silu"): (71.217152e6 + 26.989824e6) / 11520,
 }
 
@@ -538,7 +558,7 @@ def run_reference(args, cfg):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=0, choices=sorted(CONFIGS))

@@ -392,10 +392,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 const int s = g % C::STAGES;
                 const uint32_t ph = (g / C::STAGES) & 1;
                 const int l = g % C::LO;
+                // split as soon as the tile has landed; wait for the TMEM slot
+                // (freed when the MMAs of k-block g - LO complete) only before
+                // storing into it
                 bool w = mbar_wait(full(s), ph, 5);
-                w = w && mbar_wait(a_empty(l), ((g / C::LO) & 1) ^ 1, 7);
-                if (!__all_sync(0xffffffffu, w)) { ok = false; break; }  // tcgen05.st is warp-wide
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
                 // this thread's row of the 128B-swizzled A tile: logical 16-byte
                 // chunk c sits at physical chunk c ^ (row & 7)
                 const uint8_t *arow = gbase + (tile(s, 0) - base) + row * 128;
@@ -411,6 +412,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         lo[4 * c + e] = __float_as_uint(tf32_rn(a[e] - h));
                     }
                 }
+                w = mbar_wait(a_empty(l), ((g / C::LO) & 1) ^ 1, 7);
+                if (!__all_sync(0xffffffffu, w)) { ok = false; break; }  // tcgen05.st is warp-wide
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + C::A_COL + l * 64;
                 tmem_st32(ta, hi);
                 tmem_st32(ta + 32, lo);
