@@ -46,8 +46,8 @@ __device__ int g_mb2_device_error = 0;  // 0 = ok; else a code of where a wait e
 
 namespace tc {
 
-constexpr int BM = 128, BN = 128;
-constexpr int TILE_BYTES = 128 * 128;   // one operand tile: 128 rows x 128 B
+constexpr int BM = 128;
+constexpr int TILE_BYTES = 128 * 128;   // 128 operand rows x 128 B
 constexpr uint64_t WAIT_NS = 2000000000ull;  // 2 s bound on any wait
 
 enum Mode { F32X3 = 0, BF16 = 1 };
@@ -56,41 +56,51 @@ template <int MODE> struct Cfg;
 // F32X3: 3-deep TMA ring of (A raw, W_hi, W_lo) tiles; the split A (hi, lo)
 // lives in two TMEM slots of 64 columns next to the three accumulators.
 template <> struct Cfg<F32X3> {
+    static constexpr int BN = 128;            // tile columns (MMA N)
     static constexpr int STAGES = 3;
-    static constexpr int TILES = 3;           // A raw, B_hi, B_lo
     static constexpr int LO = 2;              // TMEM slots for the split A
     static constexpr int BK = 32;             // fp32 elements per 128 B row
     static constexpr int KSTEP = 8;           // K per tf32 MMA
-    static constexpr uint32_t TX = 3 * TILE_BYTES;  // bytes by TMA per stage
+    static constexpr uint32_t STAGE_BYTES = (BM + 2 * BN) * 128;  // A raw | W_hi | W_lo
+    static constexpr uint32_t TX = STAGE_BYTES;  // bytes by TMA per stage
     static constexpr int NACC = 1;            // accumulator sets (3 x BN columns)
     static constexpr int ACC_COLS = 3 * BN;
     static constexpr int TMEM_COLS = 512;
     static constexpr int A_COL = 3 * BN;      // split-A slot l at 384 + 64 l (hi), +32 (lo)
     static constexpr int WARPS = 10;
     static constexpr int EPI0 = 6;            // first epilogue warp
+    static constexpr int SPLIT = 1;           // output staged in one piece
 };
-// BF16: 5-deep ring of (A, W) tiles, two accumulators so the MMAs of the next
-// tile overlap the epilogue of the previous one.
+// BF16: 128 x 256 tiles (N = 256 MMAs: the 128-wide ones ran the tensor pipe
+// at about half its rate), 4-deep ring of (A, W) tiles, two 256-column
+// accumulators (all 512 TMEM columns) so the MMAs of the next tile overlap the
+// epilogue of the previous one; the output is staged in two column halves.
 template <> struct Cfg<BF16> {
-    static constexpr int STAGES = 5;
-    static constexpr int TILES = 2;           // A, B
+    static constexpr int BN = 256;
+    static constexpr int STAGES = 4;
     static constexpr int LO = 1;              // (no split A; one unused barrier)
     static constexpr int BK = 64;
     static constexpr int KSTEP = 16;
-    static constexpr uint32_t TX = 2 * TILE_BYTES;
+    static constexpr uint32_t STAGE_BYTES = (BM + BN) * 128;       // A | W
+    static constexpr uint32_t TX = STAGE_BYTES;
     static constexpr int NACC = 2;
     static constexpr int ACC_COLS = BN;
-    static constexpr int TMEM_COLS = 256;
+    static constexpr int TMEM_COLS = 512;
     static constexpr int A_COL = 0;
     static constexpr int WARPS = 6;
     static constexpr int EPI0 = 2;
+    static constexpr int SPLIT = 2;
 };
 
-// shared memory: ring | output staging (BM x BN of TO) | barriers
+// shared memory: ring | output staging (BM x BN/SPLIT of TO) | barriers
+template <int MODE, typename TO>
+__host__ __device__ constexpr size_t staging_bytes() {
+    return (size_t)BM * (Cfg<MODE>::BN / Cfg<MODE>::SPLIT) * sizeof(TO);
+}
 template <int MODE, typename TO>
 constexpr size_t smem_bytes() {
-    return 1024 /*align slack*/ + (size_t)Cfg<MODE>::STAGES * Cfg<MODE>::TILES * TILE_BYTES +
-           (size_t)BM * BN * sizeof(TO) + 256;
+    return 1024 /*align slack*/ + (size_t)Cfg<MODE>::STAGES * Cfg<MODE>::STAGE_BYTES +
+           staging_bytes<MODE, TO>() + 256;
 }
 
 struct Params {
@@ -168,7 +178,7 @@ __host__ __device__ constexpr uint32_t instr_desc() {
     // D fmt F32 (bits 4-5 = 1); A/B fmt (bits 7-9, 10-12): TF32 = 2, BF16 = 1;
     // K-major A and B; N >> 3 at bits 17-22; M >> 4 at bits 24-28.
     constexpr uint32_t fmt = MODE == F32X3 ? 2u : 1u;
-    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(Cfg<MODE>::BN >> 3) << 17) |
            ((uint32_t)(BM >> 4) << 24);
 }
 
@@ -262,12 +272,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                const __grid_constant__ CUtensorMap map_b1, const __grid_constant__ CUtensorMap map_y,
                const Params p) {
     using C = Cfg<MODE>;
+    constexpr int BN = C::BN;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *gbase = smem_raw + (base - raw);
-    const uint32_t out_base = base + C::STAGES * C::TILES * TILE_BYTES;   // 1024-aligned
-    const uint32_t bars = out_base + BM * BN * (uint32_t)sizeof(TO);
+    const uint32_t out_base = base + C::STAGES * C::STAGE_BYTES;   // 1024-aligned
+    const uint32_t bars = out_base + (uint32_t)staging_bytes<MODE, TO>();
     // barriers: full[S] empty[S] xform[S] a_empty[LO] acc_full[NACC] acc_empty[NACC]; tmem slot
     auto full = [&](int s) { return bars + 8u * s; };
     auto empty = [&](int s) { return bars + 8u * (C::STAGES + s); };
@@ -277,7 +288,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     auto acc_empty = [&](int b) { return bars + 8u * (3 * C::STAGES + C::LO + C::NACC + b); };
     const uint32_t tmem_slot = bars + 8u * (3 * C::STAGES + C::LO + 2 * C::NACC);
     uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(gbase + (tmem_slot - base));
-    auto tile = [&](int s, int t) { return base + (uint32_t)((s * C::TILES + t) * TILE_BYTES); };
+    // stage s: A (BM rows) | W (BN rows) [| W_lo (BN rows)], each 128 B per row
+    auto tile = [&](int s, int t) {
+        return base + (uint32_t)(s * C::STAGE_BYTES) +
+               (t == 0 ? 0u : (uint32_t)(TILE_BYTES + (t - 1) * BN * 128));
+    };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -428,11 +443,47 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const int q = warp & 3;                 // TMEM lane quarter this warp may read
         constexpr int VEC = 16 / (int)sizeof(TO);     // outputs per 16-byte chunk
         constexpr int BOXC = 128 / (int)sizeof(TO);   // columns per 128-byte staging row
-        // this warp's staging: BN / BOXC boxes of 32 rows x 128 B, 128B-swizzled
-        const uint32_t wst = out_base + (uint32_t)(q * 32 * BN * sizeof(TO));
+        constexpr int HCOLS = BN / C::SPLIT;          // columns staged at a time
+        constexpr int CBH = HCOLS / 32;               // 32-column blocks per staged part
+        // this warp's staging: HCOLS / BOXC boxes of 32 rows x 128 B, 128B-swizzled
+        const uint32_t wst = out_base + (uint32_t)(q * 32 * HCOLS * sizeof(TO));
         uint8_t *wst_g = gbase + (wst - base);
         TO *Y = static_cast<TO *>(p.y);
         const TO *bias = static_cast<const TO *>(p.bias);
+        // write staged part `part` (columns part * HCOLS ...) of this warp's 32 rows
+        auto flush = [&](int part, int64_t m0, int64_t n0) {
+            const int64_t c0 = (int64_t)part * HCOLS;
+            if (p.tma_store) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+#pragma unroll
+                    for (int bx = 0; bx < HCOLS / BOXC; ++bx)
+                        tma_store_2d(&map_y, wst + bx * 32 * 128, (int32_t)(n0 + c0 + bx * BOXC),
+                                     (int32_t)(m0 + q * 32));
+                    bulk_commit();
+                }
+            } else {
+                // plain stores with the column remap: row rr of this warp's slab
+                __syncwarp();
+                for (int rr = 0; rr < 32; ++rr) {
+                    const int64_t m = m0 + q * 32 + rr;
+                    if (m >= p.M) break;
+#pragma unroll
+                    for (int c4 = 0; c4 < CBH; ++c4) {
+                        const int col = c4 * 32 + lane;
+                        const int64_t n = n0 + c0 + col;
+                        if (n >= p.N) continue;
+                        const int box = col / BOXC, ce = col % BOXC;
+                        const uint8_t *src = wst_g + box * (32 * 128) + rr * 128 +
+                                             (((ce / VEC) ^ (rr & 7)) << 4) + (ce % VEC) * sizeof(TO);
+                        const int64_t dst = n + (n >= p.n1 ? p.off1 : 0) + (n >= p.n2 ? p.off2 : 0);
+                        Y[m * p.ld_y + dst] = *reinterpret_cast<const TO *>(src);
+                    }
+                }
+                __syncwarp();
+            }
+        };
         int it = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
             const int64_t m0 = (int64_t)(t / num_n) * BM, n0 = (int64_t)(t % num_n) * BN;
@@ -448,11 +499,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             const bool row_ok = m_row < p.M;
             const float rscale = (p.row_scale && row_ok) ? p.row_scale[m_row] : 1.0f;
             const TO *rrow = static_cast<const TO *>(p.resid) + (row_ok ? m_row : 0) * p.ld_r;
-            // BF16: the whole 128-column accumulator in one round trip
             uint32_t ra[32], rb[32], rc[32];
-            static_assert(BN == 128, "epilogue assumes 4 column blocks");
 #pragma unroll 1
             for (int cb = 0; cb < BN / 32; ++cb) {
+                if (C::SPLIT > 1 && cb > 0 && cb % CBH == 0) {
+                    // staging full: store the finished part, then reuse the buffer
+                    flush(cb / CBH - 1, m0, n0);
+                    if (p.tma_store && lane == 0) bulk_wait_read0();
+                    __syncwarp();
+                }
                 float v[32];
                 if (MODE == F32X3) {
                     // the three accumulators of this 32-column block in one round trip
@@ -504,9 +559,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                         }
                     }
                 }
-                // row `lane` of box cb*32/BOXC: its 16-byte chunks at c ^ (row & 7)
-                const int box = (cb * 32) / BOXC;
-                const int col0 = (cb * 32) % BOXC;          // element offset in the box row
+                // row `lane` of box cbl*32/BOXC: its 16-byte chunks at c ^ (row & 7)
+                const int cbl = cb % CBH;
+                const int box = (cbl * 32) / BOXC;
+                const int col0 = (cbl * 32) % BOXC;         // element offset in the box row
                 uint8_t *rowp = wst_g + box * (32 * 128) + lane * 128;
 #pragma unroll
                 for (int c = 0; c < 32 / VEC; ++c) {
@@ -530,36 +586,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             // TMEM drained: the MMA warp may start the next tile in this buffer
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(acc_empty(b));
-            if (p.tma_store) {
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) {
-#pragma unroll
-                    for (int bx = 0; bx < BN / BOXC; ++bx)
-                        tma_store_2d(&map_y, wst + bx * 32 * 128, (int32_t)(n0 + bx * BOXC),
-                                     (int32_t)(m0 + q * 32));
-                    bulk_commit();
-                }
-            } else {
-                // plain stores with the column remap: row rr of this warp's slab
-                __syncwarp();
-                for (int rr = 0; rr < 32; ++rr) {
-                    const int64_t m = m0 + q * 32 + rr;
-                    if (m >= p.M) break;
-#pragma unroll
-                    for (int c4 = 0; c4 < BN / 32; ++c4) {
-                        const int col = c4 * 32 + lane;
-                        const int64_t n = n0 + col;
-                        if (n >= p.N) continue;
-                        const int box = col / BOXC, ce = col % BOXC;
-                        const uint8_t *src = wst_g + box * (32 * 128) + rr * 128 +
-                                             (((ce / VEC) ^ (rr & 7)) << 4) + (ce % VEC) * sizeof(TO);
-                        const int64_t dst = n + (n >= p.n1 ? p.off1 : 0) + (n >= p.n2 ? p.off2 : 0);
-                        Y[m * p.ld_y + dst] = *reinterpret_cast<const TO *>(src);
-                    }
-                }
-                __syncwarp();
-            }
+            flush(C::SPLIT - 1, m0, n0);
         }
         if (lane == 0) bulk_wait0();   // stores complete before the CTA exits
     }
@@ -611,7 +638,7 @@ static int launch_tc(const CUtensorMap &a, const CUtensorMap &b0, const CUtensor
         cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
         if (g_num_sms <= 0) g_num_sms = 148;
     }
-    const int64_t tiles = ceil_div(p.M, tc::BM) * ceil_div(p.N, tc::BN);
+    const int64_t tiles = ceil_div(p.M, (int64_t)tc::BM) * ceil_div(p.N, (int64_t)tc::Cfg<MODE>::BN);
     const unsigned grid = (unsigned)(tiles < g_num_sms ? tiles : g_num_sms);
     kern<<<grid, tc::Cfg<MODE>::WARPS * 32, smem, st>>>(a, b0, b1, ym, p);
     return check_launch("gemm_tc_kernel");
@@ -638,8 +665,9 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
     MB2_TRY(get_encode());
     CUtensorMap ma, mb0, mb1, my;
     MB2_TRY(make_map(&ma, x, M, K, ld_x, bf16, 128));
-    MB2_TRY(make_map(&mb0, b0, N, K, K, bf16, 128));
-    MB2_TRY(make_map(&mb1, b1, N, K, K, bf16, 128));
+    const int bn = bf16 ? tc::Cfg<tc::BF16>::BN : tc::Cfg<tc::F32X3>::BN;
+    MB2_TRY(make_map(&mb0, b0, N, K, K, bf16, bn));
+    MB2_TRY(make_map(&mb1, b1, N, K, K, bf16, bn));
     const bool remap = (n1 < N && off1 != 0) || (n2 < N && off2 != 0);
     const bool tma_store = !remap && aligned(y, 16) && (ld_y * es) % 16 == 0;
     if (tma_store) MB2_TRY(make_map(&my, y, M, N, ld_y, bf16, 32));
