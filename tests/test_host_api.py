@@ -125,3 +125,46 @@ def test_stack_state_dict_layout_and_slices():
         assert all(b[i][1] == b[i + 1][0] for i in range(n - 1))
     b = slice_bounds(151, 6, 0.5)
     assert b[0][1] - b[0][0] < b[2][1] - b[2][0]
+
+
+def test_surgery_stub_and_swap(monkeypatch):
+    """surgery.py's two routes: the mamba_ssm stub hands out this package's
+    block; the swap replaces foreign blocks and keeps their weights."""
+    import sys
+    import types
+
+    import torch.nn as nn
+
+    from cpu_mamba_b200 import surgery
+
+    monkeypatch.delitem(sys.modules, "mamba_ssm", raising=False)
+    surgery.install_mamba_ssm_stub()
+    from mamba_ssm import Mamba
+    assert Mamba is CPUMamba
+    assert surgery.swap_mamba_to_cpu is surgery.swap_mamba_to_b200
+    assert surgery.swap_mamba_to_b200(nn.Sequential(CPUMamba(32))) == 0   # nothing foreign
+
+    class ForeignMamba(nn.Module):
+        """Stands in for mamba_ssm.Mamba: same attributes and parameter names."""
+
+        def __init__(self, d_model, d_state=16, d_conv=4, expand=2):
+            super().__init__()
+            src = CPUMamba(d_model, d_state=d_state, d_conv=d_conv, expand=expand)
+            for k, v in src._modules.items():
+                self.add_module(k, v)
+            for k, v in src._parameters.items():
+                self.register_parameter(k, v)
+            self.d_model, self.d_state, self.d_conv, self.expand = d_model, d_state, d_conv, expand
+
+    fake = types.ModuleType("mamba_ssm")
+    fake.Mamba = ForeignMamba
+    monkeypatch.setitem(sys.modules, "mamba_ssm", fake)
+    model = nn.Sequential(ForeignMamba(32, d_state=8), nn.Linear(32, 32),
+                          nn.ModuleList([ForeignMamba(32).eval()]))
+    before = {k: v.clone() for k, v in model.state_dict().items()}
+    assert surgery.swap_mamba_to_b200(model) == 2
+    assert isinstance(model[0], CPUMamba) and isinstance(model[2][0], CPUMamba)
+    assert model[0].d_state == 8 and not model[2][0].training
+    after = model.state_dict()
+    assert set(after) == set(before)
+    assert all(torch.equal(after[k], before[k]) for k in before)
