@@ -35,7 +35,8 @@ class MambaB200Error(RuntimeError):
 
 class LinearW(ctypes.Structure):
     _fields_ = [("weight", _vp), ("weight_split", _vp), ("weight_q", _vp),
-                ("scale", _vp), ("bias", _vp), ("scheme", ctypes.c_int)]
+                ("scale", _vp), ("bias", _vp), ("scheme", ctypes.c_int),
+                ("group_size", _c_i64)]
 
 
 class Block(ctypes.Structure):
@@ -67,6 +68,13 @@ _SIGS = {
     "mb2_dequantize": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _c_i64, _c_i64, _vp, _vp]),
     "mb2_qlinear": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _vp, _c_i64, _vp, _vp, _vp,
                                    _vp, _c_i64, _c_i64, _c_i64, _c_i64, ctypes.c_int, _vp]),
+    "mb2_quantize_grouped": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp,
+                                            _vp]),
+    "mb2_dequantize_grouped": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _c_i64, _c_i64, _c_i64,
+                                              _vp, _vp]),
+    "mb2_qlinear_grouped": (ctypes.c_int, [ctypes.c_int, _c_i64, ctypes.c_int, _vp, _c_i64, _vp,
+                                           _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64,
+                                           ctypes.c_int, _vp]),
     "mb2_block_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Block), _c_i64, _c_i64]),
     "mb2_block_forward": (ctypes.c_int, [ctypes.POINTER(Block), _vp, _vp, _c_i64, _c_i64,
                                          _vp, _vp, _vp, ctypes.c_size_t, _vp]),

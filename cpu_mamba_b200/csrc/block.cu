@@ -30,7 +30,8 @@ int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, vo
         // dequantises tile by tile in its loader
         if (M >= 256 && ex.scratch &&
             ex.scratch_bytes >= dequant_operand_bytes(dtype, N, K)) {
-            MB2_TRY(dequant_operand(dtype, L.scheme, L.weight_q, L.scale, N, K, ex.scratch, st));
+            MB2_TRY(dequant_operand(dtype, L.scheme, L.weight_q, L.scale, N, K, L.group_size,
+                                    ex.scratch, st));
             const bool bf = dtype == MB2_BF16;
             bool used = false;
             EpiExtra ex2 = ex;
@@ -42,7 +43,7 @@ int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, vo
             if (used) return MB2_OK;
         }
         return gemm_simt(dtype, L.scheme, x, ld_x, L.weight_q, L.scale, L.bias, y, ld_y, M, N, K,
-                         n1, off1, n2, off2, epi, st, ex);
+                         n1, off1, n2, off2, epi, st, ex, L.group_size);
     }
     MB2_REQUIRE(L.weight, MB2_ERR_ARG, "linear: null weight");
     bool used = false;
@@ -183,10 +184,10 @@ extern "C" int mb2_linear(int dtype, const void *x, int64_t ld_x, const void *w,
     return linear_any(dtype, L, x, ld_x, y, ld_y, M, N, K, epilogue, (cudaStream_t)stream);
 }
 
-extern "C" int mb2_qlinear(int scheme, int dtype, const void *x, int64_t ld_x,
-                           const void *weight_q, const float *scale, const void *bias, void *y,
-                           int64_t ld_y, int64_t M, int64_t N, int64_t K, int epilogue,
-                           mb2_stream_t stream) {
+static int qlinear_any(int scheme, int64_t group, int dtype, const void *x, int64_t ld_x,
+                       const void *weight_q, const float *scale, const void *bias, void *y,
+                       int64_t ld_y, int64_t M, int64_t N, int64_t K, int epilogue,
+                       mb2_stream_t stream) {
     MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "qlinear: bad dtype");
     MB2_REQUIRE(scheme == MB2_Q_INT8 || scheme == MB2_Q_INT4 || scheme == MB2_Q_NF4, MB2_ERR_ARG,
                 "unknown scheme %d", scheme);
@@ -194,7 +195,23 @@ extern "C" int mb2_qlinear(int scheme, int dtype, const void *x, int64_t ld_x,
     MB2_REQUIRE(epilogue == MB2_EPI_NONE || epilogue == MB2_EPI_SOFTPLUS, MB2_ERR_ARG,
                 "qlinear: bad epilogue");
     return gemm_simt(dtype, scheme, x, ld_x, weight_q, scale, bias, y, ld_y, M, N, K, N, 0, N, 0,
-                     epilogue, (cudaStream_t)stream);
+                     epilogue, (cudaStream_t)stream, EpiExtra{}, group);
+}
+
+extern "C" int mb2_qlinear(int scheme, int dtype, const void *x, int64_t ld_x,
+                           const void *weight_q, const float *scale, const void *bias, void *y,
+                           int64_t ld_y, int64_t M, int64_t N, int64_t K, int epilogue,
+                           mb2_stream_t stream) {
+    return qlinear_any(scheme, 0, dtype, x, ld_x, weight_q, scale, bias, y, ld_y, M, N, K,
+                       epilogue, stream);
+}
+
+extern "C" int mb2_qlinear_grouped(int scheme, int64_t group_size, int dtype, const void *x,
+                                   int64_t ld_x, const void *weight_q, const float *scale,
+                                   const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N,
+                                   int64_t K, int epilogue, mb2_stream_t stream) {
+    return qlinear_any(scheme, group_size, dtype, x, ld_x, weight_q, scale, bias, y, ld_y, M, N,
+                       K, epilogue, stream);
 }
 
 // The five launches of one block forward over N = batch * seqlen rows.

@@ -35,4 +35,4 @@ int check_launch(const char *what) {
 
 extern "C" const char *mb2_last_error(void) { return mb2::g_last_error.c_str(); }
 
-extern "C" int mb2_version(void) { return 1; }
+extern "C" int mb2_version(void) { return 2; }

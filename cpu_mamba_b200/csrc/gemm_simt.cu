@@ -27,7 +27,8 @@ enum BMode { BM_DENSE = 0, BM_INT8 = 1, BM_INT4 = 2, BM_NF4 = 3 };
 struct GemmArgs {
     const void *x; int64_t ld_x;
     const void *w;                 // dense W (N, K) or codes
-    const float *scale;            // per-row scale (quantised)
+    const float *scale;            // scale per row, or per (row, group) (quantised)
+    int64_t group, ngroups;        // columns per scale group (0: one scale per row)
     const void *bias;
     void *y; int64_t ld_y;
     int64_t M, N, K;
@@ -70,7 +71,7 @@ void nf4_lut(float *out16) {
 template <typename T, int MODE>
 __device__ __forceinline__ float load_w(const GemmArgs &a, int64_t n, int64_t k) {
     if (MODE == BM_DENSE) return io<T>::to_f(static_cast<const T *>(a.w)[n * a.K + k]);
-    const float s = a.scale[n];
+    const float s = a.group ? a.scale[n * a.ngroups + k / a.group] : a.scale[n];
     if (MODE == BM_INT8) {
         const int8_t q = static_cast<const int8_t *>(a.w)[n * a.K + k];
         return io<T>::round((float)q * s);
@@ -315,8 +316,9 @@ static int launch_simt(GemmArgs a, const EpiExtra &ex, cudaStream_t st) {
 int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
               const float *scale, const void *bias, void *y, int64_t ld_y, int64_t M,
               int64_t N, int64_t K, int64_t n1, int64_t off1, int64_t n2, int64_t off2,
-              int epi, cudaStream_t st, const EpiExtra &ex) {
+              int epi, cudaStream_t st, const EpiExtra &ex, int64_t group) {
     MB2_REQUIRE(M >= 0 && N >= 0 && K >= 0, MB2_ERR_SHAPE, "linear: negative size");
+    MB2_REQUIRE(group >= 0, MB2_ERR_ARG, "linear: negative group size");
     MB2_REQUIRE(ceil_div(M, (int64_t)64) <= 65535, MB2_ERR_SHAPE, "linear: M too large");
     if (M == 0 || N == 0) return MB2_OK;
     MB2_REQUIRE(x && w && y, MB2_ERR_ARG, "linear: null pointer");
@@ -325,7 +327,8 @@ int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
     // 4-element groups of x rows (and of dense W rows) as single loads
     const int vec = K % 4 == 0 && ld_x % 4 == 0 && aligned(x, 4 * es) &&
                     (scheme != MB2_Q_NONE || aligned(w, 4 * es));
-    GemmArgs a{x, ld_x, w, scale, bias, y, ld_y, M, N, K, n1, n2, off1, off2, epi, {},
+    GemmArgs a{x, ld_x, w, scale, group, group ? ceil_div(K, group) : 1, bias, y, ld_y, M, N, K,
+               n1, n2, off1, off2, epi, {},
                ex.row_scale, ex.resid, ex.ld_r, nullptr, K, vec};
     nf4_lut(a.lut);
     const bool f32 = dtype == MB2_F32;

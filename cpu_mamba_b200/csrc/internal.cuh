@@ -27,7 +27,7 @@ struct EpiExtra {
 int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
               const float *scale, const void *bias, void *y, int64_t ld_y, int64_t M,
               int64_t N, int64_t K, int64_t n1, int64_t off1, int64_t n2, int64_t off2,
-              int epi, cudaStream_t st, const EpiExtra &ex = EpiExtra{});
+              int epi, cudaStream_t st, const EpiExtra &ex = EpiExtra{}, int64_t group = 0);
 int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *w_split,
             const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
             int64_t n1, int64_t off1, int64_t n2, int64_t off2, int epi, cudaStream_t st,
@@ -62,7 +62,7 @@ int scan_step(int dtype, const void *xc, int64_t ld_x, const void *dt_pre, int64
 // values; fp32: TF32 hi / lo planes, bf16: rounded) and its size in bytes.
 size_t dequant_operand_bytes(int dtype, int64_t rows, int64_t in_dim);
 int dequant_operand(int dtype, int scheme, const void *wq, const float *scale, int64_t rows,
-                    int64_t in_dim, void *out, cudaStream_t st);
+                    int64_t in_dim, int64_t group, void *out, cudaStream_t st);
 
 // Dense or quantised linear y = x W^T (+ bias, + extras): the tensor-core
 // kernel where it applies, the CUDA-core kernel otherwise.  n1/off1/n2/off2

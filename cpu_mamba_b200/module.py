@@ -116,6 +116,7 @@ class CPUMamba(nn.Module):
             keep.append(scale)
             d.scale = scale.data_ptr()
             d.scheme = _lib.SCHEMES[mod.scheme]
+            d.group_size = mod.group_size or 0
             if name == "dt_proj":
                 # dt_proj runs densely (the tensor-core dt GEMM, or W_dt's rows
                 # in the fused scan): pass deq(W) and, in fp32, its TF32 halves

@@ -162,8 +162,11 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
     return y if out is not None else y.reshape(*lead, N)
 
 
-def quantize(scheme: str, w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, int]:
-    """(weight_q, scale, in_dim) with quant.py's exact codes, on the GPU."""
+def quantize(scheme: str, w: torch.Tensor, group_size: Optional[int] = None
+             ) -> Tuple[torch.Tensor, torch.Tensor, int]:
+    """(weight_q, scale, in_dim) with quant.py's exact codes, on the GPU.
+    group_size: None for quant.py's one scale per row, or the number of input
+    columns per scale (blockwise; scale is then (rows, ceil(cols / group)))."""
     require_cuda(w, what="quantize")
     w = w.detach().to(torch.float32).contiguous()
     rows, cols = w.shape
@@ -171,25 +174,32 @@ def quantize(scheme: str, w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor, 
         q = torch.empty(rows, cols, device=w.device, dtype=torch.int8)
     else:
         q = torch.empty(rows, (cols + 1) // 2, device=w.device, dtype=torch.uint8)
-    s = torch.empty(rows, device=w.device, dtype=torch.float32)
-    check(lib().mb2_quantize(_lib.SCHEMES[scheme], ptr(w), rows, cols, ptr(q), ptr(s),
-                             stream_of(w)), f"quantize_{scheme}")
+    if group_size:
+        s = torch.empty(rows, -(-cols // group_size), device=w.device, dtype=torch.float32)
+        check(lib().mb2_quantize_grouped(_lib.SCHEMES[scheme], ptr(w), rows, cols, group_size,
+                                         ptr(q), ptr(s), stream_of(w)), f"quantize_{scheme}")
+    else:
+        s = torch.empty(rows, device=w.device, dtype=torch.float32)
+        check(lib().mb2_quantize(_lib.SCHEMES[scheme], ptr(w), rows, cols, ptr(q), ptr(s),
+                                 stream_of(w)), f"quantize_{scheme}")
     return q, s, cols
 
 
-def dequantize(scheme: str, weight_q: torch.Tensor, scale: torch.Tensor, in_dim: int) -> torch.Tensor:
+def dequantize(scheme: str, weight_q: torch.Tensor, scale: torch.Tensor, in_dim: int,
+               group_size: Optional[int] = None) -> torch.Tensor:
     require_cuda(weight_q, scale, what="dequantize")
     weight_q = weight_q.contiguous()
     scale = scale.to(torch.float32).contiguous()
     out = torch.empty(weight_q.shape[0], in_dim, device=weight_q.device, dtype=torch.float32)
-    check(lib().mb2_dequantize(_lib.SCHEMES[scheme], ptr(weight_q), ptr(scale),
-                               weight_q.shape[0], in_dim, ptr(out), stream_of(weight_q)),
-          f"dequantize_{scheme}")
+    check(lib().mb2_dequantize_grouped(_lib.SCHEMES[scheme], ptr(weight_q), ptr(scale),
+                                       weight_q.shape[0], in_dim, group_size or 0, ptr(out),
+                                       stream_of(weight_q)), f"dequantize_{scheme}")
     return out
 
 
 def qlinear(x: torch.Tensor, scheme: str, weight_q: torch.Tensor, scale: torch.Tensor,
-            bias: Optional[torch.Tensor], in_features: int, softplus: bool = False) -> torch.Tensor:
+            bias: Optional[torch.Tensor], in_features: int, softplus: bool = False,
+            group_size: Optional[int] = None) -> torch.Tensor:
     """QuantizedLinear.forward: y = x deq(W)^T + b with W dequantised in-kernel."""
     require_cuda(x, weight_q, scale, bias, what="qlinear")
     N = weight_q.shape[0]
@@ -199,9 +209,9 @@ def qlinear(x: torch.Tensor, scheme: str, weight_q: torch.Tensor, scale: torch.T
         x2 = x2.contiguous()
     y = torch.empty(x2.shape[0], N, device=x.device, dtype=x.dtype)
     weight_q, scale = weight_q.contiguous(), scale.to(torch.float32).contiguous()
-    check(lib().mb2_qlinear(_lib.SCHEMES[scheme], dtype_code(x.dtype), ptr(x2), x2.stride(0),
-                            ptr(weight_q), ptr(scale), ptr(bias), ptr(y),
-                            N, x2.shape[0], N, in_features,
+    check(lib().mb2_qlinear_grouped(_lib.SCHEMES[scheme], group_size or 0, dtype_code(x.dtype),
+                                    ptr(x2), x2.stride(0), ptr(weight_q), ptr(scale), ptr(bias),
+                                    ptr(y), N, x2.shape[0], N, in_features,
                             _lib.EPI_SOFTPLUS if softplus else _lib.EPI_NONE, stream_of(x)),
           f"qlinear_{scheme}")
     return y.reshape(*lead, N)

@@ -32,12 +32,26 @@ _NF4_LUT_VALUES = (
 
 @dataclass
 class QuantConfig:
-    """quant.py:47-53."""
+    """quant.py:47-53, plus ``group_size``: None keeps the reference's one scale
+    per output channel; an integer (e.g. 64) quantises blockwise, one scale per
+    run of that many input columns (the reference's roadmap item "blockwise
+    NF4 (group_size=64)", README.md:115, :201)."""
     scheme: str = "int8"  # "int8" | "int4" | "nf4"
+    group_size: Optional[int] = None
 
     def __post_init__(self):
         if self.scheme not in ("int8", "int4", "nf4"):
             raise ValueError(f"unknown scheme {self.scheme!r}")
+        _check_group(self.scheme, self.group_size)
+
+
+def _check_group(scheme, group_size):
+    if group_size is None:
+        return
+    if not isinstance(group_size, int) or group_size < 1:
+        raise ValueError(f"group_size must be a positive int or None, got {group_size!r}")
+    if scheme != "int8" and group_size % 2:
+        raise ValueError("4-bit schemes pack column pairs: group_size must be even")
 
 
 def _on_gpu(t: torch.Tensor) -> torch.Tensor:
@@ -48,14 +62,14 @@ def _on_gpu(t: torch.Tensor) -> torch.Tensor:
     return t.to("cuda")
 
 
-def _quant(scheme, weight):
+def _quant(scheme, weight, group_size=None):
     w = _on_gpu(weight.detach())
-    q, s, in_dim = ops.quantize(scheme, w)
+    q, s, in_dim = ops.quantize(scheme, w, group_size)
     return q.to(weight.device), s.to(weight.device), in_dim
 
 
-def _dequant(scheme, wq, scale, in_dim):
-    out = ops.dequantize(scheme, _on_gpu(wq), _on_gpu(scale), in_dim)
+def _dequant(scheme, wq, scale, in_dim, group_size=None):
+    out = ops.dequantize(scheme, _on_gpu(wq), _on_gpu(scale), in_dim, group_size)
     return out.to(wq.device)
 
 
@@ -91,18 +105,22 @@ class QuantizedLinear(nn.Module):
     """Drop-in for nn.Linear with weight-only quantisation (quant.py:141-194).
 
     Buffers: ``weight_q`` (int8, or uint8 packed pairs) and ``scale`` (out,)
-    float32; optional ``bias`` parameter.  ``scheme`` and ``_packed_in_dim``
-    are plain attributes, as in the reference.
+    float32 -- or (out, ceil(in / group_size)) when quantised blockwise;
+    optional ``bias`` parameter.  ``scheme``, ``group_size`` and
+    ``_packed_in_dim`` are plain attributes, as in the reference.
     """
 
-    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor], scheme: str):
+    def __init__(self, weight: torch.Tensor, bias: Optional[torch.Tensor], scheme: str,
+                 group_size: Optional[int] = None):
         super().__init__()
         if scheme not in ("int8", "int4", "nf4"):
             raise ValueError(f"unknown scheme {scheme!r}")
+        _check_group(scheme, group_size)
         self.scheme = scheme
+        self.group_size = group_size
         self.in_features = weight.shape[1]
         self.out_features = weight.shape[0]
-        q, s, in_dim = _quant(scheme, weight)
+        q, s, in_dim = _quant(scheme, weight, group_size)
         self.register_buffer("weight_q", q)
         self.register_buffer("scale", s)
         self._packed_in_dim = in_dim
@@ -112,7 +130,8 @@ class QuantizedLinear(nn.Module):
             self.register_parameter("bias", None)
 
     def dequantize_weight(self) -> torch.Tensor:
-        return _dequant(self.scheme, self.weight_q, self.scale, self._packed_in_dim)
+        return _dequant(self.scheme, self.weight_q, self.scale, self._packed_in_dim,
+                        self.group_size)
 
     def dense_weight(self, dtype: torch.dtype) -> torch.Tensor:
         """deq(W).to(dtype), cached while the buffers are unchanged.  The block's
@@ -127,10 +146,12 @@ class QuantizedLinear(nn.Module):
         return cache[1]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return ops.qlinear(x, self.scheme, self.weight_q, self.scale, self.bias, self.in_features)
+        return ops.qlinear(x, self.scheme, self.weight_q, self.scale, self.bias, self.in_features,
+                           group_size=self.group_size)
 
     def extra_repr(self) -> str:
-        return f"in={self.in_features}, out={self.out_features}, scheme={self.scheme!r}"
+        g = f", group_size={self.group_size}" if self.group_size else ""
+        return f"in={self.in_features}, out={self.out_features}, scheme={self.scheme!r}{g}"
 
 
 _QUANTIZABLE_LINEARS = ("in_proj", "x_proj", "dt_proj", "out_proj")
@@ -148,7 +169,7 @@ def quantize_block(module: nn.Module, config: QuantConfig,
                 qlin = QuantizedLinear(
                     weight=child.weight.detach(),
                     bias=child.bias.detach() if child.bias is not None else None,
-                    scheme=config.scheme)
+                    scheme=config.scheme, group_size=config.group_size)
                 qlin = qlin.to(device=child.weight.device)
                 setattr(parent, child_name, qlin)
                 n_replaced += 1

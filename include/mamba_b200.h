@@ -166,6 +166,22 @@ int mb2_qlinear(int scheme, int dtype, const void *x, int64_t ld_x,
                 void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
                 int epilogue, mb2_stream_t stream);
 
+/* Blockwise (grouped) variants -- the reference's roadmap "blockwise NF4
+ * (group_size=64)" (README.md:115, :201; not in the reference's code): the
+ * formulas above applied to each run of group_size consecutive input columns
+ * of a row, scale (rows, ceil(cols / group_size)).  group_size 0 equals the
+ * per-row functions; 4-bit schemes need an even group_size. */
+int mb2_quantize_grouped(int scheme, const float *w, int64_t rows, int64_t cols,
+                         int64_t group_size, void *weight_q, float *scale,
+                         mb2_stream_t stream);
+int mb2_dequantize_grouped(int scheme, const void *weight_q, const float *scale,
+                           int64_t rows, int64_t in_dim, int64_t group_size,
+                           float *w_out, mb2_stream_t stream);
+int mb2_qlinear_grouped(int scheme, int64_t group_size, int dtype, const void *x,
+                        int64_t ld_x, const void *weight_q, const float *scale,
+                        const void *bias, void *y, int64_t ld_y, int64_t M,
+                        int64_t N, int64_t K, int epilogue, mb2_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Whole block.  Weights follow the mamba_ssm state_dict (_mamba.py:67-84);
  * a quantised linear passes weight_q/scale instead of weight.
@@ -174,9 +190,12 @@ typedef struct mb2_linear_w {
     const void *weight;     /* (out, in) in dtype, or NULL when quantised   */
     const float *weight_split; /* optional (2, out, in) TF32 halves (F32 path)  */
     const void *weight_q;   /* quantised codes, or NULL                      */
-    const float *scale;     /* (out) per-channel scale when quantised        */
+    const float *scale;     /* quantised: (out) per-channel scale, or        */
+                            /* (out, ceil(in / group_size)) per group        */
     const void *bias;       /* (out) or NULL                                 */
     int scheme;             /* mb2_scheme                                    */
+    int64_t group_size;     /* 0: one scale per row (quant.py); else columns */
+                            /* per scale group (blockwise, e.g. 64)          */
 } mb2_linear_w;
 
 typedef struct mb2_block {

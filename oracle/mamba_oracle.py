@@ -28,7 +28,7 @@ __all__ = [
     "block_forward_with_final_state", "block_step", "init_state",
     "quant_int8", "quant_int4", "quant_nf4", "dequant_int8", "dequant_int4",
     "dequant_nf4", "nf4_lut", "linear", "dequant", "load_ref_scan_op",
-    "make_block_params", "stack_forward",
+    "make_block_params", "stack_forward", "quant_grouped", "dequant_grouped",
 ]
 
 _HERE = pathlib.Path(__file__).resolve().parent
@@ -165,6 +165,53 @@ def dequant_nf4(packed, scale, in_dim):
     return _dequant4("oracle_dequant_nf4", packed, scale, in_dim)
 
 
+def quant_grouped(scheme: str, w: torch.Tensor, group: int):
+    """Blockwise quantisation -- the reference's roadmap item "blockwise NF4
+    (group_size=64)" (README.md:115, :201), which its code does not implement:
+    quant.py's per-row formulas (:60-65 int8, :72-87 int4, :104-121 nf4)
+    applied to each run of ``group`` consecutive columns of a row, in the same
+    float32 torch ops.  Returns (codes, scale (rows, ceil(cols / group))); 4-bit
+    codes are packed as quant.py packs them (even column in the high nibble,
+    odd widths padded with code 0 / nibble 7)."""
+    w = _cpu_f32(w)
+    rows, cols = w.shape
+    ng = -(-cols // group)
+    g = F.pad(w, (0, ng * group - cols)).view(rows, ng, group)
+    amax = g.abs().amax(dim=2).clamp(min=1e-8)
+    if scheme == "int8":
+        s = amax / 127.0
+        q = torch.round(g / s[..., None]).clamp(-127, 127).reshape(rows, -1)[:, :cols]
+        return q.to(torch.int8).contiguous(), s
+    if scheme == "int4":
+        s = amax / 7.0
+        q = torch.round(g / s[..., None]).clamp(-7, 7).reshape(rows, -1)[:, :cols]
+        codes, pad = (q + 7).to(torch.uint8), 7
+    elif scheme == "nf4":
+        s = amax
+        wn = (g / s[..., None]).clamp(-1.0, 1.0).reshape(rows, -1)[:, :cols]
+        codes, pad = (wn[..., None] - nf4_lut()).abs().argmin(-1).to(torch.uint8), 0
+    else:
+        raise ValueError(scheme)
+    if cols % 2:
+        codes = torch.cat([codes, torch.full((rows, 1), pad, dtype=torch.uint8)], 1)
+    return ((codes[:, 0::2] << 4) | codes[:, 1::2]).contiguous(), s
+
+
+def dequant_grouped(scheme: str, weight_q: torch.Tensor, scale: torch.Tensor, in_dim: int,
+                    group: int) -> torch.Tensor:
+    """Inverse of quant_grouped: code value x its group's scale (float32)."""
+    scale = _cpu_f32(scale)
+    rows = weight_q.shape[0]
+    if scheme == "int8":
+        v = weight_q.to(torch.float32)
+    else:
+        b = weight_q.to(torch.int64)
+        nib = torch.stack([b >> 4, b & 0xF], -1).reshape(rows, -1)[:, :in_dim]
+        v = (nib - 7).to(torch.float32) if scheme == "int4" else nf4_lut()[nib]
+    col_scale = scale.repeat_interleave(group, dim=1)[:, :in_dim]
+    return v * col_scale
+
+
 def dequant(scheme: str, weight_q, scale, in_dim: int) -> torch.Tensor:
     if scheme == "int8":
         return dequant_int8(weight_q, scale)
@@ -180,11 +227,16 @@ def dequant(scheme: str, weight_q, scale, in_dim: int) -> torch.Tensor:
 # ---------------------------------------------------------------------------
 def linear(p: Dict[str, torch.Tensor], name: str, x: torch.Tensor,
            quant: Optional[Dict[str, Tuple[str, int]]] = None) -> torch.Tensor:
-    """nn.Linear, or QuantizedLinear.forward (quant.py:188-190) when quantised."""
+    """nn.Linear, or QuantizedLinear.forward (quant.py:188-190) when quantised;
+    quant[name] = (scheme, in_dim) or (scheme, in_dim, group_size)."""
     bias = p.get(f"{name}.bias")
     if quant and name in quant:
-        scheme, in_dim = quant[name]
-        w = dequant(scheme, p[f"{name}.weight_q"], p[f"{name}.scale"], in_dim)
+        scheme, in_dim = quant[name][:2]
+        group = quant[name][2] if len(quant[name]) > 2 else None
+        if group:
+            w = dequant_grouped(scheme, p[f"{name}.weight_q"], p[f"{name}.scale"], in_dim, group)
+        else:
+            w = dequant(scheme, p[f"{name}.weight_q"], p[f"{name}.scale"], in_dim)
         return F.linear(x, w.to(x.dtype), bias)
     return F.linear(x, p[f"{name}.weight"], bias)
 

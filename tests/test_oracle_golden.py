@@ -109,3 +109,36 @@ def test_quantized_linear_and_block_match_reference(golden):
             quant[name] = (scheme, p[f"{name}.weight"].shape[1])
         y = oracle.block_forward(pq, c["block_x"], quant)
         assert (y - c["qblock"][scheme]["y"]).abs().max().item() <= 2e-6, scheme
+
+
+def test_grouped_oracle_reduces_to_per_row_when_one_group_spans_the_row():
+    """Blockwise quantisation with one group per row is quant.py's per-channel
+    scheme: bit-exact with the oracle pinned to the reference."""
+    import oracle
+    g = torch.Generator().manual_seed(5)
+    for cols in (64, 33):
+        w = torch.randn(7, cols, generator=g)
+        w[0, 3] = 4.0
+        for scheme, per_row in (("int8", oracle.quant_int8), ("int4", oracle.quant_int4),
+                                ("nf4", oracle.quant_nf4)):
+            qg, sg = oracle.quant_grouped(scheme, w, 2 * cols)
+            ref = per_row(w)
+            assert torch.equal(qg, ref[0]), scheme
+            assert torch.equal(sg[:, 0], ref[1].reshape(-1)), scheme
+            dq = oracle.dequant_grouped(scheme, qg, sg, cols, 2 * cols)
+            dr = oracle.dequant(scheme, ref[0], ref[1], cols)
+            assert torch.equal(dq, dr), scheme
+
+
+def test_grouped_nf4_is_tighter_than_per_row_on_outlier_rows():
+    """The roadmap's reason for blockwise NF4: an outlier only coarsens its own
+    group's scale."""
+    import oracle
+    g = torch.Generator().manual_seed(6)
+    w = torch.randn(32, 256, generator=g) * 0.02
+    w[torch.rand(32, 256, generator=g) < 0.01] = 0.5
+    q, s = oracle.quant_grouped("nf4", w, 64)
+    err_g = (oracle.dequant_grouped("nf4", q, s, 256, 64) - w).abs().mean()
+    qr, sr, _ = oracle.quant_nf4(w)
+    err_r = (oracle.dequant("nf4", qr, sr, 256) - w).abs().mean()
+    assert err_g < 0.7 * err_r
