@@ -257,8 +257,17 @@ __global__ void splitk_reduce_kernel(const GemmArgs a, int splits) {
     if (i >= a.M * a.N) return;
     const int64_t m = i / a.N, n = i - m * a.N;
     const int64_t mn = a.M * a.N;
-    float v = 0.0f;
-    for (int z = 0; z < splits; ++z) v += a.partial[z * mn + i];
+    // four loads in flight; fixed combination order (deterministic)
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    int z = 0;
+    for (; z + 4 <= splits; z += 4) {
+        a0 += a.partial[(z + 0) * mn + i];
+        a1 += a.partial[(z + 1) * mn + i];
+        a2 += a.partial[(z + 2) * mn + i];
+        a3 += a.partial[(z + 3) * mn + i];
+    }
+    for (; z < splits; ++z) a0 += a.partial[z * mn + i];
+    float v = (a0 + a1) + (a2 + a3);
     if (a.row_scale) v *= a.row_scale[m];
     if (a.bias) v += io<T>::to_f(static_cast<const T *>(a.bias)[n]);
     if (a.epi == MB2_EPI_SOFTPLUS) v = softplus_f(io<T>::round(v));

@@ -112,6 +112,9 @@ struct Params {
     int tma_store;                // 1: store through map_y
     const float *row_scale;       // EpiExtra terms (internal.cuh)
     const void *resid; int64_t ld_r;
+    // split-K (few rows): tiles = (m, n, split), each split a range of kbs
+    // k-blocks, raw fp32 partial sums stored through a 3D map (N, M, split)
+    int ksplit, kbs;
 };
 
 // ------------------------------------------------------------- primitives
@@ -256,6 +259,12 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t sr
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
                  ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(c0), "r"(c1) : "memory");
 }
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, uint32_t src, int32_t c0,
+                                             int32_t c1, int32_t c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(src), "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;"); }
 __device__ __forceinline__ void bulk_wait_read0() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
@@ -297,8 +306,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int num_n = (int)ceil_div(p.N, BN);
-    const int num_tiles = (int)ceil_div(p.M, BM) * num_n;
+    const int num_mn = (int)ceil_div(p.M, BM) * num_n;
+    const int nsplit = p.ksplit > 1 ? p.ksplit : 1;
+    const int num_tiles = num_mn * nsplit;
     const int nk = (int)ceil_div(p.K, C::BK);
+    const int kbs = nsplit > 1 ? p.kbs : nk;         // k-blocks per split
+    // tile t -> output tile origin and its k-block range [kb0, kb1)
+    auto coords = [&](int t, int64_t &m0, int64_t &n0, int &z, int &kb0, int &kb1) {
+        z = t / num_mn;
+        const int r = t - z * num_mn;
+        m0 = (int64_t)(r / num_n) * BM;
+        n0 = (int64_t)(r % num_n) * BN;
+        kb0 = z * kbs;
+        kb1 = kb0 + kbs < nk ? kb0 + kbs : nk;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
@@ -329,16 +350,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             uint32_t g = 0;  // k-blocks issued by this CTA
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                const int32_t m0 = (t / num_n) * BM, n0 = (t % num_n) * BN;
-                for (int kb = 0; kb < nk; ++kb, ++g) {
+                int64_t m0, n0;
+                int z, kb0, kb1;
+                coords(t, m0, n0, z, kb0, kb1);
+                for (int kb = kb0; kb < kb1; ++kb, ++g) {
                     const int s = g % C::STAGES;
                     const uint32_t ph = (g / C::STAGES) & 1;
                     if (!mbar_wait(empty(s), ph ^ 1, 1)) { ok = false; break; }
                     mbar_expect_tx(full(s), C::TX);
                     const int32_t kc = kb * C::BK;
-                    tma_load_2d(tile(s, 0), &map_a, full(s), kc, m0);
-                    tma_load_2d(tile(s, 1), &map_b0, full(s), kc, n0);
-                    if (MODE == F32X3) tma_load_2d(tile(s, 2), &map_b1, full(s), kc, n0);
+                    tma_load_2d(tile(s, 0), &map_a, full(s), kc, (int32_t)m0);
+                    tma_load_2d(tile(s, 1), &map_b0, full(s), kc, (int32_t)n0);
+                    if (MODE == F32X3) tma_load_2d(tile(s, 2), &map_b1, full(s), kc, (int32_t)n0);
                 }
             }
         }
@@ -354,7 +377,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 if (!ok) break;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t acc = tmem + (uint32_t)(b * C::ACC_COLS);
-                for (int kb = 0; kb < nk; ++kb, ++g) {
+                int64_t m0, n0;
+                int z, kb0, kb1;
+                coords(t, m0, n0, z, kb0, kb1);
+                for (int kb = kb0; kb < kb1; ++kb, ++g) {
                     const int s = g % C::STAGES;
                     const uint32_t ph = (g / C::STAGES) & 1;
                     ok = mbar_wait(full(s), ph, 2);
@@ -364,7 +390,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
                     for (int kk = 0; kk < C::BK / C::KSTEP; ++kk) {
                         const uint32_t koff = kk * 32;  // 32 bytes of K per MMA
-                        const uint32_t acc0 = (kb > 0 || kk > 0) ? 1u : 0u;
+                        const uint32_t acc0 = (kb > kb0 || kk > 0) ? 1u : 0u;
                         if (MODE == F32X3) {
                             const uint32_t ah = tmem + C::A_COL + (uint32_t)((g % C::LO) * 64 + kk * C::KSTEP);
                             const uint32_t al = ah + 32;
@@ -372,7 +398,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                             const uint64_t bl = smem_desc(tile(s, 2) + koff);
                             // big: accumulator (kk & 1) (4 K slices per k-block,
                             // so both are initialised in k-block 0)
-                            mma_ts(acc + (uint32_t)((kk & 1) * BN), ah, bh, (kb > 0 || kk > 1) ? 1u : 0u);
+                            mma_ts(acc + (uint32_t)((kk & 1) * BN), ah, bh, (kb > kb0 || kk > 1) ? 1u : 0u);
                             mma_ts(acc + 2 * BN, ah, bl, acc0);
                             mma_ts(acc + 2 * BN, al, bh, 1u);
                         } else {
@@ -403,7 +429,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         uint32_t g = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-            for (int kb = 0; kb < nk; ++kb, ++g) {
+            int64_t m0, n0;
+            int z, kb0, kb1;
+            coords(t, m0, n0, z, kb0, kb1);
+            for (int kb = kb0; kb < kb1; ++kb, ++g) {
                 const int s = g % C::STAGES;
                 const uint32_t ph = (g / C::STAGES) & 1;
                 const int l = g % C::LO;
@@ -451,16 +480,21 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         TO *Y = static_cast<TO *>(p.y);
         const TO *bias = static_cast<const TO *>(p.bias);
         // write staged part `part` (columns part * HCOLS ...) of this warp's 32 rows
-        auto flush = [&](int part, int64_t m0, int64_t n0) {
+        auto flush = [&](int part, int64_t m0, int64_t n0, int z) {
             const int64_t c0 = (int64_t)part * HCOLS;
             if (p.tma_store) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) {
 #pragma unroll
-                    for (int bx = 0; bx < HCOLS / BOXC; ++bx)
-                        tma_store_2d(&map_y, wst + bx * 32 * 128, (int32_t)(n0 + c0 + bx * BOXC),
-                                     (int32_t)(m0 + q * 32));
+                    for (int bx = 0; bx < HCOLS / BOXC; ++bx) {
+                        if (nsplit > 1)   // split-K partials: (N, M, split), rows >= M clipped
+                            tma_store_3d(&map_y, wst + bx * 32 * 128, (int32_t)(n0 + c0 + bx * BOXC),
+                                         (int32_t)(m0 + q * 32), z);
+                        else
+                            tma_store_2d(&map_y, wst + bx * 32 * 128, (int32_t)(n0 + c0 + bx * BOXC),
+                                         (int32_t)(m0 + q * 32));
+                    }
                     bulk_commit();
                 }
             } else {
@@ -486,7 +520,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         };
         int it = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
-            const int64_t m0 = (int64_t)(t / num_n) * BM, n0 = (int64_t)(t % num_n) * BN;
+            int64_t m0, n0;
+            int z, kb0, kb1;
+            coords(t, m0, n0, z, kb0, kb1);
             const int b = it % C::NACC;
             bool w = mbar_wait(acc_full(b), (it / C::NACC) & 1, 6);
             if (!__all_sync(0xffffffffu, w)) break;   // tcgen05.ld is warp-collective
@@ -504,7 +540,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             for (int cb = 0; cb < BN / 32; ++cb) {
                 if (C::SPLIT > 1 && cb > 0 && cb % CBH == 0) {
                     // staging full: store the finished part, then reuse the buffer
-                    flush(cb / CBH - 1, m0, n0);
+                    flush(cb / CBH - 1, m0, n0, z);
                     if (p.tma_store && lane == 0) bulk_wait_read0();
                     __syncwarp();
                 }
@@ -586,7 +622,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             // TMEM drained: the MMA warp may start the next tile in this buffer
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             mbar_arrive(acc_empty(b));
-            flush(C::SPLIT - 1, m0, n0);
+            flush(C::SPLIT - 1, m0, n0, z);
         }
         if (lane == 0) bulk_wait0();   // stores complete before the CTA exits
     }
@@ -638,10 +674,101 @@ static int launch_tc(const CUtensorMap &a, const CUtensorMap &b0, const CUtensor
         cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
         if (g_num_sms <= 0) g_num_sms = 148;
     }
-    const int64_t tiles = ceil_div(p.M, (int64_t)tc::BM) * ceil_div(p.N, (int64_t)tc::Cfg<MODE>::BN);
+    const int64_t tiles = ceil_div(p.M, (int64_t)tc::BM) * ceil_div(p.N, (int64_t)tc::Cfg<MODE>::BN) *
+                          (p.ksplit > 1 ? p.ksplit : 1);
     const unsigned grid = (unsigned)(tiles < g_num_sms ? tiles : g_num_sms);
     kern<<<grid, tc::Cfg<MODE>::WARPS * 32, smem, st>>>(a, b0, b1, ym, p);
     return check_launch("gemm_tc_kernel");
+}
+
+// Partial sums of a split-K launch: (split, M, N) fp32 in scratch, written
+// through a 3D map whose box clips at M (a 128-row tile of a few-row GEMM
+// must not spill into the next split's rows).
+static int make_map_partials(CUtensorMap *map, float *ptr, int64_t M, int64_t N, int64_t ks) {
+    cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)ks};
+    cuuint64_t strides[2] = {(cuuint64_t)(N * 4), (cuuint64_t)(M * N * 4)};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MB2_ERR_CUDA, "cuTensorMapEncodeTiled (3D) failed (%d)", (int)r);
+    return MB2_OK;
+}
+
+// The splits added in a fixed order (deterministic), then the epilogue terms
+// in the order of the single-pass epilogue; one output element per thread.
+__global__ void tc_splitk_reduce_kernel(const float *__restrict__ P, int ks, int64_t M, int64_t N,
+                                        const float *__restrict__ bias,
+                                        const float *__restrict__ row_scale, int epi,
+                                        const float *__restrict__ resid, int64_t ld_r,
+                                        float *__restrict__ y, int64_t ld_y, int64_t n1,
+                                        int64_t off1, int64_t n2, int64_t off2) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= M * N) return;
+    const int64_t m = i / N, n = i - m * N;
+    // four independent partial sums keep four loads in flight; combined in a
+    // fixed order, so the result does not depend on timing
+    const int64_t mn = M * N;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    int z = 0;
+    for (; z + 4 <= ks; z += 4) {
+        a0 += P[(z + 0) * mn + i];
+        a1 += P[(z + 1) * mn + i];
+        a2 += P[(z + 2) * mn + i];
+        a3 += P[(z + 3) * mn + i];
+    }
+    for (; z < ks; ++z) a0 += P[z * mn + i];
+    float v = (a0 + a1) + (a2 + a3);
+    if (row_scale) v *= row_scale[m];
+    if (bias) v += bias[n];
+    if (epi == MB2_EPI_SOFTPLUS) v = softplus_f(v);
+    if (resid) v += resid[m * ld_r + n];
+    y[m * ld_y + n + (n >= n1 ? off1 : 0) + (n >= n2 ? off2 : 0)] = v;
+}
+
+// fp32 GEMM of few rows (the decode step) on the tensor cores: K split over
+// about one CTA per SM, partial sums in scratch, then the reduction.
+static int gemm_tc_splitk(const void *x, int64_t ld_x, const float *w_split, const void *bias,
+                          void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K, int64_t n1,
+                          int64_t off1, int64_t n2, int64_t off2, int epi, cudaStream_t st,
+                          bool *used, const EpiExtra &ex) {
+    using CF = tc::Cfg<tc::F32X3>;
+    if (!aligned(x, 16) || (ld_x * 4) % 16 != 0 || (K * 4) % 16 != 0 || (N * 4) % 16 != 0)
+        return MB2_OK;
+    const float *b0 = w_split, *b1 = w_split + N * K;
+    if (!aligned(b0, 16) || !aligned(b1, 16) || !aligned(ex.scratch, 16)) return MB2_OK;
+    if (g_num_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    const int64_t nk = ceil_div(K, (int64_t)CF::BK);
+    const int64_t mn = ceil_div(M, (int64_t)tc::BM) * ceil_div(N, (int64_t)CF::BN);
+    int64_t ks = ceil_div((int64_t)g_num_sms, mn);
+    ks = ks < nk / 2 ? ks : nk / 2;                      // >= 2 k-blocks per split
+    const int64_t cap = (int64_t)(ex.scratch_bytes / ((size_t)M * N * sizeof(float)));
+    ks = ks < cap ? ks : cap;
+    if (ks < 2) return MB2_OK;
+    const int64_t kbs = ceil_div(nk, ks);
+    ks = ceil_div(nk, kbs);
+    MB2_TRY(get_encode());
+    CUtensorMap ma, mb0, mb1, my;
+    MB2_TRY(make_map(&ma, x, M, K, ld_x, false, 128));
+    MB2_TRY(make_map(&mb0, b0, N, K, K, false, CF::BN));
+    MB2_TRY(make_map(&mb1, b1, N, K, K, false, CF::BN));
+    MB2_TRY(make_map_partials(&my, ex.scratch, M, N, ks));
+    tc::Params p{ex.scratch, N, nullptr, M, N, K, N, N, 0, 0, MB2_EPI_NONE, 1, nullptr, nullptr, 0,
+                 (int)ks, (int)kbs};
+    MB2_TRY((launch_tc<tc::F32X3, float, false>(ma, mb0, mb1, my, p, st)));
+    tc_splitk_reduce_kernel<<<(unsigned)ceil_div(M * N, (int64_t)256), 256, 0, st>>>(
+        ex.scratch, (int)ks, M, N, static_cast<const float *>(bias), ex.row_scale, epi,
+        static_cast<const float *>(ex.resid), ex.ld_r, static_cast<float *>(y), ld_y, n1, off1, n2,
+        off2);
+    MB2_TRY(check_launch("tc_splitk_reduce_kernel"));
+    *used = true;
+    return MB2_OK;
 }
 
 // Tensor-core path when it applies (large M, aligned operands); *used reports it.
@@ -652,8 +779,15 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
     *used = false;
     const bool bf16 = dtype == MB2_BF16;
     const size_t es = bf16 ? 2 : 4;
-    if (M < 256 || N < 16 || K < 16) return MB2_OK;         // skinny: CUDA-core kernel
+    if (N < 16 || K < 16 || M < 1) return MB2_OK;
     if (!bf16 && !w_split) return MB2_OK;                   // exact-fp32 path requested
+    if (M < 256) {
+        // few rows: fp32 with scratch splits K on the tensor cores; else the
+        // CUDA-core kernel
+        if (bf16 || !ex.scratch) return MB2_OK;
+        return gemm_tc_splitk(x, ld_x, w_split, bias, y, ld_y, M, N, K, n1, off1, n2, off2, epi, st,
+                              used, ex);
+    }
     // TMA: 16-byte aligned bases and row strides
     if (!aligned(x, 16) || (ld_x * es) % 16 != 0 || (K * es) % 16 != 0) return MB2_OK;
     // the residual is read in 16-byte pieces
@@ -673,7 +807,7 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
     if (tma_store) MB2_TRY(make_map(&my, y, M, N, ld_y, bf16, 32));
     else my = mb0;  // unused
     tc::Params p{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0,
-                 ex.row_scale, ex.resid, ex.ld_r};
+                 ex.row_scale, ex.resid, ex.ld_r, 1, 0};
     *used = true;
     const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS;
     if (bf16)
