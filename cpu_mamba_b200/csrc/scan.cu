@@ -39,7 +39,9 @@ namespace mb2 {
 constexpr int SCAN_THREADS = 128;  // threads per CTA
 constexpr int SCAN_TC = 16;        // timesteps per staged chunk
 
-enum ScanMode { PLAIN = 0, FUSED = 1, GATED = 2 };
+// SUMMARY: the first pass of a T-segmented GATED scan -- from h = 0, no y;
+// writes the segment's final state and the sum of its dt.
+enum ScanMode { PLAIN = 0, FUSED = 1, GATED = 2, SUMMARY = 3 };
 
 struct ScanParams {
     const void *x;  int64_t ld_x;    // (N, ld_x)  x / conv output
@@ -60,7 +62,6 @@ struct ScanParams {
     // b * nseg + g runs steps [g * seg_len, (g + 1) * seg_len) of sequence b
     int nseg;                        // <= 1: no segments
     int64_t seg_len;
-    int summary;                     // 1: pass 1 -- h from 0, writes h_end and sum(dt), no y
     float *seg_hend;                 // (batch, nseg, d_inner, S)
     float *seg_sdt;                  // (batch, nseg, d_inner)
     const float *seg_hstart;         // pass 3: (batch, nseg, d_inner, S) starting states
@@ -288,7 +289,7 @@ scan_kernel(const ScanParams p) {
                     a[e] = static_cast<const float *>(p.A)[d * S + s];
                 if (p.seg_hstart)
                     hi[e] = p.seg_hstart[(segidx * p.d_inner + d) * S + s];
-                else if (p.h0 && !p.summary)
+                else if (p.h0 && MODE != SUMMARY)
                     hi[e] = p.h0[((int64_t)b * p.d_inner + d) * S + s];
             }
         }
@@ -334,8 +335,9 @@ scan_kernel(const ScanParams p) {
                                    p.vec16 & ARR_D2, tid);
         stage_rows<T, SCAN_TC, Gm::SPP>(st + 2 * Gm::NX, bg + t0 * p.ld_b, p.ld_b, rv, S,
                                         p.vec16 & ARR_B, tid);
-        stage_rows<T, SCAN_TC, Gm::SPP>(st + 2 * Gm::NX + Gm::NBC, cg + t0 * p.ld_c, p.ld_c, rv,
-                                        S, p.vec16 & ARR_C, tid);
+        if (MODE != SUMMARY)   // C only enters y
+            stage_rows<T, SCAN_TC, Gm::SPP>(st + 2 * Gm::NX + Gm::NBC, cg + t0 * p.ld_c, p.ld_c,
+                                            rv, S, p.vec16 & ARR_C, tid);
         if (MODE == FUSED)
             stage_rows<T, SCAN_TC, Gm::RP>(st + 2 * Gm::NX + 2 * Gm::NBC, dlg + t0 * p.ld_dl,
                                            p.ld_dl, rv, p.dt_rank, p.vec16 & ARR_DL, tid);
@@ -409,7 +411,7 @@ scan_kernel(const ScanParams p) {
             }
             __syncwarp();   // a channel's L lanes share one warp
         }
-        if (MODE == GATED) {
+        if (MODE == GATED || MODE == SUMMARY) {
             // ---- dt = softplus(dt_proj output) once per token-channel: lane j
             // takes steps j, j + L, ... (rows >= tn are zero-filled, unused)
 #pragma unroll
@@ -421,7 +423,7 @@ scan_kernel(const ScanParams p) {
 #pragma unroll 8
         for (int tt = 0; tt < tn; ++tt) {
             const float dtv = MODE != PLAIN ? dts[tt * CH + c] : io<T>::to_f(d2s[tt * CH]);
-            sdt += dtv;
+            if (MODE == SUMMARY) sdt += dtv;
             const float dtx = dtv * io<T>::to_f(xs[tt * CH]);
             const f2 dt2 = pk(dtv, dtv), dtx2 = pk(dtx, dtx);
             float bv[SPL], cv[SPL];
@@ -434,19 +436,23 @@ scan_kernel(const ScanParams p) {
                 upk(mul2(dt2, A2[q]), e0, e1);
                 const f2 dA = pk(ex2(e0), ex2(e1));
                 h[q] = fma2(dA, h[q], mul2(dtx2, pk(bv[2 * q], bv[2 * q + 1])));
-                if (q & 1) yb = fma2(h[q], pk(cv[2 * q], cv[2 * q + 1]), yb);
-                else ya = fma2(h[q], pk(cv[2 * q], cv[2 * q + 1]), ya);
+                if (MODE != SUMMARY) {
+                    if (q & 1) yb = fma2(h[q], pk(cv[2 * q], cv[2 * q + 1]), yb);
+                    else ya = fma2(h[q], pk(cv[2 * q], cv[2 * q + 1]), ya);
+                }
             }
-            float y0, y1, y2, y3;
-            upk(ya, y0, y1);
-            upk(yb, y2, y3);
-            ys[tt * SCAN_THREADS + tid] = (y0 + y1) + (y2 + y3);
+            if (MODE != SUMMARY) {
+                float y0, y1, y2, y3;
+                upk(ya, y0, y1);
+                upk(yb, y2, y3);
+                ys[tt * SCAN_THREADS + tid] = (y0 + y1) + (y2 + y3);
+            }
         }
         __syncthreads();
         // ---- read-out: sum lane partials, D skip, (FUSED) cast + SiLU(z) gate
         const T *xrow = st + cc;
         const T *zrow = st + (MODE == FUSED ? Gm::NX : 2 * Gm::NX + 2 * Gm::NBC) + cc;
-        if (col_ok && !p.summary) {
+        if (MODE != SUMMARY && col_ok) {
 #pragma unroll 4
             for (int tt = rr0; tt < tn; tt += RSTEP) {
                 float yv = 0.0f;
@@ -463,7 +469,7 @@ scan_kernel(const ScanParams p) {
     cp_async_wait<0>();
     // final state: of the sequence (no segments), or of the segment (pass 1);
     // with segments the carry kernel produces the sequence's final state
-    float *hout = p.summary ? p.seg_hend + segidx * p.d_inner * S
+    float *hout = MODE == SUMMARY ? p.seg_hend + segidx * p.d_inner * S
                             : ((nseg == 1 && p.h_last) ? p.h_last + (int64_t)b * p.d_inner * S
                                                        : nullptr);
     if (hout && active) {
@@ -477,7 +483,7 @@ scan_kernel(const ScanParams p) {
                 if (s < S) hout[d * S + s] = hv[e];
             }
         }
-        if (p.summary && j == 0) p.seg_sdt[segidx * p.d_inner + d] = sdt;
+        if (MODE == SUMMARY && j == 0) p.seg_sdt[segidx * p.d_inner + d] = sdt;
     }
 }
 
@@ -649,13 +655,14 @@ static int run_segmented(ScanParams p, int nseg, float *ws, cudaStream_t st) {
     const int64_t nstates = p.batch * p.nseg * p.d_inner * S;
     float *hend = ws, *hstart = ws + nstates, *sdt = ws + 2 * nstates;
     float *h_last = p.h_last;
-    p.summary = 1; p.seg_hend = hend; p.seg_sdt = sdt; p.seg_hstart = nullptr;
-    MB2_TRY((dispatch_scan<T, MODE>(p, st)));
+    static_assert(MODE == GATED, "segments are run for the gated scan");
+    p.seg_hend = hend; p.seg_sdt = sdt; p.seg_hstart = nullptr;
+    MB2_TRY((dispatch_scan<T, SUMMARY>(p, st)));
     const int64_t n = p.batch * p.d_inner * S;
     seg_carry_kernel<T, MODE == PLAIN><<<(unsigned)ceil_div(n, (int64_t)256), 256, 0, st>>>(
         p.A, p.h0, hend, sdt, hstart, h_last, p.batch, p.d_inner, (int)S, p.nseg);
     MB2_TRY(check_launch("seg_carry_kernel"));
-    p.summary = 0; p.seg_hstart = hstart;
+    p.seg_hstart = hstart;
     return dispatch_scan<T, MODE>(p, st);
 }
 
