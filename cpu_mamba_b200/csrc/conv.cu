@@ -5,9 +5,10 @@
 // forward_with_final_state (_mamba.py:180): the last K-1 pre-conv inputs per
 // (b, d), zero-left-padded for short sequences.
 //
-// HBM-bound: each thread owns one channel and CONV_TT consecutive timesteps,
-// keeping the K-1 history in registers; consecutive threads are consecutive
-// channels, so every row access is a coalesced 128-byte-per-warp segment.
+// HBM-bound: each thread owns one channel (two adjacent channels in bf16, so
+// that a warp still moves 128 bytes per row access) and CONV_TT consecutive
+// timesteps, keeping the K-1 history in registers; consecutive threads are
+// consecutive channels, so every row access is one coalesced segment.
 #include "common.cuh"
 
 namespace mb2 {
@@ -36,6 +37,7 @@ conv1d_silu_kernel(const T *__restrict__ x, int64_t ld_in, const T *__restrict__
         hist[k] = (t >= 0) ? io<T>::to_f(x[(row0 + t) * ld_in + d]) : 0.0f;
     }
     const int64_t t_end = (t0 + CONV_TT < seqlen) ? t0 + CONV_TT : seqlen;
+#pragma unroll 4
     for (int64_t t = t0; t < t_end; ++t) {
         hist[K - 1] = io<T>::to_f(x[(row0 + t) * ld_in + d]);
         float acc = bv;
@@ -54,10 +56,82 @@ conv1d_silu_kernel(const T *__restrict__ x, int64_t ld_in, const T *__restrict__
     }
 }
 
+// bf16, two channels per thread: one 4-byte load / store per row
+template <int K>
+__global__ void __launch_bounds__(128)
+conv1d_silu_bf16x2_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ld_in,
+                          const __nv_bfloat16 *__restrict__ w, const __nv_bfloat16 *__restrict__ bias,
+                          __nv_bfloat16 *__restrict__ xc, int64_t ld_out,
+                          __nv_bfloat16 *__restrict__ tail, int64_t seqlen, int64_t d_inner) {
+    using T = __nv_bfloat16;
+    const int64_t d = 2 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
+    const int64_t t0 = (int64_t)blockIdx.y * CONV_TT;
+    const int64_t b = blockIdx.z;
+    if (d >= d_inner) return;
+    float wk[2][K];
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int k = 0; k < K; ++k) wk[c][k] = io<T>::to_f(w[(d + c) * K + k]);
+    const float bv0 = bias ? io<T>::to_f(bias[d]) : 0.0f;
+    const float bv1 = bias ? io<T>::to_f(bias[d + 1]) : 0.0f;
+    const int64_t row0 = b * seqlen;
+    auto ld2 = [&](int64_t t, float &a, float &c) {
+        const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162 *>(x + (row0 + t) * ld_in + d);
+        a = __low2float(v);
+        c = __high2float(v);
+    };
+    float h0[K], h1[K];
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) {
+        const int64_t t = t0 - (K - 1) + k;
+        if (t >= 0) ld2(t, h0[k], h1[k]);
+        else h0[k] = h1[k] = 0.0f;
+    }
+    const int64_t t_end = (t0 + CONV_TT < seqlen) ? t0 + CONV_TT : seqlen;
+#pragma unroll 4
+    for (int64_t t = t0; t < t_end; ++t) {
+        ld2(t, h0[K - 1], h1[K - 1]);
+        float a0 = bv0, a1 = bv1;
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            a0 = fmaf(wk[0][k], h0[k], a0);
+            a1 = fmaf(wk[1][k], h1[k], a1);
+        }
+        const float v0 = silu_f(io<T>::round(a0)), v1 = silu_f(io<T>::round(a1));
+        *reinterpret_cast<__nv_bfloat162 *>(xc + (row0 + t) * ld_out + d) =
+            __floats2bfloat162_rn(v0, v1);
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k) {
+            h0[k] = h0[k + 1];
+            h1[k] = h1[k + 1];
+        }
+    }
+    if (tail && t_end == seqlen) {
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k) {
+            tail[(b * d_inner + d) * (K - 1) + k] = io<T>::from_f(h0[k]);
+            tail[(b * d_inner + d + 1) * (K - 1) + k] = io<T>::from_f(h1[k]);
+        }
+    }
+}
+
 template <typename T, int K>
 static int launch_conv(const void *x, int64_t ld_in, const void *w, const void *bias, void *xc,
                        int64_t ld_out, void *tail, int64_t batch, int64_t seqlen, int64_t di,
                        cudaStream_t st) {
+    if constexpr (sizeof(T) == 2) {
+        // pairs of channels: even d_inner, 4-byte aligned rows
+        if (di % 2 == 0 && ld_in % 2 == 0 && ld_out % 2 == 0 && aligned(x, 4) && aligned(xc, 4)) {
+            dim3 g2((unsigned)ceil_div(di / 2, 128), (unsigned)ceil_div(seqlen, CONV_TT),
+                    (unsigned)batch);
+            conv1d_silu_bf16x2_kernel<K><<<g2, 128, 0, st>>>(
+                static_cast<const __nv_bfloat16 *>(x), ld_in, static_cast<const __nv_bfloat16 *>(w),
+                static_cast<const __nv_bfloat16 *>(bias), static_cast<__nv_bfloat16 *>(xc), ld_out,
+                static_cast<__nv_bfloat16 *>(tail), seqlen, di);
+            return check_launch("conv1d_silu_bf16x2_kernel");
+        }
+    }
     dim3 grid((unsigned)ceil_div(di, 128), (unsigned)ceil_div(seqlen, CONV_TT), (unsigned)batch);
     conv1d_silu_kernel<T, K><<<grid, 128, 0, st>>>(
         static_cast<const T *>(x), ld_in, static_cast<const T *>(w), static_cast<const T *>(bias),
