@@ -83,6 +83,14 @@ _SIGS = {
                                       _vp, ctypes.c_size_t, _vp]),
     "mb2_block_step_static": (ctypes.c_int, [ctypes.POINTER(Block), _vp, _vp, _vp, _vp, _c_i64,
                                              _vp]),
+    "mb2_block_shard_xdbl": (ctypes.c_int, [ctypes.POINTER(Block), _c_i64, ctypes.c_int,
+                                            ctypes.POINTER(ctypes.c_size_t),
+                                            ctypes.POINTER(_c_i64)]),
+    "mb2_block_forward_shard": (ctypes.c_int, [ctypes.POINTER(Block), ctypes.c_int, _vp, _vp,
+                                               _c_i64, _c_i64, _vp, _vp, _vp, ctypes.c_size_t,
+                                               _vp]),
+    "mb2_block_step_shard": (ctypes.c_int, [ctypes.POINTER(Block), ctypes.c_int, _vp, _vp, _vp,
+                                            _vp, _c_i64, _vp, ctypes.c_size_t, _vp]),
     "mb2_fold_norm": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _c_i64, _c_i64, _vp]),
     "mb2_stack_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Block), _c_i64, _c_i64,
                                                     _c_i64]),

@@ -214,25 +214,26 @@ extern "C" int mb2_qlinear_grouped(int scheme, int64_t group_size, int dtype, co
                        K, epilogue, stream);
 }
 
-// The five launches of one block forward over N = batch * seqlen rows.
+// One block forward over N = batch * seqlen rows runs as a head (in_proj ->
+// conv -> x_proj, leaving x_dbl in the workspace) and a tail (dt_proj -> scan
+// -> gate -> out_proj).  A channel-sharded block all-reduces x_dbl between
+// the two (x_proj contracts over the sharded channels).
 // row_scale (N floats) scales in_proj's output rows (a pre-norm folded into
 // in_proj); resid (N, d_model) is added to out_proj's output (may alias out).
-static int block_pipeline(const mb2_block &b, const Layout &l, const void *x, void *out,
-                          int64_t batch, int64_t seqlen, float *h_last, void *conv_tail,
-                          char *ws, cudaStream_t st, const float *row_scale,
-                          const void *resid) {
+static EpiExtra scratch_extra(const Layout &l, char *ws) {
+    EpiExtra e;    // scratch for dequantised weights (quantised projections)
+    e.scratch = l.deq_bytes ? reinterpret_cast<float *>(ws + l.off_deq) : nullptr;
+    e.scratch_bytes = l.deq_bytes;
+    return e;
+}
+
+static int pipeline_head(const mb2_block &b, const Layout &l, const void *x, int64_t batch,
+                         int64_t seqlen, void *conv_tail, char *ws, cudaStream_t st,
+                         const float *row_scale) {
     void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
     const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
-    const size_t es = l.es;
-    EpiExtra in_ex, out_ex, mid_ex;
+    EpiExtra in_ex = scratch_extra(l, ws), mid_ex = scratch_extra(l, ws);
     in_ex.row_scale = row_scale;
-    out_ex.resid = resid;
-    out_ex.ld_r = l.dm;
-    // scratch for dequantised weights (quantised projections)
-    for (EpiExtra *e : {&in_ex, &out_ex, &mid_ex}) {
-        e->scratch = l.deq_bytes ? reinterpret_cast<float *>(ws + l.off_deq) : nullptr;
-        e->scratch_bytes = l.deq_bytes;
-    }
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, N, 2 * di, l.dm, MB2_EPI_NONE,
                            st, -1, 0, -1, 0, in_ex));
@@ -241,6 +242,18 @@ static int block_pipeline(const mb2_block &b, const Layout &l, const void *x, vo
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, MB2_EPI_NONE,
                            st, R, l.RB - R, R + S, l.RC - l.RB - S, mid_ex));
+    return MB2_OK;
+}
+
+static int pipeline_tail(const mb2_block &b, const Layout &l, void *out, int64_t batch,
+                         int64_t seqlen, float *h_last, char *ws, cudaStream_t st,
+                         const void *resid) {
+    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
+    const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
+    const size_t es = l.es;
+    EpiExtra out_ex = scratch_extra(l, ws);
+    out_ex.resid = resid;
+    out_ex.ld_r = l.dm;
     // dt_proj (_mamba.py:219) on the tensor cores, bias in the epilogue,
     // written over the x half of xz (dead once the conv has run); the gated
     // scan applies the softplus (:220) as it stages the rows.  A quantised
@@ -269,6 +282,14 @@ static int block_pipeline(const mb2_block &b, const Layout &l, const void *x, vo
     return MB2_OK;
 }
 
+static int block_pipeline(const mb2_block &b, const Layout &l, const void *x, void *out,
+                          int64_t batch, int64_t seqlen, float *h_last, void *conv_tail,
+                          char *ws, cudaStream_t st, const float *row_scale,
+                          const void *resid) {
+    MB2_TRY(pipeline_head(b, l, x, batch, seqlen, conv_tail, ws, st, row_scale));
+    return pipeline_tail(b, l, out, batch, seqlen, h_last, ws, st, resid);
+}
+
 extern "C" size_t mb2_block_workspace_bytes(const mb2_block *blk, int64_t batch, int64_t seqlen) {
     if (!blk || batch < 0 || seqlen < 0) return 0;
     return make_layout(blk, batch * seqlen, false, batch, seqlen).total;
@@ -295,6 +316,46 @@ extern "C" size_t mb2_step_workspace_bytes(const mb2_block *blk, int64_t batch) 
     return make_layout(blk, batch, true).total;
 }
 
+// A decode step as a head (in_proj -> ring conv -> x_proj) and a tail
+// (dt_proj -> one scan step -> gate -> out_proj), split like the forward.
+static int step_head(const mb2_block &b, const Layout &l, const void *x, void *conv_state,
+                     int64_t batch, char *ws, cudaStream_t st) {
+    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
+    const int64_t di = l.di, S = l.S, R = l.R;
+    EpiExtra sk;                    // split-K scratch for the few-row projections
+    sk.scratch = reinterpret_cast<float *>(ws + l.off_part);
+    sk.scratch_bytes = l.part_bytes;
+    MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, batch, 2 * di, l.dm, MB2_EPI_NONE,
+                       st, -1, 0, -1, 0, sk));
+    if (b.dtype == MB2_F32)
+        MB2_TRY(launch_conv_step<float>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b, conv_state,
+                                        xc, batch, di, st));
+    else
+        MB2_TRY(launch_conv_step<__nv_bfloat16>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b,
+                                                conv_state, xc, batch, di, st));
+    return linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, batch, R + 2 * S, di, MB2_EPI_NONE,
+                      st, R, l.RB - R, R + S, l.RC - l.RB - S, sk);
+}
+
+static int step_tail(const mb2_block &b, const Layout &l, void *out, float *h, int64_t batch,
+                     char *ws, cudaStream_t st) {
+    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
+    const int64_t di = l.di, S = l.S, R = l.R;
+    const size_t es = l.es;
+    EpiExtra sk;
+    sk.scratch = reinterpret_cast<float *>(ws + l.off_part);
+    sk.scratch_bytes = l.part_bytes;
+    // dt_proj (bias in the epilogue) over the x half of xz, dead after the conv
+    MB2_TRY(linear_any(b.dtype, b.dt_proj, xdbl, l.ldx, xz, 2 * di, batch, di, R, MB2_EPI_NONE,
+                       st, -1, 0, -1, 0, sk));
+    // one timestep: softplus, exp(dt A), h updated in place, y = C.h + D x, gate
+    MB2_TRY(scan_step(b.dtype, xc, di, xz, 2 * di, (char *)xdbl + l.RB * es,
+                      (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log, b.D,
+                      h, xc, di, batch, di, S, st));
+    return linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, batch, l.dm, di, MB2_EPI_NONE, st,
+                      -1, 0, -1, 0, sk);
+}
+
 extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, float *h,
                               void *conv_state, int64_t batch, void *workspace,
                               size_t workspace_bytes, mb2_stream_t stream) {
@@ -308,31 +369,66 @@ extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, fl
     if (batch == 0) return MB2_OK;
     MB2_REQUIRE(x && out && h && conv_state && workspace, MB2_ERR_ARG, "step: null pointer");
     char *ws = static_cast<char *>(workspace);
-    void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
-    const int64_t di = l.di, S = l.S, R = l.R;
-    const size_t es = l.es;
-    EpiExtra sk;                    // split-K scratch for the few-row projections
-    sk.scratch = reinterpret_cast<float *>(ws + l.off_part);
-    sk.scratch_bytes = l.part_bytes;
-    MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, batch, 2 * di, l.dm, MB2_EPI_NONE,
-                       st, -1, 0, -1, 0, sk));
-    if (b.dtype == MB2_F32)
-        MB2_TRY(launch_conv_step<float>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b, conv_state,
-                                        xc, batch, di, st));
-    else
-        MB2_TRY(launch_conv_step<__nv_bfloat16>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b,
-                                                conv_state, xc, batch, di, st));
-    MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, batch, R + 2 * S, di, MB2_EPI_NONE,
-                       st, R, l.RB - R, R + S, l.RC - l.RB - S, sk));
-    // dt_proj (bias in the epilogue) over the x half of xz, dead after the conv
-    MB2_TRY(linear_any(b.dtype, b.dt_proj, xdbl, l.ldx, xz, 2 * di, batch, di, R, MB2_EPI_NONE,
-                       st, -1, 0, -1, 0, sk));
-    // one timestep: softplus, exp(dt A), h updated in place, y = C.h + D x, gate
-    MB2_TRY(scan_step(b.dtype, xc, di, xz, 2 * di, (char *)xdbl + l.RB * es,
-                      (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log, b.D,
-                      h, xc, di, batch, di, S, st));
-    return linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, batch, l.dm, di, MB2_EPI_NONE, st,
-                      -1, 0, -1, 0, sk);
+    MB2_TRY(step_head(b, l, x, conv_state, batch, ws, st));
+    return step_tail(b, l, out, h, batch, ws, st);
+}
+
+// ------------------------------------------------------- channel shards ---
+// A block whose d_inner channels are split over ranks: every rank runs the
+// head on its channels, the caller all-reduces x_dbl (x_proj contracts over
+// d_inner), every rank runs the tail, and the caller all-reduces out
+// (out_proj contracts over d_inner too).  x_dbl's pad columns are zeroed in
+// the head so the reduced buffer holds no uninitialised values.
+
+extern "C" int mb2_block_shard_xdbl(const mb2_block *blk, int64_t rows, int step, size_t *offset,
+                                    int64_t *ld) {
+    MB2_TRY(check_block(blk));
+    MB2_REQUIRE(rows >= 0 && offset && ld, MB2_ERR_ARG, "shard_xdbl: bad argument");
+    const Layout l = make_layout(blk, rows, step != 0);
+    *offset = l.off_xdbl;
+    *ld = l.ldx;
+    return MB2_OK;
+}
+
+extern "C" int mb2_block_forward_shard(const mb2_block *blk, int phase, const void *x, void *out,
+                                       int64_t batch, int64_t seqlen, float *h_last,
+                                       void *conv_tail, void *workspace, size_t workspace_bytes,
+                                       mb2_stream_t stream) {
+    MB2_TRY(check_block(blk));
+    MB2_REQUIRE(phase == 1 || phase == 2, MB2_ERR_ARG, "forward_shard: phase must be 1 or 2");
+    MB2_REQUIRE(batch >= 0 && seqlen >= 0, MB2_ERR_SHAPE, "forward_shard: negative size");
+    cudaStream_t st = (cudaStream_t)stream;
+    const Layout l = make_layout(blk, batch * seqlen, false, batch, seqlen);
+    MB2_REQUIRE(workspace_bytes >= l.total, MB2_ERR_WORKSPACE,
+                "forward_shard: workspace %zu < required %zu", workspace_bytes, l.total);
+    if (l.N == 0) return MB2_OK;
+    MB2_REQUIRE(workspace && (phase == 1 ? x != nullptr : out != nullptr), MB2_ERR_ARG,
+                "forward_shard: null pointer");
+    char *ws = static_cast<char *>(workspace);
+    if (phase == 2) return pipeline_tail(*blk, l, out, batch, seqlen, h_last, ws, st, nullptr);
+    cudaMemsetAsync(ws + l.off_xdbl, 0, (size_t)l.N * l.ldx * l.es, st);
+    MB2_TRY(check_launch("forward_shard: x_dbl clear"));
+    return pipeline_head(*blk, l, x, batch, seqlen, conv_tail, ws, st, nullptr);
+}
+
+extern "C" int mb2_block_step_shard(const mb2_block *blk, int phase, const void *x, void *out,
+                                    float *h, void *conv_state, int64_t batch, void *workspace,
+                                    size_t workspace_bytes, mb2_stream_t stream) {
+    MB2_TRY(check_block(blk));
+    MB2_REQUIRE(phase == 1 || phase == 2, MB2_ERR_ARG, "step_shard: phase must be 1 or 2");
+    MB2_REQUIRE(batch >= 0, MB2_ERR_SHAPE, "step_shard: negative batch");
+    cudaStream_t st = (cudaStream_t)stream;
+    const Layout l = make_layout(blk, batch, true);
+    MB2_REQUIRE(workspace_bytes >= l.total, MB2_ERR_WORKSPACE,
+                "step_shard: workspace %zu < required %zu", workspace_bytes, l.total);
+    if (batch == 0) return MB2_OK;
+    MB2_REQUIRE(workspace && (phase == 1 ? (x && conv_state) : (out && h)), MB2_ERR_ARG,
+                "step_shard: null pointer");
+    char *ws = static_cast<char *>(workspace);
+    if (phase == 2) return step_tail(*blk, l, out, h, batch, ws, st);
+    cudaMemsetAsync(ws + l.off_xdbl, 0, (size_t)batch * l.ldx * l.es, st);
+    MB2_TRY(check_launch("step_shard: x_dbl clear"));
+    return step_head(*blk, l, x, conv_state, batch, ws, st);
 }
 
 // ------------------------------------------------------------------ stack ---

@@ -48,13 +48,15 @@ class CPUMamba(nn.Module):
                  dt_min: float = 0.001, dt_max: float = 0.1, dt_init: str = "random",
                  dt_scale: float = 1.0, dt_init_floor: float = 1e-4,
                  conv_bias: bool = True, bias: bool = False, device=None, dtype=None,
-                 **_unused):
+                 *, d_inner: int | None = None, **_unused):
+        """d_inner (keyword only, not a reference argument) overrides expand *
+        d_model: the channel count of one shard of a channel-sharded block."""
         super().__init__()
         self.d_model = d_model
         self.d_state = d_state
         self.d_conv = d_conv
         self.expand = expand
-        self.d_inner = expand * d_model
+        self.d_inner = int(d_inner) if d_inner is not None else expand * d_model
         self.dt_rank = math.ceil(d_model / 16) if dt_rank == "auto" else int(dt_rank)
         fk = {"device": device, "dtype": dtype}
         self.in_proj = nn.Linear(d_model, self.d_inner * 2, bias=bias, **fk)

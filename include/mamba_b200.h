@@ -257,6 +257,31 @@ int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, float eps, void
                       int64_t batch, int64_t seqlen, void *workspace,
                       size_t workspace_bytes, mb2_stream_t stream);
 
+/* ---- d_inner channel shards ------------------------------------------------
+ * A block whose d_inner channels are split over ranks (one GPU each): blk
+ * describes this rank's shard -- d_inner = its channel count; in_proj rows
+ * = its channels of the x half then of the z half; conv1d, dt_proj, A_log and
+ * D the channels' rows; x_proj and out_proj the channels' COLUMNS (both
+ * contract over d_inner); out_proj's bias on one rank only.  A forward or a
+ * step runs in two phases with an all-reduce (sum over ranks) after each:
+ *   phase 1: in_proj -> conv -> x_proj's partial x_dbl, left in the workspace
+ *            at the offset mb2_block_shard_xdbl gives ((rows, ld) elements of
+ *            the activation dtype, pad columns zeroed)  -> all-reduce x_dbl
+ *   phase 2: dt_proj -> scan -> gate -> out_proj's partial into out
+ *            -> all-reduce out
+ * Both phases take the same workspace (mb2_block_workspace_bytes /
+ * mb2_step_workspace_bytes of the shard).  h_last / conv_tail (forward) and h
+ * / conv_state (step) are the shard's channels.  The split of _mamba.py:204-265
+ * / :103-163 over devices; the reference runs on one host. */
+int mb2_block_shard_xdbl(const mb2_block *blk, int64_t rows, int step, size_t *offset,
+                         int64_t *ld);
+int mb2_block_forward_shard(const mb2_block *blk, int phase, const void *x, void *out,
+                            int64_t batch, int64_t seqlen, float *h_last, void *conv_tail,
+                            void *workspace, size_t workspace_bytes, mb2_stream_t stream);
+int mb2_block_step_shard(const mb2_block *blk, int phase, const void *x, void *out, float *h,
+                         void *conv_state, int64_t batch, void *workspace,
+                         size_t workspace_bytes, mb2_stream_t stream);
+
 /* Size of the device array mb2_block_step_static uses as its workspace. */
 #define MB2_STEP_STATIC_SCRATCH_BYTES (8u << 20)
 
