@@ -208,7 +208,7 @@ def stack_roofline(cfg, batch, hbm_gbs, src, ms_per_step):
 
 # ------------------------------------------------------------- our arm
 def run_ours(args, cfg):
-    from cpu_mamba_b200 import CPUMamba, QuantConfig, quantize_block
+    from cpu_mamba_b200 import CPUMamba, QuantConfig, StepGraph, quantize_block
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -229,6 +229,14 @@ def run_ours(args, cfg):
         if cfg.get("quant"):
             quantize_block(m, QuantConfig(cfg["quant"]))
         B = cfg["batch"]
+    channels = args.shard == "channels" and not stack_mode
+    reducer = None
+    if channels:
+        # every rank runs the whole batch on its d_inner channels (strong scaling)
+        from cpu_mamba_b200.shard import ChannelShardedMamba, PeerReducer
+        if args.reduce == "peer" and ws > 1:
+            reducer = PeerReducer(max_elems=1 << 22)
+        m = ChannelShardedMamba(m, reduce=reducer)
     T, dm = cfg["seqlen"], cfg["d_model"]
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
     step_mode = cfg["mode"] == "step"
@@ -239,10 +247,15 @@ def run_ours(args, cfg):
     state = None
     if step_mode:
         with torch.no_grad():
-            prompt = torch.randn(B, T, dm, generator=g, device=dev).to(dtype)
+            g_prompt = torch.Generator(device=dev).manual_seed(99)     # same prompt on all ranks
+            prompt = torch.randn(B, T, dm, generator=g_prompt if channels else g,
+                                 device=dev).to(dtype)
             _, state = m.forward_with_final_state(prompt)
+    if channels:          # every rank feeds the same tokens
+        g_in = torch.Generator(device=dev).manual_seed(1234)
+        xs = [torch.randn(in_shape, generator=g_in, device=dev).to(dtype) for _ in range(nbuf)]
 
-    graph = m.capture_step(state, xs[0]) if step_mode else None   # decode: one graph per step
+    graph = StepGraph(m, state, xs[0]) if step_mode else None   # decode: one graph per step
 
     def step(i):
         with torch.no_grad():
@@ -269,7 +282,8 @@ def run_ours(args, cfg):
     dist.barrier()
     ms = dist.max_over_ranks(e0.elapsed_time(e1), dev)      # the slowest rank's time
     tokens_per_step = B * (1 if step_mode else T)
-    tokens_all = dist.sum_over_ranks(tokens_per_step, dev)  # whole job, all shards
+    # whole job: batch shards add up; channel shards all process the same tokens
+    tokens_all = tokens_per_step if channels else dist.sum_over_ranks(tokens_per_step, dev)
     value = tokens_all * args.steps / (ms / 1e3)
 
     # end to end through the public API from pinned host buffers
@@ -280,7 +294,7 @@ def run_ours(args, cfg):
     for i in range(max(3, min(args.steps, 10)) + 1):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        step_e2e(m, host_in, host_out, graph, step_mode, dev)
+        step_e2e(m, host_in, host_out, graph, step_mode, dev, channels)
         b.record(stream)
         torch.cuda.synchronize(dev)
         if i > 0:
@@ -289,27 +303,37 @@ def run_ours(args, cfg):
     e2e = {"value": tokens_all / (e2e_t / 1e3), "unit": "tokens/s",
            "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": in_bytes}
 
-    stages = profile_stages(m, xs[0], cfg, dtype, args.steps) if cfg["mode"] == "forward" else {}
+    stages = (profile_stages(m, xs[0], cfg, dtype, args.steps)
+              if cfg["mode"] == "forward" and not channels else {})
     result = None
     if rank == 0:
         hbm, bf16, bf16_s, src = peaks()
         if stack_mode:
             roof = stack_roofline(cfg, B, hbm, src, ms / args.steps)
             launches_per_step = 7 * cfg["n_layers"]
+        elif step_mode:
+            roof = decode_roofline(cfg, hbm, src, ms / args.steps, ws if channels else 1)
+            launches_per_step = 5 + (2 if reducer is not None else 0)
         else:
             roof = roofline(stages, cfg, hbm, bf16, src, ms / args.steps)
-            launches_per_step = 6 if cfg["mode"] == "forward" else 5
+            launches_per_step = 6 + (2 if reducer is not None else 0)
+        par = f"batch-sharded x{ws}"
+        if channels:
+            par = (f"d_inner channel-sharded x{ws}, all-reduce: "
+                   f"{'peer-memory kernel' if reducer is not None else 'NCCL'}" if ws > 1
+                   else "d_inner channel-sharded x1")
         result = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-            "higher_is_better": True, "scaling": "strong" if stack_mode else "weak",
+            "higher_is_better": True,
+            "scaling": "strong" if stack_mode or channels else "weak",
             "vs_baseline": None,
             "dtype": cfg["dtype"], "data": "synthetic (seeded; shapes of the configuration)",
             "config": {"workload": cfg["workload"], "batch_per_gpu": B,
                        "global_batch": int(tokens_all) // (1 if step_mode else T),
                        "seq_len": T if not step_mode else 1, "d_model": dm,
                        "d_inner": 2 * dm, "d_state": cfg["d_state"], "dt_rank": R,
-                       "quant": cfg.get("quant"), "parallelism": f"batch-sharded x{ws}",
+                       "quant": cfg.get("quant"), "parallelism": par,
                        "layers": cfg.get("n_layers", 1),
                        "decode": "forward_step captured as one CUDA graph" if step_mode else None,
                        "l2": f"inputs rotated over {nbuf} buffers ({nbuf * in_bytes / 2**20:.0f} MB > L2)"},
@@ -317,11 +341,14 @@ def run_ours(args, cfg):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),
         }
+    del graph                       # graphs holding collectives go before the group
+    if reducer is not None:
+        reducer.close()
     dist.shutdown()
     return result
 
 
-def step_e2e(m, host_in, host_out, graph, step_mode, dev):
+def step_e2e(m, host_in, host_out, graph, step_mode, dev, channels=False):
     """One step through the public API from pinned host memory to pinned host
     memory.  A forward streams batch slices with the copies overlapping the
     kernels (CPUMamba.forward_host); a decode step copies the token in,
@@ -331,6 +358,8 @@ def step_e2e(m, host_in, host_out, graph, step_mode, dev):
         if step_mode:
             y = graph(host_in.to(dev, non_blocking=True))
             host_out.copy_(y, non_blocking=True)
+        elif channels:
+            host_out.copy_(m(host_in.to(dev, non_blocking=True)), non_blocking=True)
         else:
             m.forward_host(host_in, out=host_out)
 
@@ -414,6 +443,23 @@ def realistic_block_bytes(cfg):
     act = N * es * (2 * dm + 7 * di + 2 * xd)
     w = es * (2 * di * dm + xd * di + di * R + dm * di)
     return act + w
+
+
+def decode_roofline(cfg, hbm_gbs, src, ms_per_step, shards):
+    """A decode step against HBM: every weight read once, h (fp32) and the
+    conv state read and written once, per GPU (channel shards each hold
+    1/shards of all of them); the token rows in and out are negligible."""
+    B, dm, S = cfg["batch"], cfg["d_model"], cfg["d_state"]
+    di = 2 * dm
+    R = cfg.get("dt_rank", math.ceil(dm / 16))
+    es = 4 if cfg["dtype"] == "f32" else 2
+    w = es * (2 * di * dm + (R + 2 * S) * di + di * R + dm * di)
+    state = 2 * (B * di * S * 4 + B * di * 3 * es)
+    nbytes = (w + state) / shards
+    ach = nbytes / (ms_per_step / 1e3) / 1e9
+    return {"kernel": "decode step (all launches)", "bound": "hbm", "achieved": ach,
+            "peak": hbm_gbs, "unit": "GB/s", "frac": ach / hbm_gbs, "traffic": None,
+            "bytes_per_step_per_gpu": nbytes, "peak_source": f"{src} HBM copy"}
 
 
 def roofline(stages, cfg, hbm_gbs, bf16_tflops, src, ms_per_step):
@@ -563,6 +609,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", type=int, default=0, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shard", default="batch", choices=["batch", "channels"],
+                    help="multi-GPU split: batch rows (no collective) or d_inner channels "
+                         "(two all-reduces per block; for batches smaller than the GPU count "
+                         "and decode latency)")
+    ap.add_argument("--reduce", default="peer", choices=["peer", "nccl"],
+                    help="all-reduce of the channel shards: the library's peer-memory kernel "
+                         "or NCCL")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the configuration's batch (small cases for profiling)")
     args = ap.parse_args()
@@ -572,6 +625,8 @@ def main():
     if args.batch:
         cfg["batch"] = args.batch
         cfg["workload"] += f"_batch{args.batch}"
+    if args.shard == "channels" and cfg["mode"] != "stack":
+        cfg["workload"] += "_dinner_sharded"
     if args.impl == "reference":
         res = run_reference(args, cfg)
     else:

@@ -39,6 +39,12 @@ class LinearW(ctypes.Structure):
                 ("group_size", _c_i64)]
 
 
+class PeerGroup(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+                ("slot_elems", ctypes.c_int64), ("timeout_ns", ctypes.c_int64),
+                ("bufs", ctypes.c_void_p * 8)]
+
+
 class Block(ctypes.Structure):
     _fields_ = [("d_model", _c_i64), ("d_inner", _c_i64), ("d_state", _c_i64),
                 ("d_conv", _c_i64), ("dt_rank", _c_i64), ("dtype", ctypes.c_int),
@@ -91,6 +97,15 @@ _SIGS = {
                                                _vp]),
     "mb2_block_step_shard": (ctypes.c_int, [ctypes.POINTER(Block), ctypes.c_int, _vp, _vp, _vp,
                                             _vp, _c_i64, _vp, ctypes.c_size_t, _vp]),
+    "mb2_peer_buffer_bytes": (ctypes.c_size_t, [ctypes.c_int, _c_i64]),
+    "mb2_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(_vp), ctypes.c_char_p]),
+    "mb2_peer_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "mb2_peer_close": (ctypes.c_int, [_vp]),
+    "mb2_peer_free": (ctypes.c_int, [_vp]),
+    "mb2_peer_allreduce": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, ctypes.POINTER(PeerGroup),
+                                          _vp]),
+    "mb2_peer_status": (ctypes.c_int, [ctypes.POINTER(PeerGroup), ctypes.POINTER(ctypes.c_int),
+                                       ctypes.c_int]),
     "mb2_fold_norm": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _c_i64, _c_i64, _vp]),
     "mb2_stack_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Block), _c_i64, _c_i64,
                                                     _c_i64]),

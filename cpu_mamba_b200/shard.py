@@ -30,8 +30,9 @@ from typing import Callable, Optional
 import torch
 import torch.nn as nn
 
+from . import _lib
 from . import dist as _dist
-from ._lib import check, lib, stream_of
+from ._lib import check, dtype_code, lib, stream_of
 from .module import CPUMamba
 from .quant import QuantizedLinear
 
@@ -67,11 +68,98 @@ def _allreduce(group):
     return reduce
 
 
+class PeerReducer:
+    """Sum over the ranks of ``group`` (one GPU each, one node) through peer
+    memory: mb2_peer_allreduce, one kernel per call that pushes this rank's
+    tensor into every rank's buffer over NVLink and sums all contributions in
+    rank order.  For the small, latency-bound reductions of a decode step;
+    tensors above ``max_elems`` elements go to NCCL's all-reduce (its
+    bandwidth-optimal ring) instead.  Every rank must make the same calls in
+    the same order, each on its current stream; they may be captured in a
+    CUDA graph.  A wait longer than ``timeout_s`` is recorded (``status()``)
+    instead of hanging the GPU.  ``close()`` releases the buffers (all ranks)."""
+
+    def __init__(self, group=None, max_elems: int = 1 << 20, timeout_s: float = 5.0):
+        import torch.distributed as td
+        self.group = group
+        self.max_elems = int(max_elems)
+        on = td.is_initialized()
+        world = td.get_world_size(group) if on else 1
+        rank = td.get_rank(group) if on else 0
+        L = lib()
+        nbytes = L.mb2_peer_buffer_bytes(world, self.max_elems)
+        if nbytes == 0:
+            raise ValueError(f"PeerReducer: world {world} outside 1..8")
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        check(L.mb2_peer_alloc(nbytes, ctypes.byref(own), handle), "peer alloc")
+        handles = [handle.raw] * world
+        if world > 1:
+            handles = [None] * world
+            td.all_gather_object(handles, handle.raw, group=group)
+        g = _lib.PeerGroup()
+        g.world, g.rank, g.slot_elems = world, rank, self.max_elems
+        g.timeout_ns = int(timeout_s * 1e9)
+        self._opened = []
+        for r in range(world):
+            if r == rank:
+                g.bufs[r] = own.value
+                continue
+            p = ctypes.c_void_p()
+            check(L.mb2_peer_open(handles[r], ctypes.byref(p)), "peer open")
+            g.bufs[r] = p.value
+            self._opened.append(p.value)
+        self._own, self._g = own.value, g
+        if world > 1:
+            td.barrier(group=group)
+
+    @property
+    def world(self) -> int:
+        return self._g.world
+
+    def __call__(self, t: torch.Tensor) -> None:
+        if self._g is None:
+            raise RuntimeError("PeerReducer: closed")
+        if not t.is_contiguous():
+            raise RuntimeError("PeerReducer: tensor must be contiguous")
+        if t.numel() > self.max_elems:
+            import torch.distributed as td
+            td.all_reduce(t, group=self.group)
+            return
+        check(lib().mb2_peer_allreduce(dtype_code(t.dtype), t.data_ptr(), t.numel(),
+                                       ctypes.byref(self._g), stream_of(t)), "peer all-reduce")
+
+    def status(self, clear: bool = True) -> int:
+        """0, or MB2_PEER_TIMEOUT if a wait on this rank expired (synchronous)."""
+        code = ctypes.c_int()
+        check(lib().mb2_peer_status(ctypes.byref(self._g), ctypes.byref(code), int(clear)),
+              "peer status")
+        return code.value
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective: every
+        rank calls it, after its last use)."""
+        if self._g is None:
+            return
+        import torch.distributed as td
+        torch.cuda.synchronize()
+        if td.is_initialized() and self._g.world > 1:
+            td.barrier(group=self.group)
+        for p in self._opened:
+            check(lib().mb2_peer_close(p), "peer close")
+        if td.is_initialized() and self._g.world > 1:
+            td.barrier(group=self.group)
+        check(lib().mb2_peer_free(self._own), "peer free")
+        self._g = None
+
+
 class ChannelShardedMamba(nn.Module):
     """This rank's channel shard of ``block`` (a CPUMamba with dense
     projections).  ``world`` / ``rank`` default to the launcher's environment
-    and ``reduce`` to an NCCL all-reduce over ``group``; with one rank the
-    shard is the whole block and nothing is reduced."""
+    and ``reduce`` to NCCL's all-reduce over ``group``; ``reduce`` may also be
+    a PeerReducer (the library's peer-memory all-reduce) or any callable that
+    sums a tensor over the ranks in place.  With one rank the shard is the
+    whole block and nothing is reduced."""
 
     def __init__(self, block: CPUMamba, world: Optional[int] = None, rank: Optional[int] = None,
                  group=None, device=None,

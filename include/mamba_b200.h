@@ -282,6 +282,37 @@ int mb2_block_step_shard(const mb2_block *blk, int phase, const void *x, void *o
                          void *conv_state, int64_t batch, void *workspace,
                          size_t workspace_bytes, mb2_stream_t stream);
 
+/* ---- all-reduce through peer memory ---------------------------------------
+ * The sum over ranks (one GPU each, one node) that the shards above need,
+ * as one kernel over NVLink: each rank pushes its data (as fp32) into every
+ * rank's buffer, raises per-chunk flags there, waits for every rank's flags
+ * in its own buffer and sums the contributions in rank order (every rank gets
+ * the same bits; bf16 data is summed in fp32 and rounded once).  Buffers come
+ * from mb2_peer_alloc (cudaMalloc + a CUDA IPC handle, exchanged by the
+ * caller) and mb2_peer_open in the other ranks' processes.  No counterpart in
+ * the reference (one host, no collectives).  Every rank must make the same
+ * sequence of calls (same counts) on one stream; calls may be captured in a
+ * CUDA graph (the call counter lives in the buffer).  A wait that exceeds
+ * timeout_ns records MB2_PEER_TIMEOUT in the rank's status word
+ * (mb2_peer_status) and the kernel returns; the data is then not the sum. */
+#define MB2_PEER_MAX_RANKS 8
+#define MB2_PEER_TIMEOUT 0x7e01
+#define MB2_PEER_HANDLE_BYTES 64
+typedef struct mb2_peer_group {
+    int32_t world, rank;
+    int64_t slot_elems;                    /* largest count per call */
+    int64_t timeout_ns;                    /* bound of every wait */
+    void *bufs[MB2_PEER_MAX_RANKS];        /* every rank's buffer, mapped here */
+} mb2_peer_group;
+size_t mb2_peer_buffer_bytes(int world, int64_t slot_elems);
+int mb2_peer_alloc(size_t bytes, void **ptr, void *ipc_handle /* 64 bytes out */);
+int mb2_peer_open(const void *ipc_handle, void **ptr);
+int mb2_peer_close(void *ptr);
+int mb2_peer_free(void *ptr);
+int mb2_peer_allreduce(int dtype, void *data, int64_t count, const mb2_peer_group *g,
+                       mb2_stream_t stream);
+int mb2_peer_status(const mb2_peer_group *g, int *code, int clear);
+
 /* Size of the device array mb2_block_step_static uses as its workspace. */
 #define MB2_STEP_STATIC_SCRATCH_BYTES (8u << 20)
 

@@ -6,7 +6,10 @@ shard's workspace, every shard runs its tail, the test sums the outputs.
 That is the library's shard path with the all-reduces done by hand; it must
 match the oracle (fp32 1e-5 max abs, bf16 mean rel err 2e-2) and, for one
 shard, the unsharded block bit for bit.  On two GPUs the same runs as two
-processes over NCCL (skipped with fewer GPUs)."""
+processes over NCCL and over the library's peer-memory all-reduce (skipped
+with fewer GPUs); that all-reduce's bounded wait is checked on one GPU with a
+peer that never arrives."""
+import ctypes
 import multiprocessing as mp
 import os
 import socket
@@ -15,8 +18,11 @@ import pytest
 import torch
 
 import oracle
-from cpu_mamba_b200 import CPUMamba, QuantConfig, quantize_block
-from cpu_mamba_b200.shard import ChannelShardedMamba
+from cpu_mamba_b200 import CPUMamba, QuantConfig, StepGraph, quantize_block
+from cpu_mamba_b200._lib import PeerGroup, check, lib
+from cpu_mamba_b200.shard import ChannelShardedMamba, PeerReducer
+
+PEER_TIMEOUT = 0x7e01
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -122,6 +128,58 @@ def test_quantised_block_is_not_channel_sharded():
         ChannelShardedMamba(m, world=2, rank=0)
 
 
+def test_peer_reducer_single_rank_is_identity():
+    red = PeerReducer(max_elems=4096)
+    try:
+        for dtype in (torch.float32, torch.bfloat16):
+            for n in (1, 7, 1024, 4096):
+                t = torch.randn(n, device=DEV).to(dtype)
+                ref = t.clone()
+                red(t)
+                torch.cuda.synchronize()
+                assert torch.equal(t, ref)
+        assert red.status() == 0
+    finally:
+        red.close()
+
+
+def test_peer_wait_times_out_without_hanging():
+    """A two-rank group whose second rank never runs: rank 0's kernel waits
+    for flags nothing sets, gives up after the group's 50 ms bound, records
+    MB2_PEER_TIMEOUT, and the context stays usable."""
+    L = lib()
+    nbytes = L.mb2_peer_buffer_bytes(2, 1024)
+    ptrs = []
+    try:
+        for _ in range(2):
+            p, h = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+            check(L.mb2_peer_alloc(nbytes, ctypes.byref(p), h), "alloc")
+            ptrs.append(p.value)
+        g = PeerGroup()
+        g.world, g.rank, g.slot_elems, g.timeout_ns = 2, 0, 1024, 50_000_000
+        g.bufs[0], g.bufs[1] = ptrs
+        t = torch.ones(1000, device=DEV)
+        torch.cuda.synchronize()
+        check(L.mb2_peer_allreduce(0, t.data_ptr(), t.numel(), ctypes.byref(g),
+                                   torch.cuda.current_stream().cuda_stream), "allreduce")
+        torch.cuda.synchronize()
+        code = ctypes.c_int()
+        check(L.mb2_peer_status(ctypes.byref(g), ctypes.byref(code), 1), "status")
+        assert code.value == PEER_TIMEOUT
+        check(L.mb2_peer_status(ctypes.byref(g), ctypes.byref(code), 0), "status")
+        assert code.value == 0                          # cleared
+        assert torch.ones(4, device=DEV).sum().item() == 4.0
+        bad = PeerGroup()
+        bad.world, bad.rank, bad.slot_elems, bad.timeout_ns = 2, 0, 1024, 1
+        bad.bufs[0] = ptrs[0]                           # rank 1's buffer missing
+        assert L.mb2_peer_allreduce(0, t.data_ptr(), 10, ctypes.byref(bad), None) != 0
+        g.slot_elems = 10
+        assert L.mb2_peer_allreduce(0, t.data_ptr(), 11, ctypes.byref(g), None) != 0
+    finally:
+        for p in ptrs:
+            check(L.mb2_peer_free(p), "free")
+
+
 # ------------------------------------------------------------ two GPUs ---
 def _free_port():
     with socket.socket() as s:
@@ -152,6 +210,33 @@ def _nccl_rank(rank, world, port, q):
                 ys, _ = sh.forward_step(x[:, t].to(dev), st)
                 yf, _ = m.forward_step(x[:, t].to(dev), full_state)
                 errs.append((ys - yf).abs().max().item())
+            # the peer-memory all-reduce: exact rank-order sums, eager and in a graph
+            import torch.distributed as td
+            red = PeerReducer(max_elems=1 << 16, timeout_s=10.0)
+            for dtype in (torch.float32, torch.bfloat16):
+                for n in (1, 1000, 4099, 1 << 16):
+                    t = torch.randn(n, generator=torch.Generator().manual_seed(n + rank)).to(dev, dtype)
+                    parts = [torch.empty_like(t) for _ in range(world)]
+                    td.all_gather(parts, t)
+                    want = parts[0].float()
+                    for pt in parts[1:]:
+                        want = want + pt.float()
+                    red(t)
+                    errs.append(0.0 if torch.equal(t, want.to(dtype)) else float("inf"))
+            shp = ChannelShardedMamba(m, world=world, rank=rank, reduce=red)
+            y2, st2 = shp.forward_with_final_state(x[:, :T].to(dev))
+            errs.append((y2.cpu() - oracle.block_forward(p, x[:, :T])).abs().max().item())
+            full_state = m.forward_with_final_state(x[:, :T].to(dev))[1]
+            graph = StepGraph(shp, st2, x[:, T].to(dev))
+            for t in range(T, T + 4):
+                ys = graph(x[:, t].to(dev)).clone()
+                yf, _ = m.forward_step(x[:, t].to(dev), full_state)
+                errs.append((ys - yf).abs().max().item())
+            torch.cuda.synchronize()
+            if red.status() != 0:
+                errs.append(float("inf"))
+            del graph
+            red.close()
         torch.cuda.synchronize()
         d.shutdown()
         q.put(("ok", rank, max(errs)))
