@@ -129,6 +129,28 @@ class QuantizedLinear(nn.Module):
         else:
             self.register_parameter("bias", None)
 
+    @classmethod
+    def from_packed(cls, weight_q: torch.Tensor, scale: torch.Tensor,
+                    bias: Optional[torch.Tensor], scheme: str, in_features: int,
+                    group_size: Optional[int] = None) -> "QuantizedLinear":
+        """A QuantizedLinear around already-quantised buffers (a loaded file),
+        without quantising anything."""
+        if scheme not in ("int8", "int4", "nf4"):
+            raise ValueError(f"unknown scheme {scheme!r}")
+        _check_group(scheme, group_size)
+        self = cls.__new__(cls)
+        nn.Module.__init__(self)
+        self.scheme, self.group_size = scheme, group_size
+        self.in_features, self.out_features = int(in_features), weight_q.shape[0]
+        self.register_buffer("weight_q", weight_q)
+        self.register_buffer("scale", scale)
+        self._packed_in_dim = int(in_features)
+        if bias is not None:
+            self.bias = nn.Parameter(bias.detach().clone())
+        else:
+            self.register_parameter("bias", None)
+        return self
+
     def dequantize_weight(self) -> torch.Tensor:
         return _dequant(self.scheme, self.weight_q, self.scale, self._packed_in_dim,
                         self.group_size)
