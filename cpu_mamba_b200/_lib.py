@@ -89,6 +89,13 @@ _SIGS = {
                                       _vp, ctypes.c_size_t, _vp]),
     "mb2_block_step_static": (ctypes.c_int, [ctypes.POINTER(Block), _vp, _vp, _vp, _vp, _c_i64,
                                              _vp]),
+    "mb2_stack_forward_state": (ctypes.c_int, [ctypes.POINTER(Block), _c_i64, ctypes.c_float,
+                                               _vp, _c_i64, _c_i64, ctypes.POINTER(_vp),
+                                               ctypes.POINTER(_vp), _vp, ctypes.c_size_t, _vp]),
+    "mb2_stack_step_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Block), _c_i64, _c_i64]),
+    "mb2_stack_step": (ctypes.c_int, [ctypes.POINTER(Block), _c_i64, ctypes.c_float, _vp,
+                                      ctypes.POINTER(_vp), ctypes.POINTER(_vp), _c_i64, _vp,
+                                      ctypes.c_size_t, _vp]),
     "mb2_block_shard_xdbl": (ctypes.c_int, [ctypes.POINTER(Block), _c_i64, ctypes.c_int,
                                             ctypes.POINTER(ctypes.c_size_t),
                                             ctypes.POINTER(_c_i64)]),

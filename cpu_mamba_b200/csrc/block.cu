@@ -319,14 +319,16 @@ extern "C" size_t mb2_step_workspace_bytes(const mb2_block *blk, int64_t batch) 
 // A decode step as a head (in_proj -> ring conv -> x_proj) and a tail
 // (dt_proj -> one scan step -> gate -> out_proj), split like the forward.
 static int step_head(const mb2_block &b, const Layout &l, const void *x, void *conv_state,
-                     int64_t batch, char *ws, cudaStream_t st) {
+                     int64_t batch, char *ws, cudaStream_t st, const float *row_scale = nullptr) {
     void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
     const int64_t di = l.di, S = l.S, R = l.R;
     EpiExtra sk;                    // split-K scratch for the few-row projections
     sk.scratch = reinterpret_cast<float *>(ws + l.off_part);
     sk.scratch_bytes = l.part_bytes;
+    EpiExtra in_ex = sk;
+    in_ex.row_scale = row_scale;
     MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, batch, 2 * di, l.dm, MB2_EPI_NONE,
-                       st, -1, 0, -1, 0, sk));
+                       st, -1, 0, -1, 0, in_ex));
     if (b.dtype == MB2_F32)
         MB2_TRY(launch_conv_step<float>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b, conv_state,
                                         xc, batch, di, st));
@@ -338,7 +340,7 @@ static int step_head(const mb2_block &b, const Layout &l, const void *x, void *c
 }
 
 static int step_tail(const mb2_block &b, const Layout &l, void *out, float *h, int64_t batch,
-                     char *ws, cudaStream_t st) {
+                     char *ws, cudaStream_t st, const void *resid = nullptr) {
     void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
     const int64_t di = l.di, S = l.S, R = l.R;
     const size_t es = l.es;
@@ -352,8 +354,11 @@ static int step_tail(const mb2_block &b, const Layout &l, void *out, float *h, i
     MB2_TRY(scan_step(b.dtype, xc, di, xz, 2 * di, (char *)xdbl + l.RB * es,
                       (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log, b.D,
                       h, xc, di, batch, di, S, st));
+    EpiExtra out_ex = sk;
+    out_ex.resid = resid;
+    out_ex.ld_r = l.dm;
     return linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, batch, l.dm, di, MB2_EPI_NONE, st,
-                      -1, 0, -1, 0, sk);
+                      -1, 0, -1, 0, out_ex);
 }
 
 extern "C" int mb2_block_step(const mb2_block *blk, const void *x, void *out, float *h,
@@ -534,11 +539,8 @@ extern "C" size_t mb2_stack_workspace_bytes(const mb2_block *layers, int64_t n_l
     return stack_bytes(layers, n_layers, batch, seqlen, &off_r);
 }
 
-extern "C" int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, float eps, void *x,
-                                 int64_t batch, int64_t seqlen, void *workspace,
-                                 size_t workspace_bytes, mb2_stream_t stream) {
+static int check_stack(const mb2_block *layers, int64_t n_layers, float eps) {
     MB2_REQUIRE(layers && n_layers > 0, MB2_ERR_ARG, "stack: no layers");
-    MB2_REQUIRE(batch >= 0 && seqlen >= 0, MB2_ERR_SHAPE, "stack: negative size");
     MB2_REQUIRE(eps >= 0.0f, MB2_ERR_ARG, "stack: negative eps");
     for (int64_t i = 0; i < n_layers; ++i) {
         MB2_TRY(check_block(&layers[i]));
@@ -546,6 +548,23 @@ extern "C" int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, floa
                     MB2_ERR_SHAPE, "stack: layer %lld differs in d_model or dtype",
                     (long long)i);
     }
+    return MB2_OK;
+}
+
+extern "C" int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, float eps, void *x,
+                                 int64_t batch, int64_t seqlen, void *workspace,
+                                 size_t workspace_bytes, mb2_stream_t stream) {
+    return mb2_stack_forward_state(layers, n_layers, eps, x, batch, seqlen, nullptr, nullptr,
+                                   workspace, workspace_bytes, stream);
+}
+
+extern "C" int mb2_stack_forward_state(const mb2_block *layers, int64_t n_layers, float eps,
+                                       void *x, int64_t batch, int64_t seqlen,
+                                       float *const *h_last, void *const *conv_tail,
+                                       void *workspace, size_t workspace_bytes,
+                                       mb2_stream_t stream) {
+    MB2_TRY(check_stack(layers, n_layers, eps));
+    MB2_REQUIRE(batch >= 0 && seqlen >= 0, MB2_ERR_SHAPE, "stack: negative size");
     const int64_t N = batch * seqlen;
     size_t off_r;
     const size_t need = stack_bytes(layers, n_layers, batch, seqlen, &off_r);
@@ -560,7 +579,56 @@ extern "C" int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, floa
         const mb2_block &b = layers[i];
         const Layout l = make_layout(&b, N, false, batch, seqlen);
         MB2_TRY(rms_scale(b.dtype, x, N, b.d_model, eps, r, st));
-        MB2_TRY(block_pipeline(b, l, x, x, batch, seqlen, nullptr, nullptr, ws, st, r, x));
+        MB2_TRY(block_pipeline(b, l, x, x, batch, seqlen, h_last ? h_last[i] : nullptr,
+                               conv_tail ? conv_tail[i] : nullptr, ws, st, r, x));
+    }
+    return MB2_OK;
+}
+
+// One decode step of the stack: per layer the row-rms of the token rows, then
+// the block's step with 1/rms in in_proj's epilogue (norm weight folded into
+// in_proj) and the residual added in place by out_proj's epilogue.
+static size_t stack_step_bytes(const mb2_block *layers, int64_t n_layers, int64_t batch,
+                               size_t *off_r) {
+    size_t ws = 0;
+    for (int64_t i = 0; i < n_layers; ++i) {
+        const size_t t = make_layout(&layers[i], batch, true).total;
+        ws = t > ws ? t : ws;
+    }
+    *off_r = ws;
+    return ws + align256((size_t)batch * sizeof(float));
+}
+
+extern "C" size_t mb2_stack_step_workspace_bytes(const mb2_block *layers, int64_t n_layers,
+                                                 int64_t batch) {
+    if (!layers || n_layers <= 0 || batch < 0) return 0;
+    size_t off_r;
+    return stack_step_bytes(layers, n_layers, batch, &off_r);
+}
+
+extern "C" int mb2_stack_step(const mb2_block *layers, int64_t n_layers, float eps, void *x,
+                              float *const *h, void *const *conv_state, int64_t batch,
+                              void *workspace, size_t workspace_bytes, mb2_stream_t stream) {
+    MB2_TRY(check_stack(layers, n_layers, eps));
+    MB2_REQUIRE(batch >= 0, MB2_ERR_SHAPE, "stack step: negative batch");
+    size_t off_r;
+    const size_t need = stack_step_bytes(layers, n_layers, batch, &off_r);
+    MB2_REQUIRE(workspace_bytes >= need, MB2_ERR_WORKSPACE,
+                "stack step: workspace %zu < required %zu", workspace_bytes, need);
+    if (batch == 0) return MB2_OK;
+    MB2_REQUIRE(x && h && conv_state && workspace, MB2_ERR_ARG, "stack step: null pointer");
+    for (int64_t i = 0; i < n_layers; ++i)
+        MB2_REQUIRE(h[i] && conv_state[i], MB2_ERR_ARG, "stack step: layer %lld state missing",
+                    (long long)i);
+    cudaStream_t st = (cudaStream_t)stream;
+    char *ws = static_cast<char *>(workspace);
+    float *r = reinterpret_cast<float *>(ws + off_r);
+    for (int64_t i = 0; i < n_layers; ++i) {
+        const mb2_block &b = layers[i];
+        const Layout l = make_layout(&b, batch, true);
+        MB2_TRY(rms_scale(b.dtype, x, batch, b.d_model, eps, r, st));
+        MB2_TRY(step_head(b, l, x, conv_state[i], batch, ws, st, r));
+        MB2_TRY(step_tail(b, l, x, h[i], batch, ws, st, x));
     }
     return MB2_OK;
 }

@@ -117,6 +117,66 @@ class MambaStack(nn.Module):
         self._run_inplace(hidden_states, self._descriptors(keep))
         return hidden_states
 
+    # ------------------------------------------------------------ decode
+    def init_state(self, batch_size: int, device=None, dtype=None) -> list:
+        """Zero decode state, one CPUMamba.init_state dict per layer."""
+        return [layer.mixer.init_state(batch_size, device, dtype) for layer in self.layers]
+
+    def _state_ptrs(self, states: list, B: int, x: torch.Tensor):
+        n = len(self.layers)
+        if len(states) != n:
+            raise RuntimeError(f"expected {n} layer states, got {len(states)}")
+        hs, cs = (ctypes.c_void_p * n)(), (ctypes.c_void_p * n)()
+        for i, (layer, st) in enumerate(zip(self.layers, states)):
+            m, h, c = layer.mixer, st["h"], st["conv_state"]
+            if (h.shape != (B, m.d_inner, m.d_state) or h.dtype != torch.float32
+                    or not h.is_contiguous() or h.device != x.device
+                    or c.shape != (B, m.d_inner, m.d_conv - 1) or c.dtype != x.dtype
+                    or not c.is_contiguous() or c.device != x.device):
+                raise RuntimeError(f"layer {i}: state must be init_state's layout on the "
+                                   "input's device")
+            hs[i], cs[i] = h.data_ptr(), c.data_ptr()
+        return hs, cs
+
+    def forward_with_final_state(self, hidden_states: torch.Tensor) -> tuple:
+        """(y, [per-layer {"h", "conv_state"}]): forward() plus every layer's
+        final state (CPUMamba.forward_with_final_state per layer)."""
+        self._check(hidden_states)
+        x = hidden_states.contiguous().clone()
+        B, T, _ = x.shape
+        states = self.init_state(B, x.device, x.dtype)
+        hs, cs = self._state_ptrs(states, B, x)
+        keep = []
+        arr = self._descriptors(keep)
+        n = len(self.layers)
+        ws_bytes = lib().mb2_stack_workspace_bytes(arr, n, B, T)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+        check(lib().mb2_stack_forward_state(arr, n, ctypes.c_float(self.eps), x.data_ptr(), B, T,
+                                            hs, cs, ws.data_ptr(), ws_bytes, stream_of(x)),
+              "stack_forward_state")
+        return x, states
+
+    def forward_step(self, x_step: torch.Tensor, states: list) -> tuple:
+        """One token through every layer: (B, d_model) or (B, 1, d_model) ->
+        the residual stream after the last layer (B, d_model); each layer's
+        state is advanced in place (CPUMamba.forward_step per layer)."""
+        if x_step.dim() == 3:
+            x_step = x_step.squeeze(1)
+        if x_step.dim() != 2 or x_step.shape[-1] != self.d_model:
+            raise RuntimeError(f"expected (B, {self.d_model}), got {tuple(x_step.shape)}")
+        self.layers[0].mixer._check_io(x_step, "MambaStack.forward_step")
+        x = x_step.contiguous().clone()
+        B = x.shape[0]
+        hs, cs = self._state_ptrs(states, B, x)
+        keep = []
+        arr = self._descriptors(keep)
+        n = len(self.layers)
+        ws_bytes = lib().mb2_stack_step_workspace_bytes(arr, n, B)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+        check(lib().mb2_stack_step(arr, n, ctypes.c_float(self.eps), x.data_ptr(), hs, cs, B,
+                                   ws.data_ptr(), ws_bytes, stream_of(x)), "stack_step")
+        return x, states
+
     def forward_host(self, hidden_states: torch.Tensor, out: torch.Tensor | None = None,
                      chunks: int | None = None) -> torch.Tensor:
         """forward() for a batch in host memory, streamed through the GPU in

@@ -3,7 +3,8 @@
  *
  * Every entry point takes DEVICE pointers (caller-allocated inputs, outputs
  * and workspace), int64 shapes, a cudaStream_t, and returns an int status
- * (MB2_OK == 0).  Nothing here allocates device memory.  On failure
+ * (MB2_OK == 0).  Nothing here allocates device memory (except
+ * mb2_peer_alloc, whose purpose that is).  On failure
  * mb2_last_error() returns a thread-local message; the Python host layer
  * turns it into RuntimeError / ValueError like the reference's TORCH_CHECK.
  *
@@ -256,6 +257,26 @@ size_t mb2_stack_workspace_bytes(const mb2_block *layers, int64_t n_layers,
 int mb2_stack_forward(const mb2_block *layers, int64_t n_layers, float eps, void *x,
                       int64_t batch, int64_t seqlen, void *workspace,
                       size_t workspace_bytes, mb2_stream_t stream);
+
+/* mb2_stack_forward that also leaves each layer's final state, as
+ * CPUMamba.forward_with_final_state does for one block (_mamba.py:165-202):
+ * h_last[i] (batch, d_inner, d_state) fp32 and conv_tail[i] (batch, d_inner,
+ * d_conv-1) of layer i; either array (or an entry) may be NULL. */
+int mb2_stack_forward_state(const mb2_block *layers, int64_t n_layers, float eps, void *x,
+                            int64_t batch, int64_t seqlen, float *const *h_last,
+                            void *const *conv_tail, void *workspace, size_t workspace_bytes,
+                            mb2_stream_t stream);
+
+/* One decode step of the stack: x (batch, d_model) is the residual stream,
+ * updated in place (x <- x + block_i(RMSNorm_i(x)) for every layer i), each
+ * layer's h[i] and conv_state[i] advanced as mb2_block_step does
+ * (_mamba.py:103-163 per layer).  layers[i].in_proj.weight is the norm-folded
+ * weight, as for mb2_stack_forward. */
+size_t mb2_stack_step_workspace_bytes(const mb2_block *layers, int64_t n_layers,
+                                      int64_t batch);
+int mb2_stack_step(const mb2_block *layers, int64_t n_layers, float eps, void *x,
+                   float *const *h, void *const *conv_state, int64_t batch, void *workspace,
+                   size_t workspace_bytes, mb2_stream_t stream);
 
 /* ---- d_inner channel shards ------------------------------------------------
  * A block whose d_inner channels are split over ranks (one GPU each): blk
