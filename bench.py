@@ -126,9 +126,18 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        # samples inside the timed region (give or take one period); a region
+        # shorter than nvidia-smi's actual cadence takes the samples nearest it
+        for pad_ms in (self.PERIOD_MS, 100, 250):
+            r = self._summary(pad_ms / 1e3)
+            if r is not None:
+                r["window_pad_ms"] = pad_ms
+                return r
+        return None
+
+    def _summary(self, pad):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        pad = self.PERIOD_MS / 1e3
         for t, ln in list(self.lines):
             if self.t0 is None or self.t1 is None or not (self.t0 - pad <= t <= self.t1 + pad):
                 continue
@@ -627,13 +636,23 @@ def main():
         cfg["workload"] += f"_batch{args.batch}"
     if args.shard == "channels" and cfg["mode"] != "stack":
         cfg["workload"] += "_dinner_sharded"
-    if args.impl == "reference":
-        res = run_reference(args, cfg)
-    else:
-        res = run_ours(args, cfg)
-        ws, rank, _ = dist_env()
-        if res is not None and ws == 1 and not args.no_cpu_baseline:
-            res["cpu_baseline"] = cpu_baseline(cfg)
+    # stdout carries the one result line: whatever the libraries write there
+    # (NCCL's version banner, for one) goes to stderr until then
+    sys.stdout.flush()
+    saved_stdout = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        if args.impl == "reference":
+            res = run_reference(args, cfg)
+        else:
+            res = run_ours(args, cfg)
+            ws, rank, _ = dist_env()
+            if res is not None and ws == 1 and not args.no_cpu_baseline:
+                res["cpu_baseline"] = cpu_baseline(cfg)
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved_stdout, 1)
+        os.close(saved_stdout)
     if res is not None:
         print(json.dumps(res), flush=True)
 
