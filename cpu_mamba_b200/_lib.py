@@ -67,6 +67,11 @@ _SIGS = {
     "mb2_scan_gated": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _vp, _c_i64, _vp, _c_i64,
                                       _vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp,
                                       _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp]),
+    "mb2_scan_workspace_bytes": (ctypes.c_size_t, [_c_i64] * 4),
+    "mb2_scan_gated_ws": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _vp, _c_i64, _vp, _c_i64,
+                                         _vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp,
+                                         _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp,
+                                         ctypes.c_size_t, _vp]),
     "mb2_linear": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _vp, _vp, _vp, _vp, _c_i64,
                                   _c_i64, _c_i64, _c_i64, ctypes.c_int, _vp]),
     "mb2_split_tf32": (ctypes.c_int, [_vp, _vp, _c_i64, _vp]),

@@ -890,3 +890,21 @@ extern "C" int mb2_scan_gated(int dtype, const void *xc, int64_t ld_xc, const vo
                       h_last, y, ld_y, batch, seqlen, d_inner, d_state, (cudaStream_t)stream,
                       nullptr, 0);
 }
+
+extern "C" size_t mb2_scan_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inner,
+                                           int64_t d_state) {
+    if (batch < 0 || seqlen < 0 || d_inner < 0 || d_state < 1) return 0;
+    return scan_segment_bytes(batch, d_inner, seqlen, d_state);
+}
+
+extern "C" int mb2_scan_gated_ws(int dtype, const void *xc, int64_t ld_xc, const void *dt,
+                                 int64_t ld_dt, const void *B, int64_t ld_b, const void *C,
+                                 int64_t ld_c, const void *z, int64_t ld_z, const void *A_log,
+                                 const void *D, const float *h0, float *h_last, void *y,
+                                 int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
+                                 int64_t d_state, void *workspace, size_t workspace_bytes,
+                                 mb2_stream_t stream) {
+    return scan_gated(dtype, xc, ld_xc, dt, ld_dt, B, ld_b, C, ld_c, z, ld_z, A_log, D, h0,
+                      h_last, y, ld_y, batch, seqlen, d_inner, d_state, (cudaStream_t)stream,
+                      static_cast<float *>(workspace), workspace ? workspace_bytes : 0);
+}

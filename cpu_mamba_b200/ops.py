@@ -111,10 +111,14 @@ def scan_gated(xc, dt, Bm, Cm, z, A_log, D, batch, seqlen, h0=None, return_last_
               if return_last_state else None)
     A_log = A_log.contiguous()
     h0 = None if h0 is None else h0.contiguous()
-    check(lib().mb2_scan_gated(dtype_code(xc.dtype), ptr(xc), xc.stride(0), ptr(dt), dt.stride(0),
-                               ptr(Bm), Bm.stride(0), ptr(Cm), Cm.stride(0), ptr(z), z.stride(0),
-                               ptr(A_log), ptr(D), ptr(h0), ptr(h_last), ptr(y), y.stride(0),
-                               batch, seqlen, di, S, stream_of(xc)), "scan_gated")
+    # T-segment scratch for long sequences over few chains (0 bytes otherwise)
+    ws_bytes = lib().mb2_scan_workspace_bytes(batch, seqlen, di, S)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=xc.device) if ws_bytes else None
+    check(lib().mb2_scan_gated_ws(dtype_code(xc.dtype), ptr(xc), xc.stride(0), ptr(dt),
+                                  dt.stride(0), ptr(Bm), Bm.stride(0), ptr(Cm), Cm.stride(0),
+                                  ptr(z), z.stride(0), ptr(A_log), ptr(D), ptr(h0), ptr(h_last),
+                                  ptr(y), y.stride(0), batch, seqlen, di, S, ptr(ws), ws_bytes,
+                                  stream_of(xc)), "scan_gated")
     return (y, h_last) if return_last_state else y
 
 

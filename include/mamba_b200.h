@@ -124,6 +124,20 @@ int mb2_scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt_pre,
                    int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
                    int64_t d_state, mb2_stream_t stream);
 
+/* mb2_scan_gated with a workspace of mb2_scan_workspace_bytes(batch, seqlen,
+ * d_inner, d_state) bytes (0 = none needed): long sequences over few
+ * (batch, channel) chains then run in T segments in parallel (segment
+ * summaries, a carry pass, the outputs), as the block forward does. */
+size_t mb2_scan_workspace_bytes(int64_t batch, int64_t seqlen, int64_t d_inner,
+                                int64_t d_state);
+int mb2_scan_gated_ws(int dtype, const void *xc, int64_t ld_xc, const void *dt_pre,
+                      int64_t ld_dt, const void *B, int64_t ld_b, const void *C,
+                      int64_t ld_c, const void *z, int64_t ld_z, const void *A_log,
+                      const void *D, const float *h0, float *h_last, void *y,
+                      int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
+                      int64_t d_state, void *workspace, size_t workspace_bytes,
+                      mb2_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Linear layer y = x W^T (+ bias): nn.Linear as used by in_proj, x_proj,
  * dt_proj, out_proj (_mamba.py:67,74-75,84).

@@ -6,7 +6,7 @@ import pytest
 import torch
 
 import oracle
-from cpu_mamba_b200 import ops, selective_scan, selective_scan_assoc_chunked
+from cpu_mamba_b200 import _lib, ops, selective_scan, selective_scan_assoc_chunked
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-5
@@ -180,6 +180,40 @@ def test_scan_with_given_dt_matches_composition(dtype, b, T, S):
     y, h = ops.scan_gated(xc.cuda(), dt, xd[:, R:R + S], xd[:, R + S:], z.cuda(),
                           p["A_log"].cuda(), p["D"].cuda(), b, T, return_last_state=True)
     assert (h.cpu() - h_ref).abs().max().item() <= TOL
+    if dtype == torch.float32:
+        assert (y.cpu() - y_ref).abs().max().item() <= TOL
+    else:
+        rel = (y.cpu().float() - y_ref.float()).abs() / (y_ref.float().abs().clamp(min=1e-3) + 1e-6)
+        assert rel.mean().item() <= 2e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("with_h0", [False, True])
+def test_scan_op_long_sequence_runs_in_segments(dtype, with_h0):
+    """ops.scan_gated on one long sequence over few chains takes the T-segment
+    path (its workspace is non-empty) and matches the composition, with and
+    without an initial state."""
+    b, T, S = 1, 3000, 16
+    p = oracle.make_block_params(96, S, seed=31, dtype=dtype)
+    di = p["A_log"].shape[0]
+    assert _lib.lib().mb2_scan_workspace_bytes(b, T, di, S) > 0
+    g = torch.Generator().manual_seed(32)
+    xc = torch.nn.functional.silu(torch.randn(b * T, di, generator=g)).to(dtype)
+    dt_pre = (torch.randn(b * T, di, generator=g) * 0.5 - 3).to(dtype)
+    bc = (torch.randn(b * T, 2 * S, generator=g) * 0.5).to(dtype)
+    z = torch.randn(b * T, di, generator=g).to(dtype)
+    h0 = torch.randn(b, di, S, generator=g) * 0.1 if with_h0 else None
+    A = -torch.exp(p["A_log"].float())
+    dt = torch.nn.functional.softplus(dt_pre.float()).to(dtype).float()
+    y_scan, h_ref = oracle.selective_scan(
+        xc.float().view(b, T, di), dt.view(b, T, di), A, bc[:, :S].float().view(b, T, S),
+        bc[:, S:].float().view(b, T, S), p["D"].float(), h0=h0, return_last_state=True)
+    y_ref = y_scan.view(b * T, di).to(dtype) * torch.nn.functional.silu(z)
+    bcd = bc.cuda()
+    y, h = ops.scan_gated(xc.cuda(), dt_pre.cuda(), bcd[:, :S], bcd[:, S:], z.cuda(),
+                          p["A_log"].cuda(), p["D"].cuda(), b, T,
+                          h0=None if h0 is None else h0.cuda(), return_last_state=True)
+    assert (h.cpu() - h_ref).abs().max().item() <= 2e-5
     if dtype == torch.float32:
         assert (y.cpu() - y_ref).abs().max().item() <= TOL
     else:
