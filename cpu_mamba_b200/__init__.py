@@ -12,7 +12,7 @@ from .quant import QuantConfig, QuantizedLinear, memory_footprint, quantize_bloc
 from .ops import selective_scan
 from .scan_assoc import selective_scan_assoc, selective_scan_assoc_chunked
 from .stack import MambaLayer, MambaStack
-from . import export, surgery
+from . import export, surgery, torch_ops
 
 B200Mamba = CPUMamba
 
