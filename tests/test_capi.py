@@ -68,3 +68,64 @@ def test_status_raises_runtime_error():
     with pytest.raises(RuntimeError, match="d_state > 256"):
         _lib.check(_lib.lib().mb2_selective_scan(None, None, None, None, None, None, None,
                                                  1, 1, 1, 512, None, None, None), "selective_scan")
+
+
+def _sentinel_block():
+    blk = _lib.Block()
+    blk.d_model, blk.d_inner, blk.d_state, blk.d_conv, blk.dt_rank = 64, 128, 16, 4, 4
+    blk.dtype = 0
+    blk.conv_w = blk.A_log = 1   # non-null sentinels; validation stops before any use
+    blk.dt_proj.weight = 1
+    return blk
+
+
+def test_shard_phases_validate_before_any_launch():
+    lib = _lib.lib()
+    blk = _sentinel_block()
+    for phase in (0, 3):
+        assert lib.mb2_block_forward_shard(ctypes.byref(blk), phase, None, None, 1, 1, None,
+                                           None, None, 0, None) == 1
+        assert b"phase" in lib.mb2_last_error()
+        assert lib.mb2_block_step_shard(ctypes.byref(blk), phase, None, None, None, None, 1,
+                                        None, 0, None) == 1
+    # too small a workspace is reported before anything runs
+    assert lib.mb2_block_forward_shard(ctypes.byref(blk), 1, None, None, 2, 16, None, None,
+                                       None, 0, None) == 6
+    off, ld = ctypes.c_size_t(), ctypes.c_int64()
+    assert lib.mb2_block_shard_xdbl(ctypes.byref(blk), 32, 0, ctypes.byref(off),
+                                    ctypes.byref(ld)) == 0
+    # x_dbl rows: dt_rank, B and C segments each rounded up to 8 elements
+    assert ld.value == 8 + 16 + 16 and off.value % 256 == 0
+    assert off.value + 32 * ld.value * 4 <= lib.mb2_block_workspace_bytes(ctypes.byref(blk),
+                                                                           2, 16)
+
+
+def test_peer_allreduce_validates_group():
+    lib = _lib.lib()
+    assert lib.mb2_peer_buffer_bytes(0, 16) == 0 and lib.mb2_peer_buffer_bytes(9, 16) == 0
+    small, big = lib.mb2_peer_buffer_bytes(2, 1024), lib.mb2_peer_buffer_bytes(2, 2048)
+    assert big - small == 2 * 2 * 1024 * 4          # two parities x two ranks x fp32
+    g = _lib.PeerGroup()
+    g.world, g.rank, g.slot_elems, g.timeout_ns = 2, 2, 16, 1
+    assert lib.mb2_peer_allreduce(0, None, 4, ctypes.byref(g), None) == 1       # rank >= world
+    g.rank = 0
+    assert lib.mb2_peer_allreduce(0, None, 17, ctypes.byref(g), None) == 2      # count > slot
+    assert lib.mb2_peer_allreduce(5, None, 4, ctypes.byref(g), None) == 1       # dtype
+    g.timeout_ns = 0
+    assert lib.mb2_peer_allreduce(0, None, 4, ctypes.byref(g), None) == 1       # no bound
+    g.timeout_ns = 1
+    assert lib.mb2_peer_allreduce(0, None, 0, ctypes.byref(g), None) == 0       # nothing to do
+
+
+def test_stack_step_validates_before_any_launch():
+    lib = _lib.lib()
+    arr = (_lib.Block * 2)(_sentinel_block(), _sentinel_block())
+    assert lib.mb2_stack_step(arr, 2, ctypes.c_float(-1.0), None, None, None, 1, None, 0,
+                              None) == 1                                        # eps < 0
+    need = lib.mb2_stack_step_workspace_bytes(arr, 2, 8)
+    assert need > 0
+    assert lib.mb2_stack_step(arr, 2, ctypes.c_float(1e-5), None, None, None, 8, None, 0,
+                              None) == 6                                        # workspace
+    arr[1].d_model = 32
+    assert lib.mb2_stack_step(arr, 2, ctypes.c_float(1e-5), None, None, None, 8, None, need,
+                              None) == 2                                        # mismatched
