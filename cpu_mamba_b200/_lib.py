@@ -72,6 +72,8 @@ _SIGS = {
                                          _vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _vp, _vp,
                                          _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp,
                                          ctypes.c_size_t, _vp]),
+    "mb2_linear_recurrence": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _vp, _c_i64, _c_i64,
+                                             _c_i64, _vp]),
     "mb2_linear": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _vp, _vp, _vp, _vp, _c_i64,
                                   _c_i64, _c_i64, _c_i64, ctypes.c_int, _vp]),
     "mb2_split_tf32": (ctypes.c_int, [_vp, _vp, _c_i64, _vp]),

@@ -122,6 +122,23 @@ def scan_gated(xc, dt, Bm, Cm, z, A_log, D, batch, seqlen, h0=None, return_last_
     return (y, h_last) if return_last_state else y
 
 
+def linear_recurrence(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """h[t] = a[t] * h[t-1] + b[t] (h[-1] = 0) along dim 1 of (B, T, ...)
+    tensors: the reference's _associative_prefix_scan (scan_assoc.py:24-55)."""
+    require_cuda(a, b, what="linear_recurrence")
+    if a.shape != b.shape or a.dim() < 2:
+        raise RuntimeError("linear_recurrence: a and b must have the same (B, T, ...) shape")
+    if a.dtype != b.dtype:
+        raise RuntimeError("linear_recurrence: a and b must share a dtype")
+    a, b = a.contiguous(), b.contiguous()
+    h = torch.empty_like(a)
+    Bt, T = a.shape[0], a.shape[1]
+    inner = a.numel() // max(Bt * T, 1) if a.numel() else 0
+    check(lib().mb2_linear_recurrence(dtype_code(a.dtype), ptr(a), ptr(b), ptr(h), Bt, T, inner,
+                                      stream_of(a)), "linear_recurrence")
+    return h
+
+
 def split_tf32(w: torch.Tensor) -> torch.Tensor:
     """(2, *w.shape) float32: TF32 hi and lo halves of w (a derived cache)."""
     require_cuda(w, what="split_tf32")

@@ -8,7 +8,15 @@ both names map to it; chunk_T is accepted for API compatibility.
 """
 from __future__ import annotations
 
-from .ops import selective_scan
+from .ops import linear_recurrence, selective_scan
+
+
+def _associative_prefix_scan(a, b):
+    """h[t] = a[t] * h[t-1] + b[t], h[-1] = 0, along dim 1 of (B, T, ...)
+    tensors (scan_assoc.py:24-55): one sequential-in-time GPU kernel
+    (mb2_linear_recurrence) instead of recursive doubling; equal to within
+    fp32 reassociation."""
+    return linear_recurrence(a, b)
 
 
 def selective_scan_assoc(x, dt, A, Bp, Cp, D):

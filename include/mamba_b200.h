@@ -138,6 +138,14 @@ int mb2_scan_gated_ws(int dtype, const void *xc, int64_t ld_xc, const void *dt_p
                       int64_t d_state, void *workspace, size_t workspace_bytes,
                       mb2_stream_t stream);
 
+/* First-order linear recurrence h[t] = a[t] * h[t-1] + b[t], h[-1] = 0, over
+ * the time axis of contiguous (batch, seqlen, inner) tensors: the primitive
+ * of the reference's associative scans (src/cpu_mamba/scan_assoc.py:24-55,
+ * _associative_prefix_scan, whose trailing dims are flattened into inner).
+ * fp32 state; a, b, h all F32 or all BF16.  h may not alias a or b. */
+int mb2_linear_recurrence(int dtype, const void *a, const void *b, void *h, int64_t batch,
+                          int64_t seqlen, int64_t inner, mb2_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Linear layer y = x W^T (+ bias): nn.Linear as used by in_proj, x_proj,
  * dt_proj, out_proj (_mamba.py:67,74-75,84).

@@ -29,6 +29,7 @@ __all__ = [
     "quant_int8", "quant_int4", "quant_nf4", "dequant_int8", "dequant_int4",
     "dequant_nf4", "nf4_lut", "linear", "dequant", "load_ref_scan_op",
     "make_block_params", "stack_forward", "quant_grouped", "dequant_grouped",
+    "associative_prefix_scan",
 ]
 
 _HERE = pathlib.Path(__file__).resolve().parent
@@ -92,6 +93,22 @@ def selective_scan(x, dt, A, B, C, D, h0=None, return_last_state=False):
     if rc != 0:
         raise RuntimeError("d_state > 256 not supported (stack limit)")
     return (y, h_last) if return_last_state else y
+
+
+def associative_prefix_scan(a, b):
+    """Recursive-doubling prefix scan over dim 1 (scan_assoc.py:24-55):
+    h[t] = a[t] h[t-1] + b[t], h[-1] = 0.  Step stride s combines each
+    position with the one s earlier, (a_l, b_l) then (a_r, b_r) ->
+    (a_r a_l, a_r b_l + b_r), out of place, s doubling until it covers T."""
+    a_p, b_p = _cpu_f32(a), _cpu_f32(b)
+    T = a_p.shape[1]
+    s = 1
+    while s < T:
+        a_new = torch.cat([a_p[:, :s], a_p[:, s:] * a_p[:, :-s]], dim=1)
+        b_new = torch.cat([b_p[:, :s], a_p[:, s:] * b_p[:, :-s] + b_p[:, s:]], dim=1)
+        a_p, b_p = a_new, b_new
+        s *= 2
+    return b_p
 
 
 def load_ref_scan_op():
