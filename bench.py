@@ -575,8 +575,26 @@ def cpu_baseline(cfg, min_seconds=10.0, max_runs=10):
         oracle.block_forward(p, x, scan_op=op)
         ts.append(time.perf_counter() - t0)
     tok = batch * cfg["seqlen"]
-    return {"value": tok / statistics.median(ts), "unit": "tokens/s", "cores": cores,
-            "kind": kind, "sample": f"{batch} x {cfg['seqlen']} tokens per forward, median of {len(ts)}"}
+    res = {"value": tok / statistics.median(ts), "unit": "tokens/s", "cores": cores,
+           "kind": kind, "sample": f"{batch} x {cfg['seqlen']} tokens per forward, median of {len(ts)}"}
+    # the scan op alone (selective_scan_cpu, or the oracle's C restatement) on
+    # the same sample's shapes, timed apart as the reference's bench does
+    T, di, S = cfg["seqlen"], 2 * cfg["d_model"], cfg["d_state"]
+    g = torch.Generator().manual_seed(7)
+    args = (torch.randn(batch, T, di, generator=g), torch.rand(batch, T, di, generator=g) * 0.1,
+            -torch.rand(di, S, generator=g), torch.randn(batch, T, S, generator=g),
+            torch.randn(batch, T, S, generator=g), torch.ones(di))
+    scan = (lambda: op.selective_scan_cpu(*args)) if op is not None else \
+        (lambda: oracle.selective_scan(*args))
+    scan()
+    st = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        scan()
+        st.append(time.perf_counter() - t0)
+    res["scan_only"] = {"value": tok / statistics.median(st), "unit": "tokens/s",
+                        "ms": statistics.median(st) * 1e3}
+    return res
 
 
 def run_reference(args, cfg):
