@@ -259,8 +259,11 @@ scan_kernel(const ScanParams p) {
     const int c = tid / L;          // channel within CTA
     const int j = tid % L;          // lane within the channel's group
     const int nseg = p.nseg > 1 ? p.nseg : 1;
-    const int b = blockIdx.y / nseg;
-    const int g = blockIdx.y - b * nseg;              // T segment
+    // the summary pass skips each sequence's last segment (nothing needs its
+    // summary: the output pass runs it from its start state to the final state)
+    const int gsegs = (MODE == SUMMARY && nseg > 1) ? nseg - 1 : nseg;
+    const int b = blockIdx.y / gsegs;
+    const int g = blockIdx.y - b * gsegs;             // T segment
     const int64_t tb = (int64_t)g * p.seg_len;        // first step of the segment
     int64_t tl = nseg > 1 ? p.seqlen - tb : p.seqlen;
     if (nseg > 1 && tl > p.seg_len) tl = p.seg_len;
@@ -467,11 +470,11 @@ scan_kernel(const ScanParams p) {
         __syncthreads();
     }
     cp_async_wait<0>();
-    // final state: of the sequence (no segments), or of the segment (pass 1);
-    // with segments the carry kernel produces the sequence's final state
+    // final state: of the segment (pass 1), or of the sequence, which the
+    // sequence's last segment (the whole sequence without segments) ends in
     float *hout = MODE == SUMMARY ? p.seg_hend + segidx * p.d_inner * S
-                            : ((nseg == 1 && p.h_last) ? p.h_last + (int64_t)b * p.d_inner * S
-                                                       : nullptr);
+                            : ((g == nseg - 1 && p.h_last) ? p.h_last + (int64_t)b * p.d_inner * S
+                                                           : nullptr);
     if (hout && active) {
 #pragma unroll
         for (int q = 0; q < NP; ++q) {
@@ -490,13 +493,14 @@ scan_kernel(const ScanParams p) {
 // Segments' carry (between pass 1 and pass 3): per (b, d, s), in segment
 // order, start(g) = h, then h = exp(A sum(dt_g)) h + h_end(g) -- the product of
 // the segment's per-step decays exp(dt_t A) is the exponential of A times the
-// sum of its dt.  The state after the last segment is the sequence's final
+// sum of its dt.  Only the start states are needed: the last segment has no
+// summary, and pass 3 runs it from its start state to the sequence's final
 // state.  A: fp32 (PLAIN) or A_log in T (A = -exp(A_log)).
 template <typename T, bool A_F32>
 __global__ void seg_carry_kernel(const void *A, const float *__restrict__ h0,
                                  const float *__restrict__ hend, const float *__restrict__ sdt,
-                                 float *__restrict__ hstart, float *__restrict__ h_last,
-                                 int64_t batch, int64_t di, int S, int nseg) {
+                                 float *__restrict__ hstart, int64_t batch, int64_t di, int S,
+                                 int nseg) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= batch * di * S) return;
     const int64_t s = i % S, bd = i / S;
@@ -508,9 +512,8 @@ __global__ void seg_carry_kernel(const void *A, const float *__restrict__ h0,
     for (int g = 0; g < nseg; ++g) {
         const int64_t idx = (b * nseg + g) * di + d;
         hstart[idx * S + s] = hv;
-        hv = fmaf(ex2(a2 * sdt[idx]), hv, hend[idx * S + s]);
+        if (g + 1 < nseg) hv = fmaf(ex2(a2 * sdt[idx]), hv, hend[idx * S + s]);
     }
-    if (h_last) h_last[i] = hv;
 }
 
 // -------------------------------------------------------------- dispatch ---
@@ -537,8 +540,8 @@ static int launch_scan(ScanParams p, cudaStream_t st) {
     if (rows16(p.bm, p.ld_b, es)) p.vec16 |= ARR_B;
     if (rows16(p.cm, p.ld_c, es)) p.vec16 |= ARR_C;
     if (MODE == FUSED && rows16(p.dl, p.ld_dl, es)) p.vec16 |= ARR_DL;
-    dim3 grid((unsigned)ceil_div(p.d_inner, Gm::CH),
-              (unsigned)(p.batch * (p.nseg > 1 ? p.nseg : 1)));
+    const int gsegs = p.nseg > 1 ? (MODE == SUMMARY ? p.nseg - 1 : p.nseg) : 1;
+    dim3 grid((unsigned)ceil_div(p.d_inner, Gm::CH), (unsigned)(p.batch * gsegs));
     kern<<<grid, SCAN_THREADS, Gm::BYTES, st>>>(p);
     return check_launch("scan_kernel");
 }
@@ -652,15 +655,18 @@ static int run_segmented(ScanParams p, int nseg, float *ws, cudaStream_t st) {
     const int64_t S = p.d_state;
     p.seg_len = round_up(ceil_div(p.seqlen, (int64_t)nseg), (int64_t)SCAN_TC);
     p.nseg = (int)ceil_div(p.seqlen, p.seg_len);
+    if (p.nseg < 2) {                    // rounding left one segment: run it whole
+        p.nseg = 0;
+        return dispatch_scan<T, MODE>(p, st);
+    }
     const int64_t nstates = p.batch * p.nseg * p.d_inner * S;
     float *hend = ws, *hstart = ws + nstates, *sdt = ws + 2 * nstates;
-    float *h_last = p.h_last;
     static_assert(MODE == GATED, "segments are run for the gated scan");
     p.seg_hend = hend; p.seg_sdt = sdt; p.seg_hstart = nullptr;
     MB2_TRY((dispatch_scan<T, SUMMARY>(p, st)));
     const int64_t n = p.batch * p.d_inner * S;
     seg_carry_kernel<T, MODE == PLAIN><<<(unsigned)ceil_div(n, (int64_t)256), 256, 0, st>>>(
-        p.A, p.h0, hend, sdt, hstart, h_last, p.batch, p.d_inner, (int)S, p.nseg);
+        p.A, p.h0, hend, sdt, hstart, p.batch, p.d_inner, (int)S, p.nseg);
     MB2_TRY(check_launch("seg_carry_kernel"));
     p.seg_hstart = hstart;
     return dispatch_scan<T, MODE>(p, st);
