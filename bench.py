@@ -19,10 +19,11 @@ Multi-GPU: one process per GPU (torchrun); each rank runs its own batch
 CUDA-event time of the K timed steps.  Inputs rotate over >= 4 buffers whose
 total exceeds the 126 MB L2, and every step moves > 1 GB through HBM.
 
---impl reference times the reference's CPU implementation on the host cores:
-the block composition in torch CPU ops (the same ATen calls the reference
-makes) around the reference's own compiled C++ scan op from oracle/_ref (the
-oracle's C restatement when that was not built).
+--impl reference times the reference's CPU implementation on the host cores,
+on the same workload (config 0: all 151 x 180 tokens per step): the block
+composition in torch CPU ops (the same ATen calls the reference makes) around
+the reference's own compiled C++ scan op from oracle/_ref; without that op the
+arm prints an "unavailable" line.
 """
 from __future__ import annotations
 
@@ -338,14 +339,10 @@ def run_ours(args, cfg):
             "scaling": "strong" if stack_mode or channels else "weak",
             "vs_baseline": None,
             "dtype": cfg["dtype"], "data": "synthetic (seeded; shapes of the configuration)",
-            "config": {"workload": cfg["workload"], "batch_per_gpu": B,
-                       "global_batch": int(tokens_all) // (1 if step_mode else T),
-                       "seq_len": T if not step_mode else 1, "d_model": dm,
-                       "d_inner": 2 * dm, "d_state": cfg["d_state"], "dt_rank": R,
-                       "quant": cfg.get("quant"), "parallelism": par,
-                       "layers": cfg.get("n_layers", 1),
-                       "decode": "forward_step captured as one CUDA graph" if step_mode else None,
-                       "l2": f"inputs rotated over {nbuf} buffers ({nbuf * in_bytes / 2**20:.0f} MB > L2)"},
+            "config": dict(workload_config(cfg, B, int(tokens_all) // (1 if step_mode else T),
+                                           ws_label=par),
+                           l2=f"inputs rotated over {nbuf} buffers "
+                              f"({nbuf * in_bytes / 2**20:.0f} MB > L2)"),
             "roofline": roof, "stages_ms": stages, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk.summary(),
@@ -355,6 +352,18 @@ def run_ours(args, cfg):
         reducer.close()
     dist.shutdown()
     return result
+
+
+def workload_config(cfg, batch_per_gpu, global_batch, ws_label):
+    """The line's ``config``: the workload and its sizes (both arms)."""
+    step_mode = cfg["mode"] == "step"
+    dm = cfg["d_model"]
+    return {"workload": cfg["workload"], "batch_per_gpu": batch_per_gpu,
+            "global_batch": global_batch, "seq_len": 1 if step_mode else cfg["seqlen"],
+            "d_model": dm, "d_inner": 2 * dm, "d_state": cfg["d_state"],
+            "dt_rank": cfg.get("dt_rank", math.ceil(dm / 16)), "quant": cfg.get("quant"),
+            "parallelism": ws_label, "layers": cfg.get("n_layers", 1),
+            "decode": "forward_step captured as one CUDA graph" if step_mode else None}
 
 
 def step_e2e(m, host_in, host_out, graph, step_mode, dev, channels=False):
@@ -422,10 +431,10 @@ def profile_stages(m, x, cfg, dtype, steps):
     return {k: statistics.mean(v) for k, v in times.items()}
 
 
-# DRAM bytes (read + write) per token of each launch, from ncu captures of the
-# config-0 shapes at batch 64 (profiles/gemm_tc_f32x3_b64_t180.md,
-# profiles/scan_gated_f32_b64_t180.md, profiles/conv1d_silu_f32_b64_t180.md);
-# every tensor these kernels touch grows with the token count, so a full-size
+# DRAM bytes (read + write) per token of each launch of the fp32 block at
+# d_model 768, d_state 24: ncu's dram__bytes_read.sum and dram__bytes_write.sum
+# of one launch over batch 64 x 180 tokens (11,520 rows), divided by the rows.
+# Every tensor these kernels touch grows with the token count, so a full-size
 # launch moves (bytes per token) x N.  (dt_proj's output mostly stays in L2
 # at batch 64, so its figure under-counts a full-size launch.)
 TRAFFIC_PER_TOKEN = {
@@ -598,30 +607,45 @@ def cpu_baseline(cfg, min_seconds=10.0, max_runs=10):
 
 
 def run_reference(args, cfg):
+    """The reference's CPU block forward on the host cores, on the arm's own
+    workload: every step is one forward over the configuration's whole batch
+    (config 0: 151 x 180 tokens).  The scan is the reference's own compiled op
+    (oracle/_ref); the torch CPU ops around it are the oracle's restatement of
+    _mamba.py:204-265, which makes the reference's ATen calls (the reference's
+    Python tree cannot be imported where this runs).  Without the compiled op
+    there is no reference to time, and the arm says so."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return None
     if cfg["mode"] != "forward" or cfg.get("quant"):
-        return {"impl": "reference", "unavailable": "reference arm covers the forward workloads only"}
+        return {"impl": "reference", "unavailable": "the reference arm times the block forward "
+                "workloads (configs 0 and 1); this configuration has no CPU reference arm"}
     cores = cpu_cores()
     torch.set_num_threads(cores)
-    batch = min(cfg["batch"], 16) if cfg["batch"] * cfg["seqlen"] <= 30000 else 1
+    batch = cfg["batch"]
     oracle, p, op, kind, x = cpu_forward_setup(cfg, batch)
+    if op is None:
+        return {"impl": "reference", "unavailable": "the reference's compiled scan op "
+                "(oracle/_ref/selective_scan_cpu.so) was not built"}
     for _ in range(args.warmup):
         oracle.block_forward(p, x, scan_op=op)
-    t0 = time.perf_counter()
+    ts = []
     for _ in range(args.steps):
+        t0 = time.perf_counter()
         oracle.block_forward(p, x, scan_op=op)
-    dt = time.perf_counter() - t0
+        ts.append(time.perf_counter() - t0)
+    dt = sum(ts)
     tok = batch * cfg["seqlen"]
     value = tok * args.steps / dt
-    sample = f"{batch} x {cfg['seqlen']} tokens per step (batch rows are independent)"
+    sample = (f"the whole workload, {batch} x {cfg['seqlen']} tokens, per step; "
+              f"{cores} host threads")
     return {"metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference",
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": cfg["dtype"], "data": "synthetic (seeded)",
-            "config": {"workload": cfg["workload"], "batch_sample": batch, "seq_len": cfg["seqlen"],
-                       "d_model": cfg["d_model"], "d_state": cfg["d_state"]},
+            "vs_baseline": None, "dtype": cfg["dtype"],
+            "data": "synthetic (seeded; shapes of the configuration)",
+            "config": dict(workload_config(cfg, batch, batch, ws_label="batch-sharded x1"),
+                           l2="inputs in host memory (CPU arm)"),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind,
                              "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,

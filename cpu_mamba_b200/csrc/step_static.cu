@@ -12,10 +12,13 @@
 // The array (MB2_STEP_STATIC_SCRATCH_BYTES, 8 MiB) is a file-scope __device__
 // variable: every GPU that loads the library holds it until the process exits.
 // Its host-side name is only a stand-in, so its device address is looked up
-// with cudaGetSymbolAddress, once per device, the first time this entry point
-// runs on that device (with that device current).  That lookup can load the
-// module onto the device, so the first call on each device should come before
-// any stream capture.
+// with cudaGetSymbolAddress, with the device current, the first time this
+// entry point runs on a device.  That lookup can load the module onto the
+// device, so the first call on each device should come before any stream
+// capture.  The address is kept per device together with the id of the CUDA
+// context it was found in: after cudaDeviceReset (which unloads the module and
+// frees the array) the device has a new context, the ids differ, and the next
+// call looks the address up again instead of handing a freed one to the kernels.
 //
 // All calls on a device share the one array, and it keeps whatever the last
 // call left in it.  The step writes every scratch byte it reads before reading
@@ -24,6 +27,8 @@
 // between calls.  Calls whose work overlaps on the GPU (on different streams,
 // or from different host threads without ordering) race on the array; callers
 // must order them.
+#include <cuda.h>
+
 #include "common.cuh"
 
 #include <mutex>
@@ -34,9 +39,42 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 std::mutex g_setup_mu;
-void *g_scratch_ptr[kMaxDevices];   // device address of g_step_scratch, per device
+struct ScratchAddr {
+    void *ptr;              // device address of g_step_scratch
+    unsigned long long ctx; // id of the context it belongs to
+};
+ScratchAddr g_scratch[kMaxDevices];
 
-// device address of the scratch array on the current device (looked up once)
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+
+// id of the current CUDA context (unique for the process's lifetime), or 0
+// when the driver cannot tell; 0 makes the caller look the address up again
+unsigned long long current_context_id() {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static bool tried = false;
+    if (!tried) {    // called under g_setup_mu
+        tried = true;
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+        fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(fn);
+    }
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx ||
+        get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
+
+// device address of the scratch array in the current device's context
 int scratch_for_current_device(void **out) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
@@ -45,15 +83,20 @@ int scratch_for_current_device(void **out) {
     MB2_REQUIRE(dev >= 0 && dev < kMaxDevices, MB2_ERR_UNSUPPORTED,
                 "step_static: device ordinal %d above %d", dev, kMaxDevices - 1);
     std::lock_guard<std::mutex> lock(g_setup_mu);
-    if (!g_scratch_ptr[dev]) {
+    const unsigned long long ctx = current_context_id();
+    ScratchAddr &a = g_scratch[dev];
+    if (!a.ptr || ctx == 0 || a.ctx != ctx) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_step_scratch);
         MB2_REQUIRE(e == cudaSuccess && p, MB2_ERR_CUDA,
                     "step_static: cudaGetSymbolAddress on device %d: %s", dev,
                     cudaGetErrorString(e));
-        g_scratch_ptr[dev] = p;
+        a.ptr = p;
+        // read again: the lookup makes the device's primary context current
+        // when nothing had used the device yet
+        a.ctx = current_context_id();
     }
-    *out = g_scratch_ptr[dev];
+    *out = a.ptr;
     return MB2_OK;
 }
 

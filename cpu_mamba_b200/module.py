@@ -305,15 +305,15 @@ class StepGraph:
 
 
 def assert_state_dict_compatible(cpu_mamba: CPUMamba, sd: dict):
-    """Raise ValueError naming extra / missing keys or the first shape mismatch
-    (_mamba.py:268-279)."""
-    own = dict(cpu_mamba.state_dict())
-    extra = set(sd.keys()) - set(own.keys())
-    missing = set(own.keys()) - set(sd.keys())
-    if extra:
-        raise ValueError(f"unexpected keys in source state_dict: {sorted(extra)}")
-    if missing:
-        raise ValueError(f"missing keys in source state_dict: {sorted(missing)}")
-    for k in own:
-        if own[k].shape != sd[k].shape:
-            raise ValueError(f"shape mismatch on {k}: own {own[k].shape} vs src {sd[k].shape}")
+    """Raise ValueError when ``sd`` cannot be loaded into ``cpu_mamba``: keys it
+    has and the module lacks, keys it lacks, or the first tensor whose shape
+    differs (the messages of _mamba.py:268-279)."""
+    own = cpu_mamba.state_dict()
+    for label, keys in (("unexpected keys in source state_dict", set(sd) - set(own)),
+                        ("missing keys in source state_dict", set(own) - set(sd))):
+        if keys:
+            raise ValueError(f"{label}: {sorted(keys)}")
+    mismatched = [k for k in own if own[k].shape != sd[k].shape]
+    if mismatched:
+        k = mismatched[0]
+        raise ValueError(f"shape mismatch on {k}: own {own[k].shape} vs src {sd[k].shape}")

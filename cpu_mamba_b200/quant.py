@@ -179,36 +179,53 @@ class QuantizedLinear(nn.Module):
 _QUANTIZABLE_LINEARS = ("in_proj", "x_proj", "dt_proj", "out_proj")
 
 
+def _linear_sites(module: nn.Module, names: Iterable[str]):
+    """Every (parent, attribute, nn.Linear) whose attribute name is one of
+    ``names``, found by a depth-first walk that visits each module once and
+    does not descend into the linears it returns."""
+    wanted = frozenset(names)
+    sites, visited, pending = [], set(), [module]
+    while pending:
+        parent = pending.pop()
+        if id(parent) in visited:
+            continue
+        visited.add(id(parent))
+        for attr, child in parent._modules.items():
+            if child is None:
+                continue
+            if attr in wanted and isinstance(child, nn.Linear):
+                sites.append((parent, attr, child))
+            else:
+                pending.append(child)
+    return sites
+
+
 def quantize_block(module: nn.Module, config: QuantConfig,
                    target_names: Iterable[str] = _QUANTIZABLE_LINEARS) -> int:
-    """Replace nn.Linear children named in target_names by QuantizedLinear,
-    recursively and in place; returns the number replaced (quant.py:205-226)."""
-    n_replaced = 0
-    target_set = set(target_names)
-    for _, parent in list(module.named_modules()):
-        for child_name, child in list(parent.named_children()):
-            if isinstance(child, nn.Linear) and child_name in target_set:
-                qlin = QuantizedLinear(
-                    weight=child.weight.detach(),
-                    bias=child.bias.detach() if child.bias is not None else None,
-                    scheme=config.scheme, group_size=config.group_size)
-                qlin = qlin.to(device=child.weight.device)
-                setattr(parent, child_name, qlin)
-                n_replaced += 1
-    return n_replaced
+    """Swap, in place, every nn.Linear held under one of ``target_names``
+    (at any depth of ``module``) for a QuantizedLinear of ``config``'s scheme on
+    the linear's device, and return how many were swapped -- four per block
+    (the interface of quant.py:205-226).  Sites are collected before any swap,
+    so the new modules are never revisited."""
+    sites = _linear_sites(module, target_names)
+    for parent, attr, lin in sites:
+        bias = None if lin.bias is None else lin.bias.detach()
+        q = QuantizedLinear(lin.weight.detach(), bias, config.scheme, group_size=config.group_size)
+        setattr(parent, attr, q.to(device=lin.weight.device))
+    return len(sites)
 
 
 def memory_footprint(module: nn.Module) -> dict:
-    """Parameter bytes vs quantised-buffer bytes (quant.py:229-245)."""
-    fp_bytes = 0
-    quant_bytes = 0
-    for p in module.parameters():
-        fp_bytes += p.numel() * p.element_size()
-    for name, b in module.named_buffers():
-        nbytes = b.numel() * b.element_size()
-        if name.endswith(".weight_q") or name.endswith(".scale"):
-            quant_bytes += nbytes
-        else:
-            fp_bytes += nbytes
-    return {"param_bytes": fp_bytes, "quant_buffer_bytes": quant_bytes,
-            "total_bytes": fp_bytes + quant_bytes}
+    """Bytes held by ``module``: quantised buffers (names ending in
+    ``.weight_q`` / ``.scale``) apart from everything else (parameters and the
+    other buffers), with the keys of quant.py:229-245."""
+    def nbytes(t):
+        return t.numel() * t.element_size()
+
+    quantised = {".weight_q", ".scale"}
+    split = {True: 0, False: 0}
+    for name, buf in module.named_buffers():
+        split[any(name.endswith(sfx) for sfx in quantised)] += nbytes(buf)
+    dense = sum(nbytes(p) for p in module.parameters()) + split[False]
+    return {"param_bytes": dense, "quant_buffer_bytes": split[True],
+            "total_bytes": dense + split[True]}

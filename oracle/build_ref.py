@@ -9,7 +9,11 @@ reference tree.
 
 The system g++ is used because the toolchain under /opt/gcc lacks libgomp.spec.
 
-    python oracle/build_ref.py --src <path to selective_scan_cpu.cpp> --out oracle/_ref
+    python oracle/build_ref.py [--src <path to selective_scan_cpu.cpp>] [--out oracle/_ref]
+
+Without --src the source is looked up in the reference tree that
+oracle/refpath.py locates (MB2_REFERENCE_DIR, or a ``reference`` directory
+beside this repository).
 """
 from __future__ import annotations
 
@@ -19,12 +23,16 @@ import pathlib
 import sys
 
 HERE = pathlib.Path(__file__).resolve().parent
-DEFAULT_SRC = "/root/reference/src/cpu_mamba/selective_scan_cpu.cpp"
+sys.path.insert(0, str(HERE))
+from refpath import scan_source  # noqa: E402
 
 
-def build(src: str = DEFAULT_SRC, out: str | os.PathLike = HERE / "_ref",
+def build(src: str | os.PathLike | None = None, out: str | os.PathLike = HERE / "_ref",
           verbose: bool = False) -> pathlib.Path | None:
     """Build the reference op; returns the .so path, or None when the source is absent."""
+    src = src if src is not None else scan_source()
+    if src is None:
+        return None
     src_p = pathlib.Path(src)
     if not src_p.exists():
         return None
@@ -47,12 +55,13 @@ def build(src: str = DEFAULT_SRC, out: str | os.PathLike = HERE / "_ref",
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--src", default=DEFAULT_SRC)
+    ap.add_argument("--src", default=None)
     ap.add_argument("--out", default=str(HERE / "_ref"))
     args = ap.parse_args()
     so = build(args.src, args.out, verbose=True)
     if so is None:
-        print(f"reference source not found: {args.src}", file=sys.stderr)
+        print(f"reference source not found: {args.src or 'set MB2_REFERENCE_DIR'}",
+              file=sys.stderr)
         return 1
     print(so)
     return 0

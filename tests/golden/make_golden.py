@@ -2,7 +2,10 @@
 
 Run in a container that has the reference source tree (it cannot travel):
 
-    CXX=/usr/bin/g++ python tests/golden/make_golden.py --ref /root/reference/src
+    MB2_REFERENCE_DIR=<cpu-mamba checkout> python tests/golden/make_golden.py
+
+(or --ref <checkout>/src; without either, a ``reference`` directory beside this
+repository is used when it exists).
 
 The reference's JIT C++ scan op is built and REQUIRED: the reference silently
 falls back to its Python time loop when the build fails
@@ -21,6 +24,7 @@ import math
 import os
 import pathlib
 import sys
+import tempfile
 
 import torch
 
@@ -31,7 +35,8 @@ REPO = HERE.parent.parent
 def _import_reference(ref_src: str):
     if os.path.exists("/usr/bin/g++"):       # /opt/gcc cannot link OpenMP here
         os.environ["CXX"] = "/usr/bin/g++"
-    os.environ.setdefault("TORCH_EXTENSIONS_DIR", str(REPO / "_work" / "torch_ext"))
+    # the op's JIT build goes to a throwaway directory, never into the repository
+    os.environ.setdefault("TORCH_EXTENSIONS_DIR", tempfile.mkdtemp(prefix="mb2_golden_ext_"))
     sys.path.insert(0, ref_src)
     import cpu_mamba  # noqa: F401
     from cpu_mamba import _mamba, quant
@@ -171,10 +176,18 @@ def quant_cases(_mamba, quant):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference/src")
+    ap.add_argument("--ref", default=None, help="the reference's src/ directory")
     args = ap.parse_args()
+    ref = args.ref
+    if ref is None:
+        sys.path.insert(0, str(REPO / "oracle"))
+        from refpath import reference_root
+        root = reference_root()
+        if root is None:
+            sys.exit("reference tree not found: pass --ref or set MB2_REFERENCE_DIR")
+        ref = str(root / "src")
     torch.manual_seed(0)
-    _mamba, quant, op = _import_reference(args.ref)
+    _mamba, quant, op = _import_reference(ref)
     torch.save(scan_cases(op), HERE / "scan.pt")
     torch.save(block_cases(_mamba), HERE / "block.pt")
     torch.save(stateful_cases(_mamba), HERE / "stateful.pt")

@@ -168,3 +168,33 @@ def test_surgery_stub_and_swap(monkeypatch):
     after = model.state_dict()
     assert set(after) == set(before)
     assert all(torch.equal(after[k], before[k]) for k in before)
+
+
+def test_quantize_block_finds_every_named_linear_once():
+    """quantize_block's site walk (no quantisation, so no GPU): the linears
+    named like a block's projections at any depth, each parent visited once,
+    nothing found inside a matching linear, other names left alone."""
+    from cpu_mamba_b200.quant import _QUANTIZABLE_LINEARS, _linear_sites
+    inner = CPUMamba(32, 8)
+    outer = torch.nn.Module()
+    outer.a = inner
+    outer.b = inner                      # the same block under two names: one visit
+    outer.c = torch.nn.Sequential(CPUMamba(32, 8))
+    outer.in_proj = torch.nn.Sequential(torch.nn.Linear(4, 4))   # not a Linear itself
+    outer.head = torch.nn.Linear(4, 4)                          # not a target name
+    sites = _linear_sites(outer, _QUANTIZABLE_LINEARS)
+    assert len(sites) == 8
+    assert sorted({a for _, a, _ in sites}) == sorted(_QUANTIZABLE_LINEARS)
+    assert all(isinstance(lin, torch.nn.Linear) and getattr(p, a) is lin for p, a, lin in sites)
+
+
+def test_memory_footprint_splits_quantised_buffers():
+    m = torch.nn.Module()
+    m.lin = torch.nn.Linear(8, 4, bias=True)                  # 36 floats
+    q = torch.nn.Module()
+    q.register_buffer("weight_q", torch.zeros(4, 8, dtype=torch.int8))
+    q.register_buffer("scale", torch.zeros(4))
+    q.register_buffer("other", torch.zeros(3))
+    m.q = q
+    assert memory_footprint(m) == {"param_bytes": 36 * 4 + 12, "quant_buffer_bytes": 32 + 16,
+                                   "total_bytes": 36 * 4 + 12 + 48}

@@ -3,8 +3,9 @@ fixed device array (for callers that cannot allocate device memory).
 
 Checked through the C ABI against mb2_block_step with a caller workspace, on
 two calls in a row (the second call finds the first call's leftovers in the
-shared array).  Named so that pytest collects it last; it also passes alone in
-a fresh process, where its first call performs the per-device set-up."""
+shared array), and with the device's free memory unchanged across a warmed-up
+call.  Named so that pytest collects it last; it also passes alone in a fresh
+process, where its first call performs the per-device set-up."""
 import ctypes
 
 import pytest
@@ -36,13 +37,11 @@ def _step_workspace(m, blk, x, h, conv):
     return out
 
 
-def _step_static(blk, x, h, conv):
-    out = torch.empty_like(x)
+def _step_static_into(blk, x, out, h, conv):
     _lib.check(_lib.lib().mb2_block_step_static(ctypes.byref(blk), x.data_ptr(), out.data_ptr(),
                                                 h.data_ptr(), conv.data_ptr(), x.shape[0],
                                                 _lib.stream_of(x)),
                "mb2_block_step_static")
-    return out
 
 
 def _close(a, b, dtype):
@@ -65,11 +64,16 @@ def test_static_step_matches_workspace_step(dtype, batch):
     _, state = m.forward_with_final_state(prompt)
     h_a, conv_a = state["h"].clone(), state["conv_state"].clone()
     h_b, conv_b = state["h"].clone(), state["conv_state"].clone()
-    for _ in range(2):   # two calls in a row
+    for i in range(2):   # two calls in a row
         x = torch.randn(batch, m.d_model, device="cuda", generator=g).to(dtype)
         y_ref = _step_workspace(m, blk, x, h_a, conv_a)
-        y = _step_static(blk, x, h_b, conv_b)
+        y = torch.empty_like(x)
         torch.cuda.synchronize()
+        free_before = torch.cuda.mem_get_info()[0]
+        _step_static_into(blk, x, y, h_b, conv_b)
+        torch.cuda.synchronize()
+        if i > 0:   # the first call may still load kernels lazily
+            assert torch.cuda.mem_get_info()[0] == free_before, "the static step allocated"
         assert torch.isfinite(y.float()).all()
         assert _close(y, y_ref, dtype)
         assert (h_b - h_a).abs().max().item() <= 1e-5
