@@ -29,7 +29,7 @@ __all__ = [
     "quant_int8", "quant_int4", "quant_nf4", "dequant_int8", "dequant_int4",
     "dequant_nf4", "nf4_lut", "linear", "dequant", "load_ref_scan_op",
     "make_block_params", "stack_forward", "quant_grouped", "dequant_grouped",
-    "associative_prefix_scan",
+    "associative_prefix_scan", "block_forward_f64",
 ]
 
 _HERE = pathlib.Path(__file__).resolve().parent
@@ -293,6 +293,41 @@ def block_forward(p, x, quant=None, scan_op=None):
         y = scan_op.selective_scan_cpu(*args) if scan_op is not None else selective_scan(*args)
         y = y.to(xc.dtype) * F.silu(z)                         # :263-264
         return linear(p, "out_proj", y, quant)                 # :265
+
+
+def block_forward_f64(p, x, quant=None):
+    """CPUMamba.forward (_mamba.py:204-265) evaluated in float64 throughout,
+    with a float64 time-loop scan (_mamba.py:245-261): the yardstick for how
+    far a float32 evaluation (the reference's own, or the GPU's) sits from the
+    exact result.  Quantised linears use their dequantised float32 weights
+    (quant.py:188-190), widened."""
+    with torch.no_grad():
+        d = {k: v.double() for k, v in p.items() if v.is_floating_point()}
+        for name in (quant or {}):
+            scheme, in_dim = quant[name][:2]
+            d[f"{name}.weight"] = dequant(scheme, p[f"{name}.weight_q"], p[f"{name}.scale"],
+                                          in_dim).double()
+        x = _cpu_f32(x).double()
+        bsz, T, _ = x.shape
+        di, S = d["A_log"].shape
+        K = d["conv1d.weight"].shape[-1]
+        R = d["dt_proj.weight"].shape[1]
+        xz = F.linear(x, d["in_proj.weight"], d.get("in_proj.bias"))
+        x_pre, z = xz.chunk(2, dim=-1)
+        xc = F.conv1d(x_pre.transpose(1, 2), d["conv1d.weight"], d.get("conv1d.bias"),
+                      padding=K - 1, groups=di)[..., :T]
+        xc = F.silu(xc.transpose(1, 2))
+        dt_low, Bm, Cm = torch.split(F.linear(xc, d["x_proj.weight"]), [R, S, S], dim=-1)
+        dt = F.softplus(F.linear(dt_low, d["dt_proj.weight"], d.get("dt_proj.bias")))
+        A = -torch.exp(d["A_log"])
+        h = torch.zeros(bsz, di, S, dtype=torch.float64)
+        ys = []
+        for t in range(T):
+            h = torch.exp(dt[:, t, :, None] * A) * h + \
+                (dt[:, t, :, None] * Bm[:, t, None, :]) * xc[:, t, :, None]
+            ys.append((h * Cm[:, t, None, :]).sum(-1))
+        y = (torch.stack(ys, 1) + d["D"] * xc) * F.silu(z)
+        return F.linear(y, d["out_proj.weight"], d.get("out_proj.bias"))
 
 
 def stack_forward(layers, x, eps=1e-5, scan_op=None):
