@@ -396,8 +396,13 @@ def profile_stages(m, x, cfg, dtype, steps):
     B, T, dm = x.shape
     di, S, R = m.d_inner, m.d_state, m.dt_rank
     stream = torch.cuda.current_stream(dev)
-    split = {n: (m._tf32_split(n, getattr(m, n).weight) if dtype == torch.float32 else None)
+    # the weight caches the block forward uses: the fp16 split (F16X3) for the
+    # three large projections, the TF32 split for dt_proj (K = dt_rank)
+    fp32 = dtype == torch.float32
+    split = {n: (m._tf32_split(n, getattr(m, n).weight) if fp32 and n == "dt_proj" else None)
              for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
+    s16 = {n: (m._f16_split(n, getattr(m, n).weight) if fp32 and n != "dt_proj" else None)
+           for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
     x2 = x.reshape(B * T, dm)
     times = {k: [] for k in STAGES}
     # outputs allocated once: the timed region holds only the launches
@@ -410,11 +415,13 @@ def profile_stages(m, x, cfg, dtype, steps):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)]
         with torch.no_grad():
             ev[0].record(stream)
-            ops.linear(x2, m.in_proj.weight, None, split["in_proj"], out=xz)
+            ops.linear(x2, m.in_proj.weight, None, split["in_proj"], out=xz,
+                       weight_f16=s16["in_proj"])
             ev[1].record(stream)
             ops.conv1d_silu(xz, m.conv1d.weight, m.conv1d.bias, B, T, di, out=xc)
             ev[2].record(stream)
-            ops.linear(xc, m.x_proj.weight, None, split["x_proj"], out=xdbl)
+            ops.linear(xc, m.x_proj.weight, None, split["x_proj"], out=xdbl,
+                       weight_f16=s16["x_proj"])
             ev[3].record(stream)
             ops.linear(xdbl[:, :R], m.dt_proj.weight, m.dt_proj.bias, split["dt_proj"],
                        out=xz[:, :di])
@@ -422,7 +429,8 @@ def profile_stages(m, x, cfg, dtype, steps):
             y = ops.scan_gated(xc, xz[:, :di], xdbl[:, R:R + S], xdbl[:, R + S:], xz[:, di:],
                                m.A_log, m.D, B, T, out=xc)
             ev[5].record(stream)
-            ops.linear(y, m.out_proj.weight, None, split["out_proj"], out=out)
+            ops.linear(y, m.out_proj.weight, None, split["out_proj"], out=out,
+                       weight_f16=s16["out_proj"])
             ev[6].record(stream)
         torch.cuda.synchronize(dev)
         if it > 0:
@@ -509,12 +517,12 @@ def roofline(stages, cfg, hbm_gbs, bf16_tflops, src, ms_per_step):
              "unit": "TFLOP/s", "frac": ach / bf16_tflops, "traffic": traffic,
              "peak_source": f"{src} bf16 dense"}
         if cfg["dtype"] == "f32":
-            # fp32-faithful path: three TF32 MMAs per multiply-add; the dense TF32
-            # rate of the tensor core is half its bf16 rate
+            # fp32-faithful path (F16X3): three fp16 MMAs per multiply-add, at the
+            # tensor core's fp16 rate (= its bf16 rate)
             ex = 3 * flops[top] / t / 1e12
-            r["tensor_pipe"] = {"tf32_tflops_executed": ex, "tf32_peak": bf16_tflops / 2,
-                                "frac": ex / (bf16_tflops / 2),
-                                "peak_source": f"{src} bf16 dense / 2"}
+            r["tensor_pipe"] = {"f16_tflops_executed": ex, "f16_peak": bf16_tflops,
+                                "frac": ex / bf16_tflops,
+                                "peak_source": f"{src} bf16 dense (fp16 rate)"}
         r["block"] = block
         return r
     ach = nbytes[top] / t / 1e9

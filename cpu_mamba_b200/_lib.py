@@ -36,7 +36,7 @@ class MambaB200Error(RuntimeError):
 class LinearW(ctypes.Structure):
     _fields_ = [("weight", _vp), ("weight_split", _vp), ("weight_q", _vp),
                 ("scale", _vp), ("bias", _vp), ("scheme", ctypes.c_int),
-                ("group_size", _c_i64)]
+                ("group_size", _c_i64), ("weight_f16", _vp)]
 
 
 class PeerGroup(ctypes.Structure):
@@ -77,6 +77,11 @@ _SIGS = {
     "mb2_linear": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _vp, _vp, _vp, _vp, _c_i64,
                                   _c_i64, _c_i64, _c_i64, ctypes.c_int, _vp]),
     "mb2_split_tf32": (ctypes.c_int, [_vp, _vp, _c_i64, _vp]),
+    "mb2_split_f16_bytes": (ctypes.c_size_t, [_c_i64, _c_i64]),
+    "mb2_split_f16": (ctypes.c_int, [_vp, _c_i64, _c_i64, _vp, _vp]),
+    "mb2_linear_f16_scratch_bytes": (ctypes.c_size_t, []),
+    "mb2_linear_f16": (ctypes.c_int, [_vp, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
+                                      _c_i64, ctypes.c_int, _vp, _vp]),
     "mb2_quantize": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _c_i64, _vp, _vp, _vp]),
     "mb2_dequantize": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _c_i64, _c_i64, _vp, _vp]),
     "mb2_qlinear": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _vp, _c_i64, _vp, _vp, _vp,

@@ -30,6 +30,19 @@ int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, vo
         // dequantises tile by tile in its loader
         if (M >= 256 && ex.scratch &&
             ex.scratch_bytes >= dequant_operand_bytes(dtype, N, K)) {
+            if (dtype == MB2_F32 && ex.amax_parts && K % 8 == 0) {
+                // fp32: the dequantised weight (quant.py's values, bit-exact),
+                // its scaled fp16 split, then the F16X3 GEMM
+                const size_t split = (split_f16_bytes(N, K) + 255) & ~size_t(255);
+                float *deq = reinterpret_cast<float *>(reinterpret_cast<char *>(ex.scratch) + split);
+                MB2_TRY(dequantize_f32(L.scheme, L.weight_q, L.scale, N, K, L.group_size, deq, st));
+                MB2_TRY(split_f16(deq, N, K, ex.scratch, st));
+                bool used = false;
+                MB2_TRY(gemm_f16x3(static_cast<const float *>(x), ld_x, ex.scratch, L.bias,
+                                   static_cast<float *>(y), ld_y, M, N, K, n1, off1, n2, off2, epi,
+                                   st, &used, ex, ex.amax_parts));
+                if (used) return MB2_OK;
+            }
             MB2_TRY(dequant_operand(dtype, L.scheme, L.weight_q, L.scale, N, K, L.group_size,
                                     ex.scratch, st));
             const bool bf = dtype == MB2_BF16;
@@ -47,6 +60,12 @@ int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, vo
     }
     MB2_REQUIRE(L.weight, MB2_ERR_ARG, "linear: null weight");
     bool used = false;
+    if (dtype == MB2_F32 && L.weight_f16 && M >= 256 && ex.amax_parts) {
+        MB2_TRY(gemm_f16x3(static_cast<const float *>(x), ld_x, L.weight_f16, L.bias,
+                           static_cast<float *>(y), ld_y, M, N, K, n1, off1, n2, off2, epi, st,
+                           &used, ex, ex.amax_parts));
+        if (used) return MB2_OK;
+    }
     MB2_TRY(gemm_tc(dtype, x, ld_x, L.weight, L.weight_split, L.bias, y, ld_y, M, N, K, n1, off1,
                     n2, off2, epi, st, &used, ex));
     if (used) return MB2_OK;
@@ -62,6 +81,7 @@ struct Layout {
     size_t off_part, part_bytes;              // step: split-K partial sums
     size_t off_seg, seg_bytes;                // forward: scan T-segment state
     size_t off_deq, deq_bytes;                // forward: a quantised weight, dequantised
+    size_t off_aux;                           // forward: partial maxima for F16X3 (2 KB)
 };
 
 static size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -105,6 +125,8 @@ static Layout make_layout(const mb2_block *b, int64_t rows, bool step = false,
         need(b->out_proj, l.dm, l.di);
         off = align256(off + l.deq_bytes);
     }
+    l.off_aux = off;
+    if (!step) off = align256(off + 512 * sizeof(float));
     l.total = off;
     return l;
 }
@@ -180,7 +202,7 @@ extern "C" int mb2_linear(int dtype, const void *x, int64_t ld_x, const void *w,
     MB2_REQUIRE(epilogue == MB2_EPI_NONE || epilogue == MB2_EPI_SOFTPLUS, MB2_ERR_ARG,
                 "linear: bad epilogue");
     MB2_REQUIRE(ld_x >= K && ld_y >= N, MB2_ERR_SHAPE, "linear: leading dimension too small");
-    mb2_linear_w L{w, w_split, nullptr, nullptr, bias, MB2_Q_NONE};
+    mb2_linear_w L{w, w_split, nullptr, nullptr, bias, MB2_Q_NONE, 0, nullptr};
     return linear_any(dtype, L, x, ld_x, y, ld_y, M, N, K, epilogue, (cudaStream_t)stream);
 }
 
@@ -224,6 +246,7 @@ static EpiExtra scratch_extra(const Layout &l, char *ws) {
     EpiExtra e;    // scratch for dequantised weights (quantised projections)
     e.scratch = l.deq_bytes ? reinterpret_cast<float *>(ws + l.off_deq) : nullptr;
     e.scratch_bytes = l.deq_bytes;
+    e.amax_parts = reinterpret_cast<float *>(ws + l.off_aux);
     return e;
 }
 

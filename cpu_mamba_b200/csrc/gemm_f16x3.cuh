@@ -1,0 +1,409 @@
+// fp32-faithful GEMM on the fp16 tensor cores ("F16X3"), included by gemm_tc.cu
+// inside namespace mb2::tc (it shares that file's primitives and device status).
+//
+// y = x W^T for fp32 x (M, K) and W (N, K), to fp32 accuracy:
+//
+//   * Scaled fp16 split.  x and W are each multiplied by a power of two (one per
+//     tensor: x by 2^ex so that max|x| 2^ex lies in [2^14, 2^15), W likewise by
+//     2^ew, fixed when W is split) and written as hi = fp16_rn(v), lo =
+//     fp16_rn(v - hi): 11 + 11 significant bits, the precision of the TF32
+//     split, and with the scale no element overflows fp16, while the smallest
+//     ones lose only what lies 2^-40 below the tensor's largest element.  W's
+//     halves are a derived cache (mb2_split_f16); x is split on the fly by four
+//     transform warps that write both halves into tensor memory.
+//   * Three kind::f16 MMAs per K step (x_hi W_hi, x_hi W_lo, x_lo W_hi) at the
+//     fp16 rate, twice the TF32 rate: the same work as the 3xTF32 path in half
+//     the tensor-pipe time.
+//   * Bounded accumulation error.  The tensor core truncates when it adds into
+//     an fp32 accumulator, so every MMA issued into an accumulator adds up to
+//     one ulp of the running sum.  The big x_hi W_hi products go to one of two
+//     TMEM accumulators P0 / P1 for a segment of SEG k-blocks only (16 MMAs);
+//     the epilogue warps then drain the segment into fp32 registers (round to
+//     nearest) while the next segment accumulates into the other one.  The two
+//     cross terms, 2^-11 of the result, accumulate over the whole K in a third
+//     accumulator Q, where their truncation is 2^-11 smaller again.  The result
+//     is 2^-(ex+ew) (sum of segments + Q): exact scalings.
+//
+// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2-5 transform, 6-9
+// epilogue (segment drains, output staging and TMA stores).  TMEM: P0 | P1 | Q
+// (128 columns each) | two A slots of 64 columns (hi 32 | lo 32: 64 fp16 of K
+// per row, two per 32-bit column).  Shared memory: 3 stages of (A fp32 as two
+// 128-row x 32-float boxes | W_hi | W_lo, 128 rows x 64 fp16 each) = 192 KB,
+// plus a 32 KB output staging half.  Every mbarrier wait is bounded.
+
+struct F16Cfg {
+    static constexpr int BN = 128;
+    static constexpr int BK = 64;              // fp16 K elements per k-block
+    static constexpr int STAGES = 3;
+    static constexpr int SEG = 4;              // k-blocks per hi*hi segment (16 MMAs)
+    static constexpr uint32_t W_BYTES = BN * 128;
+    static constexpr uint32_t STAGE_BYTES = 2 * TILE_BYTES + 2 * W_BYTES;   // 64 KB
+    static constexpr int WARPS = 10;
+    static constexpr int EPI0 = 6;
+    static constexpr uint32_t COL_P = 0;       // P0 at 0, P1 at 128
+    static constexpr uint32_t COL_Q = 256;
+    static constexpr uint32_t COL_A = 384;     // A slot l at 384 + 64 l
+    static constexpr int HCOLS = 64;           // output columns staged at a time
+    static constexpr int AMAX_PARTS = 512;     // partial maxima of x (mb2_amax_parts)
+};
+
+constexpr size_t f16_staging_bytes() { return (size_t)BM * F16Cfg::HCOLS * sizeof(float); }
+constexpr size_t f16_smem_bytes() {
+    return 1024 + (size_t)F16Cfg::STAGES * F16Cfg::STAGE_BYTES + f16_staging_bytes() + 256;
+}
+static_assert(f16_smem_bytes() <= 232448, "F16X3 shared memory above the 227 KB per CTA");
+
+struct F16Params {
+    Params g;                       // shapes, output, epilogue terms (split-K unused)
+    const float *x_parts;           // partial maxima of |x| (float bits of non-negative values)
+    int n_parts;
+    const float *w_inv;             // 2^-ew (header of the split weight)
+};
+
+// Exponent e with amax * 2^e in [2^14, 2^15); 0 for zero or non-finite amax.
+__device__ __forceinline__ int f16_scale_exp(float amax) {
+    const uint32_t bits = __float_as_uint(amax) & 0x7FFFFFFFu;
+    const int be = (int)(bits >> 23);
+    if (bits == 0 || be == 0xFF) return 0;
+    int e = be == 0 ? 126 : 141 - be;          // 14 - (be - 127); subnormal: as far as allowed
+    return e > 126 ? 126 : e;                   // 2^e and 2^-e stay normal
+}
+__device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(e + 127) << 23); }
+
+// max over the partial maxima, reduced by one warp (every lane gets it)
+__device__ __forceinline__ float warp_amax(const float *parts, int n) {
+    float m = 0.0f;
+    for (int i = (int)(threadIdx.x & 31); i < n; i += 32) m = fmaxf(m, parts[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    return m;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo_elem, float hi_elem) {
+    const __half2 h = __floats2half2_rn(lo_elem, hi_elem);   // .x (low half) = lo_elem
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ float2 unpack_h2(uint32_t v) {
+    return __half22float2(*reinterpret_cast<const __half2 *>(&v));
+}
+
+// kind::f16 MMA (fp16 A and B, fp32 accumulator), A from tensor memory.
+__device__ __forceinline__ void mma_ts_f16(uint32_t tmem_d, uint32_t tmem_a, uint64_t db,
+                                           uint32_t accum) {
+    // D F32 (bits 4-5 = 1), A / B F16 (0), K-major, N >> 3 at 17, M >> 4 at 24
+    constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(F16Cfg::BN >> 3) << 17) |
+                               ((uint32_t)(BM >> 4) << 24);
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accum));
+}
+
+template <bool EXTRA>
+__global__ void __maxnreg__(200)
+gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wh,
+                  const __grid_constant__ CUtensorMap map_wl, const __grid_constant__ CUtensorMap map_y,
+                  const F16Params fp) {
+    using C = F16Cfg;
+    constexpr int BN = C::BN;
+    const Params &p = fp.g;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t *gbase = smem_raw + (base - raw);
+    const uint32_t out_base = base + C::STAGES * C::STAGE_BYTES;
+    const uint32_t bars = out_base + (uint32_t)f16_staging_bytes();
+    // full[S] empty[S] xform[S] a_empty[2] seg_full[2] seg_empty[2] q_full q_empty; tmem slot
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (C::STAGES + s); };
+    auto xform = [&](int s) { return bars + 8u * (2 * C::STAGES + s); };
+    auto a_empty = [&](int l) { return bars + 8u * (3 * C::STAGES + l); };
+    auto seg_full = [&](int b) { return bars + 8u * (3 * C::STAGES + 2 + b); };
+    auto seg_empty = [&](int b) { return bars + 8u * (3 * C::STAGES + 4 + b); };
+    const uint32_t q_full = bars + 8u * (3 * C::STAGES + 6);
+    const uint32_t q_empty = bars + 8u * (3 * C::STAGES + 7);
+    const uint32_t tmem_slot = bars + 8u * (3 * C::STAGES + 8);
+    uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(gbase + (tmem_slot - base));
+    // stage s: A box 0 (k 0-31) | A box 1 (k 32-63) | W_hi | W_lo
+    auto tile_a = [&](int s, int box) { return base + (uint32_t)(s * C::STAGE_BYTES + box * TILE_BYTES); };
+    auto tile_w = [&](int s, int lo) {
+        return base + (uint32_t)(s * C::STAGE_BYTES + 2 * TILE_BYTES + lo * C::W_BYTES);
+    };
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_n = (int)ceil_div(p.N, BN);
+    const int num_tiles = (int)ceil_div(p.M, BM) * num_n;
+    const int nk = (int)ceil_div(p.K, C::BK);
+    const int nseg = (nk + C::SEG - 1) / C::SEG;      // segments per tile
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+            mbar_init(xform(s), 128);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(a_empty(b), 1);
+            mbar_init(seg_full(b), 1);
+            mbar_init(seg_empty(b), 128);
+        }
+        mbar_init(q_full, 1);
+        mbar_init(q_empty, 128);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(tmem_slot), "r"(512));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot_ptr;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            uint32_t g = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                const int64_t m0 = (int64_t)(t / num_n) * BM, n0 = (int64_t)(t % num_n) * BN;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % C::STAGES;
+                    const uint32_t ph = (g / C::STAGES) & 1;
+                    if (!mbar_wait(empty(s), ph ^ 1, 11)) { ok = false; break; }
+                    mbar_expect_tx(full(s), C::STAGE_BYTES);
+                    const int32_t kc = kb * C::BK;
+                    tma_load_2d(tile_a(s, 0), &map_a, full(s), kc, (int32_t)m0);
+                    tma_load_2d(tile_a(s, 1), &map_a, full(s), kc + 32, (int32_t)m0);
+                    tma_load_2d(tile_w(s, 0), &map_wh, full(s), kc, (int32_t)n0);
+                    tma_load_2d(tile_w(s, 1), &map_wl, full(s), kc, (int32_t)n0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // -------------------------------------------------------- MMA issuer
+        uint32_t g = 0, gs = 0;
+        int it = 0;
+        bool ok = true;
+        if (lane == 0) {
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+                uint32_t pcol = 0;
+                for (int kb = 0; kb < nk && ok; ++kb, ++g) {
+                    const int rel = kb % C::SEG;
+                    if (rel == 0) {
+                        // this segment's accumulator was drained two segments ago
+                        ok = mbar_wait(seg_empty(gs & 1), ((gs >> 1) & 1) ^ 1, 12);
+                        if (ok && kb == 0) ok = mbar_wait(q_empty, (it & 1) ^ 1, 13);
+                        if (!ok) break;
+                        pcol = C::COL_P + (gs & 1) * BN;
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    }
+                    const int s = g % C::STAGES;
+                    const uint32_t ph = (g / C::STAGES) & 1;
+                    ok = mbar_wait(full(s), ph, 14) && mbar_wait(xform(s), ph, 15);
+                    if (!ok) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                    for (int kk = 0; kk < C::BK / 16; ++kk) {
+                        const uint32_t ah = tmem + C::COL_A + (g & 1) * 64 + kk * 8;
+                        const uint64_t bh = smem_desc(tile_w(s, 0) + kk * 32);
+                        const uint64_t bl = smem_desc(tile_w(s, 1) + kk * 32);
+                        mma_ts_f16(tmem + pcol, ah, bh, (rel > 0 || kk > 0) ? 1u : 0u);
+                        mma_ts_f16(tmem + C::COL_Q, ah, bl, (kb > 0 || kk > 0) ? 1u : 0u);
+                        mma_ts_f16(tmem + C::COL_Q, ah + 32, bh, 1u);
+                    }
+                    mma_commit(empty(s));          // stage free once these MMAs read it
+                    mma_commit(a_empty(g & 1));    // and the A slot
+                    if (rel == C::SEG - 1 || kb == nk - 1) {
+                        mma_commit(seg_full(gs & 1));
+                        ++gs;
+                    }
+                }
+                if (ok) mma_commit(q_full);
+            }
+        }
+        __syncwarp();
+        // free TMEM once the epilogue drained the last segment and Q (bounded)
+        const int it_all = __shfl_sync(0xffffffffu, it, 0);
+        const uint32_t gs_all = __shfl_sync(0xffffffffu, gs, 0);
+        if (it_all > 0) mbar_wait(q_empty, (uint32_t)((it_all - 1) & 1), 16);
+        if (gs_all > 0) mbar_wait(seg_empty((gs_all - 1) & 1), ((gs_all - 1) >> 1) & 1, 17);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    } else if (warp < C::EPI0) {
+        // --------------------------------------- x split into TMEM (scaled fp16)
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const float sx = pow2f(f16_scale_exp(warp_amax(fp.x_parts, fp.n_parts)));
+        uint32_t g = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const int s = g % C::STAGES;
+                const uint32_t ph = (g / C::STAGES) & 1;
+                bool w = mbar_wait(full(s), ph, 18);
+                if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+                uint32_t hi[32], lo[32];
+#pragma unroll
+                for (int box = 0; box < 2; ++box) {
+                    // this thread's row of the 128B-swizzled box: logical 16-byte
+                    // chunk c at physical chunk c ^ (row & 7)
+                    const uint8_t *arow = gbase + (tile_a(s, box) - base) + row * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const float4 v = *reinterpret_cast<const float4 *>(arow + ((c ^ (row & 7)) << 4));
+                        const float a0 = v.x * sx, a1 = v.y * sx, a2 = v.z * sx, a3 = v.w * sx;
+                        const uint32_t h01 = pack_h2(a0, a1), h23 = pack_h2(a2, a3);
+                        const float2 f01 = unpack_h2(h01), f23 = unpack_h2(h23);
+                        const int j = box * 16 + c * 2;          // column of elements 2j, 2j + 1
+                        hi[j] = h01;
+                        hi[j + 1] = h23;
+                        lo[j] = pack_h2(a0 - f01.x, a1 - f01.y);
+                        lo[j + 1] = pack_h2(a2 - f23.x, a3 - f23.y);
+                    }
+                }
+                w = mbar_wait(a_empty(g & 1), ((g >> 1) & 1) ^ 1, 19);
+                if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + C::COL_A + (g & 1) * 64;
+                tmem_st32(ta, hi);
+                tmem_st32(ta + 32, lo);
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                mbar_arrive(xform(s));
+            }
+        }
+    } else {
+        // ----------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const uint32_t lanes = (uint32_t)(q * 32) << 16;
+        const float inv_x = pow2f(-f16_scale_exp(warp_amax(fp.x_parts, fp.n_parts)));
+        const float inv_w = *fp.w_inv;
+        constexpr int BOXC = 32;                        // fp32 columns per 128-byte staging row
+        const uint32_t wst = out_base + (uint32_t)(q * 32 * C::HCOLS * sizeof(float));
+        uint8_t *wst_g = gbase + (wst - base);
+        float *Y = static_cast<float *>(p.y);
+        const float *bias = static_cast<const float *>(p.bias);
+        float acc[BN];
+        // add 128 TMEM columns (this warp's 32 lanes) into acc, 32 at a time
+        auto drain = [&](uint32_t col) {
+            uint32_t r[32];
+#pragma unroll
+            for (int cb = 0; cb < BN / 32; ++cb) {
+                tmem_ld32_async(tmem + lanes + col + cb * 32, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc[cb * 32 + j] += __uint_as_float(r[j]);
+            }
+        };
+        uint32_t gs = 0;
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+            const int64_t m0 = (int64_t)(t / num_n) * BM, n0 = (int64_t)(t % num_n) * BN;
+#pragma unroll
+            for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
+            for (int sg = 0; sg < nseg; ++sg, ++gs) {
+                if (sg == nseg - 1) {
+                    // Q first: the MMA warp waits for it before the next tile
+                    const bool w = mbar_wait(q_full, it & 1, 20);
+                    if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    drain(C::COL_Q);
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                    mbar_arrive(q_empty);
+                }
+                const bool w = mbar_wait(seg_full(gs & 1), (gs >> 1) & 1, 21);
+                if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                drain(C::COL_P + (gs & 1) * BN);
+                asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                mbar_arrive(seg_empty(gs & 1));
+            }
+            if (!ok) break;
+            const int64_t m_row = m0 + q * 32 + lane;
+            const bool row_ok = m_row < p.M;
+            const float rscale = (EXTRA && p.row_scale && row_ok) ? p.row_scale[m_row] : 1.0f;
+            const float *rrow = static_cast<const float *>(p.resid) + (row_ok ? m_row : 0) * p.ld_r;
+#pragma unroll
+            for (int part = 0; part < BN / C::HCOLS; ++part) {
+                // the previous stores must have read the staging buffer
+                if (lane == 0) bulk_wait_read0();
+                __syncwarp();
+#pragma unroll
+                for (int cbl = 0; cbl < C::HCOLS / 32; ++cbl) {
+                    const int cb = part * (C::HCOLS / 32) + cbl;
+                    float *v = acc + cb * 32;     // in place (constant offsets once unrolled)
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = v[j] * inv_x * inv_w;
+                    if (EXTRA && p.row_scale) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] *= rscale;
+                    }
+                    if (bias) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const int64_t n = n0 + cb * 32 + j;
+                            v[j] += (n < p.N) ? bias[n] : 0.0f;
+                        }
+                    }
+                    if (EXTRA && p.epi == MB2_EPI_SOFTPLUS) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = softplus_f(v[j]);
+                    }
+                    if (EXTRA && p.resid && row_ok) {
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) {
+                            const int64_t nb = n0 + cb * 32 + c * 4;
+                            if (nb < p.N) {
+                                const float4 u = *reinterpret_cast<const float4 *>(rrow + nb);
+                                v[c * 4] += u.x; v[c * 4 + 1] += u.y;
+                                v[c * 4 + 2] += u.z; v[c * 4 + 3] += u.w;
+                            }
+                        }
+                    }
+                    // row `lane` of box cbl: its 16-byte chunks at c ^ (row & 7)
+                    uint8_t *rowp = wst_g + cbl * (32 * 128) + lane * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; ++c)
+                        *reinterpret_cast<float4 *>(rowp + ((c ^ (lane & 7)) << 4)) =
+                            make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                }
+                const int64_t c0 = n0 + part * C::HCOLS;
+                if (p.tma_store) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+#pragma unroll
+                        for (int bx = 0; bx < C::HCOLS / BOXC; ++bx)
+                            tma_store_2d(&map_y, wst + bx * 32 * 128, (int32_t)(c0 + bx * BOXC),
+                                         (int32_t)(m0 + q * 32));
+                        bulk_commit();
+                    }
+                } else {
+                    // plain stores with the column remap, row rr of this warp's slab
+                    __syncwarp();
+                    for (int rr = 0; rr < 32; ++rr) {
+                        const int64_t m = m0 + q * 32 + rr;
+                        if (m >= p.M) break;
+#pragma unroll
+                        for (int cbl = 0; cbl < C::HCOLS / 32; ++cbl) {
+                            const int col = cbl * 32 + lane;
+                            const int64_t n = c0 + col;
+                            if (n >= p.N) continue;
+                            const float *src = reinterpret_cast<const float *>(
+                                wst_g + cbl * (32 * 128) + rr * 128 + (((lane >> 2) ^ (rr & 7)) << 4)) +
+                                (lane & 3);
+                            const int64_t dst = n + (n >= p.n1 ? p.off1 : 0) + (n >= p.n2 ? p.off2 : 0);
+                            Y[m * p.ld_y + dst] = *src;
+                        }
+                    }
+                    __syncwarp();
+                }
+            }
+        }
+        if (lane == 0) bulk_wait0();
+    }
+}

@@ -36,6 +36,7 @@
 // thread records an error in g_mb2_device_error and stops, and the allocating
 // warp still frees its TMEM.
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
 #include "internal.cuh"
@@ -628,6 +629,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     }
 }
 
+#include "gemm_f16x3.cuh"
+
 }  // namespace tc
 
 // ------------------------------------------------------------------- host
@@ -646,19 +649,23 @@ static int get_encode() {
 }
 
 // 2D row-major map: rows x cols elements, box (box_rows x 128 bytes), 128B swizzle.
-static int make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols, int64_t ld,
-                    bool bf16, int box_rows) {
-    const size_t es = bf16 ? 2 : 4;
+static int make_map_t(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols, int64_t ld,
+                      CUtensorMapDataType type, size_t es, int box_rows) {
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
     cuuint32_t box[2] = {(cuuint32_t)(128 / es), (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                          2, const_cast<void *>(ptr), dims, strides, box, estr,
+    CUresult r = g_encode(map, type, 2, const_cast<void *>(ptr), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MB2_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return MB2_OK;
+}
+static int make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols, int64_t ld,
+                    bool bf16, int box_rows) {
+    return make_map_t(map, ptr, rows, cols, ld,
+                      bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                      bf16 ? 2 : 4, box_rows);
 }
 
 template <int MODE, typename TO, bool EXTRA>
@@ -817,7 +824,191 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
                  : launch_tc<tc::F32X3, float, false>(ma, mb0, mb1, my, p, st);
 }
 
+// ------------------------------------------------------- F16X3 (fp32 GEMM) --
+// Partial maxima of |x| over row ranges: CTA b writes the maximum of its rows
+// to parts[b] (gridDim.x <= AMAX_PARTS).  Max is order-independent, so the
+// result does not depend on timing; nothing needs clearing beforehand.
+__global__ void amax_rows_kernel(const float *__restrict__ x, int64_t ld, int64_t M, int64_t K,
+                                 float *__restrict__ parts, int vec) {
+    const int64_t per = ceil_div(M, (int64_t)gridDim.x);
+    const int64_t r0 = (int64_t)blockIdx.x * per;
+    const int64_t r1 = r0 + per < M ? r0 + per : M;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    float m = 0.0f;
+    for (int64_t r = r0 + warp; r < r1; r += nw) {
+        const float *row = x + r * ld;
+        if (vec) {
+            for (int64_t c = (int64_t)lane * 4; c < K; c += 128) {
+                const float4 v = *reinterpret_cast<const float4 *>(row + c);
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            }
+        } else {
+            for (int64_t c = lane; c < K; c += 32) m = fmaxf(m, fabsf(row[c]));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    __shared__ float wm[32];
+    if (lane == 0) wm[warp] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < nw; ++w) m = fmaxf(m, wm[w]);
+        parts[blockIdx.x] = m;
+    }
+}
+
+static int amax_parts(const float *x, int64_t ld, int64_t M, int64_t K, float *parts, int *n,
+                      cudaStream_t st) {
+    int64_t g = ceil_div(M * K, (int64_t)16384);          // about 64 KB of x per CTA
+    g = g < tc::F16Cfg::AMAX_PARTS ? g : tc::F16Cfg::AMAX_PARTS;
+    g = g < M ? g : M;
+    g = g > 1 ? g : 1;
+    const int vec = aligned(x, 16) && ld % 4 == 0 && K % 4 == 0;
+    amax_rows_kernel<<<(unsigned)g, 256, 0, st>>>(x, ld, M, K, parts, vec);
+    *n = (int)g;
+    return check_launch("amax_rows_kernel");
+}
+
+// W (rows, cols) -> header | hi plane | lo plane (layout of mb2_split_f16).
+__global__ void split_f16_kernel(const float *__restrict__ w, int64_t n,
+                                 const float *__restrict__ parts, int nparts,
+                                 __half *__restrict__ hi, __half *__restrict__ lo,
+                                 float *__restrict__ inv_out) {
+    __shared__ float sm[32];
+    float m = 0.0f;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) m = fmaxf(m, parts[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) sm[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k) m = fmaxf(m, sm[k]);
+        sm[0] = m;
+    }
+    __syncthreads();
+    const int e = tc::f16_scale_exp(sm[0]);
+    const float sc = tc::pow2f(e);
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i == 0) *inv_out = tc::pow2f(-e);
+    if (i >= n) return;
+    const float v = w[i] * sc;
+    const __half h = __float2half_rn(v);
+    hi[i] = h;
+    lo[i] = __float2half_rn(v - __half2float(h));
+}
+
+constexpr size_t kF16Header = 4096;      // inv scale at 0, partial maxima from 2048
+
+size_t split_f16_bytes(int64_t rows, int64_t cols) {
+    return kF16Header + (size_t)rows * cols * 2 * sizeof(__half);
+}
+
+// fp32 GEMM through the F16X3 kernel; *used reports whether it ran.  parts:
+// scratch of AMAX_PARTS floats for x's partial maxima.
+int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, float *y,
+               int64_t ld_y, int64_t M, int64_t N, int64_t K, int64_t n1, int64_t off1,
+               int64_t n2, int64_t off2, int epi, cudaStream_t st, bool *used,
+               const EpiExtra &ex, float *parts) {
+    *used = false;
+    if (!w16 || !parts || M < 1 || N < 16 || K < 16) return MB2_OK;
+    if (!aligned(x, 16) || (ld_x * 4) % 16 != 0 || K % 8 != 0 || !aligned(w16, 256)) return MB2_OK;
+    if (ex.resid && (!aligned(ex.resid, 16) || ex.ld_r % 4 != 0 || N % 4 != 0)) return MB2_OK;
+    const char *wb = static_cast<const char *>(w16);
+    const __half *whi = reinterpret_cast<const __half *>(wb + kF16Header);
+    const __half *wlo = whi + N * K;
+    MB2_TRY(get_encode());
+    int nparts = 0;
+    MB2_TRY(amax_parts(x, ld_x, M, K, parts, &nparts, st));
+    CUtensorMap ma, mwh, mwl, my;
+    MB2_TRY(make_map(&ma, x, M, K, ld_x, false, 128));
+    MB2_TRY(make_map_t(&mwh, whi, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, tc::F16Cfg::BN));
+    MB2_TRY(make_map_t(&mwl, wlo, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, tc::F16Cfg::BN));
+    const bool remap = (n1 < N && off1 != 0) || (n2 < N && off2 != 0);
+    const bool tma_store = !remap && aligned(y, 16) && (ld_y * 4) % 16 == 0;
+    if (tma_store) MB2_TRY(make_map(&my, y, M, N, ld_y, false, 32));
+    else my = ma;  // unused
+    tc::F16Params fp{};
+    fp.g = tc::Params{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0,
+                      ex.row_scale, ex.resid, ex.ld_r, 1, 0};
+    fp.x_parts = parts;
+    fp.n_parts = nparts;
+    fp.w_inv = reinterpret_cast<const float *>(w16);
+    const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS;
+    auto kern = extra ? tc::gemm_f16x3_kernel<true> : tc::gemm_f16x3_kernel<false>;
+    constexpr size_t smem = tc::f16_smem_bytes();
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_f16x3 smem attribute: %s", cudaGetErrorString(e));
+    if (g_num_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    const int64_t tiles = ceil_div(M, (int64_t)tc::BM) * ceil_div(N, (int64_t)tc::F16Cfg::BN);
+    const unsigned grid = (unsigned)(tiles < g_num_sms ? tiles : g_num_sms);
+    kern<<<grid, tc::F16Cfg::WARPS * 32, smem, st>>>(ma, mwh, mwl, my, fp);
+    MB2_TRY(check_launch("gemm_f16x3_kernel"));
+    *used = true;
+    return MB2_OK;
+}
+
 }  // namespace mb2
+
+extern "C" size_t mb2_split_f16_bytes(int64_t rows, int64_t cols) {
+    if (rows < 0 || cols < 0) return 0;
+    return mb2::split_f16_bytes(rows, cols);
+}
+
+namespace mb2 {
+int split_f16(const float *w, int64_t rows, int64_t cols, void *out, cudaStream_t st) {
+    char *ob = static_cast<char *>(out);
+    float *parts = reinterpret_cast<float *>(ob + 2048);
+    int nparts = 0;
+    MB2_TRY(amax_parts(w, cols, rows, cols, parts, &nparts, st));
+    __half *hi = reinterpret_cast<__half *>(ob + kF16Header);
+    const int64_t n = rows * cols;
+    split_f16_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(w, n, parts, nparts, hi, hi + n,
+                                                                 reinterpret_cast<float *>(ob));
+    return check_launch("split_f16_kernel");
+}
+}  // namespace mb2
+
+extern "C" int mb2_split_f16(const float *w, int64_t rows, int64_t cols, void *out,
+                             mb2_stream_t stream) {
+    MB2_REQUIRE(rows >= 0 && cols >= 0, MB2_ERR_SHAPE, "split_f16: negative size");
+    MB2_REQUIRE(out && mb2::aligned(out, 256), MB2_ERR_ALIGN,
+                "split_f16: output must be 256-byte aligned");
+    if (rows * cols == 0) return MB2_OK;
+    MB2_REQUIRE(w, MB2_ERR_ARG, "split_f16: null pointer");
+    return mb2::split_f16(w, rows, cols, out, (cudaStream_t)stream);
+}
+
+extern "C" size_t mb2_linear_f16_scratch_bytes(void) {
+    return mb2::tc::F16Cfg::AMAX_PARTS * sizeof(float);
+}
+
+extern "C" int mb2_linear_f16(const float *x, int64_t ld_x, const void *w_f16, const float *bias,
+                              float *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
+                              int epilogue, void *scratch, mb2_stream_t stream) {
+    MB2_REQUIRE(epilogue == MB2_EPI_NONE || epilogue == MB2_EPI_SOFTPLUS, MB2_ERR_ARG,
+                "linear_f16: bad epilogue");
+    MB2_REQUIRE(M >= 0 && N >= 0 && K >= 0, MB2_ERR_SHAPE, "linear_f16: negative size");
+    MB2_REQUIRE(ld_x >= K && ld_y >= N, MB2_ERR_SHAPE, "linear_f16: leading dimension too small");
+    if (M == 0 || N == 0) return MB2_OK;
+    MB2_REQUIRE(x && w_f16 && y && scratch, MB2_ERR_ARG, "linear_f16: null pointer");
+    MB2_REQUIRE(N >= 16 && K >= 16 && K % 8 == 0, MB2_ERR_UNSUPPORTED,
+                "linear_f16: needs N >= 16, K >= 16 and K a multiple of 8 (got N %lld, K %lld)",
+                (long long)N, (long long)K);
+    MB2_REQUIRE(mb2::aligned(x, 16) && (ld_x * 4) % 16 == 0 && mb2::aligned(w_f16, 256),
+                MB2_ERR_ALIGN, "linear_f16: x rows must be 16-byte aligned, the split weight "
+                "256-byte aligned");
+    bool used = false;
+    MB2_TRY(mb2::gemm_f16x3(x, ld_x, w_f16, bias, y, ld_y, M, N, K, N, 0, N, 0, epilogue,
+                            (cudaStream_t)stream, &used, mb2::EpiExtra{},
+                            static_cast<float *>(scratch)));
+    MB2_REQUIRE(used, MB2_ERR_UNSUPPORTED, "linear_f16: operands not supported");
+    return MB2_OK;
+}
 
 // ------------------------------------------------------------- TF32 split ---
 // hi = tf32_rn(w), lo = tf32_rn(w - hi): w == hi + lo up to 2^-22 |w|.  A

@@ -22,6 +22,9 @@ struct EpiExtra {
     // the CUDA-core GEMM's split-K partial sums (few-row GEMMs) -- or null
     float *scratch = nullptr;
     size_t scratch_bytes = 0;
+    // not an epilogue term: AMAX_PARTS (512) floats of scratch for the partial
+    // maxima of x that the F16X3 fp32 GEMM scales x by, or null (no F16X3)
+    float *amax_parts = nullptr;
 };
 
 int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
@@ -32,6 +35,18 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
             const void *bias, void *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
             int64_t n1, int64_t off1, int64_t n2, int64_t off2, int epi, cudaStream_t st,
             bool *used, const EpiExtra &ex = EpiExtra{});
+// fp32 GEMM on the fp16 tensor cores (scaled fp16 split of x and of W, W from
+// mb2_split_f16); *used reports whether it ran (aligned operands, K % 8 == 0).
+int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, float *y,
+               int64_t ld_y, int64_t M, int64_t N, int64_t K, int64_t n1, int64_t off1,
+               int64_t n2, int64_t off2, int epi, cudaStream_t st, bool *used,
+               const EpiExtra &ex, float *parts);
+size_t split_f16_bytes(int64_t rows, int64_t cols);
+// W (rows, cols) fp32 -> mb2_split_f16's layout at out (256-byte aligned)
+int split_f16(const float *w, int64_t rows, int64_t cols, void *out, cudaStream_t st);
+// quant.py's dequantised weight (bit-exact), fp32 (rows, in_dim)
+int dequantize_f32(int scheme, const void *wq, const float *scale, int64_t rows, int64_t in_dim,
+                   int64_t group, float *out, cudaStream_t st);
 int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const void *bias,
                 void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
                 int64_t d_inner, int64_t d_conv, cudaStream_t st);
@@ -59,7 +74,9 @@ int scan_step(int dtype, const void *xc, int64_t ld_x, const void *dt_pre, int64
               int64_t d_inner, int64_t d_state, cudaStream_t st);
 
 // Quantised weights as the tensor-core GEMM's operand (bit-exact dequantised
-// values; fp32: TF32 hi / lo planes, bf16: rounded) and its size in bytes.
+// values; fp32: TF32 hi / lo planes, bf16: rounded) and its size in bytes --
+// for fp32 also large enough for the F16X3 operand: mb2_split_f16's layout of
+// the dequantised weight followed by that fp32 weight itself.
 size_t dequant_operand_bytes(int dtype, int64_t rows, int64_t in_dim);
 int dequant_operand(int dtype, int scheme, const void *wq, const float *scale, int64_t rows,
                     int64_t in_dim, int64_t group, void *out, cudaStream_t st);

@@ -199,7 +199,13 @@ __global__ void dequant_operand_kernel(const void *__restrict__ wq,
 }
 
 size_t dequant_operand_bytes(int dtype, int64_t rows, int64_t in_dim) {
-    return (size_t)rows * in_dim * (dtype == MB2_BF16 ? 2 : 8);
+    if (dtype == MB2_BF16) return (size_t)rows * in_dim * 2;
+    // TF32 planes (8 B per weight), or the F16X3 split (4096 + 4 B per weight,
+    // rounded to 256) plus the fp32 weight it is made from (4 B per weight)
+    const size_t split = (split_f16_bytes(rows, in_dim) + 255) & ~size_t(255);
+    const size_t f16x3 = split + (size_t)rows * in_dim * 4;
+    const size_t tf32 = (size_t)rows * in_dim * 8;
+    return f16x3 > tf32 ? f16x3 : tf32;
 }
 
 int dequant_operand(int dtype, int scheme, const void *wq, const float *scale, int64_t rows,
@@ -269,6 +275,11 @@ static int dequantize_any(int scheme, const void *weight_q, const float *scale, 
         default: dequantize_kernel<MB2_Q_NF4><<<grid, 256, 0, st>>>(weight_q, scale, rows, in_dim, group, w_out, lut); break;
     }
     return check_launch("dequantize_kernel");
+}
+
+int dequantize_f32(int scheme, const void *wq, const float *scale, int64_t rows, int64_t in_dim,
+                   int64_t group, float *out, cudaStream_t st) {
+    return dequantize_any(scheme, wq, scale, rows, in_dim, group, out, st);
 }
 
 }  // namespace mb2

@@ -109,6 +109,16 @@ class CPUMamba(nn.Module):
             self._split_cache[name] = ent
         return ent[1]
 
+    def _f16_split(self, name: str, w: torch.Tensor):
+        """Scaled fp16 halves of an fp32 weight for the F16X3 tensor-core GEMM
+        (derived cache, not module state)."""
+        key = (w.data_ptr(), w._version, tuple(w.shape))
+        ent = self._split_cache.get("f16:" + name)
+        if ent is None or ent[0] != key:
+            ent = (key, ops.split_f16(w))
+            self._split_cache["f16:" + name] = ent
+        return ent[1]
+
     def _linear_desc(self, name: str, keep: list) -> LinearW:
         mod = getattr(self, name)
         d = LinearW()
@@ -136,6 +146,9 @@ class CPUMamba(nn.Module):
             d.scheme = 0
             if w.dtype == torch.float32:
                 d.weight_split = self._tf32_split(name, w).data_ptr()
+                if name != "dt_proj" and w.shape[1] % 8 == 0:
+                    # prefill projections (>= 256 rows) on the fp16 tensor cores
+                    d.weight_f16 = self._f16_split(name, w).data_ptr()
         else:
             raise TypeError(f"{name} must be nn.Linear or QuantizedLinear, got {type(mod)}")
         d.bias = mod.bias.data_ptr() if mod.bias is not None else None

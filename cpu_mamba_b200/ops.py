@@ -150,6 +150,20 @@ def split_tf32(w: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def split_f16(w: torch.Tensor) -> torch.Tensor:
+    """The scaled fp16 halves of a float32 (N, K) weight for the F16X3 GEMM
+    (mb2_split_f16's layout, a derived cache): a uint8 device buffer."""
+    require_cuda(w, what="split_f16")
+    w = w.detach().contiguous()
+    if w.dtype != torch.float32 or w.dim() != 2:
+        raise TypeError("split_f16 needs a float32 matrix")
+    n = lib().mb2_split_f16_bytes(w.shape[0], w.shape[1])
+    out = torch.empty(n, device=w.device, dtype=torch.uint8)   # 256-byte aligned by torch
+    check(lib().mb2_split_f16(ptr(w), w.shape[0], w.shape[1], ptr(out), stream_of(w)),
+          "split_f16")
+    return out
+
+
 def fold_norm(weight: torch.Tensor, norm_weight: torch.Tensor) -> torch.Tensor:
     """weight * norm_weight[None, :] rounded to weight's dtype: an RMSNorm
     weight folded into the columns of the projection that follows it."""
@@ -166,9 +180,12 @@ def fold_norm(weight: torch.Tensor, norm_weight: torch.Tensor) -> torch.Tensor:
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
            weight_split: Optional[torch.Tensor] = None, softplus: bool = False,
-           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+           out: Optional[torch.Tensor] = None,
+           weight_f16: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = x W^T + b over the last dim of x (nn.Linear semantics); softplus=True
-    applies F.softplus to the result in the same kernel (dt_proj's epilogue)."""
+    applies F.softplus to the result in the same kernel (dt_proj's epilogue).
+    float32 with weight_f16 (split_f16(weight)): the F16X3 tensor-core GEMM;
+    with weight_split (split_tf32(weight)): the 3xTF32 one."""
     require_cuda(x, weight, bias, what="linear")
     N, K = weight.shape
     lead = x.shape[:-1]
@@ -176,6 +193,14 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
     if x2.stride(-1) != 1:
         x2 = x2.contiguous()
     y = out if out is not None else torch.empty(x2.shape[0], N, device=x.device, dtype=x.dtype)
+    if weight_f16 is not None and x.dtype == torch.float32:
+        scratch = torch.empty(lib().mb2_linear_f16_scratch_bytes(), device=x.device,
+                              dtype=torch.uint8)
+        check(lib().mb2_linear_f16(ptr(x2), x2.stride(0), ptr(weight_f16), ptr(bias), ptr(y),
+                                   y.stride(0), x2.shape[0], N, K,
+                                   _lib.EPI_SOFTPLUS if softplus else _lib.EPI_NONE,
+                                   ptr(scratch), stream_of(x)), "linear_f16")
+        return y if out is not None else y.reshape(*lead, N)
     weight = weight.contiguous()
     check(lib().mb2_linear(dtype_code(x.dtype), ptr(x2), x2.stride(0), ptr(weight),
                            ptr(weight_split), ptr(bias), ptr(y), y.stride(0), x2.shape[0], N, K,

@@ -64,10 +64,12 @@ class MambaStack(nn.Module):
         ent = self._fold_cache.get(i)
         if ent is None or ent[0] != key:
             folded = ops.fold_norm(w, g)
-            split = ops.split_tf32(folded) if folded.dtype == torch.float32 else None
-            ent = (key, folded, split)
+            fp32 = folded.dtype == torch.float32
+            split = ops.split_tf32(folded) if fp32 else None
+            split16 = ops.split_f16(folded) if fp32 and folded.shape[1] % 8 == 0 else None
+            ent = (key, folded, split, split16)
             self._fold_cache[i] = ent
-        return ent[1], ent[2]
+        return ent[1], ent[2], ent[3]
 
     def _descriptors(self, keep: list):
         n = len(self.layers)
@@ -80,10 +82,11 @@ class MambaStack(nn.Module):
             if layer.norm.eps != self.eps:
                 raise RuntimeError("MambaStack: all layers must share the stack's RMSNorm eps")
             b = layer.mixer._descriptor(keep)
-            folded, split = self._folded_in_proj(i, layer)
-            keep.extend([folded, split])
+            folded, split, split16 = self._folded_in_proj(i, layer)
+            keep.extend([folded, split, split16])
             b.in_proj.weight = folded.data_ptr()
             b.in_proj.weight_split = split.data_ptr() if split is not None else None
+            b.in_proj.weight_f16 = split16.data_ptr() if split16 is not None else None
             arr[i] = b
         return arr
 

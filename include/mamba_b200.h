@@ -167,6 +167,27 @@ int mb2_linear(int dtype, const void *x, int64_t ld_x, const void *w,
 int mb2_split_tf32(const float *w, float *out, int64_t numel,
                    mb2_stream_t stream);
 
+/* fp32-faithful linear layer on the fp16 tensor cores (F16X3): the same
+ * y = x W^T (+ bias) as mb2_linear's F32 path, in half its tensor-pipe time.
+ * x and W are each scaled by a power of two (x per call from its largest
+ * magnitude, W when split) and split into fp16 halves hi + lo (11 + 11
+ * significant bits); the MMAs form x_hi W_hi + x_hi W_lo + x_lo W_hi with the
+ * big products accumulated in segments of 256 of K that are added up in fp32
+ * round-to-nearest, so the rounding error stays that of an fp32 GEMM at any K.
+ *   x: (M, ld_x) float32, rows 16-byte aligned   y: (M, ld_y) float32
+ *   w_f16: mb2_split_f16's output for W (N, K), 256-byte aligned; K % 8 == 0
+ *   scratch: mb2_linear_f16_scratch_bytes() of device memory (x's partial maxima)
+ * No counterpart in the reference (its projections are torch's fp32 GEMMs,
+ * _mamba.py:67,74,84); mb2_block_forward uses it for in_proj, x_proj and
+ * out_proj when the descriptor carries weight_f16. */
+size_t mb2_split_f16_bytes(int64_t rows, int64_t cols);
+int mb2_split_f16(const float *w, int64_t rows, int64_t cols, void *out,
+                  mb2_stream_t stream);
+size_t mb2_linear_f16_scratch_bytes(void);
+int mb2_linear_f16(const float *x, int64_t ld_x, const void *w_f16, const float *bias,
+                   float *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
+                   int epilogue, void *scratch, mb2_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Weight-only quantisation (src/cpu_mamba/quant.py:60-134), bit-exact.
  *   w: (rows, cols) float32
@@ -219,6 +240,9 @@ typedef struct mb2_linear_w {
     int scheme;             /* mb2_scheme                                    */
     int64_t group_size;     /* 0: one scale per row (quant.py); else columns */
                             /* per scale group (blockwise, e.g. 64)          */
+    const void *weight_f16; /* optional scaled fp16 split of W (mb2_split_f16):  */
+                            /* F32 projections of >= 256 rows run on the fp16 */
+                            /* tensor cores (mb2_linear_f16)                  */
 } mb2_linear_w;
 
 typedef struct mb2_block {

@@ -91,3 +91,84 @@ def test_softplus_epilogue(dtype, M):
         assert (y - ref).abs().max().item() <= 2e-6
     else:
         assert ((y.float() - ref).abs() / (ref.abs() + 1e-3)).max().item() <= 2 ** -8
+
+
+# ------------------------------------------------------------------ F16X3 ---
+F16_SHAPES = [(256, 128, 64), (1000, 200, 104), (300, 96, 1536), (4096, 3072, 768),
+              (2049, 768, 1536), (1024, 128, 3072), (4096, 3072, 1536)]
+
+
+def _f32_err(x, w, b, ref):
+    """The float32 CPU GEMM's own distance to float64 (the yardstick)."""
+    return ((x @ w.T + b).double() - ref).abs().max().item()
+
+
+@pytest.mark.parametrize("shape", F16_SHAPES)
+@pytest.mark.parametrize("mag", [1.0, 3e3, 1e-4])
+def test_f16x3_matches_float64(shape, mag):
+    """The fp16-split GEMM as accurate as an fp32 GEMM at every K (the segment
+    drains bound the tensor core's truncation), whatever the operands' scale."""
+    M, N, K = shape
+    x, w, b = _data(M, N, K, 11 + sum(shape))
+    x = x * mag
+    w[0, :8] *= 40.0                        # a few outliers, as quantised weights have
+    ref = x.double() @ w.double().T + b.double()
+    xd, wd, bd = x.cuda(), w.cuda(), b.cuda()
+    y = ops.linear(xd, wd, bd, weight_f16=ops.split_f16(wd)).cpu()
+    assert _lib.device_status() == 0
+    e = (y.double() - ref).abs().max().item()
+    e_cpu = _f32_err(x, w, b, ref)
+    scale = ref.abs().max().item()
+    assert e <= max(3 * e_cpu, 2e-7 * scale), (e, e_cpu, scale)
+
+
+def test_f16x3_large_k_beats_tf32x3():
+    """K = 3072 at large magnitudes (config 3's x_proj / out_proj): the segment
+    drains keep the error at the fp32 GEMM's level, where the 3xTF32 kernel's
+    single accumulation over K drifts."""
+    M, N, K = 2048, 768, 3072
+    x, w, b = _data(M, N, K, 21)
+    x = x * 30
+    ref = x.double() @ w.double().T + b.double()
+    xd, wd, bd = x.cuda(), w.cuda(), b.cuda()
+    e16 = (ops.linear(xd, wd, bd, weight_f16=ops.split_f16(wd)).cpu().double() - ref).abs().max().item()
+    e_cpu = _f32_err(x, w, b, ref)
+    assert e16 <= 3 * e_cpu, (e16, e_cpu)
+
+
+def test_f16x3_zero_and_tail_shapes():
+    """All-zero x (scale 1), M not a multiple of 128, N not of 128."""
+    M, N, K = 777, 40, 64
+    x, w, b = _data(M, N, K, 3)
+    wd = w.cuda()
+    y = ops.linear(torch.zeros(M, K, device="cuda"), wd, b.cuda(), weight_f16=ops.split_f16(wd))
+    assert torch.equal(y.cpu(), b.expand(M, N))
+    y = ops.linear(x.cuda(), wd, None, weight_f16=ops.split_f16(wd)).cpu()
+    ref = x.double() @ w.double().T
+    assert (y.double() - ref).abs().max().item() <= 3 * _f32_err(x, w, torch.zeros(N), ref) + 1e-7
+
+
+def test_split_f16_layout():
+    """Header (2^-e scale), hi and lo planes: w * 2^e == hi + lo to 2^-22."""
+    w = torch.randn(37, 64, device="cuda") * 0.01
+    buf = ops.split_f16(w)
+    inv = buf[:4].view(torch.float32).item()
+    n = w.numel()
+    planes = buf[4096:4096 + 4 * n].view(torch.float16)
+    hi, lo = planes[:n].view(37, 64), planes[n:].view(37, 64)
+    scaled = w.double() / inv
+    assert 2 ** 14 <= scaled.abs().max().item() < 2 ** 15
+    err = (hi.double() + lo.double() - scaled).abs()
+    assert (err <= scaled.abs() * 2 ** -21 + 2 ** -24).all()
+
+
+@pytest.mark.parametrize("M", [300, 2048])
+def test_f16x3_softplus_epilogue(M):
+    N, K = 768, 64
+    x, w, b = _data(M, N, K, 5)
+    x = x * 6
+    xd, wd, bd = x.cuda(), w.cuda(), b.cuda()
+    s16 = ops.split_f16(wd)
+    y = ops.linear(xd, wd, bd, weight_f16=s16, softplus=True).cpu()
+    lin = ops.linear(xd, wd, bd, weight_f16=s16).cpu()
+    assert (y - torch.nn.functional.softplus(lin)).abs().max().item() <= 2e-6
