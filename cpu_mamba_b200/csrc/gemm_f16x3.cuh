@@ -24,12 +24,14 @@
 //     accumulator Q, where their truncation is 2^-11 smaller again.  The result
 //     is 2^-(ex+ew) (sum of segments + Q): exact scalings.
 //
-// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2-5 transform, 6-9
-// epilogue (segment drains, output staging and TMA stores).  TMEM: P0 | P1 | Q
+// Warps: 0 TMA producer, 1 TMEM owner + MMA issuer, 2-5 transform, 6-13
+// epilogue (segment drains, output staging and TMA stores; warps w and w + 4
+// share TMEM lane quarter w % 4, one taking columns 0-63, the other 64-127).  TMEM: P0 | P1 | Q
 // (128 columns each) | two A slots of 64 columns (hi 32 | lo 32: 64 fp16 of K
 // per row, two per 32-bit column).  Shared memory: 3 stages of (A fp32 as two
 // 128-row x 32-float boxes | W_hi | W_lo, 128 rows x 64 fp16 each) = 192 KB,
-// plus a 32 KB output staging half.  Every mbarrier wait is bounded.
+// plus 32 KB of output staging (4 KB per epilogue warp).  Every mbarrier wait
+// is bounded.
 
 struct F16Cfg {
     static constexpr int BN = 128;
@@ -38,16 +40,20 @@ struct F16Cfg {
     static constexpr int SEG = 4;              // k-blocks per hi*hi segment (16 MMAs)
     static constexpr uint32_t W_BYTES = BN * 128;
     static constexpr uint32_t STAGE_BYTES = 2 * TILE_BYTES + 2 * W_BYTES;   // 64 KB
-    static constexpr int WARPS = 10;
-    static constexpr int EPI0 = 6;
+    // 14 warps: registers are allocated in groups of four warps, so the block
+    // counts as 16 warps and every thread may use 128 registers
+    static constexpr int WARPS = 14;
+    static constexpr int EPI0 = 6;             // 8 epilogue warps, two per TMEM lane quarter
+    static constexpr int EPI_THREADS = 256;
     static constexpr uint32_t COL_P = 0;       // P0 at 0, P1 at 128
     static constexpr uint32_t COL_Q = 256;
     static constexpr uint32_t COL_A = 384;     // A slot l at 384 + 64 l
-    static constexpr int HCOLS = 64;           // output columns staged at a time
+    static constexpr int ECOLS = 64;           // accumulator columns per epilogue warp
     static constexpr int AMAX_PARTS = 512;     // partial maxima of x (mb2_amax_parts)
 };
 
-constexpr size_t f16_staging_bytes() { return (size_t)BM * F16Cfg::HCOLS * sizeof(float); }
+// output staging: 32 rows x 32 fp32 columns (one 128B-swizzled box) per epilogue warp
+constexpr size_t f16_staging_bytes() { return (size_t)8 * 32 * 32 * sizeof(float); }
 constexpr size_t f16_smem_bytes() {
     return 1024 + (size_t)F16Cfg::STAGES * F16Cfg::STAGE_BYTES + f16_staging_bytes() + 256;
 }
@@ -100,7 +106,7 @@ __device__ __forceinline__ void mma_ts_f16(uint32_t tmem_d, uint32_t tmem_a, uin
 }
 
 template <bool EXTRA>
-__global__ void __maxnreg__(200)
+__global__ void __launch_bounds__(F16Cfg::WARPS * 32, 1)
 gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wh,
                   const __grid_constant__ CUtensorMap map_wl, const __grid_constant__ CUtensorMap map_y,
                   const F16Params fp) {
@@ -146,10 +152,10 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         for (int b = 0; b < 2; ++b) {
             mbar_init(a_empty(b), 1);
             mbar_init(seg_full(b), 1);
-            mbar_init(seg_empty(b), 128);
+            mbar_init(seg_empty(b), C::EPI_THREADS);
         }
         mbar_init(q_full, 1);
-        mbar_init(q_empty, 128);
+        mbar_init(q_empty, C::EPI_THREADS);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -277,22 +283,23 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         }
     } else {
         // ----------------------------------------------------------- epilogue
-        const int q = warp & 3;
+        const int q = warp & 3;                          // TMEM lane quarter
+        const int ch = (warp - C::EPI0) >> 2;            // column half: 0 or 1
         const uint32_t lanes = (uint32_t)(q * 32) << 16;
+        const uint32_t ccol = (uint32_t)(ch * C::ECOLS);
         const float inv_x = pow2f(-f16_scale_exp(warp_amax(fp.x_parts, fp.n_parts)));
         const float inv_w = *fp.w_inv;
-        constexpr int BOXC = 32;                        // fp32 columns per 128-byte staging row
-        const uint32_t wst = out_base + (uint32_t)(q * 32 * C::HCOLS * sizeof(float));
+        const uint32_t wst = out_base + (uint32_t)((warp - C::EPI0) * 32 * 128);  // one box
         uint8_t *wst_g = gbase + (wst - base);
         float *Y = static_cast<float *>(p.y);
         const float *bias = static_cast<const float *>(p.bias);
-        float acc[BN];
-        // add 128 TMEM columns (this warp's 32 lanes) into acc, 32 at a time
+        float acc[C::ECOLS];
+        // add this warp's 64 columns of an accumulator into acc, 32 at a time
         auto drain = [&](uint32_t col) {
             uint32_t r[32];
 #pragma unroll
-            for (int cb = 0; cb < BN / 32; ++cb) {
-                tmem_ld32_async(tmem + lanes + col + cb * 32, r);
+            for (int cb = 0; cb < C::ECOLS / 32; ++cb) {
+                tmem_ld32_async(tmem + lanes + col + ccol + cb * 32, r);
                 tmem_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 32; ++j) acc[cb * 32 + j] += __uint_as_float(r[j]);
@@ -304,7 +311,7 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
             const int64_t m0 = (int64_t)(t / num_n) * BM, n0 = (int64_t)(t % num_n) * BN;
 #pragma unroll
-            for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
+            for (int j = 0; j < C::ECOLS; ++j) acc[j] = 0.0f;
             for (int sg = 0; sg < nseg; ++sg, ++gs) {
                 if (sg == nseg - 1) {
                     // Q first: the MMA warp waits for it before the next tile
@@ -328,77 +335,60 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
             const float rscale = (EXTRA && p.row_scale && row_ok) ? p.row_scale[m_row] : 1.0f;
             const float *rrow = static_cast<const float *>(p.resid) + (row_ok ? m_row : 0) * p.ld_r;
 #pragma unroll
-            for (int part = 0; part < BN / C::HCOLS; ++part) {
-                // the previous stores must have read the staging buffer
+            for (int cb = 0; cb < C::ECOLS / 32; ++cb) {
+                const int64_t c0 = n0 + ch * C::ECOLS + cb * 32;   // first output column
+                float *v = acc + cb * 32;        // in place (constant offsets once unrolled)
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = v[j] * inv_x * inv_w;
+                if (EXTRA && p.row_scale) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] *= rscale;
+                }
+                if (bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] += (c0 + j < p.N) ? bias[c0 + j] : 0.0f;
+                }
+                if (EXTRA && p.epi == MB2_EPI_SOFTPLUS) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = softplus_f(v[j]);
+                }
+                if (EXTRA && p.resid && row_ok) {
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        if (c0 + c * 4 < p.N) {
+                            const float4 u = *reinterpret_cast<const float4 *>(rrow + c0 + c * 4);
+                            v[c * 4] += u.x; v[c * 4 + 1] += u.y;
+                            v[c * 4 + 2] += u.z; v[c * 4 + 3] += u.w;
+                        }
+                    }
+                }
+                // the previous store from this warp's box must have read it
                 if (lane == 0) bulk_wait_read0();
                 __syncwarp();
+                // row `lane` of the box: its 16-byte chunks at c ^ (row & 7)
+                uint8_t *rowp = wst_g + lane * 128;
 #pragma unroll
-                for (int cbl = 0; cbl < C::HCOLS / 32; ++cbl) {
-                    const int cb = part * (C::HCOLS / 32) + cbl;
-                    float *v = acc + cb * 32;     // in place (constant offsets once unrolled)
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] = v[j] * inv_x * inv_w;
-                    if (EXTRA && p.row_scale) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] *= rscale;
-                    }
-                    if (bias) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int64_t n = n0 + cb * 32 + j;
-                            v[j] += (n < p.N) ? bias[n] : 0.0f;
-                        }
-                    }
-                    if (EXTRA && p.epi == MB2_EPI_SOFTPLUS) {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) v[j] = softplus_f(v[j]);
-                    }
-                    if (EXTRA && p.resid && row_ok) {
-#pragma unroll
-                        for (int c = 0; c < 8; ++c) {
-                            const int64_t nb = n0 + cb * 32 + c * 4;
-                            if (nb < p.N) {
-                                const float4 u = *reinterpret_cast<const float4 *>(rrow + nb);
-                                v[c * 4] += u.x; v[c * 4 + 1] += u.y;
-                                v[c * 4 + 2] += u.z; v[c * 4 + 3] += u.w;
-                            }
-                        }
-                    }
-                    // row `lane` of box cbl: its 16-byte chunks at c ^ (row & 7)
-                    uint8_t *rowp = wst_g + cbl * (32 * 128) + lane * 128;
-#pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        *reinterpret_cast<float4 *>(rowp + ((c ^ (lane & 7)) << 4)) =
-                            make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
-                }
-                const int64_t c0 = n0 + part * C::HCOLS;
+                for (int c = 0; c < 8; ++c)
+                    *reinterpret_cast<float4 *>(rowp + ((c ^ (lane & 7)) << 4)) =
+                        make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
                 if (p.tma_store) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     __syncwarp();
-                    if (lane == 0) {
-#pragma unroll
-                        for (int bx = 0; bx < C::HCOLS / BOXC; ++bx)
-                            tma_store_2d(&map_y, wst + bx * 32 * 128, (int32_t)(c0 + bx * BOXC),
-                                         (int32_t)(m0 + q * 32));
+                    if (lane == 0 && c0 < p.N) {      // boxes wholly right of N store nothing
+                        tma_store_2d(&map_y, wst, (int32_t)c0, (int32_t)(m0 + q * 32));
                         bulk_commit();
                     }
                 } else {
-                    // plain stores with the column remap, row rr of this warp's slab
+                    // plain stores with the column remap: row rr of this warp's slab
                     __syncwarp();
+                    const int64_t n = c0 + lane;
+                    const int64_t dst = n + (n >= p.n1 ? p.off1 : 0) + (n >= p.n2 ? p.off2 : 0);
                     for (int rr = 0; rr < 32; ++rr) {
                         const int64_t m = m0 + q * 32 + rr;
                         if (m >= p.M) break;
-#pragma unroll
-                        for (int cbl = 0; cbl < C::HCOLS / 32; ++cbl) {
-                            const int col = cbl * 32 + lane;
-                            const int64_t n = c0 + col;
-                            if (n >= p.N) continue;
-                            const float *src = reinterpret_cast<const float *>(
-                                wst_g + cbl * (32 * 128) + rr * 128 + (((lane >> 2) ^ (rr & 7)) << 4)) +
-                                (lane & 3);
-                            const int64_t dst = n + (n >= p.n1 ? p.off1 : 0) + (n >= p.n2 ? p.off2 : 0);
-                            Y[m * p.ld_y + dst] = *src;
-                        }
+                        if (n < p.N)
+                            Y[m * p.ld_y + dst] = *(reinterpret_cast<const float *>(
+                                wst_g + rr * 128 + (((lane >> 2) ^ (rr & 7)) << 4)) + (lane & 3));
                     }
                     __syncwarp();
                 }

@@ -946,6 +946,11 @@ int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, 
     }
     const int64_t tiles = ceil_div(M, (int64_t)tc::BM) * ceil_div(N, (int64_t)tc::F16Cfg::BN);
     const unsigned grid = (unsigned)(tiles < g_num_sms ? tiles : g_num_sms);
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess &&
+        fa.maxThreadsPerBlock < tc::F16Cfg::WARPS * 32)
+        return fail(MB2_ERR_CUDA, "gemm_f16x3_kernel: %d registers per thread allow only %d threads",
+                    fa.numRegs, fa.maxThreadsPerBlock);
     kern<<<grid, tc::F16Cfg::WARPS * 32, smem, st>>>(ma, mwh, mwl, my, fp);
     MB2_TRY(check_launch("gemm_f16x3_kernel"));
     *used = true;
