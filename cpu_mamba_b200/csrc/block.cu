@@ -125,8 +125,11 @@ static Layout make_layout(const mb2_block *b, int64_t rows, bool step = false,
         need(b->out_proj, l.dm, l.di);
         off = align256(off + l.deq_bytes);
     }
+    // forward: x's partial maxima for in_proj (512 floats), then the fused
+    // maxima slots of x_proj's input (written by the conv) and out_proj's
+    // input (written by the scan)
     l.off_aux = off;
-    if (!step) off = align256(off + 512 * sizeof(float));
+    if (!step) off = align256(off + (512 + 2 * AMAX_SLOTS) * sizeof(float));
     l.total = off;
     return l;
 }
@@ -250,6 +253,16 @@ static EpiExtra scratch_extra(const Layout &l, char *ws) {
     return e;
 }
 
+// The fused maxima slots of x_proj's (which = 0) or out_proj's (1) input,
+// zeroed for the kernel that writes that input, or null where no F16X3 GEMM
+// can read them (bf16, or too few rows).
+static unsigned *fused_amax(const Layout &l, char *ws, int dtype, int which, cudaStream_t st) {
+    if (dtype != MB2_F32 || l.N < 256) return nullptr;
+    unsigned *slots = reinterpret_cast<unsigned *>(ws + l.off_aux) + 512 + which * AMAX_SLOTS;
+    cudaMemsetAsync(slots, 0, AMAX_SLOTS * sizeof(unsigned), st);
+    return slots;
+}
+
 static int pipeline_head(const mb2_block &b, const Layout &l, const void *x, int64_t batch,
                          int64_t seqlen, void *conv_tail, char *ws, cudaStream_t st,
                          const float *row_scale) {
@@ -260,8 +273,14 @@ static int pipeline_head(const mb2_block &b, const Layout &l, const void *x, int
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, N, 2 * di, l.dm, MB2_EPI_NONE,
                            st, -1, 0, -1, 0, in_ex));
+    unsigned *xc_max = fused_amax(l, ws, b.dtype, 0, st);
+    MB2_TRY(check_launch("block: maxima clear"));
     MB2_TRY(conv1d_silu(b.dtype, xz, 2 * di, b.conv_w, b.conv_b, xc, di, conv_tail, batch, seqlen,
-                        di, b.d_conv, st));
+                        di, b.d_conv, st, xc_max));
+    if (xc_max) {
+        mid_ex.amax_parts = reinterpret_cast<float *>(xc_max);
+        mid_ex.amax_n = AMAX_SLOTS;
+    }
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, MB2_EPI_NONE,
                            st, R, l.RB - R, R + S, l.RC - l.RB - S, mid_ex));
@@ -289,16 +308,22 @@ static int pipeline_tail(const mb2_block &b, const Layout &l, void *out, int64_t
         MB2_TRY(gemm_tc(b.dtype, xdbl, l.ldx, b.dt_proj.weight, b.dt_proj.weight_split,
                         b.dt_proj.bias, xz, 2 * di, N, di, R, di, 0, di, 0, MB2_EPI_NONE, st,
                         &dt_done));
+    unsigned *y_max = fused_amax(l, ws, b.dtype, 1, st);
+    MB2_TRY(check_launch("block: maxima clear"));
     if (dt_done)
         MB2_TRY(scan_gated(b.dtype, xc, di, xz, 2 * di, (char *)xdbl + l.RB * es, l.ldx,
                            (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log,
                            b.D, nullptr, h_last, xc, di, batch, seqlen, di, S, st,
-                           reinterpret_cast<float *>(ws + l.off_seg), l.seg_bytes));
+                           reinterpret_cast<float *>(ws + l.off_seg), l.seg_bytes, y_max));
     else
         MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
                            (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
                            dt_weight(b), b.dt_proj.bias, b.A_log, b.D, nullptr, h_last, xc, di,
-                           batch, seqlen, di, S, R, st));
+                           batch, seqlen, di, S, R, st, y_max));
+    if (y_max) {
+        out_ex.amax_parts = reinterpret_cast<float *>(y_max);
+        out_ex.amax_n = AMAX_SLOTS;
+    }
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, N, l.dm, di, MB2_EPI_NONE, st,
                            -1, 0, -1, 0, out_ex));

@@ -9,7 +9,7 @@
 // that a warp still moves 128 bytes per row access) and CONV_TT consecutive
 // timesteps, keeping the K-1 history in registers; consecutive threads are
 // consecutive channels, so every row access is one coalesced segment.
-#include "common.cuh"
+#include "internal.cuh"
 
 namespace mb2 {
 
@@ -17,14 +17,37 @@ constexpr int CONV_TT = 32;   // timesteps per thread
 constexpr int CONV_KMAX = 8;  // max supported d_conv
 
 template <typename T, int K>
+__device__ __forceinline__ void conv_channel(const T *__restrict__ x, int64_t ld_in,
+                                             const T *__restrict__ w, const T *__restrict__ bias,
+                                             T *__restrict__ xc, int64_t ld_out,
+                                             T *__restrict__ tail, int64_t seqlen,
+                                             int64_t d_inner, int64_t d, int64_t t0, int64_t b,
+                                             float &vmax);
+
+// amax (or null): fused maxima of |xc| for the F16X3 GEMM that reads xc next
+// (AMAX_SLOTS slots, zeroed beforehand)
+template <typename T, int K>
 __global__ void __launch_bounds__(128)
 conv1d_silu_kernel(const T *__restrict__ x, int64_t ld_in, const T *__restrict__ w,
                    const T *__restrict__ bias, T *__restrict__ xc, int64_t ld_out,
-                   T *__restrict__ tail, int64_t seqlen, int64_t d_inner) {
+                   T *__restrict__ tail, int64_t seqlen, int64_t d_inner,
+                   unsigned *__restrict__ amax) {
     const int64_t d = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t t0 = (int64_t)blockIdx.y * CONV_TT;
     const int64_t b = blockIdx.z;
-    if (d >= d_inner) return;
+    float vmax = 0.0f;
+    if (d < d_inner) conv_channel<T, K>(x, ld_in, w, bias, xc, ld_out, tail, seqlen, d_inner, d,
+                                        t0, b, vmax);
+    if (amax) amax_publish(amax, vmax);      // block-uniform branch
+}
+
+template <typename T, int K>
+__device__ __forceinline__ void conv_channel(const T *__restrict__ x, int64_t ld_in,
+                                             const T *__restrict__ w, const T *__restrict__ bias,
+                                             T *__restrict__ xc, int64_t ld_out,
+                                             T *__restrict__ tail, int64_t seqlen,
+                                             int64_t d_inner, int64_t d, int64_t t0, int64_t b,
+                                             float &vmax) {
     float wk[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) wk[k] = io<T>::to_f(w[d * K + k]);
@@ -44,7 +67,9 @@ conv1d_silu_kernel(const T *__restrict__ x, int64_t ld_in, const T *__restrict__
 #pragma unroll
         for (int k = 0; k < K; ++k) acc = fmaf(wk[k], hist[k], acc);
         const float v = io<T>::round(acc);
-        xc[(row0 + t) * ld_out + d] = io<T>::from_f(silu_f(v));
+        const float o = silu_f(v);
+        vmax = fmaxf(vmax, fabsf(o));
+        xc[(row0 + t) * ld_out + d] = io<T>::from_f(o);
 #pragma unroll
         for (int k = 0; k < K - 1; ++k) hist[k] = hist[k + 1];
     }
@@ -119,7 +144,7 @@ conv1d_silu_bf16x2_kernel(const __nv_bfloat16 *__restrict__ x, int64_t ld_in,
 template <typename T, int K>
 static int launch_conv(const void *x, int64_t ld_in, const void *w, const void *bias, void *xc,
                        int64_t ld_out, void *tail, int64_t batch, int64_t seqlen, int64_t di,
-                       cudaStream_t st) {
+                       cudaStream_t st, unsigned *amax) {
     if constexpr (sizeof(T) == 2) {
         // pairs of channels: even d_inner, 4-byte aligned rows
         if (di % 2 == 0 && ld_in % 2 == 0 && ld_out % 2 == 0 && aligned(x, 4) && aligned(xc, 4)) {
@@ -135,17 +160,18 @@ static int launch_conv(const void *x, int64_t ld_in, const void *w, const void *
     dim3 grid((unsigned)ceil_div(di, 128), (unsigned)ceil_div(seqlen, CONV_TT), (unsigned)batch);
     conv1d_silu_kernel<T, K><<<grid, 128, 0, st>>>(
         static_cast<const T *>(x), ld_in, static_cast<const T *>(w), static_cast<const T *>(bias),
-        static_cast<T *>(xc), ld_out, static_cast<T *>(tail), seqlen, di);
+        static_cast<T *>(xc), ld_out, static_cast<T *>(tail), seqlen, di,
+        sizeof(T) == 4 ? amax : nullptr);
     return check_launch("conv1d_silu_kernel");
 }
 
 template <typename T>
 static int dispatch_conv(int K, const void *x, int64_t ld_in, const void *w, const void *bias,
                          void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
-                         int64_t di, cudaStream_t st) {
+                         int64_t di, cudaStream_t st, unsigned *amax) {
     switch (K) {
 #define MB2_CONV_CASE(KK) \
-    case KK: return launch_conv<T, KK>(x, ld_in, w, bias, xc, ld_out, tail, batch, seqlen, di, st);
+    case KK: return launch_conv<T, KK>(x, ld_in, w, bias, xc, ld_out, tail, batch, seqlen, di, st, amax);
         MB2_CONV_CASE(2) MB2_CONV_CASE(3) MB2_CONV_CASE(4) MB2_CONV_CASE(5)
         MB2_CONV_CASE(6) MB2_CONV_CASE(7) MB2_CONV_CASE(8)
 #undef MB2_CONV_CASE
@@ -162,7 +188,7 @@ __global__ void zero_kernel(T *p, int64_t n) {
 
 int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const void *bias,
                 void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
-                int64_t d_inner, int64_t d_conv, cudaStream_t st) {
+                int64_t d_inner, int64_t d_conv, cudaStream_t st, unsigned *amax) {
     MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "conv1d: bad dtype");
     MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0, MB2_ERR_SHAPE, "conv1d: negative size");
     MB2_REQUIRE(d_conv >= 2 && d_conv <= CONV_KMAX, MB2_ERR_UNSUPPORTED,
@@ -187,9 +213,9 @@ int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const
     MB2_REQUIRE(ld_in >= d_inner && ld_out >= d_inner, MB2_ERR_SHAPE, "conv1d: leading dim too small");
     if (dtype == MB2_F32)
         return dispatch_conv<float>((int)d_conv, x_in, ld_in, w, bias, xc, ld_out, tail, batch,
-                                    seqlen, d_inner, st);
+                                    seqlen, d_inner, st, amax);
     return dispatch_conv<__nv_bfloat16>((int)d_conv, x_in, ld_in, w, bias, xc, ld_out, tail,
-                                        batch, seqlen, d_inner, st);
+                                        batch, seqlen, d_inner, st, nullptr);
 }
 
 }  // namespace mb2

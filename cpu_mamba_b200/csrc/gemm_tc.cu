@@ -917,8 +917,8 @@ int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, 
     const __half *whi = reinterpret_cast<const __half *>(wb + kF16Header);
     const __half *wlo = whi + N * K;
     MB2_TRY(get_encode());
-    int nparts = 0;
-    MB2_TRY(amax_parts(x, ld_x, M, K, parts, &nparts, st));
+    int nparts = ex.amax_n;        // > 0: the kernel that wrote x left its maxima in parts
+    if (nparts <= 0) MB2_TRY(amax_parts(x, ld_x, M, K, parts, &nparts, st));
     CUtensorMap ma, mwh, mwl, my;
     MB2_TRY(make_map(&ma, x, M, K, ld_x, false, 128));
     MB2_TRY(make_map_t(&mwh, whi, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, tc::F16Cfg::BN));

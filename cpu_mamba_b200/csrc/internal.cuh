@@ -22,10 +22,35 @@ struct EpiExtra {
     // the CUDA-core GEMM's split-K partial sums (few-row GEMMs) -- or null
     float *scratch = nullptr;
     size_t scratch_bytes = 0;
-    // not an epilogue term: AMAX_PARTS (512) floats of scratch for the partial
-    // maxima of x that the F16X3 fp32 GEMM scales x by, or null (no F16X3)
+    // not an epilogue term: partial maxima of |x| that the F16X3 fp32 GEMM
+    // scales x by.  amax_n > 0: amax_parts already holds amax_n of them (the
+    // kernel that wrote x computed them); amax_n == 0: amax_parts is scratch of
+    // AMAX_PARTS (512) floats that the GEMM fills with a pass over x first;
+    // null: no F16X3.
     float *amax_parts = nullptr;
+    int amax_n = 0;
 };
+
+// Slots of the fused maxima: a kernel writing a GEMM's input takes
+// atomicMax(slot[block % AMAX_SLOTS], |value| bits) over the slots, zeroed
+// beforehand; the GEMM reduces the slots.
+constexpr int AMAX_SLOTS = 64;
+__device__ __forceinline__ void amax_publish(unsigned *slots, float m) {
+    // m >= 0 (or NaN): its bits order like the value; one atomic per block
+    // (call with every thread of the block, after its last value)
+    __shared__ float red[32];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red[wid] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int nw = (int)((blockDim.x * blockDim.y + 31) >> 5);
+        for (int w = 1; w < nw; ++w) m = fmaxf(m, red[w]);
+        const unsigned b = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+        atomicMax(slots + b % AMAX_SLOTS, __float_as_uint(m));
+    }
+}
 
 int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
               const float *scale, const void *bias, void *y, int64_t ld_y, int64_t M,
@@ -49,20 +74,20 @@ int dequantize_f32(int scheme, const void *wq, const float *scale, int64_t rows,
                    int64_t group, float *out, cudaStream_t st);
 int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const void *bias,
                 void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
-                int64_t d_inner, int64_t d_conv, cudaStream_t st);
+                int64_t d_inner, int64_t d_conv, cudaStream_t st, unsigned *amax = nullptr);
 int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t ld_dl,
                const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
                int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
                const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
                int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, int64_t dt_rank,
-               cudaStream_t stream);
+               cudaStream_t stream, unsigned *amax = nullptr);
 
 int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t ld_dt,
                const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
                int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
                void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
                int64_t d_state, cudaStream_t stream, float *seg_ws = nullptr,
-               size_t seg_bytes = 0);
+               size_t seg_bytes = 0, unsigned *amax = nullptr);
 // Long sequences over few (batch, channel) chains: the number of T segments
 // scan_gated runs in parallel (1 = none) and the scratch it needs for them.
 int scan_segments(int64_t batch, int64_t d_inner, int64_t seqlen, int64_t d_state);

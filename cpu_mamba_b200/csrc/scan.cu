@@ -65,6 +65,7 @@ struct ScanParams {
     float *seg_hend;                 // (batch, nseg, d_inner, S)
     float *seg_sdt;                  // (batch, nseg, d_inner)
     const float *seg_hstart;         // pass 3: (batch, nseg, d_inner, S) starting states
+    unsigned *amax;                  // or null: fused maxima of |y| (AMAX_SLOTS slots)
 };
 
 enum { ARR_X = 1, ARR_D2 = 2, ARR_B = 4, ARR_C = 8, ARR_DL = 16, ARR_Z = 32 };
@@ -361,6 +362,7 @@ scan_kernel(const ScanParams p) {
 
     const int nchunks = (T_ + SCAN_TC - 1) / SCAN_TC;
     float sdt = 0.0f;                                  // sum of this channel's dt (pass 1)
+    float ymax = 0.0f;                                 // max |y| written by this thread
     if (nchunks > 0) issue(0);
     cp_async_commit();
 
@@ -464,6 +466,7 @@ scan_kernel(const ScanParams p) {
                 float out = yv + d_skip * io<T>::to_f(xrow[tt * CH]);
                 if (MODE != PLAIN)
                     out = io<T>::round(out) * io<T>::round(silu_f(io<T>::to_f(zrow[tt * CH])));
+                ymax = fmaxf(ymax, fabsf(out));
                 yg[((int64_t)ch * SCAN_TC + tt) * p.ld_y] = io<T>::from_f(out);
             }
         }
@@ -488,6 +491,7 @@ scan_kernel(const ScanParams p) {
         }
         if (MODE == SUMMARY && j == 0) p.seg_sdt[segidx * p.d_inner + d] = sdt;
     }
+    if (MODE != SUMMARY && p.amax) amax_publish(p.amax, ymax);   // launch-uniform branch
 }
 
 // Segments' carry (between pass 1 and pass 3): per (b, d, s), in segment
@@ -592,7 +596,7 @@ int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t
                int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
                const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
                int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, int64_t dt_rank,
-               cudaStream_t stream) {
+               cudaStream_t stream, unsigned *amax) {
     MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "scan: bad dtype");
     MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0 && dt_rank >= 1, MB2_ERR_SHAPE,
                 "scan: bad sizes");
@@ -621,6 +625,7 @@ int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t
     p.y = y; p.ld_y = ld_y;
     p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
     p.d_state = (int)d_state; p.dt_rank = (int)dt_rank;
+    p.amax = amax;
     if (dtype == MB2_F32) return dispatch_scan<float, FUSED>(p, stream);
     return dispatch_scan<__nv_bfloat16, FUSED>(p, stream);
 }
@@ -679,7 +684,8 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
                const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
                int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
                void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
-               int64_t d_state, cudaStream_t stream, float *seg_ws, size_t seg_bytes) {
+               int64_t d_state, cudaStream_t stream, float *seg_ws, size_t seg_bytes,
+               unsigned *amax) {
     MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "scan: bad dtype");
     MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0, MB2_ERR_SHAPE, "scan: bad sizes");
     MB2_REQUIRE(d_state >= 1 && d_state <= 256, MB2_ERR_SHAPE,
@@ -706,6 +712,7 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
     p.y = y; p.ld_y = ld_y;
     p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
     p.d_state = (int)d_state;
+    p.amax = amax;
     const int nseg = scan_segments(batch, d_inner, seqlen, d_state);
     if (nseg > 1 && seg_ws && seg_bytes >= scan_segment_bytes(batch, d_inner, seqlen, d_state)) {
         if (dtype == MB2_F32) return run_segmented<float, GATED>(p, nseg, seg_ws, stream);
