@@ -396,12 +396,10 @@ def profile_stages(m, x, cfg, dtype, steps):
     B, T, dm = x.shape
     di, S, R = m.d_inner, m.d_state, m.dt_rank
     stream = torch.cuda.current_stream(dev)
-    # the weight caches the block forward uses: the fp16 split (F16X3) for the
-    # three large projections, the TF32 split for dt_proj (K = dt_rank)
+    # the weight cache the block forward uses for fp32: the fp16 split (F16X3)
     fp32 = dtype == torch.float32
-    split = {n: (m._tf32_split(n, getattr(m, n).weight) if fp32 and n == "dt_proj" else None)
-             for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
-    s16 = {n: (m._f16_split(n, getattr(m, n).weight) if fp32 and n != "dt_proj" else None)
+    split = {n: None for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
+    s16 = {n: (m._f16_split(n, getattr(m, n).weight) if fp32 else None)
            for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
     x2 = x.reshape(B * T, dm)
     times = {k: [] for k in STAGES}
@@ -424,7 +422,7 @@ def profile_stages(m, x, cfg, dtype, steps):
                        weight_f16=s16["x_proj"])
             ev[3].record(stream)
             ops.linear(xdbl[:, :R], m.dt_proj.weight, m.dt_proj.bias, split["dt_proj"],
-                       out=xz[:, :di])
+                       out=xz[:, :di], weight_f16=s16["dt_proj"])
             ev[4].record(stream)
             y = ops.scan_gated(xc, xz[:, :di], xdbl[:, R:R + S], xdbl[:, R + S:], xz[:, di:],
                                m.A_log, m.D, B, T, out=xc)

@@ -304,7 +304,14 @@ static int pipeline_tail(const mb2_block &b, const Layout &l, void *out, int64_t
     // weight, fewer than 256 rows) the fused scan computes dt itself from
     // W_dt's rows in registers.
     bool dt_done = false;
-    if (N > 0)
+    if (N >= 256 && b.dtype == MB2_F32 && b.dt_proj.weight_f16) {
+        EpiExtra dt_ex;                  // x's maxima by a pass over dt_low (N x R)
+        dt_ex.amax_parts = reinterpret_cast<float *>(ws + l.off_aux);
+        MB2_TRY(gemm_f16x3(static_cast<const float *>(xdbl), l.ldx, b.dt_proj.weight_f16,
+                           b.dt_proj.bias, static_cast<float *>(xz), 2 * di, N, di, R, di, 0, di,
+                           0, MB2_EPI_NONE, st, &dt_done, dt_ex, dt_ex.amax_parts));
+    }
+    if (N > 0 && !dt_done)
         MB2_TRY(gemm_tc(b.dtype, xdbl, l.ldx, b.dt_proj.weight, b.dt_proj.weight_split,
                         b.dt_proj.bias, xz, 2 * di, N, di, R, di, 0, di, 0, MB2_EPI_NONE, st,
                         &dt_done));

@@ -137,6 +137,8 @@ class CPUMamba(nn.Module):
                 d.weight = dense.data_ptr()
                 if dense.dtype == torch.float32:
                     d.weight_split = self._tf32_split("dt_proj_deq", dense).data_ptr()
+                    if dense.shape[1] % 8 == 0:
+                        d.weight_f16 = self._f16_split("dt_proj_deq", dense).data_ptr()
         elif isinstance(mod, nn.Linear):
             w = mod.weight
             if not w.is_contiguous():
@@ -146,7 +148,7 @@ class CPUMamba(nn.Module):
             d.scheme = 0
             if w.dtype == torch.float32:
                 d.weight_split = self._tf32_split(name, w).data_ptr()
-                if name != "dt_proj" and w.shape[1] % 8 == 0:
+                if w.shape[1] % 8 == 0:
                     # prefill projections (>= 256 rows) on the fp16 tensor cores
                     d.weight_f16 = self._f16_split(name, w).data_ptr()
         else:

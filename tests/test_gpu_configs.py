@@ -68,13 +68,12 @@ def test_config0_fp32_block_b151_t180():
         assert (y[:8] - ref_op).abs().max().item() <= TOL
 
 
-def test_config1_bf16_block_b8_t8192_segmented():
-    """d_model 768, d_state 16, B=8, T=8192 in bf16 (the scan runs in T
-    segments with carried states): rows 0 and 7 against the fp32 oracle."""
-    from cpu_mamba_b200._lib import lib
+def test_config1_bf16_block_b8_t8192():
+    """d_model 768, d_state 16, B=8, T=8192 in bf16 (few chains over a long
+    sequence: the scan's few-chain layout): rows 0 and 7 against the fp32
+    oracle."""
     p = oracle.make_block_params(768, 16, seed=1)
     x = torch.randn(8, 8192, 768, generator=torch.Generator().manual_seed(1))
-    assert lib().mb2_scan_workspace_bytes(8, 8192, 1536, 16) > 0   # segmented at this shape
     m = make_block(p, 768, 16, 48, torch.bfloat16)
     with torch.no_grad():
         y = m(x.to(device="cuda", dtype=torch.bfloat16)).float().cpu()
