@@ -81,7 +81,7 @@ _SIGS = {
     "mb2_split_f16": (ctypes.c_int, [_vp, _c_i64, _c_i64, _vp, _vp]),
     "mb2_linear_f16_scratch_bytes": (ctypes.c_size_t, []),
     "mb2_linear_f16": (ctypes.c_int, [_vp, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
-                                      _c_i64, ctypes.c_int, _vp, _vp]),
+                                      _c_i64, ctypes.c_int, ctypes.c_int, _vp, _vp]),
     "mb2_quantize": (ctypes.c_int, [ctypes.c_int, _vp, _c_i64, _c_i64, _vp, _vp, _vp]),
     "mb2_dequantize": (ctypes.c_int, [ctypes.c_int, _vp, _vp, _c_i64, _c_i64, _vp, _vp]),
     "mb2_qlinear": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _vp, _c_i64, _vp, _vp, _vp,

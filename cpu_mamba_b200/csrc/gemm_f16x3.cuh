@@ -36,10 +36,7 @@
 struct F16Cfg {
     static constexpr int BN = 128;
     static constexpr int BK = 64;              // fp16 K elements per k-block
-    static constexpr int STAGES = 3;
     static constexpr int SEG = 4;              // k-blocks per hi*hi segment (16 MMAs)
-    static constexpr uint32_t W_BYTES = BN * 128;
-    static constexpr uint32_t STAGE_BYTES = 2 * TILE_BYTES + 2 * W_BYTES;   // 64 KB
     // 14 warps: registers are allocated in groups of four warps, so the block
     // counts as 16 warps and every thread may use 128 registers
     static constexpr int WARPS = 14;
@@ -51,13 +48,27 @@ struct F16Cfg {
     static constexpr int ECOLS = 64;           // accumulator columns per epilogue warp
     static constexpr int AMAX_PARTS = 512;     // partial maxima of x (mb2_amax_parts)
 };
+// Per-CTA stage geometry.  One SM: a 128 x 128 tile per CTA, 3 stages of
+// (A 32 KB | W_hi 16 KB | W_lo 16 KB).  A pair of SMs (cta_group::2): a
+// 256 x 128 tile per pair, each CTA loading its 128 rows of A and 64 of the
+// 128 rows of W (the MMAs read the two halves from the two CTAs), so a stage
+// is 48 KB and 4 of them fit: 25 % fewer bytes from L2 per multiply-add and a
+// third more work in flight.
+template <bool PAIR> struct F16Stage {
+    static constexpr int STAGES = PAIR ? 4 : 3;
+    static constexpr int WROWS = PAIR ? 64 : 128;        // W rows per CTA
+    static constexpr uint32_t W_BYTES = WROWS * 128;
+    static constexpr uint32_t STAGE_BYTES = 2 * TILE_BYTES + 2 * W_BYTES;
+};
 
 // output staging: 32 rows x 32 fp32 columns (one 128B-swizzled box) per epilogue warp
 constexpr size_t f16_staging_bytes() { return (size_t)8 * 32 * 32 * sizeof(float); }
-constexpr size_t f16_smem_bytes() {
-    return 1024 + (size_t)F16Cfg::STAGES * F16Cfg::STAGE_BYTES + f16_staging_bytes() + 256;
+template <bool PAIR> constexpr size_t f16_smem_bytes() {
+    return 1024 + (size_t)F16Stage<PAIR>::STAGES * F16Stage<PAIR>::STAGE_BYTES +
+           f16_staging_bytes() + 256;
 }
-static_assert(f16_smem_bytes() <= 232448, "F16X3 shared memory above the 227 KB per CTA");
+static_assert(f16_smem_bytes<false>() <= 232448 && f16_smem_bytes<true>() <= 232448,
+              "F16X3 shared memory above the 227 KB per CTA");
 
 struct F16Params {
     Params g;                       // shapes, output, epilogue terms (split-K unused)
@@ -93,78 +104,147 @@ __device__ __forceinline__ float2 unpack_h2(uint32_t v) {
     return __half22float2(*reinterpret_cast<const __half2 *>(&v));
 }
 
-// kind::f16 MMA (fp16 A and B, fp32 accumulator), A from tensor memory.
+// kind::f16 MMA (fp16 A and B, fp32 accumulator), A from tensor memory; in a
+// pair (cta_group::2) one MMA computes the pair's 256 rows: A's rows 0-127 and
+// D's rows 0-127 in the first CTA's TMEM, 128-255 in the second's, B's 128
+// rows split 64 / 64 between the two CTAs' shared memory at the same offset.
+template <bool PAIR>
 __device__ __forceinline__ void mma_ts_f16(uint32_t tmem_d, uint32_t tmem_a, uint64_t db,
                                            uint32_t accum) {
     // D F32 (bits 4-5 = 1), A / B F16 (0), K-major, N >> 3 at 17, M >> 4 at 24
     constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(F16Cfg::BN >> 3) << 17) |
-                               ((uint32_t)(BM >> 4) << 24);
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
-        ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accum));
+                               ((uint32_t)((PAIR ? 2 * BM : BM) >> 4) << 24);
+    if constexpr (PAIR)
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+            ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accum));
+    else
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+            ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accum));
 }
 
-template <bool EXTRA>
+// Arrive (once MMAs complete) on the barrier at this offset in both CTAs of
+// the pair, or in this CTA.
+template <bool PAIR>
+__device__ __forceinline__ void mma_commit_to(uint32_t bar) {
+    if constexpr (PAIR)
+        asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster"
+                     ".multicast::cluster.b64 [%0], %1;" ::"r"(bar), "h"((uint16_t)3) : "memory");
+    else
+        mma_commit(bar);
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_id() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+// the shared::cluster address of `local` (a shared::cta address) in CTA `rank`
+__device__ __forceinline__ uint32_t peer_addr(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+                 ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+                 ::: "memory");
+}
+
+template <bool EXTRA, bool PAIR>
 __global__ void __launch_bounds__(F16Cfg::WARPS * 32, 1)
 gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wh,
                   const __grid_constant__ CUtensorMap map_wl, const __grid_constant__ CUtensorMap map_y,
                   const F16Params fp) {
     using C = F16Cfg;
+    using G = F16Stage<PAIR>;
     constexpr int BN = C::BN;
+    constexpr int TM = PAIR ? 2 * BM : BM;              // tile rows (per pair)
     const Params &p = fp.g;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t *gbase = smem_raw + (base - raw);
-    const uint32_t out_base = base + C::STAGES * C::STAGE_BYTES;
+    const uint32_t out_base = base + G::STAGES * G::STAGE_BYTES;
     const uint32_t bars = out_base + (uint32_t)f16_staging_bytes();
-    // full[S] empty[S] xform[S] a_empty[2] seg_full[2] seg_empty[2] q_full q_empty; tmem slot
+    // full[S] empty[S] xform[S] peer[S] a_empty[2] seg_full[2] seg_empty[2] q_full q_empty; tmem slot
     auto full = [&](int s) { return bars + 8u * s; };
-    auto empty = [&](int s) { return bars + 8u * (C::STAGES + s); };
-    auto xform = [&](int s) { return bars + 8u * (2 * C::STAGES + s); };
-    auto a_empty = [&](int l) { return bars + 8u * (3 * C::STAGES + l); };
-    auto seg_full = [&](int b) { return bars + 8u * (3 * C::STAGES + 2 + b); };
-    auto seg_empty = [&](int b) { return bars + 8u * (3 * C::STAGES + 4 + b); };
-    const uint32_t q_full = bars + 8u * (3 * C::STAGES + 6);
-    const uint32_t q_empty = bars + 8u * (3 * C::STAGES + 7);
-    const uint32_t tmem_slot = bars + 8u * (3 * C::STAGES + 8);
+    auto empty = [&](int s) { return bars + 8u * (G::STAGES + s); };
+    auto xform = [&](int s) { return bars + 8u * (2 * G::STAGES + s); };
+    auto peer = [&](int s) { return bars + 8u * (3 * G::STAGES + s); };
+    auto a_empty = [&](int l) { return bars + 8u * (4 * G::STAGES + l); };
+    auto seg_full = [&](int b) { return bars + 8u * (4 * G::STAGES + 2 + b); };
+    auto seg_empty = [&](int b) { return bars + 8u * (4 * G::STAGES + 4 + b); };
+    const uint32_t q_full = bars + 8u * (4 * G::STAGES + 6);
+    const uint32_t q_empty = bars + 8u * (4 * G::STAGES + 7);
+    const uint32_t tmem_slot = bars + 8u * (4 * G::STAGES + 8);
     uint32_t *tmem_slot_ptr = reinterpret_cast<uint32_t *>(gbase + (tmem_slot - base));
     // stage s: A box 0 (k 0-31) | A box 1 (k 32-63) | W_hi | W_lo
-    auto tile_a = [&](int s, int box) { return base + (uint32_t)(s * C::STAGE_BYTES + box * TILE_BYTES); };
+    auto tile_a = [&](int s, int box) { return base + (uint32_t)(s * G::STAGE_BYTES + box * TILE_BYTES); };
     auto tile_w = [&](int s, int lo) {
-        return base + (uint32_t)(s * C::STAGE_BYTES + 2 * TILE_BYTES + lo * C::W_BYTES);
+        return base + (uint32_t)(s * G::STAGE_BYTES + 2 * TILE_BYTES + lo * G::W_BYTES);
     };
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // pair: rank 0 issues the MMAs; rank 1 relays that its stages are ready
+    const uint32_t rank = PAIR ? cluster_rank() : 0;
+    const int unit0 = PAIR ? (int)cluster_id() : (int)blockIdx.x;     // first tile
+    const int units = PAIR ? (int)cluster_count() : (int)gridDim.x;   // tile stride
     const int num_n = (int)ceil_div(p.N, BN);
-    const int num_tiles = (int)ceil_div(p.M, BM) * num_n;
+    const int num_tiles = (int)ceil_div(p.M, TM) * num_n;
     const int nk = (int)ceil_div(p.K, C::BK);
     const int nseg = (nk + C::SEG - 1) / C::SEG;      // segments per tile
+    // the epilogue's drained-accumulator barriers live in rank 0 and count
+    // both CTAs' epilogue threads
+    constexpr int DRAINERS = (PAIR ? 2 : 1) * C::EPI_THREADS;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < C::STAGES; ++s) {
+        for (int s = 0; s < G::STAGES; ++s) {
             mbar_init(full(s), 1);
             mbar_init(empty(s), 1);
             mbar_init(xform(s), 128);
+            mbar_init(peer(s), 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(a_empty(b), 1);
             mbar_init(seg_full(b), 1);
-            mbar_init(seg_empty(b), C::EPI_THREADS);
+            mbar_init(seg_empty(b), DRAINERS);
         }
         mbar_init(q_full, 1);
-        mbar_init(q_empty, C::EPI_THREADS);
+        mbar_init(q_empty, DRAINERS);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                     ::"r"(tmem_slot), "r"(512));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        if constexpr (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                         ::"r"(tmem_slot), "r"(512));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                         ::"r"(tmem_slot), "r"(512));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
+    if constexpr (PAIR) cluster_sync();      // both CTAs' barriers exist before any remote use
+    else __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot_ptr;
 
@@ -173,13 +253,14 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         if (lane == 0) {
             uint32_t g = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                const int64_t m0 = (int64_t)(t / num_n) * BM, n0 = (int64_t)(t % num_n) * BN;
+            for (int t = unit0; t < num_tiles && ok; t += units) {
+                const int64_t m0 = (int64_t)(t / num_n) * TM + (int64_t)rank * BM;
+                const int64_t n0 = (int64_t)(t % num_n) * BN + (int64_t)rank * G::WROWS;
                 for (int kb = 0; kb < nk; ++kb, ++g) {
-                    const int s = g % C::STAGES;
-                    const uint32_t ph = (g / C::STAGES) & 1;
+                    const int s = g % G::STAGES;
+                    const uint32_t ph = (g / G::STAGES) & 1;
                     if (!mbar_wait(empty(s), ph ^ 1, 11)) { ok = false; break; }
-                    mbar_expect_tx(full(s), C::STAGE_BYTES);
+                    mbar_expect_tx(full(s), G::STAGE_BYTES);
                     const int32_t kc = kb * C::BK;
                     tma_load_2d(tile_a(s, 0), &map_a, full(s), kc, (int32_t)m0);
                     tma_load_2d(tile_a(s, 1), &map_a, full(s), kc + 32, (int32_t)m0);
@@ -189,26 +270,44 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
             }
         }
     } else if (warp == 1) {
-        // -------------------------------------------------------- MMA issuer
-        uint32_t g = 0, gs = 0;
-        int it = 0;
-        bool ok = true;
-        if (lane == 0) {
-            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+        if (lane == 0 && PAIR && rank != 0) {
+            // ------------------------------------------ pair: relay (rank 1)
+            // a stage of this CTA is ready for the pair's MMAs once it has
+            // landed and its A has been split into TMEM
+            uint32_t g = 0;
+            bool ok = true;
+            const uint32_t leader_peer0 = peer_addr(peer(0), 0);
+            for (int t = unit0; t < num_tiles && ok; t += units) {
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % G::STAGES;
+                    const uint32_t ph = (g / G::STAGES) & 1;
+                    ok = mbar_wait(full(s), ph, 22) && mbar_wait(xform(s), ph, 23);
+                    if (!ok) break;
+                    mbar_arrive_cluster(leader_peer0 + 8u * s);
+                }
+            }
+        } else if (lane == 0) {
+            // ----------------------------------------------------- MMA issuer
+            uint32_t g = 0, gs = 0;
+            int it = 0;
+            bool ok = true;
+            for (int t = unit0; t < num_tiles && ok; t += units, ++it) {
                 uint32_t pcol = 0;
                 for (int kb = 0; kb < nk && ok; ++kb, ++g) {
                     const int rel = kb % C::SEG;
                     if (rel == 0) {
                         // this segment's accumulator was drained two segments ago
-                        ok = mbar_wait(seg_empty(gs & 1), ((gs >> 1) & 1) ^ 1, 12);
-                        if (ok && kb == 0) ok = mbar_wait(q_empty, (it & 1) ^ 1, 13);
+                        // (in a pair: by both CTAs' epilogues, the other one remotely)
+                        ok = mbar_wait_cluster(seg_empty(gs & 1), ((gs >> 1) & 1) ^ 1, 12);
+                        if (ok && kb == 0) ok = mbar_wait_cluster(q_empty, (it & 1) ^ 1, 13);
                         if (!ok) break;
                         pcol = C::COL_P + (gs & 1) * BN;
                         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     }
-                    const int s = g % C::STAGES;
-                    const uint32_t ph = (g / C::STAGES) & 1;
-                    ok = mbar_wait(full(s), ph, 14) && mbar_wait(xform(s), ph, 15);
+                    const int s = g % G::STAGES;
+                    const uint32_t ph = (g / G::STAGES) & 1;
+                    ok = mbar_wait(full(s), ph, 14) && mbar_wait(xform(s), ph, 15) &&
+                         (!PAIR || mbar_wait_cluster(peer(s), ph, 24));
                     if (!ok) break;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll
@@ -216,28 +315,20 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                         const uint32_t ah = tmem + C::COL_A + (g & 1) * 64 + kk * 8;
                         const uint64_t bh = smem_desc(tile_w(s, 0) + kk * 32);
                         const uint64_t bl = smem_desc(tile_w(s, 1) + kk * 32);
-                        mma_ts_f16(tmem + pcol, ah, bh, (rel > 0 || kk > 0) ? 1u : 0u);
-                        mma_ts_f16(tmem + C::COL_Q, ah, bl, (kb > 0 || kk > 0) ? 1u : 0u);
-                        mma_ts_f16(tmem + C::COL_Q, ah + 32, bh, 1u);
+                        mma_ts_f16<PAIR>(tmem + pcol, ah, bh, (rel > 0 || kk > 0) ? 1u : 0u);
+                        mma_ts_f16<PAIR>(tmem + C::COL_Q, ah, bl, (kb > 0 || kk > 0) ? 1u : 0u);
+                        mma_ts_f16<PAIR>(tmem + C::COL_Q, ah + 32, bh, 1u);
                     }
-                    mma_commit(empty(s));          // stage free once these MMAs read it
-                    mma_commit(a_empty(g & 1));    // and the A slot
+                    mma_commit_to<PAIR>(empty(s));        // stages free once these MMAs read them
+                    mma_commit_to<PAIR>(a_empty(g & 1));  // and the A slots
                     if (rel == C::SEG - 1 || kb == nk - 1) {
-                        mma_commit(seg_full(gs & 1));
+                        mma_commit_to<PAIR>(seg_full(gs & 1));
                         ++gs;
                     }
                 }
-                if (ok) mma_commit(q_full);
+                if (ok) mma_commit_to<PAIR>(q_full);
             }
         }
-        __syncwarp();
-        // free TMEM once the epilogue drained the last segment and Q (bounded)
-        const int it_all = __shfl_sync(0xffffffffu, it, 0);
-        const uint32_t gs_all = __shfl_sync(0xffffffffu, gs, 0);
-        if (it_all > 0) mbar_wait(q_empty, (uint32_t)((it_all - 1) & 1), 16);
-        if (gs_all > 0) mbar_wait(seg_empty((gs_all - 1) & 1), ((gs_all - 1) >> 1) & 1, 17);
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
     } else if (warp < C::EPI0) {
         // --------------------------------------- x split into TMEM (scaled fp16)
         const int q = warp & 3;
@@ -245,10 +336,10 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         const float sx = pow2f(f16_scale_exp(warp_amax(fp.x_parts, fp.n_parts)));
         uint32_t g = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        for (int t = unit0; t < num_tiles && ok; t += units) {
             for (int kb = 0; kb < nk; ++kb, ++g) {
-                const int s = g % C::STAGES;
-                const uint32_t ph = (g / C::STAGES) & 1;
+                const int s = g % G::STAGES;
+                const uint32_t ph = (g / G::STAGES) & 1;
                 bool w = mbar_wait(full(s), ph, 18);
                 if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
                 uint32_t hi[32], lo[32];
@@ -305,11 +396,19 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                 for (int j = 0; j < 32; ++j) acc[cb * 32 + j] += __uint_as_float(r[j]);
             }
         };
+        // drained accumulators are reported to rank 0's barriers
+        const uint32_t seg_empty0 = PAIR ? peer_addr(seg_empty(0), 0) : seg_empty(0);
+        const uint32_t q_empty0 = PAIR ? peer_addr(q_empty, 0) : q_empty;
+        auto drained = [&](uint32_t local, uint32_t remote) {
+            if (PAIR && rank != 0) mbar_arrive_cluster(remote);
+            else mbar_arrive(local);
+        };
         uint32_t gs = 0;
         int it = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
-            const int64_t m0 = (int64_t)(t / num_n) * BM, n0 = (int64_t)(t % num_n) * BN;
+        for (int t = unit0; t < num_tiles && ok; t += units, ++it) {
+            const int64_t m0 = (int64_t)(t / num_n) * TM + (int64_t)rank * BM;
+            const int64_t n0 = (int64_t)(t % num_n) * BN;
 #pragma unroll
             for (int j = 0; j < C::ECOLS; ++j) acc[j] = 0.0f;
             for (int sg = 0; sg < nseg; ++sg, ++gs) {
@@ -320,14 +419,14 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     drain(C::COL_Q);
                     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                    mbar_arrive(q_empty);
+                    drained(q_empty, q_empty0);
                 }
                 const bool w = mbar_wait(seg_full(gs & 1), (gs >> 1) & 1, 21);
                 if (!__all_sync(0xffffffffu, w)) { ok = false; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 drain(C::COL_P + (gs & 1) * BN);
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-                mbar_arrive(seg_empty(gs & 1));
+                drained(seg_empty(gs & 1), seg_empty0 + 8u * (gs & 1));
             }
             if (!ok) break;
             const int64_t m_row = m0 + q * 32 + lane;
@@ -396,4 +495,18 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         }
         if (lane == 0) bulk_wait0();
     }
+    // every role is done with TMEM (bounded waits: also after an expired one)
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    __syncwarp();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if constexpr (PAIR)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    }
+    // neither CTA of a pair leaves while the other may still signal its barriers
+    __syncwarp();
+    if constexpr (PAIR) cluster_sync();
 }

@@ -139,6 +139,29 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Bounded wait with cluster-scope acquire: for barriers that the other CTA
+// of an SM pair arrives on remotely.
+__device__ __forceinline__ bool mbar_try_cluster(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int where) {
+    if (mbar_try_cluster(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_cluster(bar, parity)) return true;
+        if ((i & 255) == 0 && globaltimer() - t0 > WAIT_NS) {
+            atomicCAS(&g_mb2_device_error, 0, where);
+            return false;
+        }
+    }
+}
+
 // Bounded wait; false (and the device error flag set) when it expired.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int where) {
     if (mbar_try(bar, parity)) return true;
@@ -903,16 +926,76 @@ size_t split_f16_bytes(int64_t rows, int64_t cols) {
     return kF16Header + (size_t)rows * cols * 2 * sizeof(__half);
 }
 
+// Launch one F16X3 instantiation: persistent, one CTA per SM; pairs of CTAs
+// (2-SM clusters) when PAIR, as many pairs as can be resident at once.
+template <bool EXTRA, bool PAIR>
+static int launch_f16(const CUtensorMap &ma, const CUtensorMap &mwh, const CUtensorMap &mwl,
+                      const CUtensorMap &my, const tc::F16Params &fp, int64_t M, int64_t N,
+                      cudaStream_t st) {
+    auto kern = tc::gemm_f16x3_kernel<EXTRA, PAIR>;
+    constexpr size_t smem = tc::f16_smem_bytes<PAIR>();
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_f16x3 smem attribute: %s", cudaGetErrorString(e));
+    if (g_num_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    const int64_t tiles = ceil_div(M, (int64_t)(PAIR ? 2 * tc::BM : tc::BM)) *
+                          ceil_div(N, (int64_t)tc::F16Cfg::BN);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.blockDim = dim3(tc::F16Cfg::WARPS * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    int64_t units = g_num_sms;
+    if (PAIR) {
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        static int max_pairs = 0;          // resident pairs of this kernel on this GPU
+        if (max_pairs == 0) {
+            cfg.gridDim = dim3((unsigned)(2 * (g_num_sms / 2)));
+            int n = 0;
+            e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+            if (e != cudaSuccess || n <= 0)
+                return fail(MB2_ERR_CUDA, "gemm_f16x3: no resident SM pairs (%s)", cudaGetErrorString(e));
+            max_pairs = n;
+        }
+        units = max_pairs;
+    }
+    units = tiles < units ? tiles : units;
+    cfg.gridDim = dim3((unsigned)(PAIR ? 2 * units : units));
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess &&
+        fa.maxThreadsPerBlock < tc::F16Cfg::WARPS * 32)
+        return fail(MB2_ERR_CUDA, "gemm_f16x3_kernel: %d registers per thread allow only %d threads",
+                    fa.numRegs, fa.maxThreadsPerBlock);
+    e = cudaLaunchKernelEx(&cfg, kern, ma, mwh, mwl, my, fp);
+    if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_f16x3_kernel launch: %s", cudaGetErrorString(e));
+    return check_launch("gemm_f16x3_kernel");
+}
+
 // fp32 GEMM through the F16X3 kernel; *used reports whether it ran.  parts:
-// scratch of AMAX_PARTS floats for x's partial maxima.
+// scratch of AMAX_PARTS floats for x's partial maxima.  pair: 1 = 256-row
+// tiles on pairs of SMs, 0 or -1 = 128-row tiles on single SMs (the default:
+// measured on the block's projections, the pairs took 8-13 % longer -- each
+// SM loads 25 % fewer bytes per multiply-add, but every k-block waits for the
+// second CTA's ready signal, and the kernel is bound by that pipeline latency
+// rather than by L2 bandwidth).
 int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, float *y,
                int64_t ld_y, int64_t M, int64_t N, int64_t K, int64_t n1, int64_t off1,
                int64_t n2, int64_t off2, int epi, cudaStream_t st, bool *used,
-               const EpiExtra &ex, float *parts) {
+               const EpiExtra &ex, float *parts, int pair) {
     *used = false;
     if (!w16 || !parts || M < 1 || N < 16 || K < 16) return MB2_OK;
     if (!aligned(x, 16) || (ld_x * 4) % 16 != 0 || K % 8 != 0 || !aligned(w16, 256)) return MB2_OK;
     if (ex.resid && (!aligned(ex.resid, 16) || ex.ld_r % 4 != 0 || N % 4 != 0)) return MB2_OK;
+    const bool two = pair > 0;
     const char *wb = static_cast<const char *>(w16);
     const __half *whi = reinterpret_cast<const __half *>(wb + kF16Header);
     const __half *wlo = whi + N * K;
@@ -920,9 +1003,10 @@ int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, 
     int nparts = ex.amax_n;        // > 0: the kernel that wrote x left its maxima in parts
     if (nparts <= 0) MB2_TRY(amax_parts(x, ld_x, M, K, parts, &nparts, st));
     CUtensorMap ma, mwh, mwl, my;
+    const int wrows = two ? tc::F16Stage<true>::WROWS : tc::F16Stage<false>::WROWS;
     MB2_TRY(make_map(&ma, x, M, K, ld_x, false, 128));
-    MB2_TRY(make_map_t(&mwh, whi, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, tc::F16Cfg::BN));
-    MB2_TRY(make_map_t(&mwl, wlo, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, tc::F16Cfg::BN));
+    MB2_TRY(make_map_t(&mwh, whi, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, wrows));
+    MB2_TRY(make_map_t(&mwl, wlo, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, wrows));
     const bool remap = (n1 < N && off1 != 0) || (n2 < N && off2 != 0);
     const bool tma_store = !remap && aligned(y, 16) && (ld_y * 4) % 16 == 0;
     if (tma_store) MB2_TRY(make_map(&my, y, M, N, ld_y, false, 32));
@@ -934,25 +1018,14 @@ int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, 
     fp.n_parts = nparts;
     fp.w_inv = reinterpret_cast<const float *>(w16);
     const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS;
-    auto kern = extra ? tc::gemm_f16x3_kernel<true> : tc::gemm_f16x3_kernel<false>;
-    constexpr size_t smem = tc::f16_smem_bytes();
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_f16x3 smem attribute: %s", cudaGetErrorString(e));
-    if (g_num_sms == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
-    }
-    const int64_t tiles = ceil_div(M, (int64_t)tc::BM) * ceil_div(N, (int64_t)tc::F16Cfg::BN);
-    const unsigned grid = (unsigned)(tiles < g_num_sms ? tiles : g_num_sms);
-    cudaFuncAttributes fa{};
-    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess &&
-        fa.maxThreadsPerBlock < tc::F16Cfg::WARPS * 32)
-        return fail(MB2_ERR_CUDA, "gemm_f16x3_kernel: %d registers per thread allow only %d threads",
-                    fa.numRegs, fa.maxThreadsPerBlock);
-    kern<<<grid, tc::F16Cfg::WARPS * 32, smem, st>>>(ma, mwh, mwl, my, fp);
-    MB2_TRY(check_launch("gemm_f16x3_kernel"));
+    int rc;
+    if (two)
+        rc = extra ? launch_f16<true, true>(ma, mwh, mwl, my, fp, M, N, st)
+                   : launch_f16<false, true>(ma, mwh, mwl, my, fp, M, N, st);
+    else
+        rc = extra ? launch_f16<true, false>(ma, mwh, mwl, my, fp, M, N, st)
+                   : launch_f16<false, false>(ma, mwh, mwl, my, fp, M, N, st);
+    MB2_TRY(rc);
     *used = true;
     return MB2_OK;
 }
@@ -994,7 +1067,8 @@ extern "C" size_t mb2_linear_f16_scratch_bytes(void) {
 
 extern "C" int mb2_linear_f16(const float *x, int64_t ld_x, const void *w_f16, const float *bias,
                               float *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
-                              int epilogue, void *scratch, mb2_stream_t stream) {
+                              int epilogue, int sm_pair, void *scratch, mb2_stream_t stream) {
+    MB2_REQUIRE(sm_pair >= -1 && sm_pair <= 1, MB2_ERR_ARG, "linear_f16: sm_pair must be -1, 0 or 1");
     MB2_REQUIRE(epilogue == MB2_EPI_NONE || epilogue == MB2_EPI_SOFTPLUS, MB2_ERR_ARG,
                 "linear_f16: bad epilogue");
     MB2_REQUIRE(M >= 0 && N >= 0 && K >= 0, MB2_ERR_SHAPE, "linear_f16: negative size");
@@ -1010,7 +1084,7 @@ extern "C" int mb2_linear_f16(const float *x, int64_t ld_x, const void *w_f16, c
     bool used = false;
     MB2_TRY(mb2::gemm_f16x3(x, ld_x, w_f16, bias, y, ld_y, M, N, K, N, 0, N, 0, epilogue,
                             (cudaStream_t)stream, &used, mb2::EpiExtra{},
-                            static_cast<float *>(scratch)));
+                            static_cast<float *>(scratch), sm_pair));
     MB2_REQUIRE(used, MB2_ERR_UNSUPPORTED, "linear_f16: operands not supported");
     return MB2_OK;
 }

@@ -65,7 +65,7 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
 int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, float *y,
                int64_t ld_y, int64_t M, int64_t N, int64_t K, int64_t n1, int64_t off1,
                int64_t n2, int64_t off2, int epi, cudaStream_t st, bool *used,
-               const EpiExtra &ex, float *parts);
+               const EpiExtra &ex, float *parts, int pair = -1);
 size_t split_f16_bytes(int64_t rows, int64_t cols);
 // W (rows, cols) fp32 -> mb2_split_f16's layout at out (256-byte aligned)
 int split_f16(const float *w, int64_t rows, int64_t cols, void *out, cudaStream_t st);

@@ -181,11 +181,12 @@ def fold_norm(weight: torch.Tensor, norm_weight: torch.Tensor) -> torch.Tensor:
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
            weight_split: Optional[torch.Tensor] = None, softplus: bool = False,
            out: Optional[torch.Tensor] = None,
-           weight_f16: Optional[torch.Tensor] = None) -> torch.Tensor:
+           weight_f16: Optional[torch.Tensor] = None, sm_pair: int = -1) -> torch.Tensor:
     """y = x W^T + b over the last dim of x (nn.Linear semantics); softplus=True
     applies F.softplus to the result in the same kernel (dt_proj's epilogue).
-    float32 with weight_f16 (split_f16(weight)): the F16X3 tensor-core GEMM;
-    with weight_split (split_tf32(weight)): the 3xTF32 one."""
+    float32 with weight_f16 (split_f16(weight)): the F16X3 tensor-core GEMM
+    (sm_pair: 1 pairs of SMs, 0 or -1 single SMs); with
+    weight_split (split_tf32(weight)): the 3xTF32 one."""
     require_cuda(x, weight, bias, what="linear")
     N, K = weight.shape
     lead = x.shape[:-1]
@@ -199,7 +200,7 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
         check(lib().mb2_linear_f16(ptr(x2), x2.stride(0), ptr(weight_f16), ptr(bias), ptr(y),
                                    y.stride(0), x2.shape[0], N, K,
                                    _lib.EPI_SOFTPLUS if softplus else _lib.EPI_NONE,
-                                   ptr(scratch), stream_of(x)), "linear_f16")
+                                   sm_pair, ptr(scratch), stream_of(x)), "linear_f16")
         return y if out is not None else y.reshape(*lead, N)
     weight = weight.contiguous()
     check(lib().mb2_linear(dtype_code(x.dtype), ptr(x2), x2.stride(0), ptr(weight),

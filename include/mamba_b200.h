@@ -176,6 +176,10 @@ int mb2_split_tf32(const float *w, float *out, int64_t numel,
  * round-to-nearest, so the rounding error stays that of an fp32 GEMM at any K.
  *   x: (M, ld_x) float32, rows 16-byte aligned   y: (M, ld_y) float32
  *   w_f16: mb2_split_f16's output for W (N, K), 256-byte aligned; K % 8 == 0
+ *   sm_pair: 1 = 256 x 128 output tiles on pairs of SMs (cta_group::2: each
+ *   SM of a pair loads half of W's tile), 0 or -1 = 128 x 128 tiles on single
+ *   SMs (the default, what mb2_block_forward uses: 8-13 % faster on the
+ *   block's projections); both give bit-identical results
  *   scratch: mb2_linear_f16_scratch_bytes() of device memory (x's partial maxima)
  * No counterpart in the reference (its projections are torch's fp32 GEMMs,
  * _mamba.py:67,74,84); mb2_block_forward uses it for in_proj, x_proj and
@@ -186,7 +190,7 @@ int mb2_split_f16(const float *w, int64_t rows, int64_t cols, void *out,
 size_t mb2_linear_f16_scratch_bytes(void);
 int mb2_linear_f16(const float *x, int64_t ld_x, const void *w_f16, const float *bias,
                    float *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
-                   int epilogue, void *scratch, mb2_stream_t stream);
+                   int epilogue, int sm_pair, void *scratch, mb2_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Weight-only quantisation (src/cpu_mamba/quant.py:60-134), bit-exact.

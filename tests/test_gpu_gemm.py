@@ -172,3 +172,21 @@ def test_f16x3_softplus_epilogue(M):
     y = ops.linear(xd, wd, bd, weight_f16=s16, softplus=True).cpu()
     lin = ops.linear(xd, wd, bd, weight_f16=s16).cpu()
     assert (y - torch.nn.functional.softplus(lin)).abs().max().item() <= 2e-6
+
+
+@pytest.mark.parametrize("shape", [(4096, 3072, 768), (300, 96, 1536), (1000, 200, 104),
+                                   (2049, 768, 1536), (256, 128, 64)])
+def test_f16x3_sm_pairs_equal_single_sms(shape):
+    """256-row tiles on pairs of SMs (cta_group::2, each SM loading half of
+    W's tile) and 128-row tiles on single SMs: identical results (the same
+    MMAs and the same segment sums, only the tile layout differs)."""
+    M, N, K = shape
+    x, w, b = _data(M, N, K, 31 + sum(shape))
+    xd, wd, bd = x.cuda(), w.cuda(), b.cuda()
+    s16 = ops.split_f16(wd)
+    y1 = ops.linear(xd, wd, bd, weight_f16=s16, sm_pair=0)
+    y2 = ops.linear(xd, wd, bd, weight_f16=s16, sm_pair=1)
+    assert _lib.device_status() == 0
+    assert torch.equal(y1, y2)
+    ref = x.double() @ w.double().T + b.double()
+    assert (y2.cpu().double() - ref).abs().max().item() <= 3 * _f32_err(x, w, b, ref) + 1e-7
