@@ -9,8 +9,9 @@ tokens -- the shape the headline target is quoted on.  Synthetic seeded data:
 x ~ N(0,1); Kaiming-uniform linear weights; conv ~ U(-0.5, 0.5);
 A_log = log(1..S); D = 1; dt_proj.bias = softplus^-1(log-uniform[1e-3, 0.1]).
 Other configs are measurement aids: 1 = bf16 B=8 T=8192 (S=16); 2 = stateful
-decode B=64 (d_model 1024): metric over forward_step calls; 3 = int8 weights,
-d_model 1536, B=32 T=2048; 4 = 24-layer RMSNorm pre-norm residual stack in
+decode B=64 (d_model 1024): metric over forward_step calls; 3 = int8 weights
+(--quant int4 / nf4 for the others), d_model 1536, B=32 T=2048; 4 = 24-layer
+RMSNorm pre-norm residual stack in
 bf16 (d_model 768, S=16), B=1024 x T=2048 split across the ranks (strong
 scaling; tokens/s counts tokens through all 24 layers).
 
@@ -675,6 +676,8 @@ def main():
                          "or NCCL")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the configuration's batch (small cases for profiling)")
+    ap.add_argument("--quant", default=None, choices=["int8", "int4", "nf4"],
+                    help="config 3's weight scheme (default int8)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -682,6 +685,9 @@ def main():
     if args.batch:
         cfg["batch"] = args.batch
         cfg["workload"] += f"_batch{args.batch}"
+    if args.quant and cfg.get("quant"):
+        cfg["workload"] = cfg["workload"].replace(cfg["quant"], args.quant)
+        cfg["quant"] = args.quant
     if args.shard == "channels" and cfg["mode"] != "stack":
         cfg["workload"] += "_dinner_sharded"
     # stdout carries the one result line: whatever the libraries write there

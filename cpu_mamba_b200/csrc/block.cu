@@ -176,6 +176,54 @@ __global__ void conv_step_kernel(const T *__restrict__ xz, int64_t ld_xz, const 
     for (int k = 0; k < K - 1; ++k) cs[k] = io<T>::from_f(win[k + 1]);
 }
 
+// The same conv step taking in_proj's raw split-K partial sums (fp32, (ks, B,
+// 2 d_inner)) instead of its output: each thread sums its x element's splits
+// in the fixed order of the split-K reduction (four interleaved partial sums),
+// applies in_proj's row scale and bias, runs the conv ring, and also sums its
+// z element (the other half of in_proj's row) into xz for the scan.  Saves the
+// reduction's launch.
+template <int K>
+__global__ void conv_step_reduce_kernel(const float *__restrict__ P, int ks,
+                                        const float *__restrict__ row_scale,
+                                        const float *__restrict__ in_bias, float *__restrict__ xz,
+                                        int64_t ld_xz, const float *__restrict__ w,
+                                        const float *__restrict__ bias,
+                                        float *__restrict__ conv_state, float *__restrict__ xc,
+                                        int64_t batch, int64_t d_inner) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= batch * d_inner) return;
+    const int64_t b = i / d_inner, d = i - b * d_inner;
+    const int64_t N = 2 * d_inner, mn = batch * N;
+    auto total = [&](int64_t n) {
+        const float *q = P + b * N + n;
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        int z = 0;
+        for (; z + 4 <= ks; z += 4) {
+            a0 += q[(z + 0) * mn];
+            a1 += q[(z + 1) * mn];
+            a2 += q[(z + 2) * mn];
+            a3 += q[(z + 3) * mn];
+        }
+        for (; z < ks; ++z) a0 += q[z * mn];
+        float v = (a0 + a1) + (a2 + a3);
+        if (row_scale) v *= row_scale[b];
+        if (in_bias) v += in_bias[n];
+        return v;
+    };
+    xz[b * ld_xz + d_inner + d] = total(d_inner + d);      // z, for the scan
+    float *cs = conv_state + i * (K - 1);
+    float win[K];
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) win[k] = cs[k];
+    win[K - 1] = total(d);
+    float acc = bias ? bias[d] : 0.0f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) acc = fmaf(w[d * K + k], win[k], acc);
+    xc[b * d_inner + d] = silu_f(acc);
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) cs[k] = win[k + 1];
+}
+
 template <typename T>
 static int launch_conv_step(int K, const void *xz, int64_t ld_xz, const void *w, const void *bias,
                             void *conv_state, void *xc, int64_t batch, int64_t di,
@@ -382,9 +430,28 @@ static int step_head(const mb2_block &b, const Layout &l, const void *x, void *c
     sk.scratch_bytes = l.part_bytes;
     EpiExtra in_ex = sk;
     in_ex.row_scale = row_scale;
+    int splits = 0;                 // fp32 split-K in_proj: its partials, reduced by the conv
+    if (b.dtype == MB2_F32) in_ex.defer_splits = &splits;
     MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, batch, 2 * di, l.dm, MB2_EPI_NONE,
                        st, -1, 0, -1, 0, in_ex));
-    if (b.dtype == MB2_F32)
+    if (splits > 0) {
+        const unsigned grid = (unsigned)ceil_div(batch * di, (int64_t)256);
+        switch (b.d_conv) {
+#define MB2_CSR(KK)                                                                            \
+    case KK:                                                                                   \
+        conv_step_reduce_kernel<KK><<<grid, 256, 0, st>>>(                                     \
+            sk.scratch, splits, row_scale, static_cast<const float *>(b.in_proj.bias),        \
+            static_cast<float *>(xz), 2 * di, static_cast<const float *>(b.conv_w),           \
+            static_cast<const float *>(b.conv_b), static_cast<float *>(conv_state),           \
+            static_cast<float *>(xc), batch, di);                                             \
+        break;
+            MB2_CSR(2) MB2_CSR(3) MB2_CSR(4) MB2_CSR(5) MB2_CSR(6) MB2_CSR(7) MB2_CSR(8)
+#undef MB2_CSR
+            default: return fail(MB2_ERR_UNSUPPORTED, "step: d_conv %lld not in [2, 8]",
+                                 (long long)b.d_conv);
+        }
+        MB2_TRY(check_launch("conv_step_reduce_kernel"));
+    } else if (b.dtype == MB2_F32)
         MB2_TRY(launch_conv_step<float>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b, conv_state,
                                         xc, batch, di, st));
     else
@@ -402,13 +469,13 @@ static int step_tail(const mb2_block &b, const Layout &l, void *out, float *h, i
     EpiExtra sk;
     sk.scratch = reinterpret_cast<float *>(ws + l.off_part);
     sk.scratch_bytes = l.part_bytes;
-    // dt_proj (bias in the epilogue) over the x half of xz, dead after the conv
-    MB2_TRY(linear_any(b.dtype, b.dt_proj, xdbl, l.ldx, xz, 2 * di, batch, di, R, MB2_EPI_NONE,
-                       st, -1, 0, -1, 0, sk));
-    // one timestep: softplus, exp(dt A), h updated in place, y = C.h + D x, gate
-    MB2_TRY(scan_step(b.dtype, xc, di, xz, 2 * di, (char *)xdbl + l.RB * es,
-                      (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log, b.D,
-                      h, xc, di, batch, di, S, st));
+    // one timestep: dt_proj (W_dt's dense rows; a quantised dt_proj supplies
+    // its dequantised weight) + softplus, exp(dt A), h updated in place,
+    // y = C.h + D x, gate -- one kernel
+    MB2_TRY(scan_step_dt(b.dtype, xc, di, xdbl, l.ldx, b.dt_proj.weight, b.dt_proj.bias,
+                         (char *)xdbl + l.RB * es, (char *)xdbl + l.RC * es, l.ldx,
+                         (char *)xz + di * es, 2 * di, b.A_log, b.D, h, xc, di, batch, di, S, R,
+                         st));
     EpiExtra out_ex = sk;
     out_ex.resid = resid;
     out_ex.ld_r = l.dm;

@@ -792,6 +792,11 @@ static int gemm_tc_splitk(const void *x, int64_t ld_x, const float *w_split, con
     tc::Params p{ex.scratch, N, nullptr, M, N, K, N, N, 0, 0, MB2_EPI_NONE, 1, nullptr, nullptr, 0,
                  (int)ks, (int)kbs};
     MB2_TRY((launch_tc<tc::F32X3, float, false>(ma, mb0, mb1, my, p, st)));
+    *used = true;
+    if (ex.defer_splits) {            // the consumer sums the partials itself
+        *ex.defer_splits = (int)ks;
+        return MB2_OK;
+    }
     tc_splitk_reduce_kernel<<<(unsigned)ceil_div(M * N, (int64_t)256), 256, 0, st>>>(
         ex.scratch, (int)ks, M, N, static_cast<const float *>(bias), ex.row_scale, epi,
         static_cast<const float *>(ex.resid), ex.ld_r, static_cast<float *>(y), ld_y, n1, off1, n2,
@@ -850,7 +855,9 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
 // ------------------------------------------------------- F16X3 (fp32 GEMM) --
 // Partial maxima of |x| over row ranges: CTA b writes the maximum of its rows
 // to parts[b] (gridDim.x <= AMAX_PARTS).  Max is order-independent, so the
-// result does not depend on timing; nothing needs clearing beforehand.
+// result does not depend on timing; nothing needs clearing beforehand.  Each
+// warp walks rows two at a time, its lanes over the row's 16-byte pieces,
+// so every lane keeps several independent loads in flight (HBM-bound).
 __global__ void amax_rows_kernel(const float *__restrict__ x, int64_t ld, int64_t M, int64_t K,
                                  float *__restrict__ parts, int vec) {
     const int64_t per = ceil_div(M, (int64_t)gridDim.x);
@@ -858,15 +865,21 @@ __global__ void amax_rows_kernel(const float *__restrict__ x, int64_t ld, int64_
     const int64_t r1 = r0 + per < M ? r0 + per : M;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     float m = 0.0f;
-    for (int64_t r = r0 + warp; r < r1; r += nw) {
-        const float *row = x + r * ld;
+    for (int64_t r = r0 + warp; r < r1; r += 2 * nw) {
+        const float *ra = x + r * ld;
+        const float *rb = r + nw < r1 ? x + (r + nw) * ld : ra;   // second row, or the first again
         if (vec) {
-            for (int64_t c = (int64_t)lane * 4; c < K; c += 128) {
-                const float4 v = *reinterpret_cast<const float4 *>(row + c);
+            const int w = (int)(K >> 2);
+#pragma unroll 4
+            for (int c = lane; c < w; c += 32) {
+                const float4 u = reinterpret_cast<const float4 *>(ra)[c];
+                const float4 v = reinterpret_cast<const float4 *>(rb)[c];
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w))));
                 m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
             }
         } else {
-            for (int64_t c = lane; c < K; c += 32) m = fmaxf(m, fabsf(row[c]));
+#pragma unroll 4
+            for (int64_t c = lane; c < K; c += 32) m = fmaxf(m, fmaxf(fabsf(ra[c]), fabsf(rb[c])));
         }
     }
 #pragma unroll
@@ -875,14 +888,17 @@ __global__ void amax_rows_kernel(const float *__restrict__ x, int64_t ld, int64_
     if (lane == 0) wm[warp] = m;
     __syncthreads();
     if (threadIdx.x == 0) {
-        for (int w = 1; w < nw; ++w) m = fmaxf(m, wm[w]);
+        for (int k = 1; k < nw; ++k) m = fmaxf(m, wm[k]);
         parts[blockIdx.x] = m;
     }
 }
 
 static int amax_parts(const float *x, int64_t ld, int64_t M, int64_t K, float *parts, int *n,
                       cudaStream_t st) {
-    int64_t g = ceil_div(M * K, (int64_t)16384);          // about 64 KB of x per CTA
+    // about 32 KB of x per CTA, and no more than 16 rows per CTA (two per warp)
+    int64_t g = ceil_div(M * K, (int64_t)8192);
+    const int64_t by_rows = ceil_div(M, (int64_t)16);
+    g = g > by_rows ? g : by_rows;
     g = g < tc::F16Cfg::AMAX_PARTS ? g : tc::F16Cfg::AMAX_PARTS;
     g = g < M ? g : M;
     g = g > 1 ? g : 1;

@@ -29,6 +29,12 @@ struct EpiExtra {
     // null: no F16X3.
     float *amax_parts = nullptr;
     int amax_n = 0;
+    // not an epilogue term: when non-null and the fp32 tensor-core split-K
+    // path runs (few rows), the raw partial sums are left in `scratch` as
+    // (splits, M, N) fp32 without any epilogue term and *defer_splits = the
+    // split count, for the consumer kernel to reduce; 0 when the output was
+    // written as usual
+    int *defer_splits = nullptr;
 };
 
 // Slots of the fused maxima: a kernel writing a GEMM's input takes
@@ -93,10 +99,13 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
 int scan_segments(int64_t batch, int64_t d_inner, int64_t seqlen, int64_t d_state);
 size_t scan_segment_bytes(int64_t batch, int64_t d_inner, int64_t seqlen, int64_t d_state);
 
-int scan_step(int dtype, const void *xc, int64_t ld_x, const void *dt_pre, int64_t ld_dt,
-              const void *bm, const void *cm, int64_t ld_bc, const void *z, int64_t ld_z,
-              const void *A_log, const void *D, float *h, void *y, int64_t ld_y, int64_t batch,
-              int64_t d_inner, int64_t d_state, cudaStream_t st);
+// The decode step's dt_proj (fp32 dot products of dt_low with W_dt's rows),
+// softplus and state update in one kernel; y may alias xc.
+int scan_step_dt(int dtype, const void *xc, int64_t ld_x, const void *dt_low, int64_t ld_dl,
+                 const void *w_dt, const void *b_dt, const void *bm, const void *cm,
+                 int64_t ld_bc, const void *z, int64_t ld_z, const void *A_log, const void *D,
+                 float *h, void *y, int64_t ld_y, int64_t batch, int64_t d_inner, int64_t d_state,
+                 int64_t dt_rank, cudaStream_t st);
 
 // Quantised weights as the tensor-core GEMM's operand (bit-exact dequantised
 // values; fp32: TF32 hi / lo planes, bf16: rounded) and its size in bytes --

@@ -728,132 +728,197 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
 }
 
 // ------------------------------------------------------ single-token step ---
-// forward_step's scan (_mamba.py:140-164): one thread per (sequence b,
-// channel d), channels fastest so the per-channel rows are read coalesced;
-// the channel's state row h[b, d, :] is read, advanced one step and written
-// back in place, 16 states at a time in registers.  dt = softplus(dt_proj
-// output), A = -exp(A_log), dA = 2^(dt * A log2 e) (as the sequence kernel),
-// h = dA h + (dt B) x, y = C.h + D x, out = cast(y) * SiLU(z).
-template <typename T>
-__global__ void __launch_bounds__(256)
-step_scan_kernel(const T *__restrict__ xc, int64_t ld_x, const T *__restrict__ dtp,
-                 int64_t ld_dt, const T *__restrict__ bm, const T *__restrict__ cm,
-                 int64_t ld_bc, const T *__restrict__ z, int64_t ld_z,
-                 const T *__restrict__ A_log, const T *__restrict__ D, float *__restrict__ h,
-                 T *__restrict__ y, int64_t ld_y, int64_t batch, int64_t di, int S) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= batch * di) return;
-    const int64_t b = i / di, d = i - b * di;
-    const float dt = io<T>::round(softplus_fast(io<T>::to_f(dtp[b * ld_dt + d])));
-    const float x = io<T>::to_f(xc[b * ld_x + d]);
-    const T *Br = bm + b * ld_bc;
-    const T *Cr = cm + b * ld_bc;
-    float *hr = h + (b * di + d) * S;
-    const T *ar = A_log + d * S;
-    float yv = 0.0f;
-    for (int s0 = 0; s0 < S; s0 += 16) {
-        float hv[16];
+// The decode step's dt_proj, softplus and state update in one kernel
+// (_mamba.py:146-163).  A CTA takes a tile of 8 sequences x 32 channels and
+// stages the 8 dt_low rows, the 32 rows of W_dt and the 8 B and C rows in
+// shared memory (each W_dt row is read once per 8 sequences).  Phase 1: each
+// of its 256 threads forms one (sequence b, channel d)'s dt = softplus(dt_low[b]
+// . W_dt[d] + b_dt[d]) as an fp32 dot product in a fixed order (rounded to T
+// where the reference's bf16 linear output is).  Phase 2: QS = S / 4 threads
+// per (b, d) advance h[b, d, :] in place, 4 states each in one 16-byte load
+// and store (a warp moves 512 contiguous bytes of h), y = C.h summed by
+// shuffles, + D x, cast, times SiLU(z).
+constexpr int SDT_B = 8, SDT_D = 32, SDT_THREADS = 256;
+
+template <typename T, int QS>
+__global__ void __launch_bounds__(SDT_THREADS)
+step_scan_dt_kernel(const T *__restrict__ xc, int64_t ld_x, const T *__restrict__ dl,
+                    int64_t ld_dl, const T *__restrict__ w_dt, const T *__restrict__ b_dt,
+                    const T *__restrict__ bm, const T *__restrict__ cm, int64_t ld_bc,
+                    const T *__restrict__ z, int64_t ld_z, const T *__restrict__ A_log,
+                    const T *__restrict__ D, float *__restrict__ h, T *__restrict__ y,
+                    int64_t ld_y, int64_t batch, int64_t di, int R) {
+    constexpr int S = 4 * QS;
+    extern __shared__ float sdt_smem[];
+    const int RP = R + 1;                       // odd row pitch: W_dt rows conflict-free
+    float *dts = sdt_smem;                      // [SDT_B][SDT_D] dt of the tile
+    float *bs = dts + SDT_B * SDT_D;            // [SDT_B][S]
+    float *cs = bs + SDT_B * S;                 // [SDT_B][S]
+    float *dls = cs + SDT_B * S;                // [SDT_B][R]
+    float *ws = dls + SDT_B * R;                // [SDT_D][RP]
+    const int64_t d0 = (int64_t)blockIdx.x * SDT_D, b0 = (int64_t)blockIdx.y * SDT_B;
+    const int tid = threadIdx.x;
+    // this thread's QS (b, d) pairs of phase 2 (pairs pi = tid / QS + k PAIRS,
+    // channels fastest): their state, x and z are loaded first, so those
+    // loads overlap the staging and the dt dot products
+    constexpr int PAIRS = SDT_THREADS / QS;
+    const int q = tid % QS;
+    float4 hv[QS];
+    float xv[QS], zv[QS];
 #pragma unroll
-        for (int k = 0; k < 16; ++k) hv[k] = (s0 + k < S) ? hr[s0 + k] : 0.0f;
+    for (int k = 0; k < QS; ++k) {
+        const int pi = tid / QS + k * PAIRS;
+        const int bl = pi / SDT_D, dd = pi - bl * SDT_D;
+        const int64_t b = b0 + bl, d = d0 + dd;
+        const bool ok = b < batch && d < di;
+        hv[k] = ok ? *reinterpret_cast<const float4 *>(h + (b * di + d) * S + 4 * q)
+                   : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        xv[k] = ok ? io<T>::to_f(xc[b * ld_x + d]) : 0.0f;
+        zv[k] = ok ? io<T>::to_f(z[b * ld_z + d]) : 0.0f;
+    }
+    for (int i = tid; i < SDT_B * R; i += SDT_THREADS) {
+        const int bl = i / R, r = i - bl * R;
+        dls[i] = b0 + bl < batch ? io<T>::to_f(dl[(b0 + bl) * ld_dl + r]) : 0.0f;
+    }
+    for (int i = tid; i < SDT_D * R; i += SDT_THREADS) {
+        const int dd = i / R, r = i - dd * R;
+        ws[dd * RP + r] = d0 + dd < di ? io<T>::to_f(w_dt[(d0 + dd) * R + r]) : 0.0f;
+    }
+    for (int i = tid; i < SDT_B * S; i += SDT_THREADS) {
+        const int bl = i / S, sidx = i - bl * S;
+        const bool ok = b0 + bl < batch;
+        bs[i] = ok ? io<T>::to_f(bm[(b0 + bl) * ld_bc + sidx]) : 0.0f;
+        cs[i] = ok ? io<T>::to_f(cm[(b0 + bl) * ld_bc + sidx]) : 0.0f;
+    }
+    __syncthreads();
+    {   // phase 1: one dt per thread, the dot product as four interleaved sums
+        const int bl = tid / SDT_D, dd = tid - bl * SDT_D;
+        const int64_t d = d0 + dd;
+        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+        const float *dlr = dls + bl * R, *wr = ws + dd * RP;
+        int r = 0;
+        for (; r + 4 <= R; r += 4) {
+            a0 = fmaf(dlr[r], wr[r], a0);
+            a1 = fmaf(dlr[r + 1], wr[r + 1], a1);
+            a2 = fmaf(dlr[r + 2], wr[r + 2], a2);
+            a3 = fmaf(dlr[r + 3], wr[r + 3], a3);
+        }
+        for (; r < R; ++r) a0 = fmaf(dlr[r], wr[r], a0);
+        const float acc = (a0 + a1) + (a2 + a3);
+        const float pre = io<T>::round(acc + ((b_dt && d < di) ? io<T>::to_f(b_dt[d]) : 0.0f));
+        dts[tid] = io<T>::round(softplus_fast(pre));
+    }
+    __syncthreads();
+    // phase 2: QS threads per (b, d), 4 states each
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-            if (s0 + k < S) {
-                const float a = -expf(io<T>::to_f(ar[s0 + k])) * kLog2e;
-                const float dA = ex2(dt * a);
-                hv[k] = fmaf(dA, hv[k], (dt * io<T>::to_f(Br[s0 + k])) * x);
-                yv = fmaf(hv[k], io<T>::to_f(Cr[s0 + k]), yv);
+    for (int k = 0; k < QS; ++k) {
+        const int pi = tid / QS + k * PAIRS;
+        const int bl = pi / SDT_D, dd = pi - bl * SDT_D;
+        const int64_t b = b0 + bl, d = d0 + dd;
+        const bool ok = b < batch && d < di;          // every lane joins the shuffles below
+        float yv = 0.0f;
+        if (ok) {
+            const float dt = dts[pi], x = xv[k];
+            const int s0 = 4 * q;
+            float hs[4] = {hv[k].x, hv[k].y, hv[k].z, hv[k].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float a = -expf(io<T>::to_f(A_log[d * S + s0 + e])) * kLog2e;
+                hs[e] = fmaf(ex2(dt * a), hs[e], (dt * bs[bl * S + s0 + e]) * x);
+                yv = fmaf(hs[e], cs[bl * S + s0 + e], yv);
             }
+            *reinterpret_cast<float4 *>(h + (b * di + d) * S + s0) =
+                make_float4(hs[0], hs[1], hs[2], hs[3]);
         }
 #pragma unroll
-        for (int k = 0; k < 16; ++k)
-            if (s0 + k < S) hr[s0 + k] = hv[k];
+        for (int o = QS / 2; o > 0; o >>= 1) yv += __shfl_xor_sync(0xffffffffu, yv, o);
+        if (ok && q == 0) {
+            float out = yv + (D ? io<T>::to_f(D[d]) : 0.0f) * xv[k];
+            out = io<T>::round(out) * io<T>::round(silu_f(zv[k]));
+            y[b * ld_y + d] = io<T>::from_f(out);
+        }
+    }
+}
+
+// One (b, d) per thread for d_state not of the form 4 x 2^k or without 16-byte
+// aligned h rows: the same computation with the state row walked in place.
+template <typename T>
+__global__ void __launch_bounds__(SDT_THREADS)
+step_scan_dt_any_kernel(const T *__restrict__ xc, int64_t ld_x, const T *__restrict__ dl,
+                        int64_t ld_dl, const T *__restrict__ w_dt, const T *__restrict__ b_dt,
+                        const T *__restrict__ bm, const T *__restrict__ cm, int64_t ld_bc,
+                        const T *__restrict__ z, int64_t ld_z, const T *__restrict__ A_log,
+                        const T *__restrict__ D, float *__restrict__ h, T *__restrict__ y,
+                        int64_t ld_y, int64_t batch, int64_t di, int S, int R) {
+    const int64_t b = (int64_t)blockIdx.y * SDT_B + threadIdx.x / SDT_D;
+    const int64_t d = (int64_t)blockIdx.x * SDT_D + threadIdx.x % SDT_D;
+    if (b >= batch || d >= di) return;
+    float acc = 0.0f;
+    for (int r = 0; r < R; ++r)
+        acc = fmaf(io<T>::to_f(dl[b * ld_dl + r]), io<T>::to_f(w_dt[d * R + r]), acc);
+    const float pre = io<T>::round(acc + (b_dt ? io<T>::to_f(b_dt[d]) : 0.0f));
+    const float dt = io<T>::round(softplus_fast(pre));
+    const float x = io<T>::to_f(xc[b * ld_x + d]);
+    float *hr = h + (b * di + d) * S;
+    float yv = 0.0f;
+    for (int s = 0; s < S; ++s) {
+        const float a = -expf(io<T>::to_f(A_log[d * S + s])) * kLog2e;
+        const float hv = fmaf(ex2(dt * a), hr[s], (dt * io<T>::to_f(bm[b * ld_bc + s])) * x);
+        hr[s] = hv;
+        yv = fmaf(hv, io<T>::to_f(cm[b * ld_bc + s]), yv);
     }
     float out = yv + (D ? io<T>::to_f(D[d]) : 0.0f) * x;
     out = io<T>::round(out) * io<T>::round(silu_f(io<T>::to_f(z[b * ld_z + d])));
     y[b * ld_y + d] = io<T>::from_f(out);
 }
 
-// The same step with QS = S/4 threads per channel, each owning 4 consecutive
-// states (one 16-byte load and store of h), so a warp moves 32 x 16 contiguous
-// bytes of the state; y is summed over the channel's QS lanes with shuffles.
-// For S in {4, 8, 16, 32, 64, 128}.
-template <typename T, int QS>
-__global__ void __launch_bounds__(256)
-step_scan_q_kernel(const T *__restrict__ xc, int64_t ld_x, const T *__restrict__ dtp,
-                   int64_t ld_dt, const T *__restrict__ bm, const T *__restrict__ cm,
-                   int64_t ld_bc, const T *__restrict__ z, int64_t ld_z,
-                   const T *__restrict__ A_log, const T *__restrict__ D, float *__restrict__ h,
-                   T *__restrict__ y, int64_t ld_y, int64_t batch, int64_t di) {
-    constexpr int S = 4 * QS;
-    const int64_t gi = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t i = gi / QS;                 // (b, d)
-    const int q = (int)(gi - i * QS);
-    const bool ok = i < batch * di;            // every lane joins the shuffles below
-    const int64_t ii = ok ? i : 0;
-    const int64_t b = ii / di, d = ii - b * di;
-    float yv = 0.0f, x = 0.0f;
-    if (ok) {
-        const float dt = io<T>::round(softplus_fast(io<T>::to_f(dtp[b * ld_dt + d])));
-        x = io<T>::to_f(xc[b * ld_x + d]);
-        const int s0 = 4 * q;
-        float4 *hp = reinterpret_cast<float4 *>(h + (b * di + d) * S + s0);
-        float4 h4 = *hp;
-        float hv[4] = {h4.x, h4.y, h4.z, h4.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float a = -expf(io<T>::to_f(A_log[d * S + s0 + k])) * kLog2e;
-            const float dA = ex2(dt * a);
-            hv[k] = fmaf(dA, hv[k], (dt * io<T>::to_f(bm[b * ld_bc + s0 + k])) * x);
-            yv = fmaf(hv[k], io<T>::to_f(cm[b * ld_bc + s0 + k]), yv);
-        }
-        *hp = make_float4(hv[0], hv[1], hv[2], hv[3]);
-    }
-#pragma unroll
-    for (int o = QS / 2; o > 0; o >>= 1) yv += __shfl_xor_sync(0xffffffffu, yv, o);
-    if (ok && q == 0) {
-        float out = yv + (D ? io<T>::to_f(D[d]) : 0.0f) * x;
-        out = io<T>::round(out) * io<T>::round(silu_f(io<T>::to_f(z[b * ld_z + d])));
-        y[b * ld_y + d] = io<T>::from_f(out);
-    }
-}
-
-template <typename T>
-static int launch_step(const void *xc, int64_t ld_x, const void *dt_pre, int64_t ld_dt,
-                       const void *bm, const void *cm, int64_t ld_bc, const void *z,
-                       int64_t ld_z, const void *A_log, const void *D, float *h, void *y,
-                       int64_t ld_y, int64_t batch, int64_t di, int S, cudaStream_t st) {
-    const T *X = static_cast<const T *>(xc), *DT = static_cast<const T *>(dt_pre);
-    const T *Bp = static_cast<const T *>(bm), *Cp = static_cast<const T *>(cm);
-    const T *Z = static_cast<const T *>(z), *AL = static_cast<const T *>(A_log);
-    const T *Dp = static_cast<const T *>(D);
-    T *Y = static_cast<T *>(y);
-    const int64_t n = batch * di;
-    const bool h16 = aligned(h, 16);
-#define MB2_STEP_Q(QSV)                                                                        \
-    if (h16 && S == 4 * QSV) {                                                                 \
-        step_scan_q_kernel<T, QSV><<<(unsigned)ceil_div(n * QSV, (int64_t)256), 256, 0, st>>>( \
-            X, ld_x, DT, ld_dt, Bp, Cp, ld_bc, Z, ld_z, AL, Dp, h, Y, ld_y, batch, di);       \
-        return check_launch("step_scan_q_kernel");                                             \
-    }
-    MB2_STEP_Q(1) MB2_STEP_Q(2) MB2_STEP_Q(4) MB2_STEP_Q(8) MB2_STEP_Q(16) MB2_STEP_Q(32)
-#undef MB2_STEP_Q
-    step_scan_kernel<T><<<(unsigned)ceil_div(n, (int64_t)256), 256, 0, st>>>(
-        X, ld_x, DT, ld_dt, Bp, Cp, ld_bc, Z, ld_z, AL, Dp, h, Y, ld_y, batch, di, S);
-    return check_launch("step_scan_kernel");
-}
-
-int scan_step(int dtype, const void *xc, int64_t ld_x, const void *dt_pre, int64_t ld_dt,
-              const void *bm, const void *cm, int64_t ld_bc, const void *z, int64_t ld_z,
-              const void *A_log, const void *D, float *h, void *y, int64_t ld_y, int64_t batch,
-              int64_t d_inner, int64_t d_state, cudaStream_t st) {
-    MB2_REQUIRE(d_state >= 1 && d_state <= 256, MB2_ERR_SHAPE,
-                "d_state > 256 not supported (got %lld)", (long long)d_state);
+int scan_step_dt(int dtype, const void *xc, int64_t ld_x, const void *dt_low, int64_t ld_dl,
+                 const void *w_dt, const void *b_dt, const void *bm, const void *cm,
+                 int64_t ld_bc, const void *z, int64_t ld_z, const void *A_log, const void *D,
+                 float *h, void *y, int64_t ld_y, int64_t batch, int64_t d_inner, int64_t d_state,
+                 int64_t dt_rank, cudaStream_t st) {
+    MB2_REQUIRE(d_state >= 1 && d_state <= 256 && dt_rank >= 1 && dt_rank <= 1024, MB2_ERR_SHAPE,
+                "step: d_state %lld or dt_rank %lld out of range", (long long)d_state,
+                (long long)dt_rank);
     if (batch == 0 || d_inner == 0) return MB2_OK;
-    if (dtype == MB2_F32)
-        return launch_step<float>(xc, ld_x, dt_pre, ld_dt, bm, cm, ld_bc, z, ld_z, A_log, D, h, y,
-                                  ld_y, batch, d_inner, (int)d_state, st);
-    return launch_step<__nv_bfloat16>(xc, ld_x, dt_pre, ld_dt, bm, cm, ld_bc, z, ld_z, A_log, D,
-                                      h, y, ld_y, batch, d_inner, (int)d_state, st);
+    const int S = (int)d_state, R = (int)dt_rank;
+    dim3 grid((unsigned)ceil_div(d_inner, (int64_t)SDT_D), (unsigned)ceil_div(batch, (int64_t)SDT_B));
+    const size_t smem = sizeof(float) * ((size_t)SDT_B * SDT_D + 2 * (size_t)SDT_B * S +
+                                         (size_t)SDT_B * R + (size_t)SDT_D * (R + 1));
+    auto run = [&](auto tag) -> int {
+        using T = decltype(tag);
+        const T *X = static_cast<const T *>(xc), *DL = static_cast<const T *>(dt_low);
+        const T *W = static_cast<const T *>(w_dt), *BB = static_cast<const T *>(b_dt);
+        const T *Bp = static_cast<const T *>(bm), *Cp = static_cast<const T *>(cm);
+        const T *Z = static_cast<const T *>(z), *AL = static_cast<const T *>(A_log);
+        const T *Dp = static_cast<const T *>(D);
+        T *Y = static_cast<T *>(y);
+        auto tiled = [&](auto kern) -> int {
+            if (smem > 48 * 1024) {
+                cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     (int)smem);
+                if (e != cudaSuccess)
+                    return fail(MB2_ERR_CUDA, "step: smem attribute: %s", cudaGetErrorString(e));
+            }
+            kern<<<grid, SDT_THREADS, smem, st>>>(X, ld_x, DL, ld_dl, W, BB, Bp, Cp, ld_bc, Z, ld_z,
+                                                  AL, Dp, h, Y, ld_y, batch, d_inner, R);
+            return check_launch("step_scan_dt_kernel");
+        };
+        if (aligned(h, 16)) {
+            if (S == 4) return tiled(step_scan_dt_kernel<T, 1>);
+            if (S == 8) return tiled(step_scan_dt_kernel<T, 2>);
+            if (S == 16) return tiled(step_scan_dt_kernel<T, 4>);
+            if (S == 32) return tiled(step_scan_dt_kernel<T, 8>);
+            if (S == 64) return tiled(step_scan_dt_kernel<T, 16>);
+            if (S == 128) return tiled(step_scan_dt_kernel<T, 32>);
+        }
+        step_scan_dt_any_kernel<T><<<grid, SDT_THREADS, 0, st>>>(
+            X, ld_x, DL, ld_dl, W, BB, Bp, Cp, ld_bc, Z, ld_z, AL, Dp, h, Y, ld_y, batch, d_inner, S,
+            R);
+        return check_launch("step_scan_dt_any_kernel");
+    };
+    if (dtype == MB2_F32) return run(float{});
+    return run(__nv_bfloat16{});
 }
 
 }  // namespace mb2
