@@ -387,54 +387,20 @@ STAGES = ("in_proj", "conv1d_silu", "x_proj", "dt_proj", "scan", "out_proj")
 
 
 def profile_stages(m, x, cfg, dtype, steps):
-    """Per-stage CUDA-event durations (same stream, averaged over up to 20 runs)
-    of the six launches of one forward, issued through the stage entry points."""
-    from cpu_mamba_b200 import ops
+    """Per-stage CUDA-event durations of the block forward's own launches
+    (mb2_block_forward_profile: events between its six stages on one
+    stream), averaged over up to 20 forwards after one untimed one."""
     from cpu_mamba_b200.quant import QuantizedLinear
     if any(isinstance(getattr(m, n), QuantizedLinear) for n in ("in_proj", "x_proj", "dt_proj", "out_proj")):
         return {}
-    dev = x.device
-    B, T, dm = x.shape
-    di, S, R = m.d_inner, m.d_state, m.dt_rank
-    stream = torch.cuda.current_stream(dev)
-    # the weight cache the block forward uses for fp32: the fp16 split (F16X3)
-    fp32 = dtype == torch.float32
-    split = {n: None for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
-    s16 = {n: (m._f16_split(n, getattr(m, n).weight) if fp32 else None)
-           for n in ("in_proj", "x_proj", "dt_proj", "out_proj")}
-    x2 = x.reshape(B * T, dm)
     times = {k: [] for k in STAGES}
-    # outputs allocated once: the timed region holds only the launches
-    xz = torch.empty(B * T, 2 * di, device=dev, dtype=dtype)
-    xc = torch.empty(B * T, di, device=dev, dtype=dtype)
-    xdbl = torch.empty(B * T, R + 2 * S, device=dev, dtype=dtype)
-    out = torch.empty(B * T, dm, device=dev, dtype=dtype)
     n = max(3, min(steps, 20))
-    for it in range(n + 1):
-        ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)]
-        with torch.no_grad():
-            ev[0].record(stream)
-            ops.linear(x2, m.in_proj.weight, None, split["in_proj"], out=xz,
-                       weight_f16=s16["in_proj"])
-            ev[1].record(stream)
-            ops.conv1d_silu(xz, m.conv1d.weight, m.conv1d.bias, B, T, di, out=xc)
-            ev[2].record(stream)
-            ops.linear(xc, m.x_proj.weight, None, split["x_proj"], out=xdbl,
-                       weight_f16=s16["x_proj"])
-            ev[3].record(stream)
-            ops.linear(xdbl[:, :R], m.dt_proj.weight, m.dt_proj.bias, split["dt_proj"],
-                       out=xz[:, :di], weight_f16=s16["dt_proj"])
-            ev[4].record(stream)
-            y = ops.scan_gated(xc, xz[:, :di], xdbl[:, R:R + S], xdbl[:, R + S:], xz[:, di:],
-                               m.A_log, m.D, B, T, out=xc)
-            ev[5].record(stream)
-            ops.linear(y, m.out_proj.weight, None, split["out_proj"], out=out,
-                       weight_f16=s16["out_proj"])
-            ev[6].record(stream)
-        torch.cuda.synchronize(dev)
-        if it > 0:
-            for i, k in enumerate(times):
-                times[k].append(ev[i].elapsed_time(ev[i + 1]))
+    with torch.no_grad():
+        for it in range(n + 1):
+            st = m.profile_stages(x)
+            if it > 0:
+                for k in STAGES:
+                    times[k].append(st[k])
     return {k: statistics.mean(v) for k, v in times.items()}
 
 

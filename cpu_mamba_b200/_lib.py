@@ -96,6 +96,8 @@ _SIGS = {
     "mb2_block_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Block), _c_i64, _c_i64]),
     "mb2_block_forward": (ctypes.c_int, [ctypes.POINTER(Block), _vp, _vp, _c_i64, _c_i64,
                                          _vp, _vp, _vp, ctypes.c_size_t, _vp]),
+    "mb2_block_forward_profile": (ctypes.c_int, [ctypes.POINTER(Block), _vp, _vp, _c_i64, _c_i64,
+                                                 _vp, ctypes.c_size_t, _vp, _vp]),
     "mb2_step_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(Block), _c_i64]),
     "mb2_block_step": (ctypes.c_int, [ctypes.POINTER(Block), _vp, _vp, _vp, _vp, _c_i64,
                                       _vp, ctypes.c_size_t, _vp]),

@@ -3,16 +3,17 @@
 // step (:103-163), plus the linear-layer entry points.
 //
 // Forward pipeline (6 launches, caller-provided workspace, no allocation):
-//   1. in_proj            x (N, dm)          -> xz (N, 2di)
+//   1. in_proj            x (N, dm)          -> xz (N, 2di): x | SiLU(z), the
+//                                               gate's SiLU applied in the epilogue
 //   2. conv1d + SiLU      xz[:, :di]         -> xc (N, di)   [+ conv tail]
 //   3. x_proj             xc                 -> xdbl (N, ldx): dt_low | B | C, each
 //                                               segment on an 8-element boundary
 //   4. dt_proj            xdbl[:, :R]        -> over xz[:, :di] (the conv's
 //                                               input, dead by now)
-//   5. gated scan         xc, dt_proj out, xdbl, xz[:, di:] -> y (N, di)
-//      [+ h_last] (softplus + exp(dt A) + recurrence + D skip + cast + SiLU(z)
-//       gate; y overwrites xc in place).  Where the dt GEMM cannot run on the tensor cores, steps 4
-//       and 5 are one fused scan that also computes dt.
+//   5. gated scan         xc, dt_proj out, xdbl, SiLU(z) -> y (N, di)
+//      [+ h_last] (softplus + exp(dt A) + recurrence + D skip + cast + gate;
+//       y overwrites xc in place).  Where the dt GEMM cannot run on the tensor
+//       cores, steps 4 and 5 are one fused scan that also computes dt.
 //   6. out_proj           y                  -> out (N, dm)
 #include "internal.cuh"
 
@@ -190,6 +191,8 @@ __global__ void conv_step_reduce_kernel(const float *__restrict__ P, int ks,
                                         const float *__restrict__ bias,
                                         float *__restrict__ conv_state, float *__restrict__ xc,
                                         int64_t batch, int64_t d_inner) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= batch * d_inner) return;
     const int64_t b = i / d_inner, d = i - b * d_inner;
@@ -311,20 +314,31 @@ static unsigned *fused_amax(const Layout &l, char *ws, int dtype, int which, cud
     return slots;
 }
 
+// Stage boundaries for mb2_block_forward_profile: ev[0] before in_proj,
+// ev[i] after stage i (in_proj, conv, x_proj, dt_proj, scan, out_proj), or
+// null (no events).
+static void mark(cudaEvent_t *ev, int i, cudaStream_t st) {
+    if (ev) cudaEventRecord(ev[i], st);
+}
+
 static int pipeline_head(const mb2_block &b, const Layout &l, const void *x, int64_t batch,
                          int64_t seqlen, void *conv_tail, char *ws, cudaStream_t st,
-                         const float *row_scale) {
+                         const float *row_scale, cudaEvent_t *ev = nullptr) {
     void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
     const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
     EpiExtra in_ex = scratch_extra(l, ws), mid_ex = scratch_extra(l, ws);
     in_ex.row_scale = row_scale;
+    in_ex.silu_from = di;       // the z half leaves in_proj as SiLU(z), the gate (:264)
+    mark(ev, 0, st);
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, N, 2 * di, l.dm, MB2_EPI_NONE,
                            st, -1, 0, -1, 0, in_ex));
+    mark(ev, 1, st);
     unsigned *xc_max = fused_amax(l, ws, b.dtype, 0, st);
     MB2_TRY(check_launch("block: maxima clear"));
     MB2_TRY(conv1d_silu(b.dtype, xz, 2 * di, b.conv_w, b.conv_b, xc, di, conv_tail, batch, seqlen,
                         di, b.d_conv, st, xc_max));
+    mark(ev, 2, st);
     if (xc_max) {
         mid_ex.amax_parts = reinterpret_cast<float *>(xc_max);
         mid_ex.amax_n = AMAX_SLOTS;
@@ -332,12 +346,13 @@ static int pipeline_head(const mb2_block &b, const Layout &l, const void *x, int
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.x_proj, xc, di, xdbl, l.ldx, N, R + 2 * S, di, MB2_EPI_NONE,
                            st, R, l.RB - R, R + S, l.RC - l.RB - S, mid_ex));
+    mark(ev, 3, st);
     return MB2_OK;
 }
 
 static int pipeline_tail(const mb2_block &b, const Layout &l, void *out, int64_t batch,
                          int64_t seqlen, float *h_last, char *ws, cudaStream_t st,
-                         const void *resid) {
+                         const void *resid, cudaEvent_t *ev = nullptr) {
     void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
     const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
     const size_t es = l.es;
@@ -346,11 +361,14 @@ static int pipeline_tail(const mb2_block &b, const Layout &l, void *out, int64_t
     out_ex.ld_r = l.dm;
     // dt_proj (_mamba.py:219) on the tensor cores, bias in the epilogue,
     // written over the x half of xz (dead once the conv has run); the gated
-    // scan applies the softplus (:220) as it stages the rows.  A quantised
-    // dt_proj passes its dequantised weight in .weight (as the fused scan
-    // needs it anyway).  Where that GEMM does not apply (an unsplit fp32
-    // weight, fewer than 256 rows) the fused scan computes dt itself from
-    // W_dt's rows in registers.
+    // scan applies the softplus (:220) once per token and channel (in T
+    // segments, the first pass writes it back over these rows for the
+    // second).  (Softplus in the GEMM epilogue measured slower: dt_proj's
+    // K = R GEMM is bound by its epilogue already.)  A quantised dt_proj
+    // passes its dequantised weight in .weight (as the fused scan needs it).
+    // Where that GEMM does not apply (an unsplit fp32 weight, fewer than 256
+    // rows) the fused scan computes dt itself from W_dt's rows in registers.
+    // Either scan reads z as SiLU(z), which in_proj's epilogue formed.
     bool dt_done = false;
     if (N >= 256 && b.dtype == MB2_F32 && b.dt_proj.weight_f16) {
         EpiExtra dt_ex;                  // x's maxima by a pass over dt_low (N x R)
@@ -363,18 +381,21 @@ static int pipeline_tail(const mb2_block &b, const Layout &l, void *out, int64_t
         MB2_TRY(gemm_tc(b.dtype, xdbl, l.ldx, b.dt_proj.weight, b.dt_proj.weight_split,
                         b.dt_proj.bias, xz, 2 * di, N, di, R, di, 0, di, 0, MB2_EPI_NONE, st,
                         &dt_done));
+    mark(ev, 4, st);
     unsigned *y_max = fused_amax(l, ws, b.dtype, 1, st);
     MB2_TRY(check_launch("block: maxima clear"));
     if (dt_done)
         MB2_TRY(scan_gated(b.dtype, xc, di, xz, 2 * di, (char *)xdbl + l.RB * es, l.ldx,
                            (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log,
                            b.D, nullptr, h_last, xc, di, batch, seqlen, di, S, st,
-                           reinterpret_cast<float *>(ws + l.off_seg), l.seg_bytes, y_max));
+                           reinterpret_cast<float *>(ws + l.off_seg), l.seg_bytes, y_max,
+                           SCAN_Z_ACT | SCAN_DT_SCRATCH));
     else
         MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
                            (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
                            dt_weight(b), b.dt_proj.bias, b.A_log, b.D, nullptr, h_last, xc, di,
-                           batch, seqlen, di, S, R, st, y_max));
+                           batch, seqlen, di, S, R, st, y_max, SCAN_Z_ACT));
+    mark(ev, 5, st);
     if (y_max) {
         out_ex.amax_parts = reinterpret_cast<float *>(y_max);
         out_ex.amax_n = AMAX_SLOTS;
@@ -382,6 +403,7 @@ static int pipeline_tail(const mb2_block &b, const Layout &l, void *out, int64_t
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.out_proj, xc, di, out, l.dm, N, l.dm, di, MB2_EPI_NONE, st,
                            -1, 0, -1, 0, out_ex));
+    mark(ev, 6, st);
     return MB2_OK;
 }
 
@@ -414,6 +436,35 @@ extern "C" int mb2_block_forward(const mb2_block *blk, const void *x, void *out,
                           static_cast<char *>(workspace), st, nullptr, nullptr);
 }
 
+extern "C" int mb2_block_forward_profile(const mb2_block *blk, const void *x, void *out,
+                                         int64_t batch, int64_t seqlen, void *workspace,
+                                         size_t workspace_bytes, float *stage_ms,
+                                         mb2_stream_t stream) {
+    MB2_TRY(check_block(blk));
+    MB2_REQUIRE(batch > 0 && seqlen > 0, MB2_ERR_SHAPE, "block profile: empty batch");
+    MB2_REQUIRE(x && out && workspace && stage_ms, MB2_ERR_ARG, "block profile: null pointer");
+    cudaStream_t st = (cudaStream_t)stream;
+    const Layout l = make_layout(blk, batch * seqlen, false, batch, seqlen);
+    MB2_REQUIRE(workspace_bytes >= l.total, MB2_ERR_WORKSPACE,
+                "block profile: workspace %zu < required %zu", workspace_bytes, l.total);
+    cudaEvent_t ev[7] = {};
+    int rc = MB2_OK;
+    for (int i = 0; i < 7 && rc == MB2_OK; ++i)
+        if (cudaEventCreate(&ev[i]) != cudaSuccess)
+            rc = fail(MB2_ERR_CUDA, "block profile: cudaEventCreate failed");
+    char *ws = static_cast<char *>(workspace);
+    if (rc == MB2_OK) rc = pipeline_head(*blk, l, x, batch, seqlen, nullptr, ws, st, nullptr, ev);
+    if (rc == MB2_OK) rc = pipeline_tail(*blk, l, out, batch, seqlen, nullptr, ws, st, nullptr, ev);
+    if (rc == MB2_OK && cudaEventSynchronize(ev[6]) != cudaSuccess)
+        rc = fail(MB2_ERR_CUDA, "block profile: %s", cudaGetErrorString(cudaGetLastError()));
+    for (int i = 0; i < 6 && rc == MB2_OK; ++i)
+        if (cudaEventElapsedTime(&stage_ms[i], ev[i], ev[i + 1]) != cudaSuccess)
+            rc = fail(MB2_ERR_CUDA, "block profile: cudaEventElapsedTime failed");
+    for (int i = 0; i < 7; ++i)
+        if (ev[i]) cudaEventDestroy(ev[i]);
+    return rc;
+}
+
 extern "C" size_t mb2_step_workspace_bytes(const mb2_block *blk, int64_t batch) {
     if (!blk || batch < 0) return 0;
     return make_layout(blk, batch, true).total;
@@ -421,6 +472,10 @@ extern "C" size_t mb2_step_workspace_bytes(const mb2_block *blk, int64_t batch) 
 
 // A decode step as a head (in_proj -> ring conv -> x_proj) and a tail
 // (dt_proj -> one scan step -> gate -> out_proj), split like the forward.
+// The fp32 step's kernels are launched as a programmatic chain (common.cuh):
+// each starts while the one before it finishes, the x_proj and out_proj
+// GEMMs loading their first weight tiles and the state update staging W_dt
+// and prefetching h before their inputs are ready.
 static int step_head(const mb2_block &b, const Layout &l, const void *x, void *conv_state,
                      int64_t batch, char *ws, cudaStream_t st, const float *row_scale = nullptr) {
     void *xz = ws + l.off_xz, *xc = ws + l.off_xc, *xdbl = ws + l.off_xdbl;
@@ -428,28 +483,35 @@ static int step_head(const mb2_block &b, const Layout &l, const void *x, void *c
     EpiExtra sk;                    // split-K scratch for the few-row projections
     sk.scratch = reinterpret_cast<float *>(ws + l.off_part);
     sk.scratch_bytes = l.part_bytes;
+    sk.pdl = PDL_WEIGHTS_EARLY;     // x_proj follows the conv step, which writes no weights
     EpiExtra in_ex = sk;
     in_ex.row_scale = row_scale;
+    in_ex.pdl = PDL_CHAIN;          // the kernel before in_proj is not known
     int splits = 0;                 // fp32 split-K in_proj: its partials, reduced by the conv
     if (b.dtype == MB2_F32) in_ex.defer_splits = &splits;
     MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, batch, 2 * di, l.dm, MB2_EPI_NONE,
                        st, -1, 0, -1, 0, in_ex));
     if (splits > 0) {
         const unsigned grid = (unsigned)ceil_div(batch * di, (int64_t)256);
+        cudaError_t le = cudaSuccess;
         switch (b.d_conv) {
 #define MB2_CSR(KK)                                                                            \
     case KK:                                                                                   \
-        conv_step_reduce_kernel<KK><<<grid, 256, 0, st>>>(                                     \
-            sk.scratch, splits, row_scale, static_cast<const float *>(b.in_proj.bias),        \
-            static_cast<float *>(xz), 2 * di, static_cast<const float *>(b.conv_w),           \
-            static_cast<const float *>(b.conv_b), static_cast<float *>(conv_state),           \
-            static_cast<float *>(xc), batch, di);                                             \
+        le = launch_kernel(true, conv_step_reduce_kernel<KK>, dim3(grid), dim3(256), 0, st,   \
+                           sk.scratch, splits, row_scale,                                     \
+                           static_cast<const float *>(b.in_proj.bias), static_cast<float *>(xz), \
+                           2 * di, static_cast<const float *>(b.conv_w),                      \
+                           static_cast<const float *>(b.conv_b),                              \
+                           static_cast<float *>(conv_state), static_cast<float *>(xc), batch, \
+                           di);                                                               \
         break;
             MB2_CSR(2) MB2_CSR(3) MB2_CSR(4) MB2_CSR(5) MB2_CSR(6) MB2_CSR(7) MB2_CSR(8)
 #undef MB2_CSR
             default: return fail(MB2_ERR_UNSUPPORTED, "step: d_conv %lld not in [2, 8]",
                                  (long long)b.d_conv);
         }
+        if (le != cudaSuccess)
+            return fail(MB2_ERR_CUDA, "conv_step_reduce_kernel launch: %s", cudaGetErrorString(le));
         MB2_TRY(check_launch("conv_step_reduce_kernel"));
     } else if (b.dtype == MB2_F32)
         MB2_TRY(launch_conv_step<float>((int)b.d_conv, xz, 2 * di, b.conv_w, b.conv_b, conv_state,
@@ -469,13 +531,14 @@ static int step_tail(const mb2_block &b, const Layout &l, void *out, float *h, i
     EpiExtra sk;
     sk.scratch = reinterpret_cast<float *>(ws + l.off_part);
     sk.scratch_bytes = l.part_bytes;
+    sk.pdl = PDL_WEIGHTS_EARLY;     // out_proj follows the state update, which writes no weights
     // one timestep: dt_proj (W_dt's dense rows; a quantised dt_proj supplies
     // its dequantised weight) + softplus, exp(dt A), h updated in place,
     // y = C.h + D x, gate -- one kernel
     MB2_TRY(scan_step_dt(b.dtype, xc, di, xdbl, l.ldx, b.dt_proj.weight, b.dt_proj.bias,
                          (char *)xdbl + l.RB * es, (char *)xdbl + l.RC * es, l.ldx,
                          (char *)xz + di * es, 2 * di, b.A_log, b.D, h, xc, di, batch, di, S, R,
-                         st));
+                         st, true));
     EpiExtra out_ex = sk;
     out_ex.resid = resid;
     out_ex.ld_r = l.dm;

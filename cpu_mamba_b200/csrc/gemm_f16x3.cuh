@@ -451,6 +451,16 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = softplus_f(v[j]);
                 }
+                if (EXTRA && p.silu_from >= 0 && c0 + 31 >= p.silu_from) {
+                    // in_proj's z half: SiLU(z)
+                    if (c0 >= p.silu_from) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = silu_f(v[j]);
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (c0 + j >= p.silu_from) v[j] = silu_f(v[j]);
+                    }
+                }
                 if (EXTRA && p.resid && row_ok) {
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {

@@ -40,6 +40,7 @@ struct GemmArgs {
     float *partial;                // split-K: (splits, M, N) fp32 partial sums, or null
     int64_t kchunk;                // K range per split (multiple of SG_BK)
     int vec;                       // dense rows of x and W start 4-element aligned: vector loads
+    int64_t silu_from;             // columns >= silu_from get SiLU (EpiExtra), < 0: none
 };
 
 // 4 consecutive elements of a row as floats, one 16-byte (fp32) or 8-byte
@@ -224,6 +225,15 @@ gemm_simt_kernel(const GemmArgs a) {
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) acc[i][jj] = softplus_f(io<T>::round(acc[i][jj]));
     }
+    if (a.silu_from >= 0 && n0 + tx * 4 + 3 >= a.silu_from) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+            const bool act = n0 + tx * 4 + jj >= a.silu_from;
+#pragma unroll
+            for (int i = 0; i < TM; ++i)
+                acc[i][jj] = act ? silu_f(io<T>::round(acc[i][jj])) : acc[i][jj];
+        }
+    }
     if (a.resid) {
         const T *R = static_cast<const T *>(a.resid);
 #pragma unroll
@@ -271,6 +281,7 @@ __global__ void splitk_reduce_kernel(const GemmArgs a, int splits) {
     if (a.row_scale) v *= a.row_scale[m];
     if (a.bias) v += io<T>::to_f(static_cast<const T *>(a.bias)[n]);
     if (a.epi == MB2_EPI_SOFTPLUS) v = softplus_f(io<T>::round(v));
+    if (a.silu_from >= 0 && n >= a.silu_from) v = silu_f(io<T>::round(v));
     if (a.resid) v += io<T>::to_f(static_cast<const T *>(a.resid)[m * a.ld_r + n]);
     const int64_t col = n + (n >= a.n1 ? a.off1 : 0) + (n >= a.n2 ? a.off2 : 0);
     static_cast<T *>(a.y)[m * a.ld_y + col] = io<T>::from_f(v);
@@ -338,7 +349,7 @@ int gemm_simt(int dtype, int scheme, const void *x, int64_t ld_x, const void *w,
                     (scheme != MB2_Q_NONE || aligned(w, 4 * es));
     GemmArgs a{x, ld_x, w, scale, group, group ? ceil_div(K, group) : 1, bias, y, ld_y, M, N, K,
                n1, n2, off1, off2, epi, {},
-               ex.row_scale, ex.resid, ex.ld_r, nullptr, K, vec};
+               ex.row_scale, ex.resid, ex.ld_r, nullptr, K, vec, ex.silu_from};
     nf4_lut(a.lut);
     const bool f32 = dtype == MB2_F32;
     switch (scheme) {

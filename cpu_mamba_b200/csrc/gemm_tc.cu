@@ -116,6 +116,11 @@ struct Params {
     // split-K (few rows): tiles = (m, n, split), each split a range of kbs
     // k-blocks, raw fp32 partial sums stored through a 3D map (N, M, split)
     int ksplit, kbs;
+    int64_t silu_from = -1;       // EpiExtra's SiLU columns (< 0: none)
+    // launched as part of a programmatic chain whose previous kernel writes
+    // nothing the weights' loads read: the first stages' weight tiles are
+    // loaded before waiting for that kernel (common.cuh, pdl_wait)
+    int w_early = 0;
 };
 
 // ------------------------------------------------------------- primitives
@@ -368,6 +373,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot_ptr;
 
+    // weight tiles of the first stages while the previous kernel of a
+    // programmatic chain finishes (the stages are free at the start)
+    int pre = 0;
+    if (p.w_early && warp == 0 && lane == 0 && (int)blockIdx.x < num_tiles) {
+        int64_t m0, n0;
+        int z, kb0, kb1;
+        coords((int)blockIdx.x, m0, n0, z, kb0, kb1);
+        for (int kb = kb0; kb < kb1 && pre < C::STAGES; ++kb, ++pre) {
+            mbar_expect_tx(full(pre), C::TX);
+            tma_load_2d(tile(pre, 1), &map_b0, full(pre), kb * C::BK, (int32_t)n0);
+            if (MODE == F32X3) tma_load_2d(tile(pre, 2), &map_b1, full(pre), kb * C::BK, (int32_t)n0);
+        }
+    }
+    pdl_wait();        // inputs (and outputs' previous readers) of a chained launch
+    pdl_trigger();
+
     if (warp == 0) {
         // ---------------------------------------------------- TMA producer
         if (lane == 0) {
@@ -380,12 +401,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 for (int kb = kb0; kb < kb1; ++kb, ++g) {
                     const int s = g % C::STAGES;
                     const uint32_t ph = (g / C::STAGES) & 1;
-                    if (!mbar_wait(empty(s), ph ^ 1, 1)) { ok = false; break; }
-                    mbar_expect_tx(full(s), C::TX);
                     const int32_t kc = kb * C::BK;
+                    if ((int)g >= pre) {     // else: stage s was armed and its W loaded above
+                        if (!mbar_wait(empty(s), ph ^ 1, 1)) { ok = false; break; }
+                        mbar_expect_tx(full(s), C::TX);
+                        tma_load_2d(tile(s, 1), &map_b0, full(s), kc, (int32_t)n0);
+                        if (MODE == F32X3) tma_load_2d(tile(s, 2), &map_b1, full(s), kc, (int32_t)n0);
+                    }
                     tma_load_2d(tile(s, 0), &map_a, full(s), kc, (int32_t)m0);
-                    tma_load_2d(tile(s, 1), &map_b0, full(s), kc, (int32_t)n0);
-                    if (MODE == F32X3) tma_load_2d(tile(s, 2), &map_b1, full(s), kc, (int32_t)n0);
                 }
             }
         }
@@ -605,6 +628,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = softplus_f(io<TO>::round(v[j]));
                 }
+                if (EXTRA && p.silu_from >= 0 && n0 + cb * 32 + 31 >= p.silu_from) {
+                    // in_proj's z half: SiLU(z) on the value stored in TO
+                    const int64_t nb = n0 + cb * 32;
+                    if (nb >= p.silu_from) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) v[j] = silu_f(io<TO>::round(v[j]));
+                    } else {
+                        for (int j = 0; j < 32; ++j)
+                            if (nb + j >= p.silu_from) v[j] = silu_f(io<TO>::round(v[j]));
+                    }
+                }
                 if (EXTRA && p.resid && row_ok) {
                     // residual add: this row's 32 columns, 16 bytes at a time
                     // (the host guarantees 16-byte rows and N % VEC == 0)
@@ -693,7 +727,7 @@ static int make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t col
 
 template <int MODE, typename TO, bool EXTRA>
 static int launch_tc(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
-                     const CUtensorMap &ym, const tc::Params &p, cudaStream_t st) {
+                     const CUtensorMap &ym, const tc::Params &p, cudaStream_t st, bool pdl = false) {
     auto kern = tc::gemm_tc_kernel<MODE, TO, EXTRA>;
     constexpr size_t smem = tc::smem_bytes<MODE, TO>();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -707,7 +741,9 @@ static int launch_tc(const CUtensorMap &a, const CUtensorMap &b0, const CUtensor
     const int64_t tiles = ceil_div(p.M, (int64_t)tc::BM) * ceil_div(p.N, (int64_t)tc::Cfg<MODE>::BN) *
                           (p.ksplit > 1 ? p.ksplit : 1);
     const unsigned grid = (unsigned)(tiles < g_num_sms ? tiles : g_num_sms);
-    kern<<<grid, tc::Cfg<MODE>::WARPS * 32, smem, st>>>(a, b0, b1, ym, p);
+    const cudaError_t le = launch_kernel(pdl, kern, dim3(grid), dim3(tc::Cfg<MODE>::WARPS * 32),
+                                         smem, st, a, b0, b1, ym, p);
+    if (le != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_tc_kernel launch: %s", cudaGetErrorString(le));
     return check_launch("gemm_tc_kernel");
 }
 
@@ -733,7 +769,10 @@ __global__ void tc_splitk_reduce_kernel(const float *__restrict__ P, int ks, int
                                         const float *__restrict__ row_scale, int epi,
                                         const float *__restrict__ resid, int64_t ld_r,
                                         float *__restrict__ y, int64_t ld_y, int64_t n1,
-                                        int64_t off1, int64_t n2, int64_t off2) {
+                                        int64_t off1, int64_t n2, int64_t off2,
+                                        int64_t silu_from) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= M * N) return;
     const int64_t m = i / N, n = i - m * N;
@@ -753,6 +792,7 @@ __global__ void tc_splitk_reduce_kernel(const float *__restrict__ P, int ks, int
     if (row_scale) v *= row_scale[m];
     if (bias) v += bias[n];
     if (epi == MB2_EPI_SOFTPLUS) v = softplus_f(v);
+    if (silu_from >= 0 && n >= silu_from) v = silu_f(v);
     if (resid) v += resid[m * ld_r + n];
     y[m * ld_y + n + (n >= n1 ? off1 : 0) + (n >= n2 ? off2 : 0)] = v;
 }
@@ -791,16 +831,20 @@ static int gemm_tc_splitk(const void *x, int64_t ld_x, const float *w_split, con
     MB2_TRY(make_map_partials(&my, ex.scratch, M, N, ks));
     tc::Params p{ex.scratch, N, nullptr, M, N, K, N, N, 0, 0, MB2_EPI_NONE, 1, nullptr, nullptr, 0,
                  (int)ks, (int)kbs};
-    MB2_TRY((launch_tc<tc::F32X3, float, false>(ma, mb0, mb1, my, p, st)));
+    p.w_early = ex.pdl == PDL_WEIGHTS_EARLY ? 1 : 0;
+    MB2_TRY((launch_tc<tc::F32X3, float, false>(ma, mb0, mb1, my, p, st, ex.pdl != PDL_NONE)));
     *used = true;
     if (ex.defer_splits) {            // the consumer sums the partials itself
         *ex.defer_splits = (int)ks;
         return MB2_OK;
     }
-    tc_splitk_reduce_kernel<<<(unsigned)ceil_div(M * N, (int64_t)256), 256, 0, st>>>(
-        ex.scratch, (int)ks, M, N, static_cast<const float *>(bias), ex.row_scale, epi,
-        static_cast<const float *>(ex.resid), ex.ld_r, static_cast<float *>(y), ld_y, n1, off1, n2,
-        off2);
+    const cudaError_t le = launch_kernel(
+        ex.pdl != PDL_NONE, tc_splitk_reduce_kernel, dim3((unsigned)ceil_div(M * N, (int64_t)256)),
+        dim3(256), 0, st, ex.scratch, (int)ks, M, N, static_cast<const float *>(bias),
+        ex.row_scale, epi, static_cast<const float *>(ex.resid), ex.ld_r, static_cast<float *>(y),
+        ld_y, n1, off1, n2, off2, ex.silu_from);
+    if (le != cudaSuccess)
+        return fail(MB2_ERR_CUDA, "tc_splitk_reduce_kernel launch: %s", cudaGetErrorString(le));
     MB2_TRY(check_launch("tc_splitk_reduce_kernel"));
     *used = true;
     return MB2_OK;
@@ -842,9 +886,9 @@ int gemm_tc(int dtype, const void *x, int64_t ld_x, const void *w, const float *
     if (tma_store) MB2_TRY(make_map(&my, y, M, N, ld_y, bf16, 32));
     else my = mb0;  // unused
     tc::Params p{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0,
-                 ex.row_scale, ex.resid, ex.ld_r, 1, 0};
+                 ex.row_scale, ex.resid, ex.ld_r, 1, 0, ex.silu_from};
     *used = true;
-    const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS;
+    const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS || ex.silu_from >= 0;
     if (bf16)
         return extra ? launch_tc<tc::BF16, __nv_bfloat16, true>(ma, mb0, mb1, my, p, st)
                      : launch_tc<tc::BF16, __nv_bfloat16, false>(ma, mb0, mb1, my, p, st);
@@ -1029,11 +1073,11 @@ int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, 
     else my = ma;  // unused
     tc::F16Params fp{};
     fp.g = tc::Params{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0,
-                      ex.row_scale, ex.resid, ex.ld_r, 1, 0};
+                      ex.row_scale, ex.resid, ex.ld_r, 1, 0, ex.silu_from};
     fp.x_parts = parts;
     fp.n_parts = nparts;
     fp.w_inv = reinterpret_cast<const float *>(w16);
-    const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS;
+    const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS || ex.silu_from >= 0;
     int rc;
     if (two)
         rc = extra ? launch_f16<true, true>(ma, mwh, mwl, my, fp, M, N, st)

@@ -12,11 +12,15 @@ namespace mb2 {
 //                                     row_scale = 1 / rms(x_m), the norm weight
 //                                     folded into W's columns)
 //   v += bias[n];  softplus if asked
+//   v = silu(v) for columns n >= silu_from, on v rounded to the output dtype
+//                                    (in_proj's z half: the gate SiLU(z) of
+//                                     _mamba.py:264 applied where z is produced)
 //   v += resid[m * ld_r + n]          (residual add; resid may alias y)
 struct EpiExtra {
     const float *row_scale = nullptr;
     const void *resid = nullptr;
     int64_t ld_r = 0;
+    int64_t silu_from = -1;            // < 0: no SiLU columns
     // not an epilogue term: device scratch for the projection -- the
     // dequantised operand of a quantised weight on the tensor-core path, or
     // the CUDA-core GEMM's split-K partial sums (few-row GEMMs) -- or null
@@ -35,7 +39,14 @@ struct EpiExtra {
     // split count, for the consumer kernel to reduce; 0 when the output was
     // written as usual
     int *defer_splits = nullptr;
+    // not an epilogue term: launch the few-row tensor-core GEMM and its
+    // reduction as links of a programmatic chain (common.cuh): PDL_CHAIN
+    // waits for the previous kernel before any load; PDL_WEIGHTS_EARLY also
+    // loads its first weight tiles before that wait (the previous kernel
+    // writes no weights)
+    int pdl = 0;
 };
+enum { PDL_NONE = 0, PDL_CHAIN = 1, PDL_WEIGHTS_EARLY = 2 };
 
 // Slots of the fused maxima: a kernel writing a GEMM's input takes
 // atomicMax(slot[block % AMAX_SLOTS], |value| bits) over the slots, zeroed
@@ -81,19 +92,24 @@ int dequantize_f32(int scheme, const void *wq, const float *scale, int64_t rows,
 int conv1d_silu(int dtype, const void *x_in, int64_t ld_in, const void *w, const void *bias,
                 void *xc, int64_t ld_out, void *tail, int64_t batch, int64_t seqlen,
                 int64_t d_inner, int64_t d_conv, cudaStream_t st, unsigned *amax = nullptr);
+// `act` (SCAN_* bits): which inputs their producer already activated -- dt =
+// softplus(dt_proj output), SiLU(z) in in_proj's epilogue; the scan applies
+// the others itself.  SCAN_DT_SCRATCH: the dt rows are the caller's scratch,
+// which a T-segmented scan may overwrite with softplus(dt) in its first pass.
+enum { SCAN_DT_ACT = 1, SCAN_Z_ACT = 2, SCAN_DT_SCRATCH = 4 };
 int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t ld_dl,
                const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
                int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
                const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
                int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, int64_t dt_rank,
-               cudaStream_t stream, unsigned *amax = nullptr);
+               cudaStream_t stream, unsigned *amax = nullptr, int act = 0);
 
 int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t ld_dt,
                const void *bm, int64_t ld_b, const void *cm, int64_t ld_c, const void *z,
                int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
                void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
                int64_t d_state, cudaStream_t stream, float *seg_ws = nullptr,
-               size_t seg_bytes = 0, unsigned *amax = nullptr);
+               size_t seg_bytes = 0, unsigned *amax = nullptr, int act = 0);
 // Long sequences over few (batch, channel) chains: the number of T segments
 // scan_gated runs in parallel (1 = none) and the scratch it needs for them.
 int scan_segments(int64_t batch, int64_t d_inner, int64_t seqlen, int64_t d_state);
@@ -105,7 +121,7 @@ int scan_step_dt(int dtype, const void *xc, int64_t ld_x, const void *dt_low, in
                  const void *w_dt, const void *b_dt, const void *bm, const void *cm,
                  int64_t ld_bc, const void *z, int64_t ld_z, const void *A_log, const void *D,
                  float *h, void *y, int64_t ld_y, int64_t batch, int64_t d_inner, int64_t d_state,
-                 int64_t dt_rank, cudaStream_t st);
+                 int64_t dt_rank, cudaStream_t st, bool pdl = false);
 
 // Quantised weights as the tensor-core GEMM's operand (bit-exact dequantised
 // values; fp32: TF32 hi / lo planes, bf16: rounded) and its size in bytes --

@@ -66,46 +66,18 @@ struct ScanParams {
     float *seg_sdt;                  // (batch, nseg, d_inner)
     const float *seg_hstart;         // pass 3: (batch, nseg, d_inner, S) starting states
     unsigned *amax;                  // or null: fused maxima of |y| (AMAX_SLOTS slots)
+    // the block forward's producers apply the activations where they write:
+    int dt_act;                      // GATED, SUMMARY: dt rows are softplus(dt_proj) already
+    int z_act;                       // FUSED, GATED: z rows are SiLU(z) already
+    // T segments with dt rows that are scratch: the summary pass overwrites
+    // them with softplus(dt), so the output pass does not evaluate it again
+    // (the last segment, which has no summary pass, still does)
+    int dt_wb;
 };
 
 enum { ARR_X = 1, ARR_D2 = 2, ARR_B = 4, ARR_C = 8, ARR_DL = 16, ARR_Z = 32 };
 
 template <typename T> __host__ __device__ constexpr int epw() { return 4 / (int)sizeof(T); }
-
-__device__ __forceinline__ float ex2(float v) {
-    float r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
-    return r;
-}
-
-// softplus(v) = max(v, 0) + log1p(e), e = exp(-|v|)  (torch's softplus with
-// beta 1; for v > 20 the sum rounds to v, torch's threshold branch).
-//   e: Cody-Waite range reduction (n = rint(-|v| log2 e), r = -|v| - n ln2 with
-//      ln2 split into a 16-significant-bit head and a tail), e = 2^n 2^(r log2 e)
-//      with 2^n built exactly in the exponent field;
-//   log1p(e) = 2 atanh(u), u = e / (2 + e) in [0, 1/3], and atanh(u) / u is a
-//      degree-4 polynomial in u^2 fitted (relative-error least squares,
-//      float64) for this library: max relative error 4e-9 on [0, 1/9].
-// fp32 result within ~4 ulp of log1p(exp(v)) (float64) for all v; about a
-// third of the instructions of log1pf(expf(v)).
-__device__ __forceinline__ float softplus_fast(float v) {
-    constexpr float kLn2Hi = 0.693145751953125f;      // 16 significant bits of ln 2
-    constexpr float kLn2Lo = 1.428606765330187e-06f;  // ln 2 - kLn2Hi
-    constexpr float c0 = 1.0f, c1 = 0.3333315849304199f, c2 = 0.20012454688549042f,
-                    c3 = 0.13980302214622498f, c4 = 0.1408916562795639f;
-    const float a = fminf(fabsf(v), 87.0f);
-    const float n = rintf(-a * kLog2e);
-    float r = fmaf(n, -kLn2Hi, -a);
-    r = fmaf(n, -kLn2Lo, r);
-    const float e = ex2(r * kLog2e) * __int_as_float(((int)n + 127) << 23);
-    const float u = __fdividef(e, 2.0f + e);
-    const float w = u * u;
-    float P = fmaf(w, c4, c3);
-    P = fmaf(w, P, c2);
-    P = fmaf(w, P, c1);
-    P = fmaf(w, P, c0);
-    return fmaxf(v, 0.0f) + (2.0f * u) * P;
-}
 
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: two IEEE fp32 round-to-nearest
 // lanes per instruction, halving the FMA-pipe instruction count of the state
@@ -361,6 +333,12 @@ scan_kernel(const ScanParams p) {
     T *yg = static_cast<T *>(p.y) + row_base * p.ld_y + d0 + cc;
 
     const int nchunks = (T_ + SCAN_TC - 1) / SCAN_TC;
+    // dt rows that hold softplus(dt) already: given so, or written back by
+    // this segment's summary pass
+    const bool dt_ready = p.dt_act || (MODE == GATED && p.dt_wb && nseg > 1 && g < nseg - 1);
+    T *dt_back = (MODE == SUMMARY && p.dt_wb && !p.dt_act)
+                     ? const_cast<T *>(static_cast<const T *>(p.dt)) + row_base * p.ld_dt + d
+                     : nullptr;
     float sdt = 0.0f;                                  // sum of this channel's dt (pass 1)
     float ymax = 0.0f;                                 // max |y| written by this thread
     if (nchunks > 0) issue(0);
@@ -411,7 +389,7 @@ scan_kernel(const ScanParams p) {
 #pragma unroll
                     for (int l = 1; l < L && k + l < HALF; ++l) v = (j == l) ? part[k + l] : v;
                     if (L <= HALF || j < HALF)
-                        dts[(t0 + k + j) * CH + c] = io<T>::round(softplus_fast(io<T>::round(v + bias_dt)));
+                        dts[(t0 + k + j) * CH + c] = io<T>::round(softplus_f(io<T>::round(v + bias_dt)));
                 }
             }
             __syncwarp();   // a channel's L lanes share one warp
@@ -420,8 +398,13 @@ scan_kernel(const ScanParams p) {
             // ---- dt = softplus(dt_proj output) once per token-channel: lane j
             // takes steps j, j + L, ... (rows >= tn are zero-filled, unused)
 #pragma unroll
-            for (int tt = j; tt < SCAN_TC; tt += L)
-                dts[tt * CH + c] = io<T>::round(softplus_fast(io<T>::to_f(d2s[tt * CH])));
+            for (int tt = j; tt < SCAN_TC; tt += L) {
+                const float v = io<T>::to_f(d2s[tt * CH]);
+                const float dv = dt_ready ? v : io<T>::round(softplus_f(v));
+                dts[tt * CH + c] = dv;
+                if (dt_back && active && tt < tn)
+                    dt_back[((int64_t)ch * SCAN_TC + tt) * p.ld_dt] = io<T>::from_f(dv);
+            }
             __syncwarp();   // a channel's L lanes share one warp
         }
         // ---- recurrence (tn is CTA-uniform)
@@ -464,8 +447,10 @@ scan_kernel(const ScanParams p) {
 #pragma unroll
                 for (int l = 0; l < L; ++l) yv += ys[tt * SCAN_THREADS + cc * L + l];
                 float out = yv + d_skip * io<T>::to_f(xrow[tt * CH]);
-                if (MODE != PLAIN)
-                    out = io<T>::round(out) * io<T>::round(silu_f(io<T>::to_f(zrow[tt * CH])));
+                if (MODE != PLAIN) {
+                    const float zv = io<T>::to_f(zrow[tt * CH]);
+                    out = io<T>::round(out) * (p.z_act ? zv : io<T>::round(silu_f(zv)));
+                }
                 ymax = fmaxf(ymax, fabsf(out));
                 yg[((int64_t)ch * SCAN_TC + tt) * p.ld_y] = io<T>::from_f(out);
             }
@@ -604,7 +589,7 @@ int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t
                int64_t ld_z, const void *w_dt, const void *b_dt, const void *A_log,
                const void *D, const float *h0, float *h_last, void *y, int64_t ld_y,
                int64_t batch, int64_t seqlen, int64_t d_inner, int64_t d_state, int64_t dt_rank,
-               cudaStream_t stream, unsigned *amax) {
+               cudaStream_t stream, unsigned *amax, int act) {
     MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "scan: bad dtype");
     MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0 && dt_rank >= 1, MB2_ERR_SHAPE,
                 "scan: bad sizes");
@@ -634,6 +619,7 @@ int scan_fused(int dtype, const void *xc, int64_t ld_xc, const void *dl, int64_t
     p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
     p.d_state = (int)d_state; p.dt_rank = (int)dt_rank;
     p.amax = amax;
+    p.z_act = (act & SCAN_Z_ACT) != 0;
     if (dtype == MB2_F32) return dispatch_scan<float, FUSED>(p, stream);
     return dispatch_scan<__nv_bfloat16, FUSED>(p, stream);
 }
@@ -690,7 +676,7 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
                int64_t ld_z, const void *A_log, const void *D, const float *h0, float *h_last,
                void *y, int64_t ld_y, int64_t batch, int64_t seqlen, int64_t d_inner,
                int64_t d_state, cudaStream_t stream, float *seg_ws, size_t seg_bytes,
-               unsigned *amax) {
+               unsigned *amax, int act) {
     MB2_REQUIRE(dtype == MB2_F32 || dtype == MB2_BF16, MB2_ERR_ARG, "scan: bad dtype");
     MB2_REQUIRE(batch >= 0 && seqlen >= 0 && d_inner >= 0, MB2_ERR_SHAPE, "scan: bad sizes");
     MB2_REQUIRE(d_state >= 1 && d_state <= 256, MB2_ERR_SHAPE,
@@ -718,6 +704,9 @@ int scan_gated(int dtype, const void *xc, int64_t ld_xc, const void *dt, int64_t
     p.batch = batch; p.seqlen = seqlen; p.d_inner = d_inner;
     p.d_state = (int)d_state;
     p.amax = amax;
+    p.dt_act = (act & SCAN_DT_ACT) != 0;
+    p.z_act = (act & SCAN_Z_ACT) != 0;
+    p.dt_wb = (act & SCAN_DT_SCRATCH) != 0;
     const int nseg = scan_segments(batch, d_inner, seqlen, d_state);
     if (nseg > 1 && seg_ws && seg_bytes >= scan_segment_bytes(batch, d_inner, seqlen, d_state)) {
         if (dtype == MB2_F32) return run_segmented<float, GATED>(p, nseg, seg_ws, stream);
@@ -776,13 +765,18 @@ step_scan_dt_kernel(const T *__restrict__ xc, int64_t ld_x, const T *__restrict_
         xv[k] = ok ? io<T>::to_f(xc[b * ld_x + d]) : 0.0f;
         zv[k] = ok ? io<T>::to_f(z[b * ld_z + d]) : 0.0f;
     }
-    for (int i = tid; i < SDT_B * R; i += SDT_THREADS) {
-        const int bl = i / R, r = i - bl * R;
-        dls[i] = b0 + bl < batch ? io<T>::to_f(dl[(b0 + bl) * ld_dl + r]) : 0.0f;
-    }
     for (int i = tid; i < SDT_D * R; i += SDT_THREADS) {
         const int dd = i / R, r = i - dd * R;
         ws[dd * RP + r] = d0 + dd < di ? io<T>::to_f(w_dt[(d0 + dd) * R + r]) : 0.0f;
+    }
+    // dt_low, B and C come from the kernel before this one in the decode
+    // step's chain (x_proj's reduction); the state, x, z and W_dt above are
+    // older (common.cuh, pdl_wait)
+    pdl_wait();
+    pdl_trigger();
+    for (int i = tid; i < SDT_B * R; i += SDT_THREADS) {
+        const int bl = i / R, r = i - bl * R;
+        dls[i] = b0 + bl < batch ? io<T>::to_f(dl[(b0 + bl) * ld_dl + r]) : 0.0f;
     }
     for (int i = tid; i < SDT_B * S; i += SDT_THREADS) {
         const int bl = i / S, sidx = i - bl * S;
@@ -806,7 +800,7 @@ step_scan_dt_kernel(const T *__restrict__ xc, int64_t ld_x, const T *__restrict_
         for (; r < R; ++r) a0 = fmaf(dlr[r], wr[r], a0);
         const float acc = (a0 + a1) + (a2 + a3);
         const float pre = io<T>::round(acc + ((b_dt && d < di) ? io<T>::to_f(b_dt[d]) : 0.0f));
-        dts[tid] = io<T>::round(softplus_fast(pre));
+        dts[tid] = io<T>::round(softplus_f(pre));
     }
     __syncthreads();
     // phase 2: QS threads per (b, d), 4 states each
@@ -850,6 +844,8 @@ step_scan_dt_any_kernel(const T *__restrict__ xc, int64_t ld_x, const T *__restr
                         const T *__restrict__ z, int64_t ld_z, const T *__restrict__ A_log,
                         const T *__restrict__ D, float *__restrict__ h, T *__restrict__ y,
                         int64_t ld_y, int64_t batch, int64_t di, int S, int R) {
+    pdl_wait();
+    pdl_trigger();
     const int64_t b = (int64_t)blockIdx.y * SDT_B + threadIdx.x / SDT_D;
     const int64_t d = (int64_t)blockIdx.x * SDT_D + threadIdx.x % SDT_D;
     if (b >= batch || d >= di) return;
@@ -857,7 +853,7 @@ step_scan_dt_any_kernel(const T *__restrict__ xc, int64_t ld_x, const T *__restr
     for (int r = 0; r < R; ++r)
         acc = fmaf(io<T>::to_f(dl[b * ld_dl + r]), io<T>::to_f(w_dt[d * R + r]), acc);
     const float pre = io<T>::round(acc + (b_dt ? io<T>::to_f(b_dt[d]) : 0.0f));
-    const float dt = io<T>::round(softplus_fast(pre));
+    const float dt = io<T>::round(softplus_f(pre));
     const float x = io<T>::to_f(xc[b * ld_x + d]);
     float *hr = h + (b * di + d) * S;
     float yv = 0.0f;
@@ -876,7 +872,7 @@ int scan_step_dt(int dtype, const void *xc, int64_t ld_x, const void *dt_low, in
                  const void *w_dt, const void *b_dt, const void *bm, const void *cm,
                  int64_t ld_bc, const void *z, int64_t ld_z, const void *A_log, const void *D,
                  float *h, void *y, int64_t ld_y, int64_t batch, int64_t d_inner, int64_t d_state,
-                 int64_t dt_rank, cudaStream_t st) {
+                 int64_t dt_rank, cudaStream_t st, bool pdl) {
     MB2_REQUIRE(d_state >= 1 && d_state <= 256 && dt_rank >= 1 && dt_rank <= 1024, MB2_ERR_SHAPE,
                 "step: d_state %lld or dt_rank %lld out of range", (long long)d_state,
                 (long long)dt_rank);
@@ -900,8 +896,11 @@ int scan_step_dt(int dtype, const void *xc, int64_t ld_x, const void *dt_low, in
                 if (e != cudaSuccess)
                     return fail(MB2_ERR_CUDA, "step: smem attribute: %s", cudaGetErrorString(e));
             }
-            kern<<<grid, SDT_THREADS, smem, st>>>(X, ld_x, DL, ld_dl, W, BB, Bp, Cp, ld_bc, Z, ld_z,
-                                                  AL, Dp, h, Y, ld_y, batch, d_inner, R);
+            const cudaError_t le = launch_kernel(pdl, kern, grid, dim3(SDT_THREADS), smem, st, X,
+                                                 ld_x, DL, ld_dl, W, BB, Bp, Cp, ld_bc, Z, ld_z,
+                                                 AL, Dp, h, Y, ld_y, batch, d_inner, R);
+            if (le != cudaSuccess)
+                return fail(MB2_ERR_CUDA, "step_scan_dt_kernel launch: %s", cudaGetErrorString(le));
             return check_launch("step_scan_dt_kernel");
         };
         if (aligned(h, 16)) {
@@ -912,9 +911,12 @@ int scan_step_dt(int dtype, const void *xc, int64_t ld_x, const void *dt_low, in
             if (S == 64) return tiled(step_scan_dt_kernel<T, 16>);
             if (S == 128) return tiled(step_scan_dt_kernel<T, 32>);
         }
-        step_scan_dt_any_kernel<T><<<grid, SDT_THREADS, 0, st>>>(
-            X, ld_x, DL, ld_dl, W, BB, Bp, Cp, ld_bc, Z, ld_z, AL, Dp, h, Y, ld_y, batch, d_inner, S,
-            R);
+        const cudaError_t le = launch_kernel(pdl, step_scan_dt_any_kernel<T>, grid,
+                                             dim3(SDT_THREADS), 0, st, X, ld_x, DL, ld_dl, W, BB,
+                                             Bp, Cp, ld_bc, Z, ld_z, AL, Dp, h, Y, ld_y, batch,
+                                             d_inner, S, R);
+        if (le != cudaSuccess)
+            return fail(MB2_ERR_CUDA, "step_scan_dt_any_kernel launch: %s", cudaGetErrorString(le));
         return check_launch("step_scan_dt_any_kernel");
     };
     if (dtype == MB2_F32) return run(float{});

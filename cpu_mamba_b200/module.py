@@ -199,6 +199,24 @@ class CPUMamba(nn.Module):
                                       ws.data_ptr(), ws_bytes, stream_of(x)), "forward")
         return out, h, conv
 
+    def profile_stages(self, hidden_states: torch.Tensor) -> dict:
+        """One forward with CUDA events between its six stages (the launches
+        forward() makes, on the current stream); returns each stage's ms."""
+        x = hidden_states.contiguous()
+        B, T, _ = x.shape
+        self._check_io(x, "forward")
+        keep = []
+        blk = self._descriptor(keep)
+        ws_bytes = lib().mb2_block_workspace_bytes(ctypes.byref(blk), B, T)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+        out = torch.empty_like(x)
+        ms = (ctypes.c_float * 6)()
+        check(lib().mb2_block_forward_profile(ctypes.byref(blk), x.data_ptr(), out.data_ptr(), B, T,
+                                              ws.data_ptr(), ws_bytes, ms, stream_of(x)),
+              "profile_stages")
+        names = ("in_proj", "conv1d_silu", "x_proj", "dt_proj", "scan", "out_proj")
+        return dict(zip(names, (float(v) for v in ms)))
+
     def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
         """hidden_states: (B, T, d_model) -> (B, T, d_model) (_mamba.py:204-265)."""
         return self._run(hidden_states, False)[0]

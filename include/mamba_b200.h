@@ -274,6 +274,16 @@ int mb2_block_forward(const mb2_block *blk, const void *x, void *out,
                       void *conv_tail, void *workspace, size_t workspace_bytes,
                       mb2_stream_t stream);
 
+/* Stage timing of mb2_block_forward: the same launches on the same stream,
+ * with CUDA events between the six stages; waits for them and writes their
+ * durations in ms to stage_ms[0..5] (in_proj, conv1d + SiLU, x_proj, dt_proj
+ * + softplus, scan + gate, out_proj).  A profiling aid without a reference
+ * counterpart (the reference times whole forwards, bench/bench.py:28-75). */
+int mb2_block_forward_profile(const mb2_block *blk, const void *x, void *out,
+                              int64_t batch, int64_t seqlen, void *workspace,
+                              size_t workspace_bytes, float *stage_ms,
+                              mb2_stream_t stream);
+
 /* Bytes of workspace mb2_block_step needs for a batch. */
 size_t mb2_step_workspace_bytes(const mb2_block *blk, int64_t batch);
 
