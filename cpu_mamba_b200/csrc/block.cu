@@ -31,6 +31,18 @@ int linear_any(int dtype, const mb2_linear_w &L, const void *x, int64_t ld_x, vo
         // dequantises tile by tile in its loader
         if (M >= 256 && ex.scratch &&
             ex.scratch_bytes >= dequant_operand_bytes(dtype, N, K)) {
+            if (dtype == MB2_F32 && ex.amax_parts && K % 8 == 0 && L.group_size == 0 &&
+                (L.scheme == MB2_Q_INT8 || L.scheme == MB2_Q_INT4)) {
+                // int8 / int4 with one scale per row: the integer codes, exact
+                // in fp16, are the tensor-core operand and the scale is applied
+                // per output column in the epilogue (two MMAs per K step)
+                MB2_TRY(codes_f16(L.scheme, L.weight_q, N, K, ex.scratch, st));
+                bool used = false;
+                MB2_TRY(gemm_f16x3_codes(static_cast<const float *>(x), ld_x, ex.scratch, L.scale,
+                                         L.bias, static_cast<float *>(y), ld_y, M, N, K, n1, off1,
+                                         n2, off2, epi, st, &used, ex, ex.amax_parts));
+                if (used) return MB2_OK;
+            }
             if (dtype == MB2_F32 && ex.amax_parts && K % 8 == 0) {
                 // fp32: the dequantised weight (quant.py's values, bit-exact),
                 // its scaled fp16 split, then the F16X3 GEMM

@@ -54,20 +54,24 @@ struct F16Cfg {
 // 128 rows of W (the MMAs read the two halves from the two CTAs), so a stage
 // is 48 KB and 4 of them fit: 25 % fewer bytes from L2 per multiply-add and a
 // third more work in flight.
-template <bool PAIR> struct F16Stage {
-    static constexpr int STAGES = PAIR ? 4 : 3;
+// CODES: the weight operand is a quantised weight's integer codes as fp16
+// (exact: |q| <= 127), one plane instead of hi / lo, so a stage is 48 KB and
+// 4 fit.
+template <bool PAIR, bool CODES = false> struct F16Stage {
+    static constexpr int STAGES = (PAIR || CODES) ? 4 : 3;
     static constexpr int WROWS = PAIR ? 64 : 128;        // W rows per CTA
     static constexpr uint32_t W_BYTES = WROWS * 128;
-    static constexpr uint32_t STAGE_BYTES = 2 * TILE_BYTES + 2 * W_BYTES;
+    static constexpr uint32_t STAGE_BYTES = 2 * TILE_BYTES + (CODES ? 1 : 2) * W_BYTES;
 };
 
 // output staging: 32 rows x 32 fp32 columns (one 128B-swizzled box) per epilogue warp
 constexpr size_t f16_staging_bytes() { return (size_t)8 * 32 * 32 * sizeof(float); }
-template <bool PAIR> constexpr size_t f16_smem_bytes() {
-    return 1024 + (size_t)F16Stage<PAIR>::STAGES * F16Stage<PAIR>::STAGE_BYTES +
+template <bool PAIR, bool CODES = false> constexpr size_t f16_smem_bytes() {
+    return 1024 + (size_t)F16Stage<PAIR, CODES>::STAGES * F16Stage<PAIR, CODES>::STAGE_BYTES +
            f16_staging_bytes() + 256;
 }
-static_assert(f16_smem_bytes<false>() <= 232448 && f16_smem_bytes<true>() <= 232448,
+static_assert(f16_smem_bytes<false>() <= 232448 && f16_smem_bytes<true>() <= 232448 &&
+                  f16_smem_bytes<false, true>() <= 232448,
               "F16X3 shared memory above the 227 KB per CTA");
 
 struct F16Params {
@@ -75,6 +79,7 @@ struct F16Params {
     const float *x_parts;           // partial maxima of |x| (float bits of non-negative values)
     int n_parts;
     const float *w_inv;             // 2^-ew (header of the split weight)
+    const float *col_scale;         // CODES: the quantised weight's scale per output column
 };
 
 // Exponent e with amax * 2^e in [2^14, 2^15); 0 for zero or non-finite amax.
@@ -167,13 +172,18 @@ __device__ __forceinline__ void cluster_sync() {
                  ::: "memory");
 }
 
-template <bool EXTRA, bool PAIR>
+// CODES (single SMs only): W is a quantised weight's codes as fp16 and the
+// epilogue multiplies column n by its scale: y = 2^-ex (x_hi + x_lo) q^T s,
+// two MMAs per K step (x_hi q, x_lo q) -- the codes are exact, so no W_lo
+// term -- and half the weight bytes of the dequantised split.
+template <bool EXTRA, bool PAIR, bool CODES = false>
 __global__ void __launch_bounds__(F16Cfg::WARPS * 32, 1)
 gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wh,
                   const __grid_constant__ CUtensorMap map_wl, const __grid_constant__ CUtensorMap map_y,
                   const F16Params fp) {
+    static_assert(!(PAIR && CODES), "codes run on single SMs");
     using C = F16Cfg;
-    using G = F16Stage<PAIR>;
+    using G = F16Stage<PAIR, CODES>;
     constexpr int BN = C::BN;
     constexpr int TM = PAIR ? 2 * BM : BM;              // tile rows (per pair)
     const Params &p = fp.g;
@@ -265,7 +275,7 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                     tma_load_2d(tile_a(s, 0), &map_a, full(s), kc, (int32_t)m0);
                     tma_load_2d(tile_a(s, 1), &map_a, full(s), kc + 32, (int32_t)m0);
                     tma_load_2d(tile_w(s, 0), &map_wh, full(s), kc, (int32_t)n0);
-                    tma_load_2d(tile_w(s, 1), &map_wl, full(s), kc, (int32_t)n0);
+                    if (!CODES) tma_load_2d(tile_w(s, 1), &map_wl, full(s), kc, (int32_t)n0);
                 }
             }
         }
@@ -314,10 +324,14 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
                     for (int kk = 0; kk < C::BK / 16; ++kk) {
                         const uint32_t ah = tmem + C::COL_A + (g & 1) * 64 + kk * 8;
                         const uint64_t bh = smem_desc(tile_w(s, 0) + kk * 32);
-                        const uint64_t bl = smem_desc(tile_w(s, 1) + kk * 32);
                         mma_ts_f16<PAIR>(tmem + pcol, ah, bh, (rel > 0 || kk > 0) ? 1u : 0u);
-                        mma_ts_f16<PAIR>(tmem + C::COL_Q, ah, bl, (kb > 0 || kk > 0) ? 1u : 0u);
-                        mma_ts_f16<PAIR>(tmem + C::COL_Q, ah + 32, bh, 1u);
+                        if (CODES) {
+                            mma_ts_f16<PAIR>(tmem + C::COL_Q, ah + 32, bh, (kb > 0 || kk > 0) ? 1u : 0u);
+                        } else {
+                            const uint64_t bl = smem_desc(tile_w(s, 1) + kk * 32);
+                            mma_ts_f16<PAIR>(tmem + C::COL_Q, ah, bl, (kb > 0 || kk > 0) ? 1u : 0u);
+                            mma_ts_f16<PAIR>(tmem + C::COL_Q, ah + 32, bh, 1u);
+                        }
                     }
                     mma_commit_to<PAIR>(empty(s));        // stages free once these MMAs read them
                     mma_commit_to<PAIR>(a_empty(g & 1));  // and the A slots
@@ -379,7 +393,7 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
         const uint32_t lanes = (uint32_t)(q * 32) << 16;
         const uint32_t ccol = (uint32_t)(ch * C::ECOLS);
         const float inv_x = pow2f(-f16_scale_exp(warp_amax(fp.x_parts, fp.n_parts)));
-        const float inv_w = *fp.w_inv;
+        const float inv_w = CODES ? 1.0f : *fp.w_inv;
         const uint32_t wst = out_base + (uint32_t)((warp - C::EPI0) * 32 * 128);  // one box
         uint8_t *wst_g = gbase + (wst - base);
         float *Y = static_cast<float *>(p.y);
@@ -437,8 +451,16 @@ gemm_f16x3_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_consta
             for (int cb = 0; cb < C::ECOLS / 32; ++cb) {
                 const int64_t c0 = n0 + ch * C::ECOLS + cb * 32;   // first output column
                 float *v = acc + cb * 32;        // in place (constant offsets once unrolled)
+                if (CODES) {
+                    // column c0 + j's scale: loaded by lane j, broadcast by shuffles
+                    const float my_s = c0 + lane < p.N ? fp.col_scale[c0 + lane] : 0.0f;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = v[j] * inv_x * inv_w;
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = (v[j] * inv_x) * __shfl_sync(0xffffffffu, my_s, j);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = v[j] * inv_x * inv_w;
+                }
                 if (EXTRA && p.row_scale) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] *= rscale;

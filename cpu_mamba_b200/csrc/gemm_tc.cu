@@ -988,12 +988,12 @@ size_t split_f16_bytes(int64_t rows, int64_t cols) {
 
 // Launch one F16X3 instantiation: persistent, one CTA per SM; pairs of CTAs
 // (2-SM clusters) when PAIR, as many pairs as can be resident at once.
-template <bool EXTRA, bool PAIR>
+template <bool EXTRA, bool PAIR, bool CODES = false>
 static int launch_f16(const CUtensorMap &ma, const CUtensorMap &mwh, const CUtensorMap &mwl,
                       const CUtensorMap &my, const tc::F16Params &fp, int64_t M, int64_t N,
                       cudaStream_t st) {
-    auto kern = tc::gemm_f16x3_kernel<EXTRA, PAIR>;
-    constexpr size_t smem = tc::f16_smem_bytes<PAIR>();
+    auto kern = tc::gemm_f16x3_kernel<EXTRA, PAIR, CODES>;
+    constexpr size_t smem = tc::f16_smem_bytes<PAIR, CODES>();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_f16x3 smem attribute: %s", cudaGetErrorString(e));
     if (g_num_sms == 0) {
@@ -1085,6 +1085,44 @@ int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, 
     else
         rc = extra ? launch_f16<true, false>(ma, mwh, mwl, my, fp, M, N, st)
                    : launch_f16<false, false>(ma, mwh, mwl, my, fp, M, N, st);
+    MB2_TRY(rc);
+    *used = true;
+    return MB2_OK;
+}
+
+// y = x (q s)^T for a quantised weight with one scale per row (int8 / int4
+// codes q given as fp16 in `codes16`, N x K, 256-byte aligned): the F16X3
+// kernel in its CODES form, the scale applied per output column in the
+// epilogue.  *used reports whether it ran.
+int gemm_f16x3_codes(const float *x, int64_t ld_x, const void *codes16, const float *col_scale,
+                     const void *bias, float *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
+                     int64_t n1, int64_t off1, int64_t n2, int64_t off2, int epi, cudaStream_t st,
+                     bool *used, const EpiExtra &ex, float *parts) {
+    *used = false;
+    if (!codes16 || !col_scale || !parts || M < 1 || N < 16 || K < 16) return MB2_OK;
+    if (!aligned(x, 16) || (ld_x * 4) % 16 != 0 || K % 8 != 0 || !aligned(codes16, 256)) return MB2_OK;
+    if (ex.resid && (!aligned(ex.resid, 16) || ex.ld_r % 4 != 0 || N % 4 != 0)) return MB2_OK;
+    MB2_TRY(get_encode());
+    int nparts = ex.amax_n;
+    if (nparts <= 0) MB2_TRY(amax_parts(x, ld_x, M, K, parts, &nparts, st));
+    CUtensorMap ma, mw, my;
+    MB2_TRY(make_map(&ma, x, M, K, ld_x, false, 128));
+    MB2_TRY(make_map_t(&mw, codes16, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                       tc::F16Stage<false, true>::WROWS));
+    const bool remap = (n1 < N && off1 != 0) || (n2 < N && off2 != 0);
+    const bool tma_store = !remap && aligned(y, 16) && (ld_y * 4) % 16 == 0;
+    if (tma_store) MB2_TRY(make_map(&my, y, M, N, ld_y, false, 32));
+    else my = ma;  // unused
+    tc::F16Params fp{};
+    fp.g = tc::Params{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0,
+                      ex.row_scale, ex.resid, ex.ld_r, 1, 0, ex.silu_from};
+    fp.x_parts = parts;
+    fp.n_parts = nparts;
+    fp.w_inv = nullptr;
+    fp.col_scale = col_scale;
+    const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS || ex.silu_from >= 0;
+    const int rc = extra ? launch_f16<true, false, true>(ma, mw, mw, my, fp, M, N, st)
+                         : launch_f16<false, false, true>(ma, mw, mw, my, fp, M, N, st);
     MB2_TRY(rc);
     *used = true;
     return MB2_OK;

@@ -83,6 +83,15 @@ int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, 
                int64_t ld_y, int64_t M, int64_t N, int64_t K, int64_t n1, int64_t off1,
                int64_t n2, int64_t off2, int epi, cudaStream_t st, bool *used,
                const EpiExtra &ex, float *parts, int pair = -1);
+// The same kernel on a quantised weight's codes (int8 / int4, one scale per
+// row) given as exact fp16 (codes_f16), the scale applied in the epilogue.
+int gemm_f16x3_codes(const float *x, int64_t ld_x, const void *codes16, const float *col_scale,
+                     const void *bias, float *y, int64_t ld_y, int64_t M, int64_t N, int64_t K,
+                     int64_t n1, int64_t off1, int64_t n2, int64_t off2, int epi, cudaStream_t st,
+                     bool *used, const EpiExtra &ex, float *parts);
+// int8 / int4 codes (rows, in_dim) as fp16 integers q (int4: nibble - 7, the
+// packing of quant.py:90-101), exact
+int codes_f16(int scheme, const void *wq, int64_t rows, int64_t in_dim, void *out, cudaStream_t st);
 size_t split_f16_bytes(int64_t rows, int64_t cols);
 // W (rows, cols) fp32 -> mb2_split_f16's layout at out (256-byte aligned)
 int split_f16(const float *w, int64_t rows, int64_t cols, void *out, cudaStream_t st);

@@ -198,6 +198,36 @@ __global__ void dequant_operand_kernel(const void *__restrict__ wq,
     }
 }
 
+// The integer codes themselves as fp16 (exact), the operand of the F16X3
+// kernel's CODES form, which applies the scale in its epilogue.
+template <int SCHEME>
+__global__ void codes_f16_kernel(const void *__restrict__ wq, int64_t rows, int64_t in_dim,
+                                 __half *__restrict__ out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * in_dim) return;
+    int q;
+    if (SCHEME == MB2_Q_INT8) {
+        q = static_cast<const int8_t *>(wq)[i];
+    } else {
+        const int64_t r = i / in_dim, j = i - r * in_dim;
+        const int64_t pcols = (in_dim + 1) >> 1;
+        const uint8_t byte = static_cast<const uint8_t *>(wq)[r * pcols + (j >> 1)];
+        q = ((j & 1) ? (byte & 0x0F) : (byte >> 4)) - 7;
+    }
+    out[i] = __int2half_rn(q);
+}
+
+int codes_f16(int scheme, const void *wq, int64_t rows, int64_t in_dim, void *out, cudaStream_t st) {
+    const int64_t n = rows * in_dim;
+    if (n == 0) return MB2_OK;
+    const unsigned grid = (unsigned)ceil_div(n, (int64_t)256);
+    __half *o = static_cast<__half *>(out);
+    if (scheme == MB2_Q_INT8) codes_f16_kernel<MB2_Q_INT8><<<grid, 256, 0, st>>>(wq, rows, in_dim, o);
+    else if (scheme == MB2_Q_INT4) codes_f16_kernel<MB2_Q_INT4><<<grid, 256, 0, st>>>(wq, rows, in_dim, o);
+    else return fail(MB2_ERR_ARG, "codes_f16: scheme %d has no integer codes", scheme);
+    return check_launch("codes_f16_kernel");
+}
+
 size_t dequant_operand_bytes(int dtype, int64_t rows, int64_t in_dim) {
     if (dtype == MB2_BF16) return (size_t)rows * in_dim * 2;
     // TF32 planes (8 B per weight), or the F16X3 split (4096 + 4 B per weight,
