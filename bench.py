@@ -316,18 +316,16 @@ def run_ours(args, cfg):
 
     stages = (profile_stages(m, xs[0], cfg, dtype, args.steps)
               if cfg["mode"] == "forward" and not channels else {})
+    launches_per_step, launch_names = count_launches(lambda: step(0), dev)
     result = None
     if rank == 0:
         hbm, bf16, bf16_s, src = peaks()
         if stack_mode:
             roof = stack_roofline(cfg, B, hbm, src, ms / args.steps)
-            launches_per_step = 7 * cfg["n_layers"]
         elif step_mode:
             roof = decode_roofline(cfg, hbm, src, ms / args.steps, ws if channels else 1)
-            launches_per_step = 5 + (2 if reducer is not None else 0)
         else:
             roof = roofline(stages, cfg, hbm, bf16, src, ms / args.steps)
-            launches_per_step = 6 + (2 if reducer is not None else 0)
         par = f"batch-sharded x{ws}"
         if channels:
             par = (f"d_inner channel-sharded x{ws}, all-reduce: "
@@ -346,6 +344,7 @@ def run_ours(args, cfg):
                               f"({nbuf * in_bytes / 2**20:.0f} MB > L2)"),
             "roofline": roof, "stages_ms": stages, "e2e": e2e,
             "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches_per_step": launch_names,
             "clocks": clk.summary(),
         }
     del graph                       # graphs holding collectives go before the group
@@ -353,6 +352,28 @@ def run_ours(args, cfg):
         reducer.close()
     dist.shutdown()
     return result
+
+
+def count_launches(fn, dev):
+    """The library's kernel launches in one untimed call of fn (one step),
+    counted by CUPTI through torch.profiler: kernels of the mb2 namespaces
+    (torch's own kernels, copies and memsets excluded).  Returns the count and
+    a per-kernel breakdown {short name: launches}."""
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize(dev)
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize(dev)
+    names = {}
+    for e in prof.events():
+        if e.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        n = e.name
+        if "mb2::" not in n:
+            continue
+        short = n.split("(")[0].replace("void ", "").split("<")[0].split("::")[-1]
+        names[short] = names.get(short, 0) + 1
+    return sum(names.values()), names
 
 
 def workload_config(cfg, batch_per_gpu, global_batch, ws_label):

@@ -213,6 +213,8 @@ __global__ void conv_step_reduce_kernel(const float *__restrict__ P, int ks,
         const float *q = P + b * N + n;
         float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
         int z = 0;
+        // unrolled so that up to 32 partial loads are in flight at once
+#pragma unroll 8
         for (; z + 4 <= ks; z += 4) {
             a0 += q[(z + 0) * mn];
             a1 += q[(z + 1) * mn];

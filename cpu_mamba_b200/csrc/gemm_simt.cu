@@ -270,6 +270,8 @@ __global__ void splitk_reduce_kernel(const GemmArgs a, int splits) {
     // four loads in flight; fixed combination order (deterministic)
     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
     int z = 0;
+    // unrolled so that up to 32 partial loads are in flight at once
+#pragma unroll 8
     for (; z + 4 <= splits; z += 4) {
         a0 += a.partial[(z + 0) * mn + i];
         a1 += a.partial[(z + 1) * mn + i];

@@ -781,6 +781,8 @@ __global__ void tc_splitk_reduce_kernel(const float *__restrict__ P, int ks, int
     const int64_t mn = M * N;
     float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
     int z = 0;
+    // unrolled so that up to 32 partial loads are in flight at once
+#pragma unroll 8
     for (; z + 4 <= ks; z += 4) {
         a0 += P[(z + 0) * mn + i];
         a1 += P[(z + 1) * mn + i];
