@@ -279,6 +279,16 @@ __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32
           "=r"(r[31])
         : "r"(taddr));
 }
+// 32 lanes x 16 columns from TMEM; asynchronous until tmem_wait_ld()
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -687,6 +697,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 }
 
 #include "gemm_f16x3.cuh"
+#include "gemm_f16w.cuh"
 
 }  // namespace tc
 
@@ -716,6 +727,19 @@ static int make_map_t(CUtensorMap *map, const void *ptr, int64_t rows, int64_t c
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MB2_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return MB2_OK;
+}
+// The same with 64-byte boxes and 64B swizzle (fp16 operands of the wide F16X3 kernel).
+static int make_map_sw64(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols,
+                         int64_t ld, CUtensorMapDataType type, size_t es, int box_rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * es)};
+    cuuint32_t box[2] = {(cuuint32_t)(64 / es), (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, type, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MB2_ERR_CUDA, "cuTensorMapEncodeTiled (64B) failed (%d)", (int)r);
     return MB2_OK;
 }
 static int make_map(CUtensorMap *map, const void *ptr, int64_t rows, int64_t cols, int64_t ld,
@@ -1042,6 +1066,32 @@ static int launch_f16(const CUtensorMap &ma, const CUtensorMap &mwh, const CUten
     return check_launch("gemm_f16x3_kernel");
 }
 
+// The wide F16X3 kernel (128 x 256 tiles): persistent, one CTA per SM.
+template <bool EXTRA>
+static int launch_f16w(const CUtensorMap &ma, const CUtensorMap &mwh, const CUtensorMap &mwl,
+                       const CUtensorMap &my, const tc::F16Params &fp, int64_t M, int64_t N,
+                       cudaStream_t st) {
+    auto kern = tc::gemm_f16w_kernel<EXTRA>;
+    constexpr size_t smem = tc::f16w_smem_bytes();
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_f16w smem attribute: %s", cudaGetErrorString(e));
+    if (g_num_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    const int64_t tiles = ceil_div(M, (int64_t)tc::BM) * ceil_div(N, (int64_t)tc::F16WCfg::BN);
+    const unsigned grid = (unsigned)(tiles < g_num_sms ? tiles : g_num_sms);
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess &&
+        fa.maxThreadsPerBlock < tc::F16WCfg::WARPS * 32)
+        return fail(MB2_ERR_CUDA, "gemm_f16w_kernel: %d registers per thread allow only %d threads",
+                    fa.numRegs, fa.maxThreadsPerBlock);
+    kern<<<grid, tc::F16WCfg::WARPS * 32, smem, st>>>(ma, mwh, mwl, my, fp);
+    return check_launch("gemm_f16w_kernel");
+}
+
 // fp32 GEMM through the F16X3 kernel; *used reports whether it ran.  parts:
 // scratch of AMAX_PARTS floats for x's partial maxima.  pair: 1 = 256-row
 // tiles on pairs of SMs, 0 or -1 = 128-row tiles on single SMs (the default:
@@ -1058,12 +1108,38 @@ int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, 
     if (!aligned(x, 16) || (ld_x * 4) % 16 != 0 || K % 8 != 0 || !aligned(w16, 256)) return MB2_OK;
     if (ex.resid && (!aligned(ex.resid, 16) || ex.ld_r % 4 != 0 || N % 4 != 0)) return MB2_OK;
     const bool two = pair > 0;
+    // 256-wide tiles for N >= 256 unless single-SM 128-wide tiles were asked
+    // for (pair == 0) or SM pairs (pair == 1)
+    const bool wide = pair < 0 && N >= 256;
     const char *wb = static_cast<const char *>(w16);
     const __half *whi = reinterpret_cast<const __half *>(wb + kF16Header);
     const __half *wlo = whi + N * K;
     MB2_TRY(get_encode());
     int nparts = ex.amax_n;        // > 0: the kernel that wrote x left its maxima in parts
     if (nparts <= 0) MB2_TRY(amax_parts(x, ld_x, M, K, parts, &nparts, st));
+    if (wide) {
+        CUtensorMap ma, mwh, mwl, my;
+        MB2_TRY(make_map(&ma, x, M, K, ld_x, false, 128));
+        MB2_TRY(make_map_sw64(&mwh, whi, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 256));
+        MB2_TRY(make_map_sw64(&mwl, wlo, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 256));
+        const bool remap = (n1 < N && off1 != 0) || (n2 < N && off2 != 0);
+        const bool tma_store = !remap && aligned(y, 16) && (ld_y * 4) % 16 == 0;
+        if (tma_store)
+            MB2_TRY(make_map_sw64(&my, y, M, N, ld_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32));
+        else my = ma;  // unused
+        tc::F16Params fp{};
+        fp.g = tc::Params{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0,
+                          ex.row_scale, ex.resid, ex.ld_r, 1, 0, ex.silu_from};
+        fp.x_parts = parts;
+        fp.n_parts = nparts;
+        fp.w_inv = reinterpret_cast<const float *>(w16);
+        const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS || ex.silu_from >= 0;
+        const int rc = extra ? launch_f16w<true>(ma, mwh, mwl, my, fp, M, N, st)
+                             : launch_f16w<false>(ma, mwh, mwl, my, fp, M, N, st);
+        MB2_TRY(rc);
+        *used = true;
+        return MB2_OK;
+    }
     CUtensorMap ma, mwh, mwl, my;
     const int wrows = two ? tc::F16Stage<true>::WROWS : tc::F16Stage<false>::WROWS;
     MB2_TRY(make_map(&ma, x, M, K, ld_x, false, 128));

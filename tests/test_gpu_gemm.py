@@ -174,6 +174,28 @@ def test_f16x3_softplus_epilogue(M):
     assert (y - torch.nn.functional.softplus(lin)).abs().max().item() <= 2e-6
 
 
+@pytest.mark.parametrize("shape", [(4096, 3072, 768), (2049, 768, 1536), (1000, 300, 104),
+                                   (300, 256, 3072), (27180, 512, 40)])
+@pytest.mark.parametrize("scale", [1e-4, 1.0, 3e3])
+def test_f16x3_wide_tiles(shape, scale):
+    """128 x 256 tiles (the default for N >= 256: 256-wide MMAs, x's split in
+    shared memory) against 128 x 128 tiles and float64: the same segment sums
+    of the same products, within 3x of an fp32 CPU GEMM's own error."""
+    M, N, K = shape
+    x, w, b = _data(M, N, K, 7 + sum(shape))
+    x = x * scale
+    xd, wd, bd = x.cuda(), w.cuda(), b.cuda()
+    s16 = ops.split_f16(wd)
+    y_wide = ops.linear(xd, wd, bd, weight_f16=s16)
+    y_narrow = ops.linear(xd, wd, bd, weight_f16=s16, sm_pair=0)
+    assert _lib.device_status() == 0
+    ref = x.double() @ w.double().T + b.double()
+    bound = 3 * _f32_err(x, w, b, ref) + 1e-7 * scale
+    err_w = (y_wide.cpu().double() - ref).abs().max().item()
+    err_n = (y_narrow.cpu().double() - ref).abs().max().item()
+    assert err_w <= bound, (err_w, err_n, bound)
+
+
 @pytest.mark.parametrize("shape", [(4096, 3072, 768), (300, 96, 1536), (1000, 200, 104),
                                    (2049, 768, 1536), (256, 128, 64)])
 def test_f16x3_sm_pairs_equal_single_sms(shape):
