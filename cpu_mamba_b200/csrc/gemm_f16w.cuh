@@ -28,15 +28,17 @@
 // fp16, 16 KB | W_lo, 16 KB) = 192 KB, plus 32 KB of output staging (2 KB a
 // warp: 32 rows x 16 columns per TMA store).  Every mbarrier wait is bounded.
 
-struct F16WCfg {
+template <int XFW = 2> struct F16WCfg {
     static constexpr int BN = 256;
     static constexpr int BK = 32;              // fp32 K values per k-block (one 128 B TMA box)
     static constexpr int SEG = 8;              // k-blocks per hi*hi segment (16 MMAs, as F16X3)
     static constexpr int STAGES = 4;
-    static constexpr int WARPS = 20;
-    static constexpr int XF0 = 2;              // transform warps 2-3, two rows a thread
-    static constexpr int XF_THREADS = 64;
-    static constexpr int EPI0 = 4;             // epilogue warps 4-19
+    static constexpr int XF0 = 2;              // transform warps from 2
+    static constexpr int XF_WARPS = XFW;
+    static constexpr int XF_THREADS = 32 * XF_WARPS;
+    static constexpr int RPT = 128 / XF_THREADS;   // rows a transform thread splits
+    static constexpr int EPI0 = XF0 + XF_WARPS;    // 16 epilogue warps after them
+    static constexpr int WARPS = EPI0 + 16;
     static constexpr int EPI_WARPS = 16;
     static constexpr int EPI_THREADS = 512;
     static constexpr int ECOLS = 64;           // accumulator columns per epilogue warp
@@ -47,9 +49,9 @@ struct F16WCfg {
     static constexpr uint32_t STAGE_BYTES = A_BYTES + 2 * W_BYTES;
 };
 // output staging: 32 rows x 16 fp32 columns (one 64B-swizzled box) per epilogue warp
-constexpr size_t f16w_staging_bytes() { return (size_t)F16WCfg::EPI_WARPS * 32 * 16 * sizeof(float); }
+constexpr size_t f16w_staging_bytes() { return (size_t)F16WCfg<>::EPI_WARPS * 32 * 16 * sizeof(float); }
 constexpr size_t f16w_smem_bytes() {
-    return 1024 + (size_t)F16WCfg::STAGES * F16WCfg::STAGE_BYTES + f16w_staging_bytes() + 256;
+    return 1024 + (size_t)F16WCfg<>::STAGES * F16WCfg<>::STAGE_BYTES + f16w_staging_bytes() + 256;
 }
 static_assert(f16w_smem_bytes() <= 232448, "wide F16X3 shared memory above the 227 KB per CTA");
 
@@ -64,7 +66,7 @@ __device__ __forceinline__ uint64_t smem_desc64(uint32_t addr) {
 __device__ __forceinline__ void mma_ss_f16w(uint32_t tmem_d, uint64_t da, uint64_t db,
                                             uint32_t accum) {
     // D F32 (bits 4-5 = 1), A / B F16 (0), K-major, N >> 3 at 17, M >> 4 at 24
-    constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(F16WCfg::BN >> 3) << 17) |
+    constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(F16WCfg<>::BN >> 3) << 17) |
                                ((uint32_t)(BM >> 4) << 24);
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -72,12 +74,16 @@ __device__ __forceinline__ void mma_ss_f16w(uint32_t tmem_d, uint64_t da, uint64
         ::"r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accum));
 }
 
-template <bool EXTRA>
-__global__ void __launch_bounds__(F16WCfg::WARPS * 32, 1)
+// XFW transform warps: 2 (two rows a thread, 20 warps of 96 registers) or 4
+// (one row a thread, 22 warps of 80 registers: a faster split, a tighter
+// epilogue); the host picks 4 for long K, where the split's latency matters
+// more than the epilogue's registers.
+template <bool EXTRA, int XFW>
+__global__ void __launch_bounds__(F16WCfg<XFW>::WARPS * 32, 1)
 gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wh,
                  const __grid_constant__ CUtensorMap map_wl, const __grid_constant__ CUtensorMap map_y,
                  const F16Params fp) {
-    using C = F16WCfg;
+    using C = F16WCfg<XFW>;
     constexpr int BN = C::BN;
     const Params &p = fp.g;
     extern __shared__ uint8_t smem_raw[];
@@ -215,7 +221,7 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         }
     } else if (warp < C::EPI0) {
         // ------------------- x split in place: fp32 rows -> x_hi | x_lo (fp16)
-        // thread rows r0 = 32 w + lane and r0 + 64 (w = transform warp 0 / 1)
+        // thread rows r0 + XF_THREADS h, h < RPT
         const int r0 = (warp - C::XF0) * 32 + lane;
         const float sx = pow2f(f16_scale_exp(warp_amax(fp.x_parts, fp.n_parts)));
         uint32_t g = 0;
@@ -228,12 +234,12 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                 if (!__all_sync(0xffffffffu, w)) ok = false;
                 // both transform warps reach the named barrier below, also after
                 // an expired wait (they then convert whatever is there)
-                uint32_t hi[2][16], lo[2][16];
+                uint32_t hi[C::RPT][16], lo[C::RPT][16];
                 uint8_t *a = gbase + (tile_a(s) - base);
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < C::RPT; ++h) {
                     // fp32 row r: 128 B, 16-byte chunk c at c ^ (r & 7)
-                    const int r = r0 + 64 * h;
+                    const int r = r0 + C::XF_THREADS * h;
                     const uint8_t *arow = a + r * 128;
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
@@ -248,12 +254,12 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                     }
                 }
                 // all 128 rows read before any is overwritten
-                asm volatile("bar.sync 1, 64;" ::: "memory");
+                asm volatile("bar.sync 1, %0;" ::"n"(C::XF_THREADS) : "memory");
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
+                for (int h = 0; h < C::RPT; ++h) {
                     // x_hi row r at +0, x_lo at +8 KB: 64 B each, 16-byte chunk c
                     // at c ^ ((r >> 1) & 3) (64B swizzle)
-                    const int r = r0 + 64 * h;
+                    const int r = r0 + C::XF_THREADS * h;
                     uint8_t *hrow = a + r * 64;
                     uint8_t *lrow = hrow + C::A_BYTES / 2;
 #pragma unroll

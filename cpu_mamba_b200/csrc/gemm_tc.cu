@@ -1067,11 +1067,12 @@ static int launch_f16(const CUtensorMap &ma, const CUtensorMap &mwh, const CUten
 }
 
 // The wide F16X3 kernel (128 x 256 tiles): persistent, one CTA per SM.
-template <bool EXTRA>
+template <bool EXTRA, int XFW>
 static int launch_f16w(const CUtensorMap &ma, const CUtensorMap &mwh, const CUtensorMap &mwl,
                        const CUtensorMap &my, const tc::F16Params &fp, int64_t M, int64_t N,
                        cudaStream_t st) {
-    auto kern = tc::gemm_f16w_kernel<EXTRA>;
+    auto kern = tc::gemm_f16w_kernel<EXTRA, XFW>;
+    using CW = tc::F16WCfg<XFW>;
     constexpr size_t smem = tc::f16w_smem_bytes();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_f16w smem attribute: %s", cudaGetErrorString(e));
@@ -1081,14 +1082,13 @@ static int launch_f16w(const CUtensorMap &ma, const CUtensorMap &mwh, const CUte
         cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
         if (g_num_sms <= 0) g_num_sms = 148;
     }
-    const int64_t tiles = ceil_div(M, (int64_t)tc::BM) * ceil_div(N, (int64_t)tc::F16WCfg::BN);
+    const int64_t tiles = ceil_div(M, (int64_t)tc::BM) * ceil_div(N, (int64_t)CW::BN);
     const unsigned grid = (unsigned)(tiles < g_num_sms ? tiles : g_num_sms);
     cudaFuncAttributes fa{};
-    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess &&
-        fa.maxThreadsPerBlock < tc::F16WCfg::WARPS * 32)
+    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess && fa.maxThreadsPerBlock < CW::WARPS * 32)
         return fail(MB2_ERR_CUDA, "gemm_f16w_kernel: %d registers per thread allow only %d threads",
                     fa.numRegs, fa.maxThreadsPerBlock);
-    kern<<<grid, tc::F16WCfg::WARPS * 32, smem, st>>>(ma, mwh, mwl, my, fp);
+    kern<<<grid, CW::WARPS * 32, smem, st>>>(ma, mwh, mwl, my, fp);
     return check_launch("gemm_f16w_kernel");
 }
 
@@ -1134,8 +1134,13 @@ int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, 
         fp.n_parts = nparts;
         fp.w_inv = reinterpret_cast<const float *>(w16);
         const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS || ex.silu_from >= 0;
-        const int rc = extra ? launch_f16w<true>(ma, mwh, mwl, my, fp, M, N, st)
-                             : launch_f16w<false>(ma, mwh, mwl, my, fp, M, N, st);
+        // four transform warps for long K (out_proj: measured 0.190 -> 0.171 ms),
+        // two otherwise (in_proj and dt_proj were slower with four)
+        const bool xf4 = K >= 1024;
+        const int rc = extra ? (xf4 ? launch_f16w<true, 4>(ma, mwh, mwl, my, fp, M, N, st)
+                                    : launch_f16w<true, 2>(ma, mwh, mwl, my, fp, M, N, st))
+                             : (xf4 ? launch_f16w<false, 4>(ma, mwh, mwl, my, fp, M, N, st)
+                                    : launch_f16w<false, 2>(ma, mwh, mwl, my, fp, M, N, st));
         MB2_TRY(rc);
         *used = true;
         return MB2_OK;
