@@ -343,6 +343,8 @@ static int pipeline_head(const mb2_block &b, const Layout &l, const void *x, int
     EpiExtra in_ex = scratch_extra(l, ws), mid_ex = scratch_extra(l, ws);
     in_ex.row_scale = row_scale;
     in_ex.silu_from = di;       // the z half leaves in_proj as SiLU(z), the gate (:264)
+    in_ex.xsplit = ws + l.off_xc;   // free until the conv writes xc
+    in_ex.xsplit_bytes = l.off_xdbl - l.off_xc;
     mark(ev, 0, st);
     if (N > 0)
         MB2_TRY(linear_any(b.dtype, b.in_proj, x, l.dm, xz, 2 * di, N, 2 * di, l.dm, MB2_EPI_NONE,

@@ -15,15 +15,15 @@
 //     to shared memory and the MMAs read both operands from there (SS form).
 //     The split is made in place: a k-block of 32 fp32 K values per row
 //     (128 B, 128B swizzle, as TMA loads it) becomes x_hi and x_lo rows of 32
-//     fp16 (64 B each, 64B swizzle) in the same 16 KB; the two transform
-//     warps (two rows a thread) read their rows, meet at a named barrier,
-//     then write.
+//     fp16 (64 B each, 64B swizzle) in the same 16 KB; the transform warps
+//     read their rows, meet at a named barrier, then write.  Or x arrives
+//     split already (see XFW below).
 //   * P is single-buffered: at a segment boundary inside a tile the MMA warp
 //     issues the k-block's Q MMAs first and waits for P's drain only before
 //     its P MMAs; at a tile boundary it issues P first and waits for Q's drain
 //     before the Q MMAs, so the drains overlap MMAs either way.
 //   * 16 epilogue warps (four per TMEM lane quarter) drain 64 accumulator
-//     columns each into fp32 running sums; 20 warps of 96 registers.
+//     columns each into fp32 running sums.
 // Shared memory: 4 stages of (A fp32 -> x_hi | x_lo, 16 KB | W_hi 256 x 32
 // fp16, 16 KB | W_lo, 16 KB) = 192 KB, plus 32 KB of output staging (2 KB a
 // warp: 32 rows x 16 columns per TMA store).  Every mbarrier wait is bounded.
@@ -36,7 +36,7 @@ template <int XFW = 2> struct F16WCfg {
     static constexpr int XF0 = 2;              // transform warps from 2
     static constexpr int XF_WARPS = XFW;
     static constexpr int XF_THREADS = 32 * XF_WARPS;
-    static constexpr int RPT = 128 / XF_THREADS;   // rows a transform thread splits
+    static constexpr int RPT = XF_WARPS ? 128 / XF_THREADS : 0;   // rows a transform thread splits
     static constexpr int EPI0 = XF0 + XF_WARPS;    // 16 epilogue warps after them
     static constexpr int WARPS = EPI0 + 16;
     static constexpr int EPI_WARPS = 16;
@@ -77,12 +77,17 @@ __device__ __forceinline__ void mma_ss_f16w(uint32_t tmem_d, uint64_t da, uint64
 // XFW transform warps: 2 (two rows a thread, 20 warps of 96 registers) or 4
 // (one row a thread, 22 warps of 80 registers: a faster split, a tighter
 // epilogue); the host picks 4 for long K, where the split's latency matters
-// more than the epilogue's registers.
+// more than the epilogue's registers.  XFW = 0: x arrives split already
+// (split_rows_kernel: x_hi | x_lo fp16 planes with one power-of-two scale per
+// row); TMA loads both halves into the stage as the split would have left
+// them, no transform warps run, and the epilogue scales row m by its own
+// 2^-e_m (map_al: the x_lo plane; map_a the x_hi plane).
 template <bool EXTRA, int XFW>
 __global__ void __launch_bounds__(F16WCfg<XFW>::WARPS * 32, 1)
 gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wh,
                  const __grid_constant__ CUtensorMap map_wl, const __grid_constant__ CUtensorMap map_y,
-                 const F16Params fp) {
+                 const __grid_constant__ CUtensorMap map_al, const F16Params fp) {
+    constexpr bool PRE = XFW == 0;
     using C = F16WCfg<XFW>;
     constexpr int BN = C::BN;
     const Params &p = fp.g;
@@ -151,7 +156,12 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                     if (!mbar_wait(empty(s), ph ^ 1, 31)) { ok = false; break; }
                     mbar_expect_tx(full(s), C::STAGE_BYTES);
                     const int32_t kc = kb * C::BK;
-                    tma_load_2d(tile_a(s), &map_a, full(s), kc, (int32_t)m0);
+                    if (PRE) {
+                        tma_load_2d(tile_a(s), &map_a, full(s), kc, (int32_t)m0);
+                        tma_load_2d(tile_a(s) + C::A_BYTES / 2, &map_al, full(s), kc, (int32_t)m0);
+                    } else {
+                        tma_load_2d(tile_a(s), &map_a, full(s), kc, (int32_t)m0);
+                    }
                     tma_load_2d(tile_w(s, 0), &map_wh, full(s), kc, (int32_t)n0);
                     tma_load_2d(tile_w(s, 1), &map_wl, full(s), kc, (int32_t)n0);
                 }
@@ -168,7 +178,7 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                     const int rel = kb % C::SEG;
                     const int s = g % C::STAGES;
                     const uint32_t ph = (g / C::STAGES) & 1;
-                    ok = mbar_wait(full(s), ph, 32) && mbar_wait(xform(s), ph, 33);
+                    ok = mbar_wait(full(s), ph, 32) && (PRE || mbar_wait(xform(s), ph, 33));
                     if (!ok) break;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t ahi = tile_a(s), alo = ahi + C::A_BYTES / 2;
@@ -219,7 +229,7 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                 if (ok) mma_commit(q_full);
             }
         }
-    } else if (warp < C::EPI0) {
+    } else if (!PRE && warp < C::EPI0) {
         // ------------------- x split in place: fp32 rows -> x_hi | x_lo (fp16)
         // thread rows r0 + XF_THREADS h, h < RPT
         const int r0 = (warp - C::XF0) * 32 + lane;
@@ -234,7 +244,7 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                 if (!__all_sync(0xffffffffu, w)) ok = false;
                 // both transform warps reach the named barrier below, also after
                 // an expired wait (they then convert whatever is there)
-                uint32_t hi[C::RPT][16], lo[C::RPT][16];
+                uint32_t hi[C::RPT > 0 ? C::RPT : 1][16], lo[C::RPT > 0 ? C::RPT : 1][16];
                 uint8_t *a = gbase + (tile_a(s) - base);
 #pragma unroll
                 for (int h = 0; h < C::RPT; ++h) {
@@ -283,7 +293,7 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         const int ch = (warp - C::EPI0) >> 2;            // column quarter: 0-3
         const uint32_t lanes = (uint32_t)(q * 32) << 16;
         const uint32_t ccol = (uint32_t)(ch * C::ECOLS);
-        const float inv_x = pow2f(-f16_scale_exp(warp_amax(fp.x_parts, fp.n_parts)));
+        const float inv_x_tensor = PRE ? 1.0f : pow2f(-f16_scale_exp(warp_amax(fp.x_parts, fp.n_parts)));
         const float inv_w = *fp.w_inv;
         const uint32_t wst = out_base + (uint32_t)((warp - C::EPI0) * 32 * 64);  // one box
         uint8_t *wst_g = gbase + (wst - base);
@@ -331,6 +341,8 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             const bool row_ok = m_row < p.M;
             const float rscale = (EXTRA && p.row_scale && row_ok) ? p.row_scale[m_row] : 1.0f;
             const float *rrow = static_cast<const float *>(p.resid) + (row_ok ? m_row : 0) * p.ld_r;
+            // x's scale: one per tensor, or (pre-split) this row's own
+            const float inv_x = PRE ? (row_ok ? fp.x_row_inv[m_row] : 0.0f) : inv_x_tensor;
 #pragma unroll
             for (int cb = 0; cb < C::ECOLS / 32; ++cb) {
                 const int64_t c0 = n0 + ch * C::ECOLS + cb * 32;   // first output column

@@ -80,6 +80,7 @@ struct F16Params {
     int n_parts;
     const float *w_inv;             // 2^-ew (header of the split weight)
     const float *col_scale;         // CODES: the quantised weight's scale per output column
+    const float *x_row_inv;         // x split by rows (split_rows_kernel): 2^-e of each row
 };
 
 // Exponent e with amax * 2^e in [2^14, 2^15); 0 for zero or non-finite amax.

@@ -1070,7 +1070,7 @@ static int launch_f16(const CUtensorMap &ma, const CUtensorMap &mwh, const CUten
 template <bool EXTRA, int XFW>
 static int launch_f16w(const CUtensorMap &ma, const CUtensorMap &mwh, const CUtensorMap &mwl,
                        const CUtensorMap &my, const tc::F16Params &fp, int64_t M, int64_t N,
-                       cudaStream_t st) {
+                       cudaStream_t st, const CUtensorMap *mal = nullptr) {
     auto kern = tc::gemm_f16w_kernel<EXTRA, XFW>;
     using CW = tc::F16WCfg<XFW>;
     constexpr size_t smem = tc::f16w_smem_bytes();
@@ -1088,8 +1088,43 @@ static int launch_f16w(const CUtensorMap &ma, const CUtensorMap &mwh, const CUte
     if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess && fa.maxThreadsPerBlock < CW::WARPS * 32)
         return fail(MB2_ERR_CUDA, "gemm_f16w_kernel: %d registers per thread allow only %d threads",
                     fa.numRegs, fa.maxThreadsPerBlock);
-    kern<<<grid, CW::WARPS * 32, smem, st>>>(ma, mwh, mwl, my, fp);
+    kern<<<grid, CW::WARPS * 32, smem, st>>>(ma, mwh, mwl, my, mal ? *mal : ma, fp);
     return check_launch("gemm_f16w_kernel");
+}
+
+// x (M, K) fp32 -> x_hi, x_lo (M, K) fp16 and inv[m] = 2^-e_m, one warp per
+// row: e_m puts the row's largest |x| in [2^14, 2^15) (the F16X3 scale, per
+// row instead of per tensor), hi = fp16_rn(x 2^e_m), lo = fp16_rn(x 2^e_m - hi).
+// Rows are 16-byte aligned and K % 4 == 0 (the wide kernel's conditions).
+__global__ void split_rows_kernel(const float *__restrict__ x, int64_t ld, int64_t M, int64_t K,
+                                  __half *__restrict__ hi, __half *__restrict__ lo,
+                                  float *__restrict__ inv) {
+    const int lane = threadIdx.x & 31;
+    const int64_t wpb = blockDim.x >> 5;
+    for (int64_t m = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5); m < M; m += gridDim.x * wpb) {
+        const float4 *row = reinterpret_cast<const float4 *>(x + m * ld);
+        const int64_t k4 = K >> 2;
+        float mx = 0.0f;
+        for (int64_t i = lane; i < k4; i += 32) {
+            const float4 v = row[i];
+            mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const int e = tc::f16_scale_exp(mx);
+        const float sc = tc::pow2f(e);
+        if (lane == 0) inv[m] = tc::pow2f(-e);
+        uint2 *hrow = reinterpret_cast<uint2 *>(hi + m * K);
+        uint2 *lrow = reinterpret_cast<uint2 *>(lo + m * K);
+        for (int64_t i = lane; i < k4; i += 32) {
+            const float4 v = row[i];
+            const float a0 = v.x * sc, a1 = v.y * sc, a2 = v.z * sc, a3 = v.w * sc;
+            const uint32_t h01 = tc::pack_h2(a0, a1), h23 = tc::pack_h2(a2, a3);
+            const float2 f01 = tc::unpack_h2(h01), f23 = tc::unpack_h2(h23);
+            hrow[i] = make_uint2(h01, h23);
+            lrow[i] = make_uint2(tc::pack_h2(a0 - f01.x, a1 - f01.y), tc::pack_h2(a2 - f23.x, a3 - f23.y));
+        }
+    }
 }
 
 // fp32 GEMM through the F16X3 kernel; *used reports whether it ran.  parts:
@@ -1115,8 +1150,42 @@ int gemm_f16x3(const float *x, int64_t ld_x, const void *w16, const void *bias, 
     const __half *whi = reinterpret_cast<const __half *>(wb + kF16Header);
     const __half *wlo = whi + N * K;
     MB2_TRY(get_encode());
+    // many 256-wide column tiles: split x once, by rows, into the caller's scratch
+    const size_t split_need = (size_t)M * K * 2 * sizeof(__half) + (size_t)M * sizeof(float) + 256;
+    const bool presplit = wide && ceil_div(N, (int64_t)256) >= 4 && ex.xsplit &&
+                          ex.xsplit_bytes >= split_need && aligned(ex.xsplit, 256);
     int nparts = ex.amax_n;        // > 0: the kernel that wrote x left its maxima in parts
-    if (nparts <= 0) MB2_TRY(amax_parts(x, ld_x, M, K, parts, &nparts, st));
+    if (nparts <= 0 && !presplit) MB2_TRY(amax_parts(x, ld_x, M, K, parts, &nparts, st));
+    if (presplit) {
+        __half *xh = static_cast<__half *>(ex.xsplit);
+        __half *xl = xh + M * K;
+        float *inv = reinterpret_cast<float *>(reinterpret_cast<char *>(xl + M * K));
+        const int64_t blocks = ceil_div(M, (int64_t)8);
+        split_rows_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(
+            x, ld_x, M, K, xh, xl, inv);
+        MB2_TRY(check_launch("split_rows_kernel"));
+        CUtensorMap mah, mal, mwh, mwl, my;
+        MB2_TRY(make_map_sw64(&mah, xh, M, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 128));
+        MB2_TRY(make_map_sw64(&mal, xl, M, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 128));
+        MB2_TRY(make_map_sw64(&mwh, whi, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 256));
+        MB2_TRY(make_map_sw64(&mwl, wlo, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 256));
+        const bool remap = (n1 < N && off1 != 0) || (n2 < N && off2 != 0);
+        const bool tma_store = !remap && aligned(y, 16) && (ld_y * 4) % 16 == 0;
+        if (tma_store)
+            MB2_TRY(make_map_sw64(&my, y, M, N, ld_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32));
+        else my = mah;  // unused
+        tc::F16Params fp{};
+        fp.g = tc::Params{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0,
+                          ex.row_scale, ex.resid, ex.ld_r, 1, 0, ex.silu_from};
+        fp.w_inv = reinterpret_cast<const float *>(w16);
+        fp.x_row_inv = inv;
+        const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS || ex.silu_from >= 0;
+        const int rc = extra ? launch_f16w<true, 0>(mah, mwh, mwl, my, fp, M, N, st, &mal)
+                             : launch_f16w<false, 0>(mah, mwh, mwl, my, fp, M, N, st, &mal);
+        MB2_TRY(rc);
+        *used = true;
+        return MB2_OK;
+    }
     if (wide) {
         CUtensorMap ma, mwh, mwl, my;
         MB2_TRY(make_map(&ma, x, M, K, ld_x, false, 128));

@@ -45,6 +45,12 @@ struct EpiExtra {
     // loads its first weight tiles before that wait (the previous kernel
     // writes no weights)
     int pdl = 0;
+    // not an epilogue term: scratch where an fp32 projection with many
+    // 256-wide column tiles may place x split into fp16 halves once (M·K·4
+    // bytes + M·4 for the row scales) instead of splitting it in every
+    // column tile; null: split inside the GEMM
+    void *xsplit = nullptr;
+    size_t xsplit_bytes = 0;
 };
 enum { PDL_NONE = 0, PDL_CHAIN = 1, PDL_WEIGHTS_EARLY = 2 };
 
