@@ -28,11 +28,13 @@
 // fp16, 16 KB | W_lo, 16 KB) = 192 KB, plus 32 KB of output staging (2 KB a
 // warp: 32 rows x 16 columns per TMA store).  Every mbarrier wait is bounded.
 
-template <int XFW = 2> struct F16WCfg {
+template <int XFW = 2, bool CODES = false> struct F16WCfg {
     static constexpr int BN = 256;
     static constexpr int BK = 32;              // fp32 K values per k-block (one 128 B TMA box)
     static constexpr int SEG = 8;              // k-blocks per hi*hi segment (16 MMAs, as F16X3)
-    static constexpr int STAGES = 4;
+    // CODES: the weight is one plane of a quantised weight's integer codes
+    // (exact in fp16), so a stage is 32 KB and 6 fit
+    static constexpr int STAGES = CODES ? 6 : 4;
     static constexpr int XF0 = 2;              // transform warps from 2
     static constexpr int XF_WARPS = XFW;
     static constexpr int XF_THREADS = 32 * XF_WARPS;
@@ -46,14 +48,16 @@ template <int XFW = 2> struct F16WCfg {
     static constexpr uint32_t COL_Q = 256;
     static constexpr uint32_t A_BYTES = 128 * 128;       // 128 rows x 32 fp32
     static constexpr uint32_t W_BYTES = 256 * 64;        // 256 rows x 32 fp16
-    static constexpr uint32_t STAGE_BYTES = A_BYTES + 2 * W_BYTES;
+    static constexpr uint32_t STAGE_BYTES = A_BYTES + (CODES ? 1 : 2) * W_BYTES;
 };
 // output staging: 32 rows x 16 fp32 columns (one 64B-swizzled box) per epilogue warp
 constexpr size_t f16w_staging_bytes() { return (size_t)F16WCfg<>::EPI_WARPS * 32 * 16 * sizeof(float); }
-constexpr size_t f16w_smem_bytes() {
-    return 1024 + (size_t)F16WCfg<>::STAGES * F16WCfg<>::STAGE_BYTES + f16w_staging_bytes() + 256;
+template <bool CODES = false> constexpr size_t f16w_smem_bytes() {
+    return 1024 + (size_t)F16WCfg<2, CODES>::STAGES * F16WCfg<2, CODES>::STAGE_BYTES +
+           f16w_staging_bytes() + 256;
 }
-static_assert(f16w_smem_bytes() <= 232448, "wide F16X3 shared memory above the 227 KB per CTA");
+static_assert(f16w_smem_bytes<false>() <= 232448 && f16w_smem_bytes<true>() <= 232448,
+              "wide F16X3 shared memory above the 227 KB per CTA");
 
 // Shared-memory matrix descriptor of a K-major operand in the 64B-swizzled
 // layout (64-byte rows, 8-row atoms of 512 bytes; layout type 4).
@@ -82,13 +86,16 @@ __device__ __forceinline__ void mma_ss_f16w(uint32_t tmem_d, uint64_t da, uint64
 // row); TMA loads both halves into the stage as the split would have left
 // them, no transform warps run, and the epilogue scales row m by its own
 // 2^-e_m (map_al: the x_lo plane; map_a the x_hi plane).
-template <bool EXTRA, int XFW>
-__global__ void __launch_bounds__(F16WCfg<XFW>::WARPS * 32, 1)
+// CODES: W is a quantised weight's codes as fp16 (map_wh; map_wl unused) and
+// column n is multiplied by col_scale[n] in the epilogue, as in the 128-wide
+// kernel's CODES form: two MMAs per K step (x_hi q, x_lo q).
+template <bool EXTRA, int XFW, bool CODES = false>
+__global__ void __launch_bounds__(F16WCfg<XFW, CODES>::WARPS * 32, 1)
 gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_wh,
                  const __grid_constant__ CUtensorMap map_wl, const __grid_constant__ CUtensorMap map_y,
                  const __grid_constant__ CUtensorMap map_al, const F16Params fp) {
     constexpr bool PRE = XFW == 0;
-    using C = F16WCfg<XFW>;
+    using C = F16WCfg<XFW, CODES>;
     constexpr int BN = C::BN;
     const Params &p = fp.g;
     extern __shared__ uint8_t smem_raw[];
@@ -163,7 +170,7 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                         tma_load_2d(tile_a(s), &map_a, full(s), kc, (int32_t)m0);
                     }
                     tma_load_2d(tile_w(s, 0), &map_wh, full(s), kc, (int32_t)n0);
-                    tma_load_2d(tile_w(s, 1), &map_wl, full(s), kc, (int32_t)n0);
+                    if (!CODES) tma_load_2d(tile_w(s, 1), &map_wl, full(s), kc, (int32_t)n0);
                 }
             }
         }
@@ -192,10 +199,15 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
                     auto issue_q = [&]() {
 #pragma unroll
                         for (int kk = 0; kk < C::BK / 16; ++kk) {
-                            mma_ss_f16w(tmem + C::COL_Q, smem_desc64(ahi + kk * 32),
-                                        smem_desc64(bl + kk * 32), (kb > 0 || kk > 0) ? 1u : 0u);
-                            mma_ss_f16w(tmem + C::COL_Q, smem_desc64(alo + kk * 32),
-                                        smem_desc64(bh + kk * 32), 1u);
+                            if (CODES) {        // x_lo q (the codes are exact: no W_lo)
+                                mma_ss_f16w(tmem + C::COL_Q, smem_desc64(alo + kk * 32),
+                                            smem_desc64(bh + kk * 32), (kb > 0 || kk > 0) ? 1u : 0u);
+                            } else {
+                                mma_ss_f16w(tmem + C::COL_Q, smem_desc64(ahi + kk * 32),
+                                            smem_desc64(bl + kk * 32), (kb > 0 || kk > 0) ? 1u : 0u);
+                                mma_ss_f16w(tmem + C::COL_Q, smem_desc64(alo + kk * 32),
+                                            smem_desc64(bh + kk * 32), 1u);
+                            }
                         }
                     };
                     if (rel != 0) {
@@ -294,7 +306,7 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
         const uint32_t lanes = (uint32_t)(q * 32) << 16;
         const uint32_t ccol = (uint32_t)(ch * C::ECOLS);
         const float inv_x_tensor = PRE ? 1.0f : pow2f(-f16_scale_exp(warp_amax(fp.x_parts, fp.n_parts)));
-        const float inv_w = *fp.w_inv;
+        const float inv_w = CODES ? 1.0f : *fp.w_inv;
         const uint32_t wst = out_base + (uint32_t)((warp - C::EPI0) * 32 * 64);  // one box
         uint8_t *wst_g = gbase + (wst - base);
         float *Y = static_cast<float *>(p.y);
@@ -347,8 +359,16 @@ gemm_f16w_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constan
             for (int cb = 0; cb < C::ECOLS / 32; ++cb) {
                 const int64_t c0 = n0 + ch * C::ECOLS + cb * 32;   // first output column
                 float *v = acc + cb * 32;
+                if (CODES) {
+                    // column c0 + j's scale: loaded by lane j, broadcast by shuffles
+                    const float my_s = c0 + lane < p.N ? fp.col_scale[c0 + lane] : 0.0f;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = v[j] * inv_x * inv_w;
+                    for (int j = 0; j < 32; ++j)
+                        v[j] = (v[j] * inv_x) * __shfl_sync(0xffffffffu, my_s, j);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] = v[j] * inv_x * inv_w;
+                }
                 if (EXTRA && p.row_scale) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] *= rscale;

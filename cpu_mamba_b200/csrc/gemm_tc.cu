@@ -1067,13 +1067,13 @@ static int launch_f16(const CUtensorMap &ma, const CUtensorMap &mwh, const CUten
 }
 
 // The wide F16X3 kernel (128 x 256 tiles): persistent, one CTA per SM.
-template <bool EXTRA, int XFW>
+template <bool EXTRA, int XFW, bool CODES = false>
 static int launch_f16w(const CUtensorMap &ma, const CUtensorMap &mwh, const CUtensorMap &mwl,
                        const CUtensorMap &my, const tc::F16Params &fp, int64_t M, int64_t N,
                        cudaStream_t st, const CUtensorMap *mal = nullptr) {
-    auto kern = tc::gemm_f16w_kernel<EXTRA, XFW>;
-    using CW = tc::F16WCfg<XFW>;
-    constexpr size_t smem = tc::f16w_smem_bytes();
+    auto kern = tc::gemm_f16w_kernel<EXTRA, XFW, CODES>;
+    using CW = tc::F16WCfg<XFW, CODES>;
+    constexpr size_t smem = tc::f16w_smem_bytes<CODES>();
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(MB2_ERR_CUDA, "gemm_f16w smem attribute: %s", cudaGetErrorString(e));
     if (g_num_sms == 0) {
@@ -1255,6 +1255,53 @@ int gemm_f16x3_codes(const float *x, int64_t ld_x, const void *codes16, const fl
     if (!aligned(x, 16) || (ld_x * 4) % 16 != 0 || K % 8 != 0 || !aligned(codes16, 256)) return MB2_OK;
     if (ex.resid && (!aligned(ex.resid, 16) || ex.ld_r % 4 != 0 || N % 4 != 0)) return MB2_OK;
     MB2_TRY(get_encode());
+    if (N >= 256) {
+        // 128 x 256 tiles; x split once by rows when there are many column tiles
+        const size_t split_need = (size_t)M * K * 2 * sizeof(__half) + (size_t)M * sizeof(float) + 256;
+        const bool presplit = ceil_div(N, (int64_t)256) >= 4 && ex.xsplit &&
+                              ex.xsplit_bytes >= split_need && aligned(ex.xsplit, 256);
+        int nparts = ex.amax_n;
+        if (nparts <= 0 && !presplit) MB2_TRY(amax_parts(x, ld_x, M, K, parts, &nparts, st));
+        CUtensorMap ma, mal, mw, my;
+        tc::F16Params fp{};
+        if (presplit) {
+            __half *xh = static_cast<__half *>(ex.xsplit);
+            __half *xl = xh + M * K;
+            float *inv = reinterpret_cast<float *>(xl + M * K);
+            const int64_t blocks = ceil_div(M, (int64_t)8);
+            split_rows_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, st>>>(
+                x, ld_x, M, K, xh, xl, inv);
+            MB2_TRY(check_launch("split_rows_kernel"));
+            MB2_TRY(make_map_sw64(&ma, xh, M, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 128));
+            MB2_TRY(make_map_sw64(&mal, xl, M, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 128));
+            fp.x_row_inv = inv;
+        } else {
+            MB2_TRY(make_map(&ma, x, M, K, ld_x, false, 128));
+            mal = ma;
+            fp.x_parts = parts;
+            fp.n_parts = nparts;
+        }
+        MB2_TRY(make_map_sw64(&mw, codes16, N, K, K, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 256));
+        const bool remap = (n1 < N && off1 != 0) || (n2 < N && off2 != 0);
+        const bool tma_store = !remap && aligned(y, 16) && (ld_y * 4) % 16 == 0;
+        if (tma_store)
+            MB2_TRY(make_map_sw64(&my, y, M, N, ld_y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, 32));
+        else my = ma;  // unused
+        fp.g = tc::Params{y, ld_y, bias, M, N, K, n1, n2, off1, off2, epi, tma_store ? 1 : 0,
+                          ex.row_scale, ex.resid, ex.ld_r, 1, 0, ex.silu_from};
+        fp.col_scale = col_scale;
+        const bool extra = ex.row_scale || ex.resid || epi == MB2_EPI_SOFTPLUS || ex.silu_from >= 0;
+        int rc;
+        if (presplit)
+            rc = extra ? launch_f16w<true, 0, true>(ma, mw, mw, my, fp, M, N, st, &mal)
+                       : launch_f16w<false, 0, true>(ma, mw, mw, my, fp, M, N, st, &mal);
+        else
+            rc = extra ? launch_f16w<true, 2, true>(ma, mw, mw, my, fp, M, N, st)
+                       : launch_f16w<false, 2, true>(ma, mw, mw, my, fp, M, N, st);
+        MB2_TRY(rc);
+        *used = true;
+        return MB2_OK;
+    }
     int nparts = ex.amax_n;
     if (nparts <= 0) MB2_TRY(amax_parts(x, ld_x, M, K, parts, &nparts, st));
     CUtensorMap ma, mw, my;
