@@ -335,6 +335,10 @@ static void mark(cudaEvent_t *ev, int i, cudaStream_t st) {
     if (ev) cudaEventRecord(ev[i], st);
 }
 
+// Where the gate's SiLU(z) is applied: in in_proj's epilogue (fp32) or in the
+// scan's output pass (bf16).
+static bool z_in_proj(const mb2_block &b) { return b.dtype == MB2_F32; }
+
 static int pipeline_head(const mb2_block &b, const Layout &l, const void *x, int64_t batch,
                          int64_t seqlen, void *conv_tail, char *ws, cudaStream_t st,
                          const float *row_scale, cudaEvent_t *ev = nullptr) {
@@ -342,7 +346,9 @@ static int pipeline_head(const mb2_block &b, const Layout &l, const void *x, int
     const int64_t N = l.N, di = l.di, S = l.S, R = l.R;
     EpiExtra in_ex = scratch_extra(l, ws), mid_ex = scratch_extra(l, ws);
     in_ex.row_scale = row_scale;
-    in_ex.silu_from = di;       // the z half leaves in_proj as SiLU(z), the gate (:264)
+    // fp32: the z half leaves in_proj as SiLU(z), the gate (:264); the bf16
+    // GEMM's four epilogue warps are the slower place for it (the scan gates)
+    in_ex.silu_from = z_in_proj(b) ? di : -1;
     in_ex.xsplit = ws + l.off_xc;   // free until the conv writes xc
     in_ex.xsplit_bytes = l.off_xdbl - l.off_xc;
     mark(ev, 0, st);
@@ -405,12 +411,12 @@ static int pipeline_tail(const mb2_block &b, const Layout &l, void *out, int64_t
                            (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di, b.A_log,
                            b.D, nullptr, h_last, xc, di, batch, seqlen, di, S, st,
                            reinterpret_cast<float *>(ws + l.off_seg), l.seg_bytes, y_max,
-                           SCAN_Z_ACT | SCAN_DT_SCRATCH));
+                           (z_in_proj(b) ? SCAN_Z_ACT : 0) | SCAN_DT_SCRATCH));
     else
         MB2_TRY(scan_fused(b.dtype, xc, di, xdbl, l.ldx, (char *)xdbl + l.RB * es, l.ldx,
                            (char *)xdbl + l.RC * es, l.ldx, (char *)xz + di * es, 2 * di,
                            dt_weight(b), b.dt_proj.bias, b.A_log, b.D, nullptr, h_last, xc, di,
-                           batch, seqlen, di, S, R, st, y_max, SCAN_Z_ACT));
+                           batch, seqlen, di, S, R, st, y_max, z_in_proj(b) ? SCAN_Z_ACT : 0));
     mark(ev, 5, st);
     if (y_max) {
         out_ex.amax_parts = reinterpret_cast<float *>(y_max);
