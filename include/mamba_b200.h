@@ -176,10 +176,11 @@ int mb2_split_tf32(const float *w, float *out, int64_t numel,
  * round-to-nearest, so the rounding error stays that of an fp32 GEMM at any K.
  *   x: (M, ld_x) float32, rows 16-byte aligned   y: (M, ld_y) float32
  *   w_f16: mb2_split_f16's output for W (N, K), 256-byte aligned; K % 8 == 0
- *   sm_pair: 1 = 256 x 128 output tiles on pairs of SMs (cta_group::2: each
- *   SM of a pair loads half of W's tile), 0 or -1 = 128 x 128 tiles on single
- *   SMs (the default, what mb2_block_forward uses: 8-13 % faster on the
- *   block's projections); both give bit-identical results
+ *   sm_pair: -1 (the default, what mb2_block_forward uses) = 128 x 256 output
+ *   tiles with 256-wide MMAs when N >= 256, else as 0; 0 = 128 x 128 tiles on
+ *   single SMs; 1 = 256 x 128 tiles on pairs of SMs (cta_group::2: each SM of
+ *   a pair loads half of W's tile; bit-identical with 0, 8-13 % slower).  All
+ *   are fp32-faithful (same segment sums of the same products).
  *   scratch: mb2_linear_f16_scratch_bytes() of device memory (x's partial maxima)
  * No counterpart in the reference (its projections are torch's fp32 GEMMs,
  * _mamba.py:67,74,84); mb2_block_forward uses it for in_proj, x_proj and
