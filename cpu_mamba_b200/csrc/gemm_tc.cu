@@ -70,12 +70,15 @@ template <> struct Cfg<F32X3> {
     static constexpr int A_COL = 3 * BN;      // split-A slot l at 384 + 64 l (hi), +32 (lo)
     static constexpr int WARPS = 10;
     static constexpr int EPI0 = 6;            // first epilogue warp
+    static constexpr int EPG = 1;             // epilogue warps per TMEM lane quarter
     static constexpr int SPLIT = 1;           // output staged in one piece
 };
 // BF16: 128 x 256 tiles (N = 256 MMAs: the 128-wide ones ran the tensor pipe
 // at about half its rate), 4-deep ring of (A, W) tiles, two 256-column
 // accumulators (all 512 TMEM columns) so the MMAs of the next tile overlap the
-// epilogue of the previous one; the output is staged in two column halves.
+// epilogue of the previous one.  Eight epilogue warps, two per TMEM lane
+// quarter (one per 128-column half), each staging its output 64 columns at a
+// time: with few k-blocks (dt_proj, K = 48) the tile's drain is the bound.
 template <> struct Cfg<BF16> {
     static constexpr int BN = 256;
     static constexpr int STAGES = 4;
@@ -88,12 +91,14 @@ template <> struct Cfg<BF16> {
     static constexpr int ACC_COLS = BN;
     static constexpr int TMEM_COLS = 512;
     static constexpr int A_COL = 0;
-    static constexpr int WARPS = 6;
+    static constexpr int WARPS = 10;
     static constexpr int EPI0 = 2;
-    static constexpr int SPLIT = 2;
+    static constexpr int EPG = 2;
+    static constexpr int SPLIT = 2;           // parts of a warp's columns staged at a time
 };
 
-// shared memory: ring | output staging (BM x BN/SPLIT of TO) | barriers
+// shared memory: ring | output staging (BM x BN/SPLIT of TO: 4 EPG warps of
+// 32 rows x BN/(EPG SPLIT) columns) | barriers
 template <int MODE, typename TO>
 __host__ __device__ constexpr size_t staging_bytes() {
     return (size_t)BM * (Cfg<MODE>::BN / Cfg<MODE>::SPLIT) * sizeof(TO);
@@ -369,7 +374,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         for (int l = 0; l < C::LO; ++l) mbar_init(a_empty(l), 1);
         for (int b = 0; b < C::NACC; ++b) {
             mbar_init(acc_full(b), 1);
-            mbar_init(acc_empty(b), 128);
+            mbar_init(acc_empty(b), 128 * C::EPG);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -529,16 +534,20 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const int q = warp & 3;                 // TMEM lane quarter this warp may read
         constexpr int VEC = 16 / (int)sizeof(TO);     // outputs per 16-byte chunk
         constexpr int BOXC = 128 / (int)sizeof(TO);   // columns per 128-byte staging row
-        constexpr int HCOLS = BN / C::SPLIT;          // columns staged at a time
+        constexpr int WCOLS = BN / C::EPG;            // accumulator columns of this warp
+        constexpr int HCOLS = WCOLS / C::SPLIT;       // columns staged at a time
         constexpr int CBH = HCOLS / 32;               // 32-column blocks per staged part
+        static_assert(HCOLS % BOXC == 0 || HCOLS < BOXC, "staging boxes");
+        // this warp's column group: columns cg0 .. cg0 + WCOLS of the tile
+        const int cg0 = ((warp - C::EPI0) >> 2) * WCOLS;
         // this warp's staging: HCOLS / BOXC boxes of 32 rows x 128 B, 128B-swizzled
-        const uint32_t wst = out_base + (uint32_t)(q * 32 * HCOLS * sizeof(TO));
+        const uint32_t wst = out_base + (uint32_t)((warp - C::EPI0) * 32 * HCOLS * sizeof(TO));
         uint8_t *wst_g = gbase + (wst - base);
         TO *Y = static_cast<TO *>(p.y);
         const TO *bias = static_cast<const TO *>(p.bias);
         // write staged part `part` (columns part * HCOLS ...) of this warp's 32 rows
         auto flush = [&](int part, int64_t m0, int64_t n0, int z) {
-            const int64_t c0 = (int64_t)part * HCOLS;
+            const int64_t c0 = cg0 + (int64_t)part * HCOLS;
             if (p.tma_store) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
@@ -594,7 +603,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             const TO *rrow = static_cast<const TO *>(p.resid) + (row_ok ? m_row : 0) * p.ld_r;
             uint32_t ra[32], rb[32], rc[32];
 #pragma unroll 1
-            for (int cb = 0; cb < BN / 32; ++cb) {
+            for (int cb = 0; cb < WCOLS / 32; ++cb) {
+                const int cbase = cg0 + cb * 32;     // tile column of this 32-column block
                 if (C::SPLIT > 1 && cb > 0 && cb % CBH == 0) {
                     // staging full: store the finished part, then reuse the buffer
                     flush(cb / CBH - 1, m0, n0, z);
@@ -604,15 +614,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 float v[32];
                 if (MODE == F32X3) {
                     // the three accumulators of this 32-column block in one round trip
-                    tmem_ld32_async(acc + cb * 32, ra);
-                    tmem_ld32_async(acc + BN + cb * 32, rb);
-                    tmem_ld32_async(acc + 2 * BN + cb * 32, rc);
+                    tmem_ld32_async(acc + cbase, ra);
+                    tmem_ld32_async(acc + BN + cbase, rb);
+                    tmem_ld32_async(acc + 2 * BN + cbase, rc);
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 32; ++j)
                         v[j] = (__uint_as_float(ra[j]) + __uint_as_float(rb[j])) + __uint_as_float(rc[j]);
                 } else {
-                    tmem_ld32_async(acc + cb * 32, ra);
+                    tmem_ld32_async(acc + cbase, ra);
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(ra[j]);
@@ -628,7 +638,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 if (bias) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        const int64_t n = n0 + cb * 32 + j;
+                        const int64_t n = n0 + cbase + j;
                         v[j] += (n < p.N) ? io<TO>::to_f(bias[n]) : 0.0f;
                     }
                 }
@@ -638,9 +648,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v[j] = softplus_f(io<TO>::round(v[j]));
                 }
-                if (EXTRA && p.silu_from >= 0 && n0 + cb * 32 + 31 >= p.silu_from) {
+                if (EXTRA && p.silu_from >= 0 && n0 + cbase + 31 >= p.silu_from) {
                     // in_proj's z half: SiLU(z) on the value stored in TO
-                    const int64_t nb = n0 + cb * 32;
+                    const int64_t nb = n0 + cbase;
                     if (nb >= p.silu_from) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) v[j] = silu_f(io<TO>::round(v[j]));
@@ -654,7 +664,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                     // (the host guarantees 16-byte rows and N % VEC == 0)
 #pragma unroll
                     for (int c = 0; c < 32 / VEC; ++c) {
-                        const int64_t nb = n0 + cb * 32 + c * VEC;
+                        const int64_t nb = n0 + cbase + c * VEC;
                         if (nb < p.N) {
                             const uint4 u = *reinterpret_cast<const uint4 *>(rrow + nb);
                             const TO *e = reinterpret_cast<const TO *>(&u);
