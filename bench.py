@@ -410,10 +410,8 @@ STAGES = ("in_proj", "conv1d_silu", "x_proj", "dt_proj", "scan", "out_proj")
 def profile_stages(m, x, cfg, dtype, steps):
     """Per-stage CUDA-event durations of the block forward's own launches
     (mb2_block_forward_profile: events between its six stages on one
-    stream), averaged over up to 20 forwards after one untimed one."""
-    from cpu_mamba_b200.quant import QuantizedLinear
-    if any(isinstance(getattr(m, n), QuantizedLinear) for n in ("in_proj", "x_proj", "dt_proj", "out_proj")):
-        return {}
+    stream), averaged over up to 20 forwards after one untimed one; quantised
+    blocks included (their stages hold the per-call code conversions)."""
     times = {k: [] for k in STAGES}
     n = max(3, min(steps, 20))
     with torch.no_grad():
@@ -504,8 +502,10 @@ def roofline(stages, cfg, hbm_gbs, bf16_tflops, src, ms_per_step):
              "peak_source": f"{src} bf16 dense"}
         if cfg["dtype"] == "f32":
             # fp32-faithful path (F16X3): three fp16 MMAs per multiply-add, at the
-            # tensor core's fp16 rate (= its bf16 rate)
-            ex = 3 * flops[top] / t / 1e12
+            # tensor core's fp16 rate (= its bf16 rate); two for int8 / int4
+            # codes (exact in fp16: no W_lo term)
+            mmas = 2 if cfg.get("quant") in ("int8", "int4") else 3
+            ex = mmas * flops[top] / t / 1e12
             r["tensor_pipe"] = {"f16_tflops_executed": ex, "f16_peak": bf16_tflops,
                                 "frac": ex / bf16_tflops,
                                 "peak_source": f"{src} bf16 dense (fp16 rate)"}
