@@ -512,9 +512,18 @@ def roofline(stages, cfg, hbm_gbs, bf16_tflops, src, ms_per_step):
         r["block"] = block
         return r
     ach = nbytes[top] / t / 1e9
-    return {"kernel": top, "bound": "hbm", "achieved": ach, "peak": hbm_gbs, "unit": "GB/s",
-            "frac": ach / hbm_gbs, "traffic": traffic, "peak_source": f"{src} HBM copy",
-            "block": block}
+    r = {"kernel": top, "bound": "hbm", "achieved": ach, "peak": hbm_gbs, "unit": "GB/s",
+         "frac": ach / hbm_gbs, "traffic": traffic, "peak_source": f"{src} HBM copy",
+         "block": block}
+    if top == "scan":
+        # the scan's other bound: d_state exponentials per token and channel on
+        # the MUFU pipe, 16 ex2 per clock per SM (148 SMs at the 1965 MHz
+        # maximum clock: an upper bound on the rate, so frac is a lower bound)
+        ex2 = N * di * S / t
+        peak = 16 * 148 * 1965e6
+        r["mufu"] = {"ex2_per_s": ex2, "peak_per_s": peak, "frac": ex2 / peak,
+                     "note": "d_state ex2 per token-channel (softplus and gate not counted)"}
+    return r
 
 
 # ------------------------------------------------------- reference arm / CPU
