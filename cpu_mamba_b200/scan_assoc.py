@@ -26,7 +26,13 @@ def selective_scan_assoc(x, dt, A, Bp, Cp, D):
 
 
 def selective_scan_assoc_chunked(x, dt, A, Bp, Cp, D, chunk_T: int = 32):
-    """Chunked variant of the reference (scan_assoc.py:81-132); same result."""
+    """Chunked variant of the reference (scan_assoc.py:81-132); same result.
+
+    The reference cuts T into chunks of chunk_T to bound the intermediates of
+    its recursive doubling (O(chunk_T) extra tensors per chunk, h carried
+    across chunks).  The GPU kernel walks T with h in registers and needs no
+    intermediates at any T, so there is nothing for chunk_T to bound; it is
+    checked and otherwise has no effect."""
     if chunk_T <= 0:
         raise ValueError("chunk_T must be positive")
     return selective_scan_assoc(x, dt, A, Bp, Cp, D)
